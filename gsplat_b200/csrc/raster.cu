@@ -1,0 +1,635 @@
+// Tile-based front-to-back alpha compositing of projected splats, forward and
+// backward.
+//
+// Reference behaviour: gsplat/cuda/csrc/RasterizeToPixels3DGSFwd.cu:40-213 and
+// RasterizeToPixels3DGSBwd.cu:38-301 (per-pixel rules: sigma = 0.5 (a dx^2 +
+// c dy^2) + b dx dy, alpha = min(0.99, o exp(-sigma)), skip when sigma < 0 or
+// alpha < 1/255, stop before the splat that would take T to <= 1e-4, last_ids =
+// index of the last contributing splat; backward walks the same list back to
+// front recovering T by division).
+//
+// Design for sm_100a:
+//  * One CTA per (image, tile). Splats of the tile's range are staged in shared
+//    memory in batches of 256 as 32-byte records plus their colours.
+//  * While staging, each splat gets a conservative pixel-space box of the region
+//    where its alpha can reach 1/255. Every warp then compacts the batch into its
+//    own list of splats whose box meets the warp's pixel rectangle (ballot +
+//    popc), so warps never evaluate splats that cannot touch their pixels.
+//    The box is inflated by 1% plus half a pixel; outside it alpha is below the
+//    threshold by more than the rounding of the exp evaluation.
+//  * Backward threads own PPT pixels each: the per-splat gradient is summed over
+//    those pixels in registers before the warp butterfly, so the shuffle cost
+//    per (pixel, splat) pair drops by PPT. One lane then issues the atomics.
+//  * Channel counts are processed in chunks of at most 32 (kernels are
+//    instantiated for 1-8, 16 and 32 channels) with strided colour access, so no
+//    padding copies are made.
+#include "common.cuh"
+#include "gsb_internal.h"
+
+namespace gsb {
+
+constexpr int kBatch = 256;
+
+struct RasterParams {
+    uint32_t I, n_isects;
+    const float *means2d, *conics, *colors, *opacities, *backgrounds;
+    const bool *masks;
+    uint32_t W, H, tile_size, tile_w, tile_h;
+    const int32_t *offsets, *flatten_ids;
+    uint32_t cstride; // floats between consecutive splats' colours (total channels)
+    uint32_t coff;    // first channel of this chunk
+    // forward outputs
+    float *renders; // [I, H, W, cstride]
+    float *alphas;  // [I, H, W]
+    int32_t *last_ids;
+    bool write_alpha;
+    // backward inputs / outputs
+    const float *v_renders, *v_alphas;
+    float *v_means2d, *v_conics, *v_colors, *v_opacities, *v_means2d_abs;
+    bool first_chunk;
+};
+
+struct __align__(16) SplatRec {
+    float x, y, o, a;
+    float b, c, pad0, pad1;
+};
+
+struct RasterSmem {
+    int32_t *ids;
+    SplatRec *recs;
+    float4 *boxes;
+    float *colors;
+    uint8_t *lists; // [nwarps][kBatch]
+};
+
+template <int CDIM> __host__ __device__ constexpr size_t raster_smem_bytes(int nwarps) {
+    return (size_t)kBatch * sizeof(SplatRec) + (size_t)kBatch * sizeof(float4) +
+           (size_t)kBatch * sizeof(int32_t) + (size_t)kBatch * CDIM * sizeof(float) +
+           (size_t)nwarps * kBatch;
+}
+
+template <int CDIM> __device__ __forceinline__ RasterSmem carve(unsigned char *base) {
+    RasterSmem s;
+    s.recs = reinterpret_cast<SplatRec *>(base);
+    base += kBatch * sizeof(SplatRec);
+    s.boxes = reinterpret_cast<float4 *>(base);
+    base += kBatch * sizeof(float4);
+    s.ids = reinterpret_cast<int32_t *>(base);
+    base += kBatch * sizeof(int32_t);
+    s.colors = reinterpret_cast<float *>(base);
+    base += kBatch * CDIM * sizeof(float);
+    s.lists = reinterpret_cast<uint8_t *>(base);
+    return s;
+}
+
+// Stage splat `g` into slot i: record, colours and the culling box
+// (x_min, x_max, y_min, y_max) in pixel-centre coordinates.
+template <int CDIM>
+__device__ __forceinline__ void stage_splat(const RasterParams &p, const RasterSmem &s, int i,
+                                            int32_t g) {
+    s.ids[i] = g;
+    const float x = p.means2d[(size_t)g * 2], y = p.means2d[(size_t)g * 2 + 1];
+    const float a = p.conics[(size_t)g * 3], b = p.conics[(size_t)g * 3 + 1],
+                c = p.conics[(size_t)g * 3 + 2];
+    const float o = p.opacities[g];
+    SplatRec r;
+    r.x = x;
+    r.y = y;
+    r.o = o;
+    r.a = a;
+    r.b = b;
+    r.c = c;
+    r.pad0 = 0.f;
+    r.pad1 = 0.f;
+    s.recs[i] = r;
+    const float *cp = p.colors + (size_t)g * p.cstride + p.coff;
+#pragma unroll
+    for (int k = 0; k < CDIM; ++k) s.colors[i * CDIM + k] = cp[k];
+    float4 box;
+    const float det = a * c - b * b;
+    const float o255 = o * 255.f;
+    if (det > 0.f && a > 0.f && o255 > 1.0001f) {
+        const float lvl = 2.f * __logf(o255);
+        const float hx = sqrtf(lvl * c / det) * 1.01f + 0.5f;
+        const float hy = sqrtf(lvl * a / det) * 1.01f + 0.5f;
+        box = make_float4(x - hx, x + hx, y - hy, y + hy);
+    } else if (o255 < 0.9999f && det > 0.f && a > 0.f) {
+        box = make_float4(1e30f, -1e30f, 1e30f, -1e30f); // never reaches the threshold
+    } else {
+        box = make_float4(-1e30f, 1e30f, -1e30f, 1e30f); // no culling
+    }
+    s.boxes[i] = box;
+}
+
+// Pixel-space rectangle of the warp's inside pixels (pixel centres); empty when
+// the warp has none.
+struct WarpRect {
+    float x0, x1, y0, y1;
+    bool any;
+};
+
+__device__ __forceinline__ WarpRect warp_rect(bool has, float px0, float px1, float py0, float py1) {
+    float a = has ? px0 : 1e30f, b = has ? px1 : -1e30f, c = has ? py0 : 1e30f, d = has ? py1 : -1e30f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a = fminf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+        c = fminf(c, __shfl_xor_sync(0xffffffffu, c, o));
+        d = fmaxf(d, __shfl_xor_sync(0xffffffffu, d, o));
+    }
+    WarpRect r;
+    r.x0 = a;
+    r.x1 = b;
+    r.y0 = c;
+    r.y1 = d;
+    r.any = __any_sync(0xffffffffu, has);
+    return r;
+}
+
+__device__ __forceinline__ bool box_hits(const float4 &bx, const WarpRect &r) {
+    return !(bx.y < r.x0 || bx.x > r.x1 || bx.w < r.y0 || bx.z > r.y1);
+}
+
+// Shared per-pair evaluation: identical in forward and backward so both make the
+// same decisions.
+struct PairEval {
+    float dx, dy, sigma, vis, alpha;
+};
+
+__device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float py) {
+    PairEval e;
+    e.dx = r.x - px;
+    e.dy = r.y - py;
+    e.sigma = 0.5f * (r.a * e.dx * e.dx + r.c * e.dy * e.dy) + r.b * e.dx * e.dy;
+    e.vis = __expf(-e.sigma);
+    e.alpha = fminf(kMaxAlpha, r.o * e.vis);
+    return e;
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+template <int CDIM, int PPT>
+__global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int nwarps = blockDim.x >> 5;
+    const RasterSmem s = carve<CDIM>(smem_raw);
+    const uint32_t image = blockIdx.y;
+    const uint32_t tile = blockIdx.x;
+    const uint32_t tx0 = (tile % p.tile_w) * p.tile_size, ty0 = (tile / p.tile_w) * p.tile_size;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t tpix = p.tile_size * p.tile_size;
+
+    float px[PPT], py[PPT], T[PPT], out[PPT][CDIM];
+    int32_t cur[PPT];
+    bool inside[PPT], done[PPT];
+    uint32_t pid[PPT];
+    bool has = false;
+    float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        const uint32_t q = threadIdx.x * PPT + k;
+        const uint32_t i = ty0 + q / p.tile_size, j = tx0 + q % p.tile_size;
+        inside[k] = q < tpix && i < p.H && j < p.W;
+        px[k] = (float)j + 0.5f;
+        py[k] = (float)i + 0.5f;
+        pid[k] = i * p.W + j;
+        T[k] = 1.f;
+        cur[k] = 0;
+        done[k] = !inside[k];
+#pragma unroll
+        for (int c = 0; c < CDIM; ++c) out[k][c] = 0.f;
+        if (inside[k]) {
+            has = true;
+            rx0 = fminf(rx0, px[k]);
+            rx1 = fmaxf(rx1, px[k]);
+            ry0 = fminf(ry0, py[k]);
+            ry1 = fmaxf(ry1, py[k]);
+        }
+    }
+    const WarpRect wr = warp_rect(has, rx0, rx1, ry0, ry1);
+    const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
+
+    const size_t tile_flat = (size_t)image * p.tile_w * p.tile_h + tile;
+    bool masked = p.masks != nullptr && !p.masks[tile_flat];
+    if (!masked) {
+        const int32_t start = p.offsets[tile_flat];
+        const int32_t end = (image == p.I - 1 && tile == p.tile_w * p.tile_h - 1)
+                                ? (int32_t)p.n_isects
+                                : p.offsets[tile_flat + 1];
+        uint8_t *mylist = s.lists + warp * kBatch;
+        for (int32_t bstart = start; bstart < end; bstart += kBatch) {
+            bool all_done = true;
+#pragma unroll
+            for (int k = 0; k < PPT; ++k) all_done &= done[k];
+            if (__syncthreads_count(all_done) == (int)blockDim.x) break;
+            const int nb = min(kBatch, end - bstart);
+            for (int i = threadIdx.x; i < nb; i += blockDim.x)
+                stage_splat<CDIM>(p, s, i, p.flatten_ids[bstart + i]);
+            __syncthreads();
+            // per-warp list of splats that can touch this warp's live pixels
+            int cnt = 0;
+            const bool warp_live = wr.any && !__all_sync(0xffffffffu, all_done);
+            if (warp_live) {
+                for (int base = 0; base < nb; base += 32) {
+                    const int i = base + lane;
+                    const bool hit = i < nb && box_hits(s.boxes[i], wr);
+                    const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+                    if (hit) mylist[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint8_t)i;
+                    cnt += __popc(bal);
+                }
+            }
+            __syncwarp();
+            for (int li = 0; li < cnt; ++li) {
+                bool stop = true;
+#pragma unroll
+                for (int k = 0; k < PPT; ++k) stop &= done[k];
+                if (stop) break;
+                const int i = mylist[li];
+                const SplatRec r = s.recs[i];
+#pragma unroll
+                for (int k = 0; k < PPT; ++k) {
+                    if (done[k]) continue;
+                    const PairEval e = eval_pair(r, px[k], py[k]);
+                    if (e.sigma < 0.f || e.alpha < kAlphaThreshold) continue;
+                    const float next_T = T[k] * (1.f - e.alpha);
+                    if (next_T <= kTransmittanceThreshold) {
+                        done[k] = true;
+                        continue;
+                    }
+                    const float w = e.alpha * T[k];
+#pragma unroll
+                    for (int c = 0; c < CDIM; ++c) out[k][c] += s.colors[i * CDIM + c] * w;
+                    cur[k] = bstart + i;
+                    T[k] = next_T;
+                }
+            }
+        }
+    }
+    const size_t img_pix = (size_t)image * p.H * p.W;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        if (!inside[k]) continue;
+        const size_t pix = img_pix + pid[k];
+        float *o = p.renders + pix * p.cstride + p.coff;
+        if (masked) {
+#pragma unroll
+            for (int c = 0; c < CDIM; ++c) o[c] = bg ? bg[c] : 0.f;
+            if (p.write_alpha) {
+                p.alphas[pix] = 0.f;
+                p.last_ids[pix] = 0;
+            }
+            continue;
+        }
+#pragma unroll
+        for (int c = 0; c < CDIM; ++c) o[c] = bg ? out[k][c] + T[k] * bg[c] : out[k][c];
+        if (p.write_alpha) {
+            p.alphas[pix] = 1.f - T[k];
+            p.last_ids[pix] = cur[k];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------
+template <int CDIM, int PPT>
+__global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const RasterSmem s = carve<CDIM>(smem_raw);
+    const uint32_t image = blockIdx.y;
+    const uint32_t tile = blockIdx.x;
+    const size_t tile_flat = (size_t)image * p.tile_w * p.tile_h + tile;
+    if (p.masks != nullptr && !p.masks[tile_flat]) return;
+    const uint32_t tx0 = (tile % p.tile_w) * p.tile_size, ty0 = (tile / p.tile_w) * p.tile_size;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t tpix = p.tile_size * p.tile_size;
+    const size_t img_pix = (size_t)image * p.H * p.W;
+    const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
+
+    float px[PPT], py[PPT], T[PPT], Tf[PPT], buf[PPT][CDIM], vc[PPT][CDIM], va[PPT], bgd[PPT];
+    int32_t bin_final[PPT];
+    bool inside[PPT];
+    bool has = false;
+    int32_t my_max = -1;
+    float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+        const uint32_t q = threadIdx.x * PPT + k;
+        const uint32_t i = ty0 + q / p.tile_size, j = tx0 + q % p.tile_size;
+        inside[k] = q < tpix && i < p.H && j < p.W;
+        px[k] = (float)j + 0.5f;
+        py[k] = (float)i + 0.5f;
+        const size_t pix = img_pix + (inside[k] ? i * p.W + j : 0);
+        Tf[k] = inside[k] ? 1.f - p.alphas[pix] : 0.f;
+        T[k] = Tf[k];
+        bin_final[k] = inside[k] ? p.last_ids[pix] : -1;
+        va[k] = (inside[k] && p.first_chunk) ? p.v_alphas[pix] : 0.f;
+        float dotbg = 0.f;
+#pragma unroll
+        for (int c = 0; c < CDIM; ++c) {
+            vc[k][c] = inside[k] ? p.v_renders[pix * p.cstride + p.coff + c] : 0.f;
+            buf[k][c] = 0.f;
+            if (bg) dotbg += bg[c] * vc[k][c];
+        }
+        bgd[k] = dotbg;
+        if (inside[k]) {
+            has = true;
+            my_max = max(my_max, bin_final[k]);
+            rx0 = fminf(rx0, px[k]);
+            rx1 = fmaxf(rx1, px[k]);
+            ry0 = fminf(ry0, py[k]);
+            ry1 = fmaxf(ry1, py[k]);
+        }
+    }
+    const WarpRect wr = warp_rect(has, rx0, rx1, ry0, ry1);
+    int32_t warp_max = my_max;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) warp_max = max(warp_max, __shfl_xor_sync(0xffffffffu, warp_max, o));
+
+    const int32_t start = p.offsets[tile_flat];
+    const int32_t end = (image == p.I - 1 && tile == p.tile_w * p.tile_h - 1) ? (int32_t)p.n_isects
+                                                                              : p.offsets[tile_flat + 1];
+    // Splats behind every pixel's last contributor in the whole block are skipped.
+    __shared__ int32_t block_max_s;
+    if (threadIdx.x == 0) block_max_s = -1;
+    __syncthreads();
+    if (lane == 0 && wr.any) atomicMax(&block_max_s, warp_max);
+    __syncthreads();
+    const int32_t block_max = block_max_s;
+    const int32_t last = min(end - 1, block_max);
+    uint8_t *mylist = s.lists + warp * kBatch;
+    for (int32_t bend = last; bend >= start; bend -= kBatch) {
+        const int nb = min(kBatch, bend + 1 - start);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nb; i += blockDim.x)
+            stage_splat<CDIM>(p, s, i, p.flatten_ids[bend - i]);
+        __syncthreads();
+        int cnt = 0;
+        if (wr.any) {
+            for (int base = 0; base < nb; base += 32) {
+                const int i = base + lane;
+                const bool hit = i < nb && (bend - i) <= warp_max && box_hits(s.boxes[i], wr);
+                const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+                if (hit) mylist[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint8_t)i;
+                cnt += __popc(bal);
+            }
+        }
+        __syncwarp();
+        for (int li = 0; li < cnt; ++li) {
+            const int i = mylist[li];
+            const int32_t gidx = bend - i;
+            const SplatRec r = s.recs[i];
+            float col[CDIM];
+#pragma unroll
+            for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
+            float g_rgb[CDIM];
+#pragma unroll
+            for (int c = 0; c < CDIM; ++c) g_rgb[c] = 0.f;
+            float g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_x = 0.f, g_y = 0.f, g_o = 0.f, g_ax = 0.f,
+                  g_ay = 0.f;
+            bool any = false;
+#pragma unroll
+            for (int k = 0; k < PPT; ++k) {
+                if (!inside[k] || gidx > bin_final[k]) continue;
+                const PairEval e = eval_pair(r, px[k], py[k]);
+                if (e.sigma < 0.f || e.alpha < kAlphaThreshold) continue;
+                any = true;
+                const float ra = 1.f / fmaxf(kMinOneMinusAlpha, 1.f - e.alpha);
+                T[k] *= ra;
+                const float fac = e.alpha * T[k];
+                float v_alpha = 0.f;
+#pragma unroll
+                for (int c = 0; c < CDIM; ++c) {
+                    g_rgb[c] += fac * vc[k][c];
+                    v_alpha += (col[c] * T[k] - buf[k][c] * ra) * vc[k][c];
+                }
+                v_alpha += Tf[k] * ra * va[k];
+                if (bg) v_alpha += -Tf[k] * ra * bgd[k];
+                if (r.o * e.vis <= kMaxAlpha) {
+                    const float v_sigma = -r.o * e.vis * v_alpha;
+                    g_ca += 0.5f * v_sigma * e.dx * e.dx;
+                    g_cb += v_sigma * e.dx * e.dy;
+                    g_cc += 0.5f * v_sigma * e.dy * e.dy;
+                    const float gx = v_sigma * (r.a * e.dx + r.b * e.dy);
+                    const float gy = v_sigma * (r.b * e.dx + r.c * e.dy);
+                    g_x += gx;
+                    g_y += gy;
+                    g_ax += fabsf(gx);
+                    g_ay += fabsf(gy);
+                    g_o += e.vis * v_alpha;
+                }
+#pragma unroll
+                for (int c = 0; c < CDIM; ++c) buf[k][c] += col[c] * fac;
+            }
+            if (!__any_sync(0xffffffffu, any)) continue;
+#pragma unroll
+            for (int c = 0; c < CDIM; ++c) g_rgb[c] = warp_sum(g_rgb[c]);
+            g_ca = warp_sum(g_ca);
+            g_cb = warp_sum(g_cb);
+            g_cc = warp_sum(g_cc);
+            g_x = warp_sum(g_x);
+            g_y = warp_sum(g_y);
+            g_o = warp_sum(g_o);
+            if (p.v_means2d_abs) {
+                g_ax = warp_sum(g_ax);
+                g_ay = warp_sum(g_ay);
+            }
+            if (lane == 0) {
+                const int32_t g = s.ids[i];
+                float *vcol = p.v_colors + (size_t)g * p.cstride + p.coff;
+#pragma unroll
+                for (int c = 0; c < CDIM; ++c) atomicAdd(vcol + c, g_rgb[c]);
+                atomicAdd(p.v_conics + (size_t)g * 3 + 0, g_ca);
+                atomicAdd(p.v_conics + (size_t)g * 3 + 1, g_cb);
+                atomicAdd(p.v_conics + (size_t)g * 3 + 2, g_cc);
+                atomicAdd(p.v_means2d + (size_t)g * 2 + 0, g_x);
+                atomicAdd(p.v_means2d + (size_t)g * 2 + 1, g_y);
+                atomicAdd(p.v_opacities + g, g_o);
+                if (p.v_means2d_abs) {
+                    atomicAdd(p.v_means2d_abs + (size_t)g * 2 + 0, g_ax);
+                    atomicAdd(p.v_means2d_abs + (size_t)g * 2 + 1, g_ay);
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+static int threads_for(uint32_t tile_size, int ppt) {
+    const uint32_t pix = tile_size * tile_size;
+    uint32_t t = (pix + ppt - 1) / ppt;
+    t = (t + 31) / 32 * 32;
+    return (int)t;
+}
+
+template <int CDIM>
+static int launch_fwd(const RasterParams &p, cudaStream_t stream) {
+    const int ppt = 1;
+    const int nt = threads_for(p.tile_size, ppt);
+    if (nt > 256) return set_error(kErrUnsupported, "tile_size %u too large", p.tile_size);
+    const size_t smem = raster_smem_bytes<CDIM>(nt / 32);
+    auto kern = raster_fwd_kernel<CDIM, 1>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid(p.tile_w * p.tile_h, p.I);
+    kern<<<grid, nt, smem, stream>>>(p);
+    return check_launch("raster_fwd_kernel");
+}
+
+// Pixels per backward thread: enough to amortise the warp reduction, few enough
+// that the per-pixel state (transmittance, colour buffer, upstream gradient)
+// stays in registers.
+template <int CDIM> constexpr int bwd_ppt() { return CDIM <= 4 ? 4 : (CDIM <= 8 ? 2 : 1); }
+
+template <int CDIM>
+static int launch_bwd(const RasterParams &p, cudaStream_t stream) {
+    constexpr int kPPT = bwd_ppt<CDIM>();
+    const bool multi = p.tile_size % kPPT == 0 && p.tile_size >= 8;
+    const int nt = threads_for(p.tile_size, multi ? kPPT : 1);
+    if (nt > 256) return set_error(kErrUnsupported, "tile_size %u too large", p.tile_size);
+    const size_t smem = raster_smem_bytes<CDIM>(nt / 32);
+    dim3 grid(p.tile_w * p.tile_h, p.I);
+    if (multi) {
+        auto kern = raster_bwd_kernel<CDIM, kPPT>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, nt, smem, stream>>>(p);
+    } else {
+        auto kern = raster_bwd_kernel<CDIM, 1>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, nt, smem, stream>>>(p);
+    }
+    return check_launch("raster_bwd_kernel");
+}
+
+template <bool FWD> static int dispatch(int cdim, const RasterParams &p, cudaStream_t s) {
+#define GSB_CASE(N)                                                                               \
+    case N: return FWD ? launch_fwd<N>(p, s) : launch_bwd<N>(p, s);
+    switch (cdim) {
+        GSB_CASE(1)
+        GSB_CASE(2)
+        GSB_CASE(3)
+        GSB_CASE(4)
+        GSB_CASE(5)
+        GSB_CASE(6)
+        GSB_CASE(7)
+        GSB_CASE(8)
+        GSB_CASE(16)
+        GSB_CASE(32)
+    default: return set_error(kErrUnsupported, "Unsupported number of channels: %d", cdim);
+    }
+#undef GSB_CASE
+}
+
+// Splits `channels` into kernel chunks: 32s, then a 16, an 8, and the rest.
+static int next_chunk(int remaining) {
+    if (remaining >= 32) return 32;
+    if (remaining >= 16) return 16;
+    if (remaining >= 8) return 8;
+    return remaining;
+}
+
+static int check_raster_args(int I, int W, int H, int tile_size, int tile_w, int tile_h, int channels) {
+    if (channels <= 0) return set_error(kErrInvalidArgument, "Unsupported number of channels: %d", channels);
+    if (tile_size <= 0 || tile_size > 16)
+        return set_error(kErrUnsupported, "tile_size %d not supported (1..16)", tile_size);
+    if ((long long)tile_w * tile_size < W || (long long)tile_h * tile_size < H)
+        return set_error(kErrInvalidArgument, "tile grid %dx%d of size %d does not cover %dx%d", tile_w,
+                         tile_h, tile_size, W, H);
+    if (I < 0) return set_error(kErrInvalidArgument, "negative image count");
+    return kOk;
+}
+
+} // namespace gsb
+
+using namespace gsb;
+
+extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, float *renders, float *alphas,
+                                 int32_t *last_ids, cudaStream_t stream) {
+    if (int e = check_raster_args(I, width, height, tile_size, tile_width, tile_height, channels)) return e;
+    if (I == 0 || width == 0 || height == 0) return kOk;
+    RasterParams p = {};
+    p.I = I;
+    p.n_isects = (uint32_t)n_isects;
+    p.means2d = means2d;
+    p.conics = conics;
+    p.colors = colors;
+    p.opacities = opacities;
+    p.backgrounds = backgrounds;
+    p.masks = masks;
+    p.W = width;
+    p.H = height;
+    p.tile_size = tile_size;
+    p.tile_w = tile_width;
+    p.tile_h = tile_height;
+    p.offsets = tile_offsets;
+    p.flatten_ids = flatten_ids;
+    p.cstride = channels;
+    p.renders = renders;
+    p.alphas = alphas;
+    p.last_ids = last_ids;
+    int coff = 0;
+    while (coff < channels) {
+        const int n = next_chunk(channels - coff);
+        p.coff = coff;
+        p.write_alpha = coff == 0;
+        if (int e = dispatch<true>(n, p, stream)) return e;
+        coff += n;
+    }
+    return kOk;
+}
+
+extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, const float *render_alphas,
+                                 const int32_t *last_ids, const float *v_render_colors,
+                                 const float *v_render_alphas, float *v_means2d_abs,
+                                 float *v_means2d, float *v_conics, float *v_colors,
+                                 float *v_opacities, cudaStream_t stream) {
+    if (int e = check_raster_args(I, width, height, tile_size, tile_width, tile_height, channels)) return e;
+    if (I == 0 || width == 0 || height == 0 || n_isects <= 0) return kOk;
+    RasterParams p = {};
+    p.I = I;
+    p.n_isects = (uint32_t)n_isects;
+    p.means2d = means2d;
+    p.conics = conics;
+    p.colors = colors;
+    p.opacities = opacities;
+    p.backgrounds = backgrounds;
+    p.masks = masks;
+    p.W = width;
+    p.H = height;
+    p.tile_size = tile_size;
+    p.tile_w = tile_width;
+    p.tile_h = tile_height;
+    p.offsets = tile_offsets;
+    p.flatten_ids = flatten_ids;
+    p.cstride = channels;
+    p.alphas = const_cast<float *>(render_alphas);
+    p.last_ids = const_cast<int32_t *>(last_ids);
+    p.v_renders = v_render_colors;
+    p.v_alphas = v_render_alphas;
+    p.v_means2d = v_means2d;
+    p.v_conics = v_conics;
+    p.v_colors = v_colors;
+    p.v_opacities = v_opacities;
+    p.v_means2d_abs = v_means2d_abs;
+    int coff = 0;
+    while (coff < channels) {
+        const int n = next_chunk(channels - coff);
+        p.coff = coff;
+        p.first_chunk = coff == 0;
+        if (int e = dispatch<false>(n, p, stream)) return e;
+        coff += n;
+    }
+    return kOk;
+}

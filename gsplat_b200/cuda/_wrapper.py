@@ -1,0 +1,633 @@
+"""Python operators of the splatting hot path, backed by the gsplat_b200 C ABI.
+
+Names, argument order, defaults, return tuples and assertion behaviour follow the
+reference's ``gsplat/cuda/_wrapper.py`` (fully_fused_projection 479-631,
+spherical_harmonics 342-372, isect_tiles 634-730, isect_offset_encode 806-826,
+rasterize_to_pixels 829-961, adam 326-339 and the autograd Functions
+_FullyFusedProjection 1464-1594, _RasterizeToPixels 1709-1836,
+_FullyFusedProjectionPacked 2107-2326, _SphericalHarmonics 2329-2364), so code and
+tests written against the reference run unchanged. Every op launches the
+hand-written sm_100a kernels of ``gsplat_b200/csrc``; there is no CPU path.
+"""
+
+import math
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+from typing_extensions import Literal
+
+from . import _backend as _B
+from ._backend import call, check_cuda, ptr, stream_of
+
+CameraModel = Literal["pinhole", "ortho", "fisheye", "ftheta", "lidar"]
+_CAMERA_IDS = {"pinhole": 0, "ortho": 1}
+
+
+def _camera_id(camera_model: str) -> int:
+    assert (
+        camera_model != "ftheta"
+    ), "ftheta camera is only supported via UT, please set with_ut=True in the rasterization()"
+    if camera_model not in _CAMERA_IDS:
+        raise NotImplementedError(
+            f"camera_model={camera_model!r} is not implemented by gsplat_b200 (pinhole, ortho)"
+        )
+    return _CAMERA_IDS[camera_model]
+
+
+def has_3dgs() -> bool:
+    return _B.is_available()
+
+
+def has_adam() -> bool:
+    return _B.is_available()
+
+
+def has_2dgs() -> bool:
+    return False
+
+
+def has_3dgut() -> bool:
+    return False
+
+
+def has_reloc() -> bool:
+    return False
+
+
+def has_camera_wrappers() -> bool:
+    return False
+
+
+# ---------------------------------------------------------------------------
+# Selective Adam
+# ---------------------------------------------------------------------------
+def adam(
+    param: Tensor,
+    param_grad: Tensor,
+    exp_avg: Tensor,
+    exp_avg_sq: Tensor,
+    valid: Tensor,
+    lr: float,
+    b1: float,
+    b2: float,
+    eps: float,
+) -> None:
+    for name, t in (("param", param), ("param_grad", param_grad), ("exp_avg", exp_avg),
+                    ("exp_avg_sq", exp_avg_sq), ("valid", valid)):
+        check_cuda(name, t)
+    N = param.size(0)
+    D = param.numel() // N if N > 0 else 0
+    with torch.cuda.device(param.device):
+        call("gsb_adam", ptr(param), ptr(param_grad), ptr(exp_avg), ptr(exp_avg_sq), ptr(valid),
+             N, D, lr, b1, b2, eps, stream_of(param))
+
+
+def adam_multi(groups, valid: Optional[Tensor], b1: float, b2: float) -> None:
+    """One launch for several (param, grad, exp_avg, exp_avg_sq, lr, eps) groups
+    that share the row visibility mask ``valid``."""
+    if not groups:
+        return
+    arr = (_B.GsbAdamGroup * len(groups))()
+    dev = groups[0][0].device
+    for i, (p, g, m, v, lr, eps) in enumerate(groups):
+        for name, t in (("param", p), ("grad", g), ("exp_avg", m), ("exp_avg_sq", v)):
+            check_cuda(name, t)
+        N = p.size(0)
+        arr[i] = _B.GsbAdamGroup(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(),
+                                 p.numel() // N if N > 0 else 1, lr, eps)
+    check_cuda("valid", valid)
+    with torch.cuda.device(dev):
+        call("gsb_adam_multi", len(groups), arr, ptr(valid), b1, b2,
+             torch.cuda.current_stream(dev).cuda_stream)
+
+
+# ---------------------------------------------------------------------------
+# Spherical harmonics
+# ---------------------------------------------------------------------------
+def spherical_harmonics(
+    degrees_to_use: int,
+    dirs: Tensor,  # [..., 3]
+    coeffs: Tensor,  # [..., K, 3]
+    masks: Optional[Tensor] = None,  # [...,]
+) -> Tensor:
+    """Computes spherical harmonics colours (reference _wrapper.py:342-372)."""
+    assert (degrees_to_use + 1) ** 2 <= coeffs.shape[-2], coeffs.shape
+    batch_dims = dirs.shape[:-1]
+    assert dirs.shape == batch_dims + (3,), dirs.shape
+    assert (
+        (len(coeffs.shape) == len(batch_dims) + 2)
+        and coeffs.shape[:-2] == batch_dims
+        and coeffs.shape[-1] == 3
+    ), coeffs.shape
+    if masks is not None:
+        assert masks.shape == batch_dims, masks.shape
+        masks = masks.contiguous()
+    return _SphericalHarmonics.apply(degrees_to_use, dirs.contiguous(), coeffs.contiguous(), masks)
+
+
+class _SphericalHarmonics(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, sh_degree: int, dirs: Tensor, coeffs: Tensor, masks: Optional[Tensor]) -> Tensor:
+        for name, t in (("dirs", dirs), ("coeffs", coeffs), ("masks", masks)):
+            check_cuda(name, t)
+        n = dirs.numel() // 3
+        K = coeffs.shape[-2]
+        colors = torch.empty(dirs.shape, dtype=dirs.dtype, device=dirs.device)
+        with torch.cuda.device(dirs.device):
+            call("gsb_spherical_harmonics_fwd", sh_degree, n, K, ptr(dirs), ptr(coeffs), ptr(masks),
+                 ptr(colors), stream_of(dirs))
+        ctx.save_for_backward(dirs, coeffs, masks)
+        ctx.sh_degree = sh_degree
+        return colors
+
+    @staticmethod
+    def backward(ctx, v_colors: Tensor):
+        dirs, coeffs, masks = ctx.saved_tensors
+        compute_v_dirs = ctx.needs_input_grad[1]
+        v_colors = v_colors.contiguous()
+        n = dirs.numel() // 3
+        K = coeffs.shape[-2]
+        v_coeffs = torch.empty_like(coeffs)
+        v_dirs = torch.empty_like(dirs) if compute_v_dirs else None
+        with torch.cuda.device(dirs.device):
+            call("gsb_spherical_harmonics_bwd", ctx.sh_degree, n, K, ptr(dirs), ptr(coeffs),
+                 ptr(masks), ptr(v_colors), ptr(v_coeffs), ptr(v_dirs), stream_of(dirs))
+        return None, v_dirs, v_coeffs, None
+
+
+# ---------------------------------------------------------------------------
+# Projection
+# ---------------------------------------------------------------------------
+def fully_fused_projection(
+    means: Tensor,  # [..., N, 3]
+    covars: Optional[Tensor],  # [..., N, 6] or None
+    quats: Optional[Tensor],  # [..., N, 4] or None
+    scales: Optional[Tensor],  # [..., N, 3] or None
+    viewmats: Tensor,  # [..., C, 4, 4]
+    Ks: Tensor,  # [..., C, 3, 3]
+    width: int,
+    height: int,
+    eps2d: float = 0.3,
+    near_plane: float = 0.01,
+    far_plane: float = 1e10,
+    radius_clip: float = 0.0,
+    packed: bool = False,
+    sparse_grad: bool = False,
+    calc_compensations: bool = False,
+    camera_model: CameraModel = "pinhole",
+    opacities: Optional[Tensor] = None,  # [..., N] or None
+) -> Tuple[Tensor, ...]:
+    """Projects Gaussians to 2D (reference _wrapper.py:479-631).
+
+    Returns (radii, means2d, depths, conics, compensations) when packed is False,
+    else (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths,
+    conics, compensations) with the pairs in COO order.
+    """
+    batch_dims = means.shape[:-2]
+    N = means.shape[-2]
+    C = viewmats.shape[-3]
+    assert means.shape == batch_dims + (N, 3), means.shape
+    assert viewmats.shape == batch_dims + (C, 4, 4), viewmats.shape
+    assert Ks.shape == batch_dims + (C, 3, 3), Ks.shape
+    means = means.contiguous()
+    if covars is not None:
+        assert covars.shape == batch_dims + (N, 6), covars.shape
+        covars = covars.contiguous()
+    else:
+        assert quats is not None, "covars or quats is required"
+        assert scales is not None, "covars or scales is required"
+        assert quats.shape == batch_dims + (N, 4), quats.shape
+        assert scales.shape == batch_dims + (N, 3), scales.shape
+        quats = quats.contiguous()
+        scales = scales.contiguous()
+    if sparse_grad:
+        assert packed, "sparse_grad is only supported when packed is True"
+        assert batch_dims == (), "sparse_grad does not support batch dimensions"
+    if opacities is not None:
+        assert opacities.shape == batch_dims + (N,), opacities.shape
+        opacities = opacities.contiguous()
+    cam = _camera_id(camera_model)
+    viewmats = viewmats.contiguous()
+    Ks = Ks.contiguous()
+    if packed:
+        return _FullyFusedProjectionPacked.apply(
+            means, covars, quats, scales, viewmats, Ks, width, height, eps2d, near_plane,
+            far_plane, radius_clip, sparse_grad, calc_compensations, cam, opacities)
+    return _FullyFusedProjection.apply(
+        means, covars, quats, scales, viewmats, Ks, width, height, eps2d, near_plane, far_plane,
+        radius_clip, calc_compensations, cam, opacities)
+
+
+def _check_proj_inputs(means, covars, quats, scales, viewmats, Ks, opacities):
+    for name, t in (("means", means), ("covars", covars), ("quats", quats), ("scales", scales),
+                    ("viewmats", viewmats), ("Ks", Ks), ("opacities", opacities)):
+        check_cuda(name, t)
+        if t is not None and t.dtype != torch.float32:
+            raise RuntimeError(f"{name} must be float32")
+
+
+class _FullyFusedProjection(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, covars, quats, scales, viewmats, Ks, width, height, eps2d, near_plane,
+                far_plane, radius_clip, calc_compensations, camera_model, opacities):
+        _check_proj_inputs(means, covars, quats, scales, viewmats, Ks, opacities)
+        batch_dims = means.shape[:-2]
+        N = means.shape[-2]
+        C = viewmats.shape[-3]
+        B = math.prod(batch_dims)
+        dev = means.device
+        radii = torch.empty(batch_dims + (C, N, 2), dtype=torch.int32, device=dev)
+        means2d = torch.empty(batch_dims + (C, N, 2), dtype=means.dtype, device=dev)
+        depths = torch.empty(batch_dims + (C, N), dtype=means.dtype, device=dev)
+        conics = torch.empty(batch_dims + (C, N, 3), dtype=means.dtype, device=dev)
+        comps = torch.zeros(batch_dims + (C, N), dtype=means.dtype, device=dev) if calc_compensations else None
+        with torch.cuda.device(dev):
+            call("gsb_projection_fused_fwd", B, C, N, ptr(means), ptr(covars), ptr(quats),
+                 ptr(scales), ptr(opacities), ptr(viewmats), ptr(Ks), width, height, eps2d,
+                 near_plane, far_plane, radius_clip, int(calc_compensations), camera_model,
+                 ptr(radii), ptr(means2d), ptr(depths), ptr(conics), ptr(comps), stream_of(means))
+        ctx.save_for_backward(means, covars, quats, scales, viewmats, Ks, radii, conics, comps)
+        ctx.width = width
+        ctx.height = height
+        ctx.eps2d = eps2d
+        ctx.camera_model = camera_model
+        ctx.mark_non_differentiable(radii)
+        return radii, means2d, depths, conics, comps
+
+    @staticmethod
+    def backward(ctx, v_radii, v_means2d, v_depths, v_conics, v_comps):
+        means, covars, quats, scales, viewmats, Ks, radii, conics, comps = ctx.saved_tensors
+        batch_dims = means.shape[:-2]
+        N = means.shape[-2]
+        C = viewmats.shape[-3]
+        B = math.prod(batch_dims)
+        v_means2d = v_means2d.contiguous()
+        v_depths = v_depths.contiguous()
+        v_conics = v_conics.contiguous()
+        if comps is None:
+            v_comps = None
+        elif v_comps is not None:
+            v_comps = v_comps.contiguous()
+        v_means = torch.empty_like(means)
+        v_covars = torch.empty_like(covars) if covars is not None else None
+        v_quats = torch.empty_like(quats) if covars is None else None
+        v_scales = torch.empty_like(scales) if covars is None else None
+        v_viewmats = torch.zeros_like(viewmats) if ctx.needs_input_grad[4] else None
+        with torch.cuda.device(means.device):
+            call("gsb_projection_fused_bwd", B, C, N, ptr(means), ptr(covars), ptr(quats),
+                 ptr(scales), ptr(viewmats), ptr(Ks), ctx.width, ctx.height, ctx.eps2d,
+                 ctx.camera_model, ptr(radii), ptr(conics), ptr(comps), ptr(v_means2d),
+                 ptr(v_depths), ptr(v_conics), ptr(v_comps), ptr(v_means), ptr(v_covars),
+                 ptr(v_quats), ptr(v_scales), ptr(v_viewmats), stream_of(means))
+        return (
+            v_means if ctx.needs_input_grad[0] else None,
+            v_covars if ctx.needs_input_grad[1] else None,
+            v_quats if ctx.needs_input_grad[2] else None,
+            v_scales if ctx.needs_input_grad[3] else None,
+            v_viewmats,
+            None, None, None, None, None, None, None, None, None, None,
+        )
+
+
+def _scan_i32(x: Tensor) -> Tensor:
+    """Inclusive int32 -> int64 prefix sum on the device (gsb_inclusive_scan_i32)."""
+    n = x.numel()
+    out = torch.empty(n, dtype=torch.int64, device=x.device)
+    if n == 0:
+        return out
+    nbytes = _B.lib().gsb_scan_scratch_bytes(n)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    call("gsb_inclusive_scan_i32", ptr(x), ptr(out), n, ptr(scratch), nbytes, stream_of(x))
+    return out
+
+
+class _FullyFusedProjectionPacked(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, covars, quats, scales, viewmats, Ks, width, height, eps2d, near_plane,
+                far_plane, radius_clip, sparse_grad, calc_compensations, camera_model, opacities):
+        _check_proj_inputs(means, covars, quats, scales, viewmats, Ks, opacities)
+        batch_dims = means.shape[:-2]
+        N = means.shape[-2]
+        C = viewmats.shape[-3]
+        B = math.prod(batch_dims)
+        dev = means.device
+        common = (B, C, N, ptr(means), ptr(covars), ptr(quats), ptr(scales), ptr(opacities),
+                  ptr(viewmats), ptr(Ks), width, height, eps2d, near_plane, far_plane, radius_clip,
+                  int(calc_compensations), camera_model)
+        with torch.cuda.device(dev):
+            stream = stream_of(means)
+            nblocks = _B.lib().gsb_projection_packed_blocks(N)
+            block_cnts = torch.empty(B * C * nblocks, dtype=torch.int32, device=dev)
+            call("gsb_projection_packed_count", *common, ptr(block_cnts), stream)
+            block_accum = _scan_i32(block_cnts)
+            nnz = int(block_accum[-1].item()) if block_accum.numel() > 0 else 0
+            indptr = torch.zeros(B * C + 1, dtype=torch.int32, device=dev)
+            batch_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+            camera_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+            gaussian_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+            radii = torch.empty((nnz, 2), dtype=torch.int32, device=dev)
+            means2d = torch.empty((nnz, 2), dtype=means.dtype, device=dev)
+            depths = torch.empty(nnz, dtype=means.dtype, device=dev)
+            conics = torch.empty((nnz, 3), dtype=means.dtype, device=dev)
+            comps = torch.zeros(nnz, dtype=means.dtype, device=dev) if calc_compensations else None
+            if block_accum.numel() > 0:
+                call("gsb_projection_packed_write", *common, ptr(block_accum), ptr(indptr),
+                     ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids), ptr(radii), ptr(means2d),
+                     ptr(depths), ptr(conics), ptr(comps), stream)
+        ctx.save_for_backward(batch_ids, camera_ids, gaussian_ids, means, covars, quats, scales,
+                              viewmats, Ks, conics, comps)
+        ctx.width = width
+        ctx.height = height
+        ctx.eps2d = eps2d
+        ctx.sparse_grad = sparse_grad
+        ctx.camera_model = camera_model
+        ctx.mark_non_differentiable(batch_ids, camera_ids, gaussian_ids, indptr, radii)
+        return batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics, comps
+
+    @staticmethod
+    def backward(ctx, v_batch_ids, v_camera_ids, v_gaussian_ids, v_indptr, v_radii, v_means2d,
+                 v_depths, v_conics, v_comps):
+        (batch_ids, camera_ids, gaussian_ids, means, covars, quats, scales, viewmats, Ks, conics,
+         comps) = ctx.saved_tensors
+        batch_dims = means.shape[:-2]
+        N = means.shape[-2]
+        C = viewmats.shape[-3]
+        B = math.prod(batch_dims)
+        nnz = batch_ids.numel()
+        sparse = ctx.sparse_grad
+        v_means2d = v_means2d.contiguous()
+        v_depths = v_depths.contiguous()
+        v_conics = v_conics.contiguous()
+        if comps is None:
+            v_comps = None
+        elif v_comps is not None:
+            v_comps = v_comps.contiguous()
+
+        def grad_buf(t, width_):
+            if t is None:
+                return None
+            return torch.zeros((nnz, width_) if sparse else t.shape, dtype=t.dtype, device=t.device)
+
+        v_means = grad_buf(means, 3)
+        v_covars = grad_buf(covars, 6)
+        v_quats = grad_buf(quats, 4) if covars is None else None
+        v_scales = grad_buf(scales, 3) if covars is None else None
+        v_viewmats = torch.zeros_like(viewmats) if ctx.needs_input_grad[4] else None
+        with torch.cuda.device(means.device):
+            call("gsb_projection_packed_bwd", B, C, N, nnz, ptr(means), ptr(covars), ptr(quats),
+                 ptr(scales), ptr(viewmats), ptr(Ks), ctx.width, ctx.height, ctx.eps2d,
+                 ctx.camera_model, ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids), ptr(conics),
+                 ptr(comps), ptr(v_means2d), ptr(v_depths), ptr(v_conics), ptr(v_comps),
+                 int(sparse), ptr(v_means), ptr(v_covars), ptr(v_quats), ptr(v_scales),
+                 ptr(v_viewmats), stream_of(means))
+
+        def finish(v, t, idx):
+            if not ctx.needs_input_grad[idx] or v is None:
+                return None
+            if sparse:
+                return torch.sparse_coo_tensor(indices=gaussian_ids[None], values=v, size=t.shape,
+                                               is_coalesced=len(viewmats) == 1)
+            return v
+
+        return (
+            finish(v_means, means, 0),
+            finish(v_covars, covars, 1),
+            finish(v_quats, quats, 2),
+            finish(v_scales, scales, 3),
+            v_viewmats,
+            None, None, None, None, None, None, None, None, None, None, None,
+        )
+
+
+# ---------------------------------------------------------------------------
+# Tile intersection
+# ---------------------------------------------------------------------------
+@torch.no_grad()
+def isect_tiles(
+    means2d: Tensor,  # [..., N, 2] or [nnz, 2]
+    radii: Tensor,  # [..., N, 2] or [nnz, 2]
+    depths: Tensor,  # [..., N] or [nnz]
+    tile_size: int,
+    tile_width: int,
+    tile_height: int,
+    sort: bool = True,
+    segmented: bool = False,
+    packed: bool = False,
+    n_images: Optional[int] = None,
+    image_ids: Optional[Tensor] = None,
+    gaussian_ids: Optional[Tensor] = None,
+    conics: Optional[Tensor] = None,
+    opacities: Optional[Tensor] = None,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Maps projected Gaussians to intersecting tiles (reference _wrapper.py:634-730).
+
+    Returns (tiles_per_gauss int32, isect_ids int64 [n_isects], flatten_ids int32
+    [n_isects]); with ``sort`` the pairs are ordered exactly like a stable sort of
+    isect_ids. ``segmented`` gives the same result (the keys of each image are
+    already contiguous), so the single global sort is used for both.
+    """
+    if packed:
+        nnz = means2d.size(0)
+        assert means2d.shape == (nnz, 2), means2d.shape
+        assert radii.shape == (nnz, 2), radii.shape
+        assert depths.shape == (nnz,), depths.shape
+        if conics is not None:
+            assert conics.shape == (nnz, 3), conics.shape
+        if opacities is not None:
+            assert opacities.shape == (nnz,), opacities.shape
+        assert image_ids is not None, "image_ids is required if packed is True"
+        assert gaussian_ids is not None, "gaussian_ids is required if packed is True"
+        assert n_images is not None, "n_images is required if packed is True"
+        image_ids = image_ids.contiguous()
+        I = n_images
+        N = 0
+        n = nnz
+    else:
+        image_dims = means2d.shape[:-2]
+        I = math.prod(image_dims)
+        N = means2d.shape[-2]
+        nnz = 0
+        assert means2d.shape == image_dims + (N, 2), means2d.shape
+        assert radii.shape == image_dims + (N, 2), radii.shape
+        assert depths.shape == image_dims + (N,), depths.shape
+        if conics is not None:
+            assert conics.shape == image_dims + (N, 3), conics.shape
+        if opacities is not None:
+            assert opacities.shape == image_dims + (N,), opacities.shape
+        n = I * N
+    means2d = means2d.contiguous()
+    radii = radii.contiguous()
+    depths = depths.contiguous()
+    conics = conics.contiguous() if conics is not None else None
+    opacities = opacities.contiguous() if opacities is not None else None
+    if image_ids is not None and image_ids.dtype != torch.int64:
+        image_ids = image_ids.long()
+    for name, t in (("means2d", means2d), ("radii", radii), ("depths", depths), ("conics", conics),
+                    ("opacities", opacities), ("image_ids", image_ids)):
+        check_cuda(name, t)
+    dev = means2d.device
+    tiles_per_gauss = torch.empty(depths.shape, dtype=torch.int32, device=dev)
+    if (conics is None) != (opacities is None):
+        conics, opacities = None, None  # AccuTile needs both; AABB otherwise
+    with torch.cuda.device(dev):
+        stream = stream_of(means2d)
+        args = (int(packed), I, N, nnz, ptr(image_ids), ptr(means2d), ptr(radii), ptr(depths),
+                ptr(conics), ptr(opacities), tile_size, tile_width, tile_height)
+        if n == 0:
+            empty = torch.empty(0, dtype=torch.int64, device=dev)
+            return tiles_per_gauss, empty, torch.empty(0, dtype=torch.int32, device=dev)
+        call("gsb_isect_count", *args, ptr(tiles_per_gauss), stream)
+        cum = _scan_i32(tiles_per_gauss.view(-1))
+        n_isects = int(cum[-1].item())
+        isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
+        flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        if n_isects:
+            call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
+        if n_isects and sort:
+            isect_ids, flatten_ids = _radix_sort(isect_ids, flatten_ids,
+                                                 _B.lib().gsb_isect_key_bits(I, tile_width, tile_height))
+    return tiles_per_gauss, isect_ids, flatten_ids
+
+
+def _radix_sort(keys: Tensor, vals: Tensor, end_bit: int) -> Tuple[Tensor, Tensor]:
+    n = keys.numel()
+    keys_alt = torch.empty_like(keys)
+    vals_alt = torch.empty_like(vals)
+    nbytes = _B.lib().gsb_radix_sort_scratch_bytes(n)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=keys.device)
+    which = call("gsb_radix_sort_pairs", ptr(keys), ptr(vals), ptr(keys_alt), ptr(vals_alt), n,
+                 end_bit, ptr(scratch), nbytes, stream_of(keys))
+    return (keys_alt, vals_alt) if which == 1 else (keys, vals)
+
+
+@torch.no_grad()
+def isect_offset_encode(isect_ids: Tensor, n_images: int, tile_width: int, tile_height: int) -> Tensor:
+    """Encodes sorted intersection ids to per-tile offsets [I, th, tw]
+    (reference _wrapper.py:806-826)."""
+    isect_ids = isect_ids.contiguous()
+    check_cuda("isect_ids", isect_ids)
+    offsets = torch.empty((n_images, tile_height, tile_width), dtype=torch.int32,
+                          device=isect_ids.device)
+    with torch.cuda.device(isect_ids.device):
+        call("gsb_isect_offset_encode", ptr(isect_ids), isect_ids.numel(), n_images, tile_width,
+             tile_height, ptr(offsets), stream_of(isect_ids))
+    return offsets
+
+
+# ---------------------------------------------------------------------------
+# Rasterization
+# ---------------------------------------------------------------------------
+def rasterize_to_pixels(
+    means2d: Tensor,  # [..., N, 2] or [nnz, 2]
+    conics: Tensor,  # [..., N, 3] or [nnz, 3]
+    colors: Tensor,  # [..., N, channels] or [nnz, channels]
+    opacities: Tensor,  # [..., N] or [nnz]
+    image_width: int,
+    image_height: int,
+    tile_size: int,
+    isect_offsets: Tensor,  # [..., tile_height, tile_width]
+    flatten_ids: Tensor,  # [n_isects]
+    backgrounds: Optional[Tensor] = None,  # [..., channels]
+    masks: Optional[Tensor] = None,  # [..., tile_height, tile_width]
+    packed: bool = False,
+    absgrad: bool = False,
+) -> Tuple[Tensor, Tensor]:
+    """Rasterizes Gaussians to pixels (reference _wrapper.py:829-961).
+
+    Returns (render_colors [..., H, W, channels], render_alphas [..., H, W, 1]).
+    Any channel count >= 1 is rendered directly (no zero padding).
+    """
+    image_dims = means2d.shape[:-2]
+    channels = colors.shape[-1]
+    if packed:
+        nnz = means2d.size(0)
+        assert means2d.shape == (nnz, 2), means2d.shape
+        assert conics.shape == (nnz, 3), conics.shape
+        assert colors.shape[0] == nnz, colors.shape
+        assert opacities.shape == (nnz,), opacities.shape
+    else:
+        N = means2d.size(-2)
+        assert means2d.shape == image_dims + (N, 2), means2d.shape
+        assert conics.shape == image_dims + (N, 3), conics.shape
+        assert colors.shape == image_dims + (N, channels), colors.shape
+        assert opacities.shape == image_dims + (N,), opacities.shape
+    if backgrounds is not None:
+        assert backgrounds.shape == image_dims + (channels,), backgrounds.shape
+        backgrounds = backgrounds.contiguous()
+    if masks is not None:
+        assert masks.shape == isect_offsets.shape, masks.shape
+        masks = masks.contiguous()
+    if channels == 0:
+        raise ValueError(f"Unsupported number of color channels: {channels}")
+    tile_height, tile_width = isect_offsets.shape[-2:]
+    assert (
+        tile_height * tile_size >= image_height
+    ), f"Assert Failed: {tile_height} * {tile_size} >= {image_height}"
+    assert (
+        tile_width * tile_size >= image_width
+    ), f"Assert Failed: {tile_width} * {tile_size} >= {image_width}"
+    return _RasterizeToPixels.apply(
+        means2d.contiguous(), conics.contiguous(), colors.contiguous(), opacities.contiguous(),
+        backgrounds, masks, image_width, image_height, tile_size, isect_offsets.contiguous(),
+        flatten_ids.contiguous(), absgrad)
+
+
+class _RasterizeToPixels(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means2d, conics, colors, opacities, backgrounds, masks, width, height,
+                tile_size, isect_offsets, flatten_ids, absgrad):
+        for name, t in (("means2d", means2d), ("conics", conics), ("colors", colors),
+                        ("opacities", opacities), ("backgrounds", backgrounds), ("masks", masks),
+                        ("isect_offsets", isect_offsets), ("flatten_ids", flatten_ids)):
+            check_cuda(name, t)
+        image_dims = isect_offsets.shape[:-2]
+        I = math.prod(image_dims)
+        th, tw = isect_offsets.shape[-2:]
+        channels = colors.shape[-1]
+        dev = means2d.device
+        renders = torch.empty(image_dims + (height, width, channels), dtype=torch.float32, device=dev)
+        alphas = torch.empty(image_dims + (height, width, 1), dtype=torch.float32, device=dev)
+        last_ids = torch.empty(image_dims + (height, width), dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            call("gsb_rasterize_fwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
+                 ptr(opacities), ptr(backgrounds), ptr(masks), width, height, tile_size, tw, th,
+                 ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(), ptr(renders),
+                 ptr(alphas), ptr(last_ids), stream_of(means2d))
+        ctx.save_for_backward(means2d, conics, colors, opacities, backgrounds, masks,
+                              isect_offsets, flatten_ids, alphas, last_ids)
+        ctx.width = width
+        ctx.height = height
+        ctx.tile_size = tile_size
+        ctx.absgrad = absgrad
+        return renders, alphas
+
+    @staticmethod
+    def backward(ctx, v_render_colors, v_render_alphas):
+        (means2d, conics, colors, opacities, backgrounds, masks, isect_offsets, flatten_ids,
+         render_alphas, last_ids) = ctx.saved_tensors
+        image_dims = isect_offsets.shape[:-2]
+        I = math.prod(image_dims)
+        th, tw = isect_offsets.shape[-2:]
+        channels = colors.shape[-1]
+        v_render_colors = v_render_colors.contiguous()
+        v_render_alphas = v_render_alphas.contiguous()
+        v_means2d = torch.zeros_like(means2d)
+        v_conics = torch.zeros_like(conics)
+        v_colors = torch.zeros_like(colors)
+        v_opacities = torch.zeros_like(opacities)
+        v_means2d_abs = torch.zeros_like(means2d) if ctx.absgrad else None
+        with torch.cuda.device(means2d.device):
+            call("gsb_rasterize_bwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
+                 ptr(opacities), ptr(backgrounds), ptr(masks), ctx.width, ctx.height,
+                 ctx.tile_size, tw, th, ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(),
+                 ptr(render_alphas), ptr(last_ids), ptr(v_render_colors), ptr(v_render_alphas),
+                 ptr(v_means2d_abs), ptr(v_means2d), ptr(v_conics), ptr(v_colors),
+                 ptr(v_opacities), stream_of(means2d))
+        if ctx.absgrad:
+            means2d.absgrad = v_means2d_abs
+        v_backgrounds = None
+        if ctx.needs_input_grad[4]:
+            v_backgrounds = (v_render_colors * (1.0 - render_alphas).float()).sum(dim=(-3, -2))
+        return (v_means2d, v_conics, v_colors, v_opacities, v_backgrounds,
+                None, None, None, None, None, None, None)

@@ -1,0 +1,151 @@
+"""Collectives of the Gaussian-sharded multi-GPU mode.
+
+Same functions and semantics as the reference's ``gsplat/distributed.py:25-272``:
+integer all-gather / all-to-all and tensor-list all-gather / all-to-all that
+concatenate the listed tensors column-wise so each exchange is one collective,
+differentiable through ``torch.distributed.nn.functional`` when the data
+requires grad. With ``world_size == 1`` every call returns its input unchanged.
+The process group is NCCL on GPUs (one process per GPU); the same code runs on
+``gloo`` for CPU tests.
+"""
+
+from typing import Callable, List, Optional, Union
+
+import torch
+import torch.distributed as dist
+import torch.distributed.nn.functional as distF
+from torch import Tensor
+
+
+def _comm_device(t_device: torch.device) -> torch.device:
+    return t_device
+
+
+def all_gather_int32(world_size: int, value: Union[int, Tensor],
+                     device: Optional[torch.device] = None) -> List:
+    """Gathers one int32 from every rank (reference distributed.py:25-66)."""
+    if world_size == 1:
+        return [value]
+    if isinstance(value, int):
+        assert device is not None, "device is required for scalar input"
+        value_tensor = torch.tensor(value, dtype=torch.int, device=device)
+    else:
+        value_tensor = value
+    collected = torch.empty(world_size, dtype=value_tensor.dtype, device=value_tensor.device)
+    dist.all_gather_into_tensor(collected, value_tensor.reshape(1))
+    if isinstance(value, int):
+        return collected.tolist()
+    return list(collected.unbind())
+
+
+def all_to_all_int32(world_size: int, values: List[Union[int, Tensor]],
+                     device: Optional[torch.device] = None) -> List:
+    """Exchanges one int32 with every rank (reference distributed.py:69-113)."""
+    if world_size == 1:
+        return values
+    assert len(values) == world_size, "The length of values should be equal to world_size"
+    if any(isinstance(v, int) for v in values):
+        assert device is not None, "device is required for scalar input"
+    values_tensor = [
+        (torch.tensor(v, dtype=torch.int, device=device) if isinstance(v, int) else v).reshape(1)
+        for v in values
+    ]
+    send = torch.cat(values_tensor)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send)
+    out = list(recv.unbind())
+    return [o.item() if isinstance(v, int) else o for o, v in zip(out, values)]
+
+
+def all_gather_tensor_list(world_size: int, tensor_list: List[Tensor]) -> List[Tensor]:
+    """Gathers tensors sharing a first dimension from all ranks
+    (reference distributed.py:116-179)."""
+    if world_size == 1:
+        return tensor_list
+    N = len(tensor_list[0])
+    for t in tensor_list:
+        assert len(t) == N, "All tensors should have the same first dimension size"
+    data = torch.cat([t.reshape(N, -1) for t in tensor_list], dim=-1)
+    sizes = [t.numel() // N for t in tensor_list]
+    if data.requires_grad:
+        collected = distF.all_gather(data)
+    else:
+        collected = [torch.empty_like(data) for _ in range(world_size)]
+        dist.all_gather(collected, data)
+    collected = torch.cat(collected, dim=0)
+    out = torch.split(collected, sizes, dim=-1)
+    return [o.reshape(-1, *t.shape[1:]) for o, t in zip(out, tensor_list)]
+
+
+def all_to_all_tensor_list(world_size: int, tensor_list: List[Tensor], splits: List,
+                           output_splits: Optional[List] = None) -> List[Tensor]:
+    """Splits rows of the listed tensors by ``splits`` and exchanges them with all
+    ranks (reference distributed.py:182-272)."""
+    if world_size == 1:
+        return tensor_list
+    N = len(tensor_list[0])
+    for t in tensor_list:
+        assert len(t) == N, "All tensors should have the same first dimension size"
+    assert len(splits) == world_size, "The length of splits should be equal to world_size"
+    data = torch.cat([t.reshape(N, -1) for t in tensor_list], dim=-1)
+    sizes = [t.numel() // N for t in tensor_list]
+    if output_splits is None:
+        output_splits = all_to_all_int32(world_size, splits, device=data.device)
+    out_splits = [int(s.item()) if isinstance(s, Tensor) else int(s) for s in output_splits]
+    in_splits = [int(s.item()) if isinstance(s, Tensor) else int(s) for s in splits]
+    # One all_to_all_single on a packed buffer (NCCL grouped send/recv under the
+    # hood) instead of a list of per-rank chunks: no torch.cat of the received
+    # pieces, and the same call works on gloo for CPU tests.
+    collected = torch.empty((sum(out_splits), *data.shape[1:]), dtype=data.dtype, device=data.device)
+    if data.requires_grad:
+        collected = distF.all_to_all_single(collected, data, out_splits, in_splits)
+    else:
+        dist.all_to_all_single(collected, data, out_splits, in_splits)
+    out = torch.split(collected, sizes, dim=-1)
+    return [o.reshape(-1, *t.shape[1:]) for o, t in zip(out, tensor_list)]
+
+
+def cli(fn: Callable, args, verbose: bool = False, backend: str = "nccl") -> bool:
+    """Runs ``fn(local_rank, world_rank, world_size, args)`` in one process per GPU
+    (reference distributed.py:287-375). Under torchrun / MPI launchers the ranks
+    come from the environment; otherwise one process is spawned per visible GPU."""
+    import os
+
+    if "OMPI_COMM_WORLD_SIZE" in os.environ:
+        local_rank = int(os.environ["OMPI_COMM_WORLD_LOCAL_RANK"])
+        world_rank = int(os.environ["OMPI_COMM_WORLD_RANK"])
+        world_size = int(os.environ["OMPI_COMM_WORLD_SIZE"])
+        return _worker(local_rank, world_rank, world_size, fn, args, backend)
+    if "WORLD_SIZE" in os.environ and "RANK" in os.environ:
+        return _worker(int(os.environ.get("LOCAL_RANK", 0)), int(os.environ["RANK"]),
+                       int(os.environ["WORLD_SIZE"]), fn, args, backend)
+    world_size = torch.cuda.device_count() if backend == "nccl" else 1
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if "MASTER_PORT" not in os.environ:
+        import socket
+
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        os.environ["MASTER_PORT"] = str(s.getsockname()[1])
+        s.close()
+    torch.multiprocessing.spawn(_spawned, args=(world_size, fn, args, backend), nprocs=world_size,
+                                join=True)
+    return True
+
+
+def _spawned(rank, world_size, fn, args, backend):
+    _worker(rank, rank, world_size, fn, args, backend)
+
+
+def _worker(local_rank, world_rank, world_size, fn, args, backend):
+    import datetime
+
+    if backend == "nccl":
+        torch.cuda.set_device(local_rank)
+    dist.init_process_group(backend=backend, rank=world_rank, world_size=world_size,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        fn(local_rank, world_rank, world_size, args)
+    finally:
+        dist.destroy_process_group()
+    return True

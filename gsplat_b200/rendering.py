@@ -1,0 +1,442 @@
+"""``rasterization()``: the 3D Gaussian splatting render call, forward + backward.
+
+Drop-in for the reference's ``gsplat/rendering.py:256-1273`` for the 3DGS pinhole /
+orthographic path: same keyword arguments and defaults, same return value
+``(render_colors, render_alphas, meta)`` and the same ``meta`` keys, so
+densification strategies that read ``meta["means2d"].grad`` / ``.absgrad`` work
+unchanged. The stages are the ops of ``gsplat_b200.cuda._wrapper`` (projection,
+SH, tile intersection + sort + offsets, rasterization); the multi-GPU mode shards
+Gaussians and exchanges projected splats per camera with NCCL all-to-all exactly
+like the reference (``rendering.py:689-706, 907-1022``).
+
+Options that belong to other pipelines of the reference (3DGUT ``with_ut``,
+``with_eval3d``, lidar, distortion, rolling shutter, fisheye) raise
+``NotImplementedError``.
+"""
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+from typing_extensions import Literal
+
+from .cuda._wrapper import (
+    fully_fused_projection,
+    isect_offset_encode,
+    isect_tiles,
+    rasterize_to_pixels,
+    spherical_harmonics,
+)
+from .distributed import (
+    all_gather_int32,
+    all_gather_tensor_list,
+    all_to_all_int32,
+    all_to_all_tensor_list,
+)
+
+RenderMode = Literal["RGB", "d", "Ed", "D", "ED", "RGB-d", "RGB-Ed", "RGB+D", "RGB+ED"]
+RasterizeMode = Literal["classic", "antialiased"]
+
+
+def render_mode_has_color(mode) -> bool:
+    return mode in {"RGB", "RGB-d", "RGB-Ed", "RGB+D", "RGB+ED"}
+
+
+def render_mode_has_hit_distance(mode) -> bool:
+    return mode in {"d", "Ed", "RGB-d", "RGB-Ed"}
+
+
+def render_mode_has_depth(mode) -> bool:
+    return mode in {"D", "ED", "RGB+D", "RGB+ED"}
+
+
+def render_mode_has_expected_depth(mode) -> bool:
+    return mode in {"Ed", "ED", "RGB-Ed", "RGB+ED"}
+
+
+def render_mode_has_depth_channel(mode) -> bool:
+    return render_mode_has_depth(mode) or render_mode_has_hit_distance(mode)
+
+
+def viewmat_to_camera_position(viewmats: Tensor) -> Tensor:
+    """Camera centre -R^T t of a world-to-camera matrix (reference rendering.py:214-224)."""
+    R = viewmats[..., :3, :3]
+    t = viewmats[..., :3, 3]
+    return -(R.mT @ t.unsqueeze(-1)).squeeze(-1)
+
+
+def compute_directions(batch_dims, means, viewmats, batch_ids=None, camera_ids=None,
+                       gaussian_ids=None, indptr=None) -> Tensor:
+    """Unit view directions from each camera to each Gaussian
+    (reference rendering.py:95-167, 227-253)."""
+    campos = viewmat_to_camera_position(viewmats)
+    if gaussian_ids is None:
+        dirs = means[..., None, :, :] - campos[..., None, :]
+    else:
+        B = math.prod(batch_dims)
+        N = means.shape[-2]
+        C = campos.shape[-2]
+        means_flat = means.reshape(B, N, 3)
+        campos_flat = campos.reshape(B, C, 3)
+        if B * C == 1:
+            dirs = means_flat[0, gaussian_ids] - campos_flat[0, 0]
+        else:
+            dirs = means_flat[batch_ids, gaussian_ids] - campos_flat[batch_ids, camera_ids]
+    return F.normalize(dirs, p=2, dim=-1)
+
+
+def normalize_features_layout(features, batch_dims, C, trailing_dims, batch_ids=None,
+                              camera_ids=None, feature_ids=None) -> Tensor:
+    """Per-view or per-Gaussian features to [nnz, *t] (packed) or [..., C, N, *t]
+    (reference rendering.py:170-213)."""
+    B = math.prod(batch_dims)
+    N = features.shape[-(len(trailing_dims) + 1)]
+    if features.shape == batch_dims + (C, N) + tuple(trailing_dims):
+        if feature_ids is not None:
+            return features.reshape(B, C, N, *trailing_dims)[batch_ids, camera_ids, feature_ids]
+        return features
+    assert features.shape == (*batch_dims, N, *trailing_dims)
+    if feature_ids is not None:
+        return features.reshape(B, N, *trailing_dims)[batch_ids, feature_ids]
+    return torch.broadcast_to(features.unsqueeze(len(batch_dims)), batch_dims + (C, N, *trailing_dims))
+
+
+def _reshape_view(C: int, world_view: Tensor, N_world) -> Tensor:
+    view_list = list(
+        map(
+            lambda x: x.split(int(x.shape[0] / C), dim=0),
+            world_view.split([C * N_i for N_i in N_world], dim=0),
+        )
+    )
+    return torch.stack([torch.cat(l, dim=0) for l in zip(*view_list)], dim=0)
+
+
+def rasterization(
+    means: Tensor,  # [..., N, 3]
+    quats: Tensor,  # [..., N, 4]
+    scales: Tensor,  # [..., N, 3]
+    opacities: Tensor,  # [..., N]
+    colors: Optional[Tensor],  # [..., (C,) N, D] or [..., (C,) N, K, 3]
+    viewmats: Tensor,  # [..., C, 4, 4]
+    Ks: Tensor,  # [..., C, 3, 3]
+    width: int,
+    height: int,
+    near_plane: float = 0.01,
+    far_plane: float = 1e10,
+    radius_clip: float = 0.0,
+    eps2d: float = 0.3,
+    sh_degree: Optional[int] = None,
+    packed: bool = True,
+    tile_size: int = 16,
+    backgrounds: Optional[Tensor] = None,
+    render_mode: RenderMode = "RGB",
+    sparse_grad: bool = False,
+    absgrad: bool = False,
+    rasterize_mode: RasterizeMode = "classic",
+    channel_chunk: int = 32,
+    distributed: bool = False,
+    camera_model: str = "pinhole",
+    segmented: bool = False,
+    covars: Optional[Tensor] = None,
+    with_ut: bool = False,
+    with_eval3d: bool = False,
+    return_normals: bool = False,
+    global_z_order: bool = True,
+    rays: Optional[Tensor] = None,
+    radial_coeffs: Optional[Tensor] = None,
+    tangential_coeffs: Optional[Tensor] = None,
+    thin_prism_coeffs: Optional[Tensor] = None,
+    ftheta_coeffs=None,
+    lidar_coeffs=None,
+    external_distortion_coeffs=None,
+    rolling_shutter=None,
+    viewmats_rs: Optional[Tensor] = None,
+    ut_params=None,
+    extra_signals: Optional[Tensor] = None,
+    extra_signals_sh_degree: Optional[int] = None,
+) -> Tuple[Tensor, Tensor, Dict]:
+    """Rasterizes N 3D Gaussians into C images (reference rendering.py:256-1273).
+
+    Returns ``(render_colors [..., C, H, W, X], render_alphas [..., C, H, W, 1],
+    meta)`` where X is D for "RGB", 1 for "D"/"ED", D+1 for "RGB+D"/"RGB+ED".
+    """
+    unsupported = {
+        "with_ut": with_ut,
+        "with_eval3d": with_eval3d,
+        "return_normals": return_normals,
+        "rays": rays is not None,
+        "radial_coeffs": radial_coeffs is not None,
+        "tangential_coeffs": tangential_coeffs is not None,
+        "thin_prism_coeffs": thin_prism_coeffs is not None,
+        "ftheta_coeffs": ftheta_coeffs is not None,
+        "lidar_coeffs": lidar_coeffs is not None,
+        "external_distortion_coeffs": external_distortion_coeffs is not None,
+        "viewmats_rs": viewmats_rs is not None,
+        "ut_params": ut_params is not None,
+        "global_z_order=False": not global_z_order,
+        "hit-distance render modes": render_mode_has_hit_distance(render_mode),
+    }
+    if rolling_shutter is not None and int(rolling_shutter) != 4:  # 4 = GLOBAL
+        unsupported["rolling_shutter"] = True
+    bad = [k for k, v in unsupported.items() if v]
+    if bad:
+        raise NotImplementedError(f"gsplat_b200.rasterization does not implement: {', '.join(bad)}")
+
+    meta: Dict = {}
+    has_color = render_mode_has_color(render_mode)
+    if colors is None and has_color:
+        raise ValueError(
+            f"colors must be provided when render_mode='{render_mode}' includes RGB. "
+            f"Pass colors=None only for depth-only render modes (D, d, Ed, ED)."
+        )
+    if colors is None and sh_degree is not None:
+        raise ValueError(f"sh_degree must be None when colors is None, got sh_degree={sh_degree}.")
+
+    batch_dims = means.shape[:-2]
+    num_batch_dims = len(batch_dims)
+    B = math.prod(batch_dims)
+    N = means.shape[-2]
+    C = viewmats.shape[-3]
+    D = colors.shape[-1] if has_color else 0
+    I = B * C
+    device = means.device
+    assert means.shape == batch_dims + (N, 3), means.shape
+    if covars is None:
+        assert quats.shape == batch_dims + (N, 4), quats.shape
+        assert scales.shape == batch_dims + (N, 3), scales.shape
+    else:
+        assert covars.shape == batch_dims + (N, 3, 3), covars.shape
+        quats, scales = None, None
+        tri = ([0, 0, 0, 1, 1, 2], [0, 1, 2, 1, 2, 2])
+        covars = covars[..., tri[0], tri[1]]
+    assert opacities.shape == batch_dims + (N,), opacities.shape
+    assert viewmats.shape == batch_dims + (C, 4, 4), viewmats.shape
+    assert Ks.shape == batch_dims + (C, 3, 3), Ks.shape
+
+    def check_features(features: Tensor, deg: Optional[int], name: str) -> None:
+        channels = features.shape[-1]
+        if deg is None:
+            assert (
+                features.dim() == num_batch_dims + 2 and features.shape[:-1] == (*batch_dims, N)
+            ) or (
+                features.dim() == num_batch_dims + 3 and features.shape[:-1] == (*batch_dims, C, N)
+            ), f"{name}'s shape {features.shape=} must be either {(*batch_dims, N, channels)} or {(*batch_dims, C, N, channels)}"
+            if distributed:
+                assert features.dim() == num_batch_dims + 2, f"Distributed mode only supports per-Gaussian {name}."
+        else:
+            assert (
+                features.dim() == num_batch_dims + 3
+                and features.shape[:-2] == batch_dims + (N,)
+                and channels == 3
+            ) or (
+                features.dim() == num_batch_dims + 4
+                and features.shape[:-2] == batch_dims + (C, N)
+                and channels == 3
+            ), f"{name}'s shape {features.shape=} must be either {(*batch_dims, N, 3)} or {(*batch_dims, C, N, 3)}"
+            assert (deg + 1) ** 2 <= features.shape[-2], features.shape
+            if distributed:
+                assert features.dim() == num_batch_dims + 3, f"Distributed mode only supports per-Gaussian {name}."
+
+    if has_color:
+        check_features(colors, sh_degree, "colors")
+    if extra_signals is not None:
+        check_features(extra_signals, extra_signals_sh_degree, "extra signals")
+    if absgrad:
+        assert not distributed, "AbsGrad is not supported in distributed mode."
+
+    if distributed:
+        assert batch_dims == (), "Distributed mode does not support batch dimensions"
+        world_rank = torch.distributed.get_rank()
+        world_size = torch.distributed.get_world_size()
+        N_world = all_gather_int32(world_size, N, device=device)
+        C_world = [C] * world_size
+        viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
+        C = len(viewmats)
+
+    proj = fully_fused_projection(
+        means, covars, quats, scales, viewmats, Ks, width, height, eps2d=eps2d, packed=packed,
+        near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
+        sparse_grad=sparse_grad, calc_compensations=(rasterize_mode == "antialiased"),
+        camera_model=camera_model, opacities=opacities)
+
+    if packed:
+        (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
+         compensations) = proj
+        opacities = opacities.reshape(B, N)[batch_ids, gaussian_ids]
+        image_ids = batch_ids * C + camera_ids
+    else:
+        radii, means2d, depths, conics, compensations = proj
+        opacities = torch.broadcast_to(opacities[..., None, :], batch_dims + (C, N))
+        indptr, batch_ids, camera_ids, gaussian_ids = None, None, None, None
+        image_ids = None
+
+    if compensations is not None:
+        opacities = opacities * compensations
+
+    valid_gaussians = (radii > 0).all(dim=-1)
+    meta.update(
+        {
+            "batch_ids": batch_ids,
+            "camera_ids": camera_ids,
+            "gaussian_ids": gaussian_ids,
+            "radii": radii,
+            "means2d": means2d,
+            "depths": depths,
+            "conics": conics,
+            "opacities": opacities,
+        }
+    )
+
+    colors_sh_degree = sh_degree if has_color else None
+    proj_features = None
+    if colors_sh_degree is None and extra_signals_sh_degree is None:
+        feature_list = []
+        if has_color:
+            feature_list.append(colors)
+        if extra_signals is not None:
+            feature_list.append(extra_signals)
+        if feature_list:
+            proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
+            proj_features = normalize_features_layout(
+                proj_features, batch_dims, C, proj_features.shape[-1:], batch_ids, camera_ids,
+                gaussian_ids)
+    else:
+        dirs = compute_directions(batch_dims, means, viewmats, batch_ids, camera_ids, gaussian_ids,
+                                  indptr)
+        feature_list = []
+        if has_color:
+            tail = colors.shape[-2:] if colors_sh_degree is not None else colors.shape[-1:]
+            colors = normalize_features_layout(colors, batch_dims, C, tail, batch_ids, camera_ids,
+                                               gaussian_ids)
+            if colors_sh_degree is not None:
+                colors = spherical_harmonics(colors_sh_degree, dirs, colors, masks=valid_gaussians)
+                colors = torch.clamp_min(colors + 0.5, 0.0)
+            feature_list.append(colors)
+        if extra_signals is not None:
+            tail = (extra_signals.shape[-2:] if extra_signals_sh_degree is not None
+                    else extra_signals.shape[-1:])
+            extra_signals = normalize_features_layout(extra_signals, batch_dims, C, tail, batch_ids,
+                                                      camera_ids, gaussian_ids)
+            if extra_signals_sh_degree is not None:
+                extra_signals = spherical_harmonics(extra_signals_sh_degree, dirs, extra_signals,
+                                                    masks=valid_gaussians)
+                extra_signals = extra_signals + 0.5
+            feature_list.append(extra_signals)
+        if feature_list:
+            proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
+
+    if distributed:
+        if packed:
+            cnts = torch.bincount(camera_ids, minlength=C)
+            cnts = cnts.split(C_world, dim=0)
+            cnts = [c.sum() for c in cnts]
+            collected_splits = all_to_all_int32(world_size, cnts, device=device)
+            (radii,) = all_to_all_tensor_list(world_size, [radii], cnts, output_splits=collected_splits)
+            tensors = [means2d, depths, conics, opacities]
+            if proj_features is not None:
+                tensors.append(proj_features)
+            out = all_to_all_tensor_list(world_size, tensors, cnts, output_splits=collected_splits)
+            means2d, depths, conics, opacities = out[:4]
+            if proj_features is not None:
+                proj_features = out[4]
+            offsets = torch.tensor([0] + C_world[:-1], device=device, dtype=camera_ids.dtype)
+            offsets = torch.cumsum(offsets, dim=0).repeat_interleave(torch.stack(cnts))
+            camera_ids = camera_ids - offsets
+            offsets = torch.tensor([0] + N_world[:-1], device=device, dtype=gaussian_ids.dtype)
+            offsets = torch.cumsum(offsets, dim=0).repeat_interleave(torch.stack(cnts))
+            gaussian_ids = gaussian_ids + offsets
+            camera_ids, gaussian_ids = all_to_all_tensor_list(
+                world_size, [camera_ids, gaussian_ids], cnts, output_splits=collected_splits)
+            C = C_world[world_rank]
+            image_ids = camera_ids
+        else:
+            C = C_world[world_rank]
+            splits = [C_i * N for C_i in C_world]
+            out_splits = [C * N_i for N_i in N_world]
+            (radii,) = all_to_all_tensor_list(world_size, [radii.flatten(0, 1)], splits=splits,
+                                              output_splits=out_splits)
+            radii = _reshape_view(C, radii, N_world)
+            tensors = [means2d.flatten(0, 1), depths.flatten(0, 1), conics.flatten(0, 1),
+                       opacities.flatten(0, 1)]
+            if proj_features is not None:
+                tensors.append(proj_features.flatten(0, 1))
+            out = all_to_all_tensor_list(world_size, tensors, splits=splits, output_splits=out_splits)
+            means2d, depths, conics, opacities = [_reshape_view(C, t, N_world) for t in out[:4]]
+            if proj_features is not None:
+                proj_features = _reshape_view(C, out[4], N_world)
+        I = B * C
+
+    if render_mode_has_depth_channel(render_mode):
+        depth_channel = depths[..., None]
+        if proj_features is not None:
+            proj_features = torch.cat((proj_features, depth_channel), dim=-1)
+            if backgrounds is not None:
+                backgrounds = torch.cat(
+                    [backgrounds, torch.zeros((*batch_dims, C, 1), device=backgrounds.device)], dim=-1)
+        else:
+            proj_features = depth_channel
+            if backgrounds is not None:
+                backgrounds = torch.zeros((*batch_dims, C, 1), device=backgrounds.device)
+    assert proj_features is not None
+
+    tile_width = math.ceil(width / float(tile_size))
+    tile_height = math.ceil(height / float(tile_size))
+    tiles_per_gauss, isect_ids, flatten_ids = isect_tiles(
+        means2d, radii, depths, tile_size, tile_width, tile_height, segmented=segmented,
+        packed=packed, n_images=I, image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics,
+        opacities=opacities)
+    isect_offsets = isect_offset_encode(isect_ids, I, tile_width, tile_height)
+    isect_offsets = isect_offsets.reshape(batch_dims + (C, tile_height, tile_width))
+
+    meta.update(
+        {
+            "tile_width": tile_width,
+            "tile_height": tile_height,
+            "tiles_per_gauss": tiles_per_gauss,
+            "isect_ids": isect_ids,
+            "flatten_ids": flatten_ids,
+            "isect_offsets": isect_offsets,
+            "width": width,
+            "height": height,
+            "tile_size": tile_size,
+            "n_batches": B,
+            "n_cameras": C,
+        }
+    )
+
+    if proj_features.shape[-1] > channel_chunk:
+        n_chunks = (proj_features.shape[-1] + channel_chunk - 1) // channel_chunk
+        render_colors, render_alphas = [], []
+        for i in range(n_chunks):
+            chunk = proj_features[..., i * channel_chunk:(i + 1) * channel_chunk]
+            bg_chunk = (backgrounds[..., i * channel_chunk:(i + 1) * channel_chunk]
+                        if backgrounds is not None else None)
+            rc, ra = rasterize_to_pixels(means2d, conics, chunk, opacities, width, height, tile_size,
+                                         isect_offsets, flatten_ids, backgrounds=bg_chunk,
+                                         packed=packed, absgrad=absgrad)
+            render_colors.append(rc)
+            render_alphas.append(ra)
+        render_colors = torch.cat(render_colors, dim=-1)
+        render_alphas = render_alphas[0]
+    else:
+        render_colors, render_alphas = rasterize_to_pixels(
+            means2d, conics, proj_features, opacities, width, height, tile_size, isect_offsets,
+            flatten_ids, backgrounds=backgrounds, packed=packed, absgrad=absgrad)
+
+    if extra_signals is not None:
+        E = extra_signals.shape[-1]
+        meta["render_extra_signals"] = render_colors[..., D:D + E]
+        if render_mode_has_depth_channel(render_mode):
+            render_depth = render_colors[..., -1:]
+            if render_mode_has_expected_depth(render_mode):
+                render_depth = render_depth / render_alphas.clamp(min=1e-10)
+            render_colors = torch.cat([render_colors[..., 0:D], render_depth], dim=-1)
+        else:
+            render_colors = render_colors[..., 0:D]
+    elif render_mode_has_expected_depth(render_mode):
+        render_colors = torch.cat(
+            [render_colors[..., :-1], render_colors[..., -1:] / render_alphas.clamp(min=1e-10)],
+            dim=-1)
+    return render_colors, render_alphas, meta

@@ -1,0 +1,217 @@
+/*
+ * gsplat_b200 C ABI: the drop-in boundary of the Gaussian-splatting training hot
+ * path (projection, spherical harmonics, tile intersection + sort + offsets,
+ * rasterization, selective Adam) for NVIDIA B200 (sm_100a).
+ *
+ * Conventions
+ *  - All tensors are device pointers to contiguous row-major fp32 / int32 / int64
+ *    arrays; the caller allocates every output and scratch buffer (the library
+ *    never allocates device memory). Optional inputs and outputs are NULL.
+ *  - Every function launches asynchronously on `stream` and returns 0 on success
+ *    or a negative status (-1 invalid argument, -2 unsupported, -3 launch error);
+ *    gsb_last_error() returns the message of the calling thread's last error.
+ *  - Functions are stateless and reentrant; call them with the device that owns
+ *    the pointers current.
+ *  - Outputs documented as "zero-initialised by the caller" are accumulated into
+ *    with atomics, matching the reference's at::zeros allocations.
+ *
+ * Each entry point names the reference interface it replaces (paths relative to
+ * the mc8max/gsplat source tree).
+ */
+#ifndef GSPLAT_B200_H_
+#define GSPLAT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+#include <cuda_runtime.h>
+
+#if defined(_WIN32)
+#define GSB_API __declspec(dllexport)
+#else
+#define GSB_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+GSB_API const char *gsb_last_error(void);
+GSB_API int gsb_version(void);
+
+/* --- Projection -----------------------------------------------------------
+ * Replaces torch op gsplat::projection_ewa_3dgs_fused_fwd
+ * (gsplat/cuda/ext.cpp:716; gsplat/cuda/csrc/Projection.cpp:129-214).
+ * means [B,N,3]; covars [B,N,6] or quats [B,N,4] + scales [B,N,3];
+ * opacities [B,N] (optional: opacity-aware radius); viewmats [B,C,4,4];
+ * Ks [B,C,3,3]. Outputs [B,C,N,...]: radii int32 x2, means2d x2, depths,
+ * conics x3, compensations (only when calc_compensations). Culled entries are
+ * written as zeros. camera_model: 0 pinhole, 1 ortho. */
+GSB_API int gsb_projection_fused_fwd(int B, int C, int N, const float *means, const float *covars,
+                             const float *quats, const float *scales, const float *opacities,
+                             const float *viewmats, const float *Ks, int width, int height,
+                             float eps2d, float near_plane, float far_plane, float radius_clip,
+                             int calc_compensations, int camera_model, int32_t *radii,
+                             float *means2d, float *depths, float *conics, float *compensations,
+                             cudaStream_t stream);
+
+/* Replaces gsplat::projection_ewa_3dgs_fused_bwd (Projection.cpp:216-306).
+ * Writes v_means [B,N,3], v_quats [B,N,4] + v_scales [B,N,3] (or v_covars
+ * [B,N,6]) completely (no pre-zeroing needed). v_viewmats [B,C,4,4] is
+ * accumulated and must be zero-initialised by the caller (NULL to skip). */
+GSB_API int gsb_projection_fused_bwd(int B, int C, int N, const float *means, const float *covars,
+                             const float *quats, const float *scales, const float *viewmats,
+                             const float *Ks, int width, int height, float eps2d, int camera_model,
+                             const int32_t *radii, const float *conics, const float *compensations,
+                             const float *v_means2d, const float *v_depths, const float *v_conics,
+                             const float *v_compensations, float *v_means, float *v_covars,
+                             float *v_quats, float *v_scales, float *v_viewmats,
+                             cudaStream_t stream);
+
+/* Packed (COO) projection, replaces gsplat::projection_ewa_3dgs_packed_fwd
+ * (Projection.cpp:308-460), as a two-call protocol equal to the reference's
+ * count pass + cumsum + .item() + write pass:
+ *   1. gsb_projection_packed_count -> block_cnts int32 [B*C*blocks], blocks =
+ *      gsb_projection_packed_blocks(N);
+ *   2. gsb_inclusive_scan_i32(block_cnts) -> block_accum int64; nnz = last entry;
+ *   3. gsb_projection_packed_write with outputs of length nnz and indptr [B*C+1].
+ * Pairs are ordered by (batch, camera) then Gaussian id. */
+GSB_API int gsb_projection_packed_blocks(int N);
+GSB_API int gsb_projection_packed_count(int B, int C, int N, const float *means, const float *covars,
+                                const float *quats, const float *scales, const float *opacities,
+                                const float *viewmats, const float *Ks, int width, int height,
+                                float eps2d, float near_plane, float far_plane, float radius_clip,
+                                int calc_compensations, int camera_model, int32_t *block_cnts,
+                                cudaStream_t stream);
+GSB_API int gsb_projection_packed_write(int B, int C, int N, const float *means, const float *covars,
+                                const float *quats, const float *scales, const float *opacities,
+                                const float *viewmats, const float *Ks, int width, int height,
+                                float eps2d, float near_plane, float far_plane, float radius_clip,
+                                int calc_compensations, int camera_model,
+                                const int64_t *block_accum, int32_t *indptr, int64_t *batch_ids,
+                                int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii,
+                                float *means2d, float *depths, float *conics,
+                                float *compensations, cudaStream_t stream);
+
+/* Replaces gsplat::projection_ewa_3dgs_packed_bwd (Projection.cpp:462-575).
+ * sparse_grad = 0: v_means/v_quats/v_scales/v_covars are dense [B,N,...] and
+ * must be zero-initialised (accumulated with atomics); sparse_grad = 1: they are
+ * [nnz,...] and written per pair. v_viewmats as in gsb_projection_fused_bwd. */
+GSB_API int gsb_projection_packed_bwd(int B, int C, int N, int nnz, const float *means,
+                              const float *covars, const float *quats, const float *scales,
+                              const float *viewmats, const float *Ks, int width, int height,
+                              float eps2d, int camera_model, const int64_t *batch_ids,
+                              const int64_t *camera_ids, const int64_t *gaussian_ids,
+                              const float *conics, const float *compensations,
+                              const float *v_means2d, const float *v_depths,
+                              const float *v_conics, const float *v_compensations,
+                              int sparse_grad, float *v_means, float *v_covars, float *v_quats,
+                              float *v_scales, float *v_viewmats, cudaStream_t stream);
+
+/* --- Spherical harmonics --------------------------------------------------
+ * Replaces gsplat::spherical_harmonics_fwd / _bwd
+ * (gsplat/cuda/csrc/SphericalHarmonics.cpp:32-93). dirs [n,3] (normalised
+ * inside), coeffs [n,K,3], masks [n] (optional) -> colors [n,3]; masked
+ * elements get 0. Backward writes v_coeffs [n,K,3] completely and, when
+ * v_dirs != NULL, v_dirs [n,3]. degree in [0,4], K <= 64. */
+GSB_API int gsb_spherical_harmonics_fwd(int degree, long long n, int K, const float *dirs,
+                                const float *coeffs, const bool *masks, float *colors,
+                                cudaStream_t stream);
+GSB_API int gsb_spherical_harmonics_bwd(int degree, long long n, int K, const float *dirs,
+                                const float *coeffs, const bool *masks, const float *v_colors,
+                                float *v_coeffs, float *v_dirs, cudaStream_t stream);
+
+/* --- Prefix sum -----------------------------------------------------------
+ * Inclusive int32 -> int64 scan (replaces the at::cumsum of Intersect.cpp:100).
+ * scratch: device buffer of gsb_scan_scratch_bytes(n) bytes. */
+GSB_API size_t gsb_scan_scratch_bytes(long long n);
+GSB_API int gsb_inclusive_scan_i32(const int32_t *in, int64_t *out, long long n, void *scratch,
+                           size_t scratch_bytes, cudaStream_t stream);
+
+/* --- Tile intersection ----------------------------------------------------
+ * Replaces gsplat::intersect_tile (Intersect.cpp:33-176) as count -> scan ->
+ * emit -> sort. Dense: means2d [I,N,2], radii [I,N,2], depths [I,N] (packed=0).
+ * Packed: [nnz,...] plus image_ids int64 [nnz]. conics [.,3] + opacities [.]
+ * select the AccuTile ellipse test, else the AABB of radii is used.
+ * tiles_per_gauss int32 [I*N or nnz]. Keys: image << (32+tile_bits) |
+ * tile << 32 | float_bits(depth); gsb_isect_key_bits() = 32+tile_bits+image_bits. */
+GSB_API int gsb_isect_key_bits(int I, int tile_width, int tile_height);
+GSB_API int gsb_isect_count(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                    const float *means2d, const int32_t *radii, const float *depths,
+                    const float *conics, const float *opacities, int tile_size, int tile_width,
+                    int tile_height, int32_t *tiles_per_gauss, cudaStream_t stream);
+GSB_API int gsb_isect_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                   const float *means2d, const int32_t *radii, const float *depths,
+                   const float *conics, const float *opacities, int tile_size, int tile_width,
+                   int tile_height, const int64_t *cum_tiles_per_gauss, int64_t *isect_ids,
+                   int32_t *flatten_ids, cudaStream_t stream);
+
+/* Stable radix sort of (int64 key, int32 value) pairs on bits [0, end_bit);
+ * replaces cub::DeviceRadixSort::SortPairs (IntersectTile.cu:478-521). Keys must
+ * be non-negative. Ping-pongs between (keys, vals) and (keys_alt, vals_alt);
+ * returns 0 if the result is in (keys, vals), 1 if in the alternates, <0 on
+ * error. scratch: gsb_radix_sort_scratch_bytes(n) bytes. */
+GSB_API size_t gsb_radix_sort_scratch_bytes(long long n);
+GSB_API int gsb_radix_sort_pairs(int64_t *keys, int32_t *vals, int64_t *keys_alt, int32_t *vals_alt,
+                         long long n, int end_bit, void *scratch, size_t scratch_bytes,
+                         cudaStream_t stream);
+
+/* Replaces gsplat::intersect_offset (Intersect.cpp:320-337): offsets int32
+ * [I, tile_height, tile_width] = index of the first sorted key of each tile
+ * (n_isects for tiles after the last key, 0 everywhere when n_isects == 0). */
+GSB_API int gsb_isect_offset_encode(const int64_t *isect_ids, long long n_isects, int I, int tile_width,
+                            int tile_height, int32_t *offsets, cudaStream_t stream);
+
+/* --- Rasterization --------------------------------------------------------
+ * Replaces gsplat::rasterize_to_pixels_3dgs_fwd (Rasterization.cpp:42-119).
+ * means2d [.,2], conics [.,3], colors [.,channels], opacities [.] indexed by
+ * flatten_ids; backgrounds [I,channels] and masks [I,th,tw] optional.
+ * Outputs renders [I,H,W,channels], alphas [I,H,W], last_ids int32 [I,H,W].
+ * Any channel count >= 1 is accepted; tile_size in [1,16]. */
+GSB_API int gsb_rasterize_fwd(int I, int channels, const float *means2d, const float *conics,
+                      const float *colors, const float *opacities, const float *backgrounds,
+                      const bool *masks, int width, int height, int tile_size, int tile_width,
+                      int tile_height, const int32_t *tile_offsets, const int32_t *flatten_ids,
+                      long long n_isects, float *renders, float *alphas, int32_t *last_ids,
+                      cudaStream_t stream);
+
+/* Replaces gsplat::rasterize_to_pixels_3dgs_bwd (Rasterization.cpp:121-214).
+ * v_means2d, v_conics, v_colors, v_opacities and v_means2d_abs (optional,
+ * absgrad) are accumulated: zero-initialise them. */
+GSB_API int gsb_rasterize_bwd(int I, int channels, const float *means2d, const float *conics,
+                      const float *colors, const float *opacities, const float *backgrounds,
+                      const bool *masks, int width, int height, int tile_size, int tile_width,
+                      int tile_height, const int32_t *tile_offsets, const int32_t *flatten_ids,
+                      long long n_isects, const float *render_alphas, const int32_t *last_ids,
+                      const float *v_render_colors, const float *v_render_alphas,
+                      float *v_means2d_abs, float *v_means2d, float *v_conics, float *v_colors,
+                      float *v_opacities, cudaStream_t stream);
+
+/* --- Selective Adam -------------------------------------------------------
+ * Replaces gsplat::adam (gsplat/cuda/csrc/Adam.cpp:37-65, AdamCUDA.cu:34-69):
+ * masked Adam without bias correction on param/grad/exp_avg/exp_avg_sq of
+ * N rows x D elements; valid [N] optional. gsb_adam_multi updates several
+ * groups (one SelectiveAdam.step, gsplat/optimizers/selective_adam.py:63-101)
+ * sharing the same visibility mask in one launch per 8 groups. */
+typedef struct GsbAdamGroup {
+    float *param;
+    const float *grad;
+    float *exp_avg;
+    float *exp_avg_sq;
+    long long numel; /* N * D */
+    int D;
+    float lr;
+    float eps;
+} GsbAdamGroup;
+
+GSB_API int gsb_adam(float *param, const float *grad, float *exp_avg, float *exp_avg_sq,
+             const bool *valid, long long N, long long D, float lr, float b1, float b2,
+             float eps, cudaStream_t stream);
+GSB_API int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bool *valid, float b1,
+                   float b2, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSPLAT_B200_H_ */

@@ -1,0 +1,57 @@
+"""Seeded synthetic scenes shared by the tests, the smoke check and the bench.
+
+Distributions follow the benchmark configurations of the reference task:
+means N(0,1) in x, y and U[2,8] in z (config 0), scales exp(N(-3.5, 0.5)),
+quats N(0,1)^4 normalised, opacities sigmoid(N(0,1)), SH degree 3 with DC
+N(0.5, 0.2) and higher bands N(0, 0.05); pinhole cameras. The golden fixtures in
+tests/golden/ come from the reference's own test data instead.
+"""
+
+import numpy as np
+import torch
+
+
+def scene(N, seed=0, width=256, height=256, fx=300.0, cx=None, cy=None, z_range=(2.0, 8.0),
+          xy_scale=1.0, C=1, sh_degree=3, viewmats=None, xy_uniform=None):
+    g = torch.Generator().manual_seed(seed)
+    means = torch.randn((N, 3), generator=g)
+    means[:, :2] *= xy_scale
+    if xy_uniform is not None:  # x, y ~ U(-xy_uniform, xy_uniform)
+        means[:, :2] = (torch.rand((N, 2), generator=g) * 2.0 - 1.0) * xy_uniform
+    means[:, 2] = torch.rand((N,), generator=g) * (z_range[1] - z_range[0]) + z_range[0]
+    scales = torch.exp(torch.randn((N, 3), generator=g) * 0.5 - 3.5)
+    quats = torch.nn.functional.normalize(torch.randn((N, 4), generator=g), dim=-1)
+    opacities = torch.sigmoid(torch.randn((N,), generator=g))
+    K = (sh_degree + 1) ** 2
+    sh = torch.randn((N, K, 3), generator=g) * 0.05
+    sh[:, 0, :] = torch.randn((N, 3), generator=g) * 0.2 + 0.5
+    cx = width / 2 if cx is None else cx
+    cy = height / 2 if cy is None else cy
+    Ks = torch.tensor([[fx, 0.0, cx], [0.0, fx, cy], [0.0, 0.0, 1.0]]).expand(C, 3, 3).contiguous()
+    if viewmats is None:
+        viewmats = torch.eye(4).expand(C, 4, 4).contiguous().clone()
+        for c in range(1, C):  # small camera offsets for multi-view cases
+            viewmats[c, 0, 3] = 0.3 * c
+            viewmats[c, 1, 3] = -0.2 * c
+    return dict(means=means, quats=quats, scales=scales, opacities=opacities, sh=sh,
+                viewmats=viewmats, Ks=Ks, width=width, height=height)
+
+
+def config0():
+    """10k Gaussians, one 256x256 camera, fx=fy=300."""
+    return scene(10_000, seed=0, width=256, height=256, fx=300.0)
+
+
+def config1(N=1_000_000, seed=1):
+    """1M Gaussians in a 10-unit cube in front of one
+    1297x840 camera (fx=fy=1150, cx=648.5, cy=420): x, y ~ U(-5, 5), z ~ U(2, 12)."""
+    return scene(N, seed=seed, width=1297, height=840, fx=1150.0, cx=648.5, cy=420.0,
+                 z_range=(2.0, 12.0), xy_uniform=5.0)
+
+
+def to(d, device):
+    return {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
+
+
+def np_(t):
+    return t.detach().cpu().numpy() if isinstance(t, torch.Tensor) else t

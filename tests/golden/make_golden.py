@@ -1,0 +1,164 @@
+"""Generates the golden vectors in tests/golden/ from the reference gsplat itself.
+
+Run in the build container, where the read-only reference checkout is available:
+
+    python tests/golden/make_golden.py /path/to/reference
+
+The reference's pure-PyTorch path (gsplat/cuda/_torch_impl.py, gsplat/cuda/_math.py)
+is imported on CPU -- its CUDA extension cannot be built there, so the JIT loader is
+told that no CUDA toolkit exists and gsplat falls back to ``_C = None``. Inputs follow
+the reference tests: a seeded subset of the reference fixture assets/test_garden.npz
+with its three real cameras (tests/test_basic.py:85-110, gsplat/_helper.py:48-100),
+the random intersection case of tests/test_basic.py:698-736 and the SH case of
+tests/test_basic.py:2903-2939. Outputs are stored as small .npz files which the
+CPU tests (tests/test_oracle_golden.py) compare with the oracle and the GPU tests
+compare with the kernels; nothing reads the reference at test time.
+"""
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def import_reference(ref_root: str):
+    import torch.utils.cpp_extension as ext
+
+    ext._find_cuda_home = lambda: None
+    sys.path.insert(0, ref_root)
+    import gsplat  # noqa: F401
+    from gsplat.cuda import _math, _torch_impl
+
+    return _torch_impl, _math
+
+
+def garden_subset(ref_root: str, n: int, seed: int):
+    d = np.load(os.path.join(ref_root, "assets", "test_garden.npz"))
+    means = d["means3d"].astype(np.float32)
+    sel = np.all((means >= -2) & (means <= 2), axis=-1)
+    means = means[sel]
+    rng = np.random.default_rng(seed)
+    means = means[rng.choice(len(means), n, replace=False)]
+    g = torch.Generator().manual_seed(seed)
+    scales = torch.rand((n, 3), generator=g) * (0.02 - 1e-4) + 1e-4
+    quats = torch.nn.functional.normalize(torch.randn((n, 4), generator=g), dim=-1)
+    opacities = torch.rand((n,), generator=g)
+    return (torch.from_numpy(means), quats, scales, opacities, torch.from_numpy(d["viewmats"]),
+            torch.from_numpy(d["Ks"]), int(d["width"]), int(d["height"]))
+
+
+def make_projection(ti, tm, ref_root):
+    means, quats, scales, opacities, viewmats, Ks, W, H = garden_subset(ref_root, 800, 7)
+    out = {}
+    for calc in (False, True):
+        m = means.clone().requires_grad_(True)
+        q = quats.clone().requires_grad_(True)
+        s = scales.clone().requires_grad_(True)
+        v = viewmats.clone().requires_grad_(True)
+        covars, _ = tm._quat_scale_to_covar_preci(q, s, compute_preci=False, triu=False)
+        radii, means2d, depths, conics, comps = ti._fully_fused_projection(
+            m, covars, v, Ks, W, H, eps2d=0.3, calc_compensations=calc)
+        valid = (radii > 0).all(dim=-1)
+        g = torch.Generator().manual_seed(11)
+        vm2 = torch.randn(means2d.shape, generator=g) * valid[..., None]
+        vd = torch.randn(depths.shape, generator=g) * valid
+        vc = torch.randn(conics.shape, generator=g) * valid[..., None]
+        loss = (means2d * vm2).sum() + (depths * vd).sum() + (conics * vc).sum()
+        vcomp = None
+        if calc:
+            vcomp = torch.randn(comps.shape, generator=g) * valid
+            loss = loss + (comps * vcomp).sum()
+        gm, gq, gs, gv = torch.autograd.grad(loss, (m, q, s, v))
+        tag = "aa" if calc else "classic"
+        out.update({
+            f"{tag}_radii": radii.numpy(), f"{tag}_means2d": means2d.detach().numpy(),
+            f"{tag}_depths": depths.detach().numpy(), f"{tag}_conics": conics.detach().numpy(),
+            f"{tag}_v_means2d": vm2.numpy(), f"{tag}_v_depths": vd.numpy(),
+            f"{tag}_v_conics": vc.numpy(), f"{tag}_v_means": gm.numpy(),
+            f"{tag}_v_quats": gq.numpy(), f"{tag}_v_scales": gs.numpy(),
+            f"{tag}_v_viewmats": gv.numpy(),
+        })
+        if calc:
+            out[f"{tag}_comps"] = comps.detach().numpy()
+            out[f"{tag}_v_comps"] = vcomp.numpy()
+    out.update({"means": means.numpy(), "quats": quats.numpy(), "scales": scales.numpy(),
+                "opacities": opacities.numpy(), "viewmats": viewmats.numpy(), "Ks": Ks.numpy(),
+                "width": W, "height": H})
+    np.savez_compressed(os.path.join(HERE, "projection_garden.npz"), **out)
+
+
+def make_covar(tm):
+    g = torch.Generator().manual_seed(3)
+    quats = torch.randn((500, 4), generator=g)
+    scales = torch.rand((500, 3), generator=g) * 0.1 + 1e-3
+    covars, precis = tm._quat_scale_to_covar_preci(quats, scales, triu=False)
+    np.savez_compressed(os.path.join(HERE, "covar.npz"), quats=quats.numpy(), scales=scales.numpy(),
+                        covars=covars.numpy(), precis=precis.numpy())
+
+
+def make_sh(ti):
+    out = {}
+    g = torch.Generator().manual_seed(42)
+    N = 300
+    coeffs = torch.randn((N, 25, 3), generator=g)
+    dirs = torch.randn((N, 3), generator=g)
+    out["coeffs"] = coeffs.numpy()
+    out["dirs"] = dirs.numpy()
+    for deg in range(5):
+        c = coeffs.clone().requires_grad_(True)
+        d = dirs.clone().requires_grad_(True)
+        colors = ti._spherical_harmonics(deg, d, c)
+        vcol = torch.randn(colors.shape, generator=g)
+        gc, gd = torch.autograd.grad((colors * vcol).sum(), (c, d), allow_unused=True)
+        out[f"deg{deg}_colors"] = colors.detach().numpy()
+        out[f"deg{deg}_v_colors"] = vcol.numpy()
+        out[f"deg{deg}_v_coeffs"] = gc.numpy()
+        out[f"deg{deg}_v_dirs"] = (gd if gd is not None else torch.zeros_like(dirs)).numpy()
+    np.savez_compressed(os.path.join(HERE, "sh.npz"), **out)
+
+
+def make_isect(ti):
+    """tests/test_basic.py:698-736: C=3, N=1000, 40x60 image, AABB tiles."""
+    import math
+
+    g = torch.Generator().manual_seed(42)
+    C, N = 3, 1000
+    width, height = 40, 60
+    means2d = torch.randn((C, N, 2), generator=g) * width
+    radii = torch.randint(0, width, (C, N, 2), generator=g, dtype=torch.int32)
+    depths = torch.rand((C, N), generator=g)
+    tile_size = 16
+    tw = math.ceil(width / tile_size)
+    th = math.ceil(height / tile_size)
+    tpg, isect_ids, flatten_ids = ti._isect_tiles(means2d, radii, depths, tile_size, tw, th)
+    # torch.sort is not guaranteed stable; re-sort stably to pin the order of
+    # equal keys like cub's stable radix sort.
+    _, unsorted_keys, unsorted_ids = ti._isect_tiles(means2d, radii, depths, tile_size, tw, th, sort=False)
+    order = np.argsort(unsorted_keys.numpy(), kind="stable")
+    offsets = ti._isect_offset_encode(isect_ids, C, tw, th)
+    np.savez_compressed(
+        os.path.join(HERE, "isect_aabb.npz"), means2d=means2d.numpy(), radii=radii.numpy(),
+        depths=depths.numpy(), tile_size=tile_size, tile_width=tw, tile_height=th,
+        tiles_per_gauss=tpg.numpy(), isect_ids=unsorted_keys.numpy()[order],
+        flatten_ids=unsorted_ids.numpy()[order], torch_sorted_keys=isect_ids.numpy(),
+        isect_offsets=offsets.numpy())
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GSPLAT_REFERENCE", "")
+    if not ref_root or not os.path.isdir(ref_root):
+        raise SystemExit("usage: make_golden.py <reference checkout>")
+    ti, tm = import_reference(ref_root)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    make_covar(tm)
+    make_sh(ti)
+    make_projection(ti, tm, ref_root)
+    make_isect(ti)
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

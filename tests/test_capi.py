@@ -1,0 +1,108 @@
+"""CPU checks of the C-ABI boundary: the library loads without a GPU, exports every
+symbol declared in include/gsplat_b200.h, the ctypes signatures match the header,
+and argument validation fails loudly (no kernel is launched in these tests)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gsplat_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return re.findall(r"GSB_API\s+[\w\s\*]+?\b(gsb_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert len(names) >= 20
+    for n in ("gsb_projection_fused_fwd", "gsb_projection_fused_bwd", "gsb_isect_emit",
+              "gsb_radix_sort_pairs", "gsb_rasterize_fwd", "gsb_rasterize_bwd", "gsb_adam"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from gsplat_b200.cuda import _backend
+
+    lib = _backend.lib()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_signatures_cover_header():
+    from gsplat_b200.cuda import _backend
+
+    declared = set(declared_functions())
+    assert declared == set(_backend.SIGNATURES), declared ^ set(_backend.SIGNATURES)
+    text = open(HEADER).read()
+    for name, (_, args) in _backend.SIGNATURES.items():
+        m = re.search(r"\b" + name + r"\s*\(([^;]*)\)\s*;", text, re.S)
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(args), (name, len(params), len(args))
+
+
+def test_invalid_arguments_return_errors_without_launch():
+    from gsplat_b200.cuda import _backend
+
+    lib = _backend.lib()
+    assert lib.gsb_version() == 1
+    rc = lib.gsb_spherical_harmonics_fwd(7, 10, 64, None, None, None, None, None)
+    assert rc == -2 and b"degree" in lib.gsb_last_error()
+    rc = lib.gsb_rasterize_fwd(1, 0, None, None, None, None, None, None, 16, 16, 16, 1, 1, None,
+                               None, 0, None, None, None, None)
+    assert rc == -1 and b"channels" in lib.gsb_last_error()
+    rc = lib.gsb_isect_count(0, 1 << 20, 1, 0, None, None, None, None, None, None, 16, 4096, 4096,
+                             None, None)
+    assert rc == -1 and b"exceed" in lib.gsb_last_error()
+    rc = lib.gsb_projection_fused_fwd(1, 1, 1, None, None, None, None, None, None, None, 1, 1, 0.3,
+                                      0.01, 100.0, 0.0, 0, 2, None, None, None, None, None, None)
+    assert rc == -2 and b"camera_model" in lib.gsb_last_error()
+
+
+def test_python_ops_raise_on_cpu_tensors():
+    import torch
+
+    import gsplat_b200
+
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        gsplat_b200.spherical_harmonics(1, torch.randn(4, 3), torch.randn(4, 4, 3))
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        gsplat_b200.fully_fused_projection(torch.randn(4, 3), None, torch.randn(4, 4),
+                                           torch.rand(4, 3), torch.eye(4)[None], torch.eye(3)[None],
+                                           8, 8)
+
+
+def test_api_signature_matches_reference():
+    """Keyword names and defaults of the drop-in API (reference rendering.py:256-310,
+    _wrapper.py:479-497, 634-651, 829-843)."""
+    import inspect
+
+    import gsplat_b200
+
+    sig = inspect.signature(gsplat_b200.rasterization)
+    defaults = {k: v.default for k, v in sig.parameters.items()}
+    expect = dict(near_plane=0.01, far_plane=1e10, radius_clip=0.0, eps2d=0.3, sh_degree=None,
+                  packed=True, tile_size=16, backgrounds=None, render_mode="RGB",
+                  sparse_grad=False, absgrad=False, rasterize_mode="classic", channel_chunk=32,
+                  distributed=False, camera_model="pinhole", segmented=False, covars=None)
+    for k, v in expect.items():
+        assert defaults[k] == v, k
+    params = list(sig.parameters)
+    assert params[:9] == ["means", "quats", "scales", "opacities", "colors", "viewmats", "Ks",
+                          "width", "height"]
+    p = list(inspect.signature(gsplat_b200.fully_fused_projection).parameters)
+    assert p == ["means", "covars", "quats", "scales", "viewmats", "Ks", "width", "height", "eps2d",
+                 "near_plane", "far_plane", "radius_clip", "packed", "sparse_grad",
+                 "calc_compensations", "camera_model", "opacities"]
+    p = list(inspect.signature(gsplat_b200.isect_tiles).parameters)
+    assert p == ["means2d", "radii", "depths", "tile_size", "tile_width", "tile_height", "sort",
+                 "segmented", "packed", "n_images", "image_ids", "gaussian_ids", "conics",
+                 "opacities"]
+    p = list(inspect.signature(gsplat_b200.rasterize_to_pixels).parameters)
+    assert p == ["means2d", "conics", "colors", "opacities", "image_width", "image_height",
+                 "tile_size", "isect_offsets", "flatten_ids", "backgrounds", "masks", "packed",
+                 "absgrad"]

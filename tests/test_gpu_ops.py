@@ -1,0 +1,448 @@
+"""Parity of the sm_100a kernels (through the C ABI / Python ops) with the CPU
+oracle and with the reference golden vectors. Mirrors the reference tests
+tests/test_basic.py test_projection, test_fully_fused_projection_packed, test_isect,
+test_rasterize_to_pixels and test_sh, with the tolerances written in each test.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import _data
+from tests._compare import as_np, assert_close, assert_equal
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def gsb():
+    import gsplat_b200
+
+    return gsplat_b200
+
+
+def project(d, packed=False, calc=False, batch=(), use_opac=True, C=None):
+    g = gsb()
+    means, quats, scales = d["means"], d["quats"], d["scales"]
+    viewmats, Ks = d["viewmats"], d["Ks"]
+    opac = d["opacities"] if use_opac else None
+    if batch:
+        means = means.expand(batch + means.shape).contiguous()
+        quats = quats.expand(batch + quats.shape).contiguous()
+        scales = scales.expand(batch + scales.shape).contiguous()
+        viewmats = viewmats.expand(batch + viewmats.shape).contiguous()
+        Ks = Ks.expand(batch + Ks.shape).contiguous()
+        opac = opac.expand(batch + opac.shape).contiguous() if opac is not None else None
+    return g.fully_fused_projection(means, None, quats, scales, viewmats, Ks, d["width"],
+                                    d["height"], packed=packed, calc_compensations=calc,
+                                    opacities=opac)
+
+
+# ---------------------------------------------------------------------------
+# Projection
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("calc", [False, True])
+@pytest.mark.parametrize("use_opac", [True, False])
+@pytest.mark.parametrize("batch", [(), (2,)])
+def test_projection_forward_vs_oracle(calc, use_opac, batch):
+    d = _data.scene(4000, seed=3, C=2)
+    ex = lambda t: t.expand(batch + t.shape).contiguous()
+    inp = {k: ex(d[k]) for k in ("means", "quats", "scales", "opacities", "viewmats", "Ks")}
+    g = inp if use_opac else dict(inp, opacities=None)
+    radii, means2d, depths, conics, comps = gsb().fully_fused_projection(
+        g["means"].to(DEV), None, g["quats"].to(DEV), g["scales"].to(DEV), g["viewmats"].to(DEV),
+        g["Ks"].to(DEV), d["width"], d["height"], calc_compensations=calc,
+        opacities=None if g["opacities"] is None else g["opacities"].to(DEV))
+    n = lambda t: None if t is None else t.numpy()
+    er, em, ed, ec, ecomp = O.projection_fwd(n(g["means"]), None, n(g["quats"]), n(g["scales"]),
+                                             n(g["opacities"]), n(g["viewmats"]), n(g["Ks"]),
+                                             d["width"], d["height"], calc_compensations=calc)
+    r = as_np(radii)
+    # radii are integers from ceil(): allow a one-pixel difference (reference test_basic.py:301)
+    assert np.abs(r.astype(np.int64) - er).max() <= 1
+    vis = (r > 0).all(-1)
+    assert (vis != (er > 0).all(-1)).mean() < 1e-3
+    both = vis & (er > 0).all(-1)
+    bt = torch.from_numpy(both).to(DEV)
+    assert_close(means2d[bt], em[both], 1e-5, 1e-4, name="means2d")
+    assert_close(depths[bt], ed[both], 1e-6, 1e-6, name="depths")
+    assert_close(conics[bt], ec[both], 1e-4, 1e-5, name="conics")
+    if calc:
+        assert_close(comps[bt], ecomp[both], 1e-4, 1e-5, name="comps")
+
+
+@pytest.mark.parametrize("calc", [False, True])
+def test_projection_backward_vs_oracle(calc):
+    d = _data.to(_data.scene(4000, seed=4, C=3), DEV)
+    means = d["means"].clone().requires_grad_(True)
+    quats = d["quats"].clone().requires_grad_(True)
+    scales = d["scales"].clone().requires_grad_(True)
+    viewmats = d["viewmats"].clone().requires_grad_(True)
+    g = gsb()
+    radii, means2d, depths, conics, comps = g.fully_fused_projection(
+        means, None, quats, scales, viewmats, d["Ks"], d["width"], d["height"],
+        calc_compensations=calc, opacities=d["opacities"])
+    valid = (radii > 0).all(-1)
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    vm2 = torch.randn(means2d.shape, device=DEV, generator=gen) * valid[..., None]
+    vd = torch.randn(depths.shape, device=DEV, generator=gen) * valid
+    vc = torch.randn(conics.shape, device=DEV, generator=gen) * valid[..., None]
+    loss = (means2d * vm2).sum() + (depths * vd).sum() + (conics * vc).sum()
+    vcomp = None
+    if calc:
+        vcomp = torch.randn(comps.shape, device=DEV, generator=gen) * valid
+        loss = loss + (comps * vcomp).sum()
+    gm, gq, gs, gv = torch.autograd.grad(loss, (means, quats, scales, viewmats))
+    em, _, eq, es, ev = O.projection_bwd(
+        as_np(d["means"]), None, as_np(d["quats"]), as_np(d["scales"]), as_np(d["viewmats"]),
+        as_np(d["Ks"]), d["width"], d["height"], 0.3, as_np(radii), as_np(conics),
+        as_np(comps) if calc else None, as_np(vm2), as_np(vd), as_np(vc),
+        as_np(vcomp) if calc else None)
+    # fp32 kernel vs float64 oracle on identical forward outputs
+    assert_close(gm, em, 1e-4, 1e-4, name="v_means")
+    assert_close(gq, eq, 1e-3, 1e-4, name="v_quats")
+    assert_close(gs, es, 1e-3, 1e-3, name="v_scales")
+    assert_close(gv, ev, 1e-3, 1e-2, name="v_viewmats")
+
+
+def test_projection_garden_golden():
+    """Reference fixture test_garden subset: kernel vs the reference torch path."""
+    gd = dict(np.load(os.path.join(GOLD, "projection_garden.npz")))
+    t = lambda k: torch.from_numpy(gd[k]).to(DEV)
+    for tag, calc in (("classic", False), ("aa", True)):
+        means = t("means").requires_grad_(True)
+        quats = t("quats").requires_grad_(True)
+        scales = t("scales").requires_grad_(True)
+        viewmats = t("viewmats").requires_grad_(True)
+        radii, means2d, depths, conics, comps = gsb().fully_fused_projection(
+            means, None, quats, scales, viewmats, t("Ks"), int(gd["width"]), int(gd["height"]),
+            calc_compensations=calc)
+        er = gd[f"{tag}_radii"]
+        assert np.abs(as_np(radii).astype(np.int64) - er).max() <= 1
+        both = torch.from_numpy((as_np(radii) > 0).all(-1) & (er > 0).all(-1)).to(DEV)
+        bn = as_np(both)
+        assert_close(means2d[both], gd[f"{tag}_means2d"][bn], 1e-5, 1e-4, name="means2d")
+        assert_close(conics[both], gd[f"{tag}_conics"][bn], 1e-4, 1e-5, name="conics")
+        loss = ((means2d * t(f"{tag}_v_means2d")).sum() + (depths * t(f"{tag}_v_depths")).sum()
+                + (conics * t(f"{tag}_v_conics")).sum())
+        if calc:
+            loss = loss + (comps * t(f"{tag}_v_comps")).sum()
+        gm, gq, gs, gv = torch.autograd.grad(loss, (means, quats, scales, viewmats))
+        # fp32 torch graph on the other side: tolerances of the reference's own
+        # test are rtol 1e-2..5e-1; ours are tighter
+        assert_close(gm, gd[f"{tag}_v_means"], 1e-3, 1e-3, name="v_means")
+        assert_close(gs, gd[f"{tag}_v_scales"], 2e-3, 2e-2, name="v_scales")
+        assert_close(gq, gd[f"{tag}_v_quats"], 2e-3, 1e-3, name="v_quats")
+        assert_close(gv, gd[f"{tag}_v_viewmats"], 1e-3, 1e-2, name="v_viewmats")
+
+
+@pytest.mark.parametrize("calc", [False, True])
+def test_projection_packed_equals_dense(calc):
+    d = _data.to(_data.scene(5000, seed=6, C=3), DEV)
+    dense = project(d, packed=False, calc=calc)
+    packed = project(d, packed=True, calc=calc)
+    batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics, comps = packed
+    r_d = dense[0]
+    valid = (r_d > 0).all(-1)
+    cam, gid = torch.nonzero(valid, as_tuple=True)
+    assert_equal(camera_ids, cam, "camera_ids")
+    assert_equal(gaussian_ids, gid, "gaussian_ids")
+    assert_equal(batch_ids, torch.zeros_like(cam), "batch_ids")
+    counts = valid.sum(-1)
+    assert_equal(indptr, torch.cat([torch.zeros(1, device=DEV, dtype=torch.int64), counts.cumsum(0)]).int(), "indptr")
+    assert_equal(radii, r_d[valid], "radii")
+    assert_equal(means2d, dense[1][valid], "means2d")
+    assert_equal(depths, dense[2][valid], "depths")
+    assert_equal(conics, dense[3][valid], "conics")
+    if calc:
+        assert_equal(comps, dense[4][valid], "comps")
+
+
+def test_projection_packed_backward_equals_dense():
+    d = _data.to(_data.scene(3000, seed=7, C=2), DEV)
+    grads = []
+    for packed in (False, True):
+        means = d["means"].clone().requires_grad_(True)
+        quats = d["quats"].clone().requires_grad_(True)
+        scales = d["scales"].clone().requires_grad_(True)
+        viewmats = d["viewmats"].clone().requires_grad_(True)
+        out = gsb().fully_fused_projection(means, None, quats, scales, viewmats, d["Ks"], d["width"],
+                                           d["height"], packed=packed, opacities=d["opacities"])
+        m2, dep, con = (out[5], out[6], out[7]) if packed else (out[1], out[2], out[3])
+        w = torch.linspace(0.5, 1.5, m2.numel(), device=DEV).reshape(m2.shape)
+        loss = (m2 * w).sum() + dep.sum() + (con * 0.1).sum()
+        grads.append(torch.autograd.grad(loss, (means, quats, scales, viewmats)))
+    for a, b, name in zip(grads[0], grads[1], ("means", "quats", "scales", "viewmats")):
+        assert_close(b, a, 1e-5, 1e-5, name=name)
+
+
+def test_projection_empty_and_culled():
+    g = gsb()
+    d = _data.to(_data.scene(0, seed=1), DEV)
+    r, m2, dep, con, comp = project(d)
+    assert r.shape == (1, 0, 2)
+    d = _data.to(_data.scene(100, seed=1), DEV)
+    d["means"][:, 2] = -5.0  # everything behind the camera
+    out = project(d, packed=True)
+    assert out[0].numel() == 0 and out[3].tolist() == [0, 0]
+
+
+# ---------------------------------------------------------------------------
+# Spherical harmonics
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("deg", [0, 1, 2, 3, 4])
+def test_sh_vs_reference_golden(deg):
+    gd = dict(np.load(os.path.join(GOLD, "sh.npz")))
+    dirs = torch.from_numpy(gd["dirs"]).to(DEV).requires_grad_(True)
+    coeffs = torch.from_numpy(gd["coeffs"]).to(DEV).requires_grad_(True)
+    colors = gsb().spherical_harmonics(deg, dirs, coeffs)
+    assert_close(colors, gd[f"deg{deg}_colors"], 1e-4, 1e-5, name="colors")
+    vcol = torch.from_numpy(gd[f"deg{deg}_v_colors"]).to(DEV)
+    gc, gdirs = torch.autograd.grad((colors * vcol).sum(), (coeffs, dirs))
+    assert_close(gc, gd[f"deg{deg}_v_coeffs"], 1e-4, 1e-5, name="v_coeffs")
+    if deg > 0:
+        assert_close(gdirs, gd[f"deg{deg}_v_dirs"], 1e-4, 1e-4, name="v_dirs")
+
+
+@pytest.mark.parametrize("batch", [(), (3,)])
+def test_sh_masked_vs_oracle(batch):
+    g = torch.Generator().manual_seed(9)
+    N = 2000
+    dirs = torch.randn(batch + (N, 3), generator=g)
+    coeffs = torch.randn(batch + (N, 16, 3), generator=g)
+    masks = torch.rand(batch + (N,), generator=g) > 0.3
+    out = gsb().spherical_harmonics(3, dirs.to(DEV), coeffs.to(DEV), masks.to(DEV))
+    ref = O.sh_fwd(3, dirs.numpy(), coeffs.numpy(), masks.numpy())
+    assert_close(out, ref, 1e-4, 1e-5, name="colors")
+
+
+# ---------------------------------------------------------------------------
+# Tile intersection, sort, offsets
+# ---------------------------------------------------------------------------
+def test_isect_aabb_bit_exact_vs_reference_golden():
+    gd = dict(np.load(os.path.join(GOLD, "isect_aabb.npz")))
+    ts, tw, th = int(gd["tile_size"]), int(gd["tile_width"]), int(gd["tile_height"])
+    t = lambda k: torch.from_numpy(gd[k]).to(DEV)
+    tpg, keys, ids = gsb().isect_tiles(t("means2d"), t("radii"), t("depths"), ts, tw, th)
+    assert_equal(tpg, gd["tiles_per_gauss"], "tiles_per_gauss")
+    assert_equal(keys, gd["isect_ids"], "isect_ids")
+    assert_equal(ids, gd["flatten_ids"], "flatten_ids")
+    off = gsb().isect_offset_encode(keys, gd["means2d"].shape[0], tw, th)
+    assert_equal(off, gd["isect_offsets"], "offsets")
+
+
+@pytest.mark.parametrize("batch", [(), (2,)])
+def test_isect_aabb_batch_dims(batch):
+    """reference test_isect with batch dims (tests/test_basic.py:698-736)."""
+    gd = dict(np.load(os.path.join(GOLD, "isect_aabb.npz")))
+    ts, tw, th = int(gd["tile_size"]), int(gd["tile_width"]), int(gd["tile_height"])
+    exp = lambda a: np.ascontiguousarray(np.broadcast_to(a, batch + a.shape))
+    m2, r, dep = exp(gd["means2d"]), exp(gd["radii"]), exp(gd["depths"])
+    tpg, keys, ids = gsb().isect_tiles(torch.from_numpy(m2).to(DEV), torch.from_numpy(r).to(DEV),
+                                       torch.from_numpy(dep).to(DEV), ts, tw, th)
+    etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th)
+    assert_equal(tpg, etpg, "tiles_per_gauss")
+    assert_equal(keys, ekeys, "isect_ids")
+    assert_equal(ids, eids, "flatten_ids")
+    I = int(np.prod(m2.shape[:-2]))
+    assert_equal(gsb().isect_offset_encode(keys, I, tw, th), O.isect_offset_encode(ekeys, I, tw, th), "offsets")
+
+
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("tile_size", [16, 8])
+def test_isect_accutile_bit_exact_vs_oracle(packed, tile_size):
+    d = _data.to(_data.scene(20000, seed=8, C=2, width=320, height=240, fx=260.0), DEV)
+    out = project(d, packed=packed, calc=True)
+    if packed:
+        bids, cids, gids, indptr, radii, means2d, depths, conics, comps = out
+        opac = d["opacities"][gids] * comps
+        image_ids = bids * 2 + cids
+    else:
+        radii, means2d, depths, conics, comps = out
+        opac = d["opacities"][None].expand(2, -1) * comps
+        image_ids = None
+        gids = None
+    tw = math.ceil(d["width"] / tile_size)
+    th = math.ceil(d["height"] / tile_size)
+    tpg, keys, ids = gsb().isect_tiles(means2d, radii, depths, tile_size, tw, th, packed=packed,
+                                       n_images=2, image_ids=image_ids, gaussian_ids=gids,
+                                       conics=conics, opacities=opac)
+    etpg, ekeys, eids = O.isect_tiles(as_np(means2d), as_np(radii), as_np(depths), tile_size, tw,
+                                      th, conics=as_np(conics), opacities=as_np(opac),
+                                      image_ids=as_np(image_ids) if packed else None, n_images=2)
+    assert keys.numel() > 10000
+    assert_equal(tpg, etpg, "tiles_per_gauss")
+    assert_equal(keys, ekeys, "isect_ids")
+    assert_equal(ids, eids, "flatten_ids")
+    assert_equal(gsb().isect_offset_encode(keys, 2, tw, th), O.isect_offset_encode(ekeys, 2, tw, th),
+                 "offsets")
+    # AccuTile never keeps more tiles than the axis-aligned box of the radii
+    tpg_aabb, _, _ = gsb().isect_tiles(means2d, radii, depths, tile_size, tw, th, packed=packed,
+                                       n_images=2, image_ids=image_ids, gaussian_ids=gids)
+    assert (tpg <= tpg_aabb).all()
+
+
+@pytest.mark.parametrize("n", [1, 4095, 4096, 4097, 300_001])
+def test_radix_sort_stable_vs_numpy(n):
+    from gsplat_b200.cuda._wrapper import _radix_sort
+
+    rng = np.random.default_rng(n)
+    keys = rng.integers(0, 1 << 46, size=n, dtype=np.int64)
+    keys[: n // 3] = keys[n // 2]  # many duplicates to exercise stability
+    vals = np.arange(n, dtype=np.int32)
+    k, v = _radix_sort(torch.from_numpy(keys).to(DEV), torch.from_numpy(vals).to(DEV), 46)
+    order = np.argsort(keys, kind="stable")
+    assert_equal(k, keys[order], "keys")
+    assert_equal(v, vals[order], "vals")
+
+
+def test_isect_empty():
+    g = gsb()
+    z = torch.zeros((1, 0, 2), device=DEV)
+    tpg, keys, ids = g.isect_tiles(z, torch.zeros((1, 0, 2), device=DEV, dtype=torch.int32),
+                                   torch.zeros((1, 0), device=DEV), 16, 4, 4)
+    assert keys.numel() == 0 and ids.numel() == 0
+    off = g.isect_offset_encode(keys, 1, 4, 4)
+    assert (off == 0).all()
+
+
+# ---------------------------------------------------------------------------
+# Rasterization
+# ---------------------------------------------------------------------------
+def raster_inputs(N=6000, seed=10, C=2, W=200, H=150, tile_size=16, channels=3, packed=False):
+    d = _data.to(_data.scene(N, seed=seed, C=C, width=W, height=H, fx=220.0), DEV)
+    d["scales"] = d["scales"] * 2.0
+    out = project(d, packed=packed, calc=False)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    if packed:
+        bids, cids, gids, indptr, radii, means2d, depths, conics, _ = out
+        opac = d["opacities"][gids]
+        image_ids = cids
+        colors = torch.rand((gids.numel(), channels), device=DEV, generator=g)
+    else:
+        radii, means2d, depths, conics, _ = out
+        opac = d["opacities"][None].expand(C, -1).contiguous()
+        image_ids, gids = None, None
+        colors = torch.rand((C, N, channels), device=DEV, generator=g)
+    tw, th = math.ceil(W / tile_size), math.ceil(H / tile_size)
+    _, keys, fids = gsb().isect_tiles(means2d, radii, depths, tile_size, tw, th, packed=packed,
+                                      n_images=C, image_ids=image_ids, gaussian_ids=gids,
+                                      conics=conics, opacities=opac)
+    offsets = gsb().isect_offset_encode(keys, C, tw, th)
+    return dict(means2d=means2d, conics=conics, colors=colors, opac=opac, W=W, H=H, C=C,
+                tile_size=tile_size, offsets=offsets, fids=fids, packed=packed)
+
+
+def run_raster(r, backgrounds=None, masks=None, absgrad=False):
+    means2d = r["means2d"].detach().clone().requires_grad_(True)
+    conics = r["conics"].detach().clone().requires_grad_(True)
+    colors = r["colors"].detach().clone().requires_grad_(True)
+    opac = r["opac"].detach().clone().requires_grad_(True)
+    rc, ra = gsb().rasterize_to_pixels(means2d, conics, colors, opac, r["W"], r["H"], r["tile_size"],
+                                       r["offsets"], r["fids"], backgrounds=backgrounds, masks=masks,
+                                       packed=r["packed"], absgrad=absgrad)
+    return means2d, conics, colors, opac, rc, ra
+
+
+@pytest.mark.parametrize("channels,tile_size", [(1, 16), (3, 16), (4, 16), (8, 16), (3, 8),
+                                                (32, 16), (33, 16), (128, 4)])
+@pytest.mark.parametrize("packed", [False, True])
+def test_rasterize_vs_oracle(channels, tile_size, packed):
+    r = raster_inputs(channels=channels, tile_size=tile_size, packed=packed)
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    bg = torch.rand((r["C"], channels), device=DEV, generator=gen)
+    means2d, conics, colors, opac, rc, ra = run_raster(r, backgrounds=bg)
+    er, ea, elast = O.raster_fwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]),
+                                 as_np(r["opac"]), r["W"], r["H"], tile_size, as_np(r["offsets"]),
+                                 as_np(r["fids"]), backgrounds=as_np(bg))
+    # Forward: fp32 on both sides, same per-pixel order. A pair whose alpha lands
+    # within an ulp of 1/255 may be kept by one side only (exp evaluations differ
+    # by a few ulp); allow 1e-4 of the pixels for that.
+    assert_close(rc, er, 1e-4, 1e-5, max_bad_frac=1e-4, name="render_colors")
+    assert_close(ra, ea, 1e-4, 1e-5, max_bad_frac=1e-4, name="render_alphas")
+    vr = torch.randn(rc.shape, device=DEV, generator=gen)
+    va = torch.randn(ra.shape, device=DEV, generator=gen)
+    grads = torch.autograd.grad((rc * vr).sum() + (ra * va).sum(), (means2d, conics, colors, opac))
+    e = O.raster_bwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]), as_np(r["opac"]),
+                     r["W"], r["H"], tile_size, as_np(r["offsets"]), as_np(r["fids"]), ea, elast,
+                     as_np(vr), as_np(va), backgrounds=as_np(bg))
+    # Backward: fp32 atomics (order-dependent) vs float64 sums.
+    for got, exp, name, rtol, atol in ((grads[0], e[0], "v_means2d", 1e-3, 1e-4),
+                                       (grads[1], e[1], "v_conics", 1e-3, 1e-4),
+                                       (grads[2], e[2], "v_colors", 1e-4, 1e-5),
+                                       (grads[3], e[3], "v_opacities", 1e-3, 1e-4)):
+        assert_close(got, exp, rtol, atol, max_bad_frac=1e-3, name=name)
+
+
+def test_rasterize_masks_and_absgrad():
+    r = raster_inputs(channels=3)
+    gen = torch.Generator(device=DEV).manual_seed(2)
+    masks = torch.rand(r["offsets"].shape, device=DEV, generator=gen) > 0.3
+    means2d, conics, colors, opac, rc, ra = run_raster(r, masks=masks, absgrad=True)
+    er, ea, elast = O.raster_fwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]),
+                                 as_np(r["opac"]), r["W"], r["H"], 16, as_np(r["offsets"]),
+                                 as_np(r["fids"]), masks=as_np(masks))
+    assert_close(rc, er, 1e-4, 1e-5, max_bad_frac=1e-4, name="render_colors")
+    vr = torch.randn(rc.shape, device=DEV, generator=gen)
+    (rc * vr).sum().backward()
+    e = O.raster_bwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]), as_np(r["opac"]),
+                     r["W"], r["H"], 16, as_np(r["offsets"]), as_np(r["fids"]), ea, elast, as_np(vr),
+                     np.zeros_like(ea), masks=as_np(masks), absgrad=True)
+    assert_close(means2d.grad, e[0], 1e-3, 1e-4, max_bad_frac=1e-3, name="v_means2d")
+    assert_close(means2d.absgrad, e[4], 1e-3, 1e-4, max_bad_frac=1e-3, name="absgrad")
+
+
+# ---------------------------------------------------------------------------
+# Adam
+# ---------------------------------------------------------------------------
+def test_adam_vs_oracle():
+    rng = np.random.default_rng(3)
+    N = 10001
+    shapes = [(N, 3), (N, 4), (N,), (N, 1, 3), (N, 15, 3)]
+    valid = rng.uniform(size=N) > 0.4
+    vt = torch.from_numpy(valid).to(DEV)
+    for shp in shapes:
+        p = rng.normal(size=shp).astype(np.float32)
+        g = rng.normal(size=shp).astype(np.float32)
+        m = rng.normal(size=shp).astype(np.float32) * 0.1
+        v = np.abs(rng.normal(size=shp)).astype(np.float32) * 0.1
+        tp, tg, tm, tv = (torch.from_numpy(x.copy()).to(DEV) for x in (p, g, m, v))
+        gsb().adam(tp, tg, tm, tv, vt, 1e-3, 0.9, 0.999, 1e-15)
+        O.adam(p, g, m, v, valid, 1e-3, 0.9, 0.999, 1e-15)
+        assert_close(tp, p, 1e-6, 1e-7, name=f"param{shp}")
+        assert_close(tm, m, 1e-6, 1e-7, name=f"exp_avg{shp}")
+        assert_close(tv, v, 1e-6, 1e-9, name=f"exp_avg_sq{shp}")
+
+
+def test_selective_adam_step_matches_per_group_adam():
+    torch.manual_seed(0)
+    N = 5000
+    params = [torch.nn.Parameter(torch.randn(N, k, device=DEV)) for k in (3, 4, 1, 48)]
+    ref = [p.detach().clone() for p in params]
+    lrs = [1.6e-4, 1e-3, 5e-2, 2.5e-3]
+    opt = gsb().SelectiveAdam([{"params": [p], "lr": lr} for p, lr in zip(params, lrs)],
+                              eps=1e-15, betas=(0.9, 0.999))
+    vis = torch.rand(N, device=DEV) > 0.5
+    ms = [torch.zeros_like(r) for r in ref]
+    vs = [torch.zeros_like(r) for r in ref]
+    for step in range(3):
+        for p in params:
+            p.grad = torch.randn_like(p)
+        grads = [p.grad.clone() for p in params]
+        opt.step(vis)
+        for r, g, m, v, lr in zip(ref, grads, ms, vs, lrs):
+            gsb().adam(r, g, m, v, vis, lr, 0.9, 0.999, 1e-15)
+    for p, r in zip(params, ref):
+        assert_equal(p.detach(), r, "param")
+    st = opt.state[params[0]]
+    assert set(st.keys()) == {"step", "exp_avg", "exp_avg_sq"}
+
+
+def test_no_cpu_fallback():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gsb().spherical_harmonics(0, torch.randn(4, 3), torch.randn(4, 1, 3))
