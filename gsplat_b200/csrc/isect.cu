@@ -31,12 +31,17 @@ struct EmitSink {
     int64_t *keys;
     int32_t *ids;
     int64_t cursor;
+    int64_t limit; // end of this splat's slot range (count pass result)
     int64_t key_hi_base; // image_id << (32 + tile_bits)
     int64_t depth_bits;
     int32_t flat_id;
     __device__ __forceinline__ void put(int64_t tile_id) {
-        keys[cursor] = key_hi_base | (tile_id << 32) | depth_bits;
-        ids[cursor] = flat_id;
+        // The emit pass repeats the count pass's arithmetic exactly; the bound
+        // only guards the output arrays should the two ever disagree.
+        if (cursor < limit) {
+            keys[cursor] = key_hi_base | (tile_id << 32) | depth_bits;
+            ids[cursor] = flat_id;
+        }
         ++cursor;
     }
 };
@@ -167,12 +172,14 @@ __global__ void __launch_bounds__(256) isect_emit_kernel(IsectParams p, const in
     const uint32_t n = p.packed ? p.nnz : p.I * p.N;
     if (idx >= n) return;
     const int64_t start = idx == 0 ? 0 : cum_tiles[idx - 1];
-    if (cum_tiles[idx] == start) return;
+    const int64_t limit = cum_tiles[idx];
+    if (limit == start) return;
     const int64_t iid = p.packed ? p.image_ids[idx] : (int64_t)(idx / p.N);
     EmitSink sink;
     sink.keys = keys;
     sink.ids = ids;
     sink.cursor = start;
+    sink.limit = limit;
     sink.key_hi_base = iid << (32 + p.tile_n_bits);
     sink.depth_bits = (int64_t)det_f2u(p.depths[idx]);
     sink.flat_id = (int32_t)idx;

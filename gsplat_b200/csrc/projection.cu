@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(256) projection_packed_count_kernel(ProjParams
 // block_accum is the inclusive scan of block_cnts; output order is row-major in
 // (b, c) and then by Gaussian id, matching the reference's BlockScan ordering.
 __global__ void __launch_bounds__(256) projection_packed_write_kernel(
-    ProjParams p, const int64_t *block_accum, int32_t *indptr, int64_t *batch_ids,
+    ProjParams p, const int64_t *block_accum, int64_t nnz, int32_t *indptr, int64_t *batch_ids,
     int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii, float *means2d, float *depths,
     float *conics, float *comps) {
     __shared__ int32_t warp_tot[8];
@@ -214,8 +214,10 @@ __global__ void __launch_bounds__(256) projection_packed_write_kernel(
     int32_t warp_off = 0;
     for (uint32_t w = 0; w < warp; ++w) warp_off += warp_tot[w];
     const int64_t base = block_idx == 0 ? 0 : block_accum[block_idx - 1];
-    if (o.valid) {
-        const int64_t pos = base + warp_off + __popc(ballot & ((1u << lane) - 1u));
+    const int64_t pos = base + warp_off + __popc(ballot & ((1u << lane) - 1u));
+    // Pass 1 evaluated the same visibility test; the bound only guards the
+    // outputs should the two passes ever disagree.
+    if (o.valid && pos < nnz) {
         batch_ids[pos] = b;
         camera_ids[pos] = c;
         gaussian_ids[pos] = g;
@@ -709,9 +711,10 @@ extern "C" int gsb_projection_packed_write(
     int B, int C, int N, const float *means, const float *covars, const float *quats,
     const float *scales, const float *opacities, const float *viewmats, const float *Ks, int width,
     int height, float eps2d, float near_plane, float far_plane, float radius_clip,
-    int calc_compensations, int camera_model, const int64_t *block_accum, int32_t *indptr,
-    int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii,
-    float *means2d, float *depths, float *conics, float *compensations, cudaStream_t stream) {
+    int calc_compensations, int camera_model, const int64_t *block_accum, long long nnz,
+    int32_t *indptr, int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids,
+    int32_t *radii, float *means2d, float *depths, float *conics, float *compensations,
+    cudaStream_t stream) {
     if (int e = check_camera_model(camera_model)) return e;
     if ((size_t)B * C == 0 || N == 0) return kOk;
     ProjParams p = make_params(B, C, N, means, covars, quats, scales, opacities, viewmats, Ks, width,
@@ -719,7 +722,7 @@ extern "C" int gsb_projection_packed_write(
                                calc_compensations, camera_model);
     dim3 grid((N + 255) / 256, B * C);
     projection_packed_write_kernel<<<grid, 256, 0, stream>>>(
-        p, block_accum, indptr, batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
+        p, block_accum, nnz, indptr, batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
         calc_compensations ? compensations : nullptr);
     return check_launch("projection_packed_write_kernel");
 }

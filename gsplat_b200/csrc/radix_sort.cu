@@ -132,8 +132,10 @@ __global__ void __launch_bounds__(kSortThreads)
         const uint64_t key = S.keys[i];
         const uint32_t dd = (uint32_t)(key >> shift) & 0xffu;
         const int64_t gp = S.gbase[dd] + (int64_t)(i - S.local_start[dd]);
-        keys_out[gp] = key;
-        vals_out[gp] = S.vals[i];
+        if (gp >= 0 && gp < (int64_t)n) {
+            keys_out[gp] = key;
+            vals_out[gp] = S.vals[i];
+        }
     }
 }
 
@@ -167,12 +169,8 @@ int radix_sort_pairs(uint64_t *keys, int32_t *vals, uint64_t *keys_alt, int32_t 
     void *scan_scratch = sp + off;
     const size_t scan_bytes = scratch_bytes - off;
 
-    static bool attr_set = false;
     const int smem = (int)sizeof(DownsweepSmem);
-    if (!attr_set) {
-        cudaFuncSetAttribute(radix_downsweep, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        attr_set = true;
-    }
+    cudaFuncSetAttribute(radix_downsweep, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     uint64_t *kin = keys, *kout = keys_alt;
     int32_t *vin = vals, *vout = vals_alt;
     int which = 0;

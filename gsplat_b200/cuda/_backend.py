@@ -52,7 +52,7 @@ SIGNATURES = {
     ),
     "gsb_projection_packed_blocks": (I32, [I32]),
     "gsb_projection_packed_count": (I32, _PROJ_COMMON + [P, P]),
-    "gsb_projection_packed_write": (I32, _PROJ_COMMON + [P, P, P, P, P, P, P, P, P, P, P]),
+    "gsb_projection_packed_write": (I32, _PROJ_COMMON + [P, I64, P, P, P, P, P, P, P, P, P, P]),
     "gsb_projection_packed_bwd": (
         I32,
         [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, F32, I32, P, P, P, P, P, P, P, P, P, I32,

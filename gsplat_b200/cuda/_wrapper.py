@@ -332,7 +332,7 @@ class _FullyFusedProjectionPacked(torch.autograd.Function):
             conics = torch.empty((nnz, 3), dtype=means.dtype, device=dev)
             comps = torch.zeros(nnz, dtype=means.dtype, device=dev) if calc_compensations else None
             if block_accum.numel() > 0:
-                call("gsb_projection_packed_write", *common, ptr(block_accum), ptr(indptr),
+                call("gsb_projection_packed_write", *common, ptr(block_accum), nnz, ptr(indptr),
                      ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids), ptr(radii), ptr(means2d),
                      ptr(depths), ptr(conics), ptr(comps), stream)
         ctx.save_for_backward(batch_ids, camera_ids, gaussian_ids, means, covars, quats, scales,

@@ -74,7 +74,7 @@ GSB_API int gsb_projection_fused_bwd(int B, int C, int N, const float *means, co
  *   1. gsb_projection_packed_count -> block_cnts int32 [B*C*blocks], blocks =
  *      gsb_projection_packed_blocks(N);
  *   2. gsb_inclusive_scan_i32(block_cnts) -> block_accum int64; nnz = last entry;
- *   3. gsb_projection_packed_write with outputs of length nnz and indptr [B*C+1].
+ *   3. gsb_projection_packed_write with nnz, outputs of length nnz and indptr [B*C+1].
  * Pairs are ordered by (batch, camera) then Gaussian id. */
 GSB_API int gsb_projection_packed_blocks(int N);
 GSB_API int gsb_projection_packed_count(int B, int C, int N, const float *means, const float *covars,
@@ -88,7 +88,8 @@ GSB_API int gsb_projection_packed_write(int B, int C, int N, const float *means,
                                 const float *viewmats, const float *Ks, int width, int height,
                                 float eps2d, float near_plane, float far_plane, float radius_clip,
                                 int calc_compensations, int camera_model,
-                                const int64_t *block_accum, int32_t *indptr, int64_t *batch_ids,
+                                const int64_t *block_accum, long long nnz, int32_t *indptr,
+                                int64_t *batch_ids,
                                 int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii,
                                 float *means2d, float *depths, float *conics,
                                 float *compensations, cudaStream_t stream);
