@@ -189,10 +189,12 @@ def run_gsb(args):
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         barrier()
+        wall0 = time.perf_counter()
         start.record()
         for _ in range(args.steps):
             loss, meta = train_step(params, opt, viewmat, K, W, H, G, Ga, distributed)
         end.record()
+        host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
         barrier()
     ms = start.elapsed_time(end) / args.steps
     timing = _backend.timing
@@ -268,6 +270,7 @@ def run_gsb(args):
         "clocks": sampler.summary(),
         "e2e": e2e,
         "ops": ops,
+        "host_issue_ms_per_step": host_ms,
     }
     if rank == 0:
         print(json.dumps(result), flush=True)

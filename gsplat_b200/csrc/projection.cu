@@ -14,123 +14,9 @@
 // Gaussians (warp butterfly + one atomic per warp and camera).
 #include "common.cuh"
 #include "gsb_internal.h"
+#include "projection_common.cuh"
 
 namespace gsb {
-
-struct ProjParams {
-    uint32_t B, C, N;
-    const float *means, *covars, *quats, *scales, *opacities, *viewmats, *Ks;
-    uint32_t W, H;
-    float eps2d, near_plane, far_plane, radius_clip;
-    bool calc_comp;
-    int camera_model;
-};
-
-struct ProjOut {
-    bool valid;
-    int32_t rx, ry;
-    float mx, my, depth, conic[3], comp;
-};
-
-__device__ inline void load_gaussian(const ProjParams &p, uint32_t b, uint32_t g, float mean[3],
-                                     M3 &covar) {
-    const float *mp = p.means + ((size_t)b * p.N + g) * 3;
-    mean[0] = mp[0];
-    mean[1] = mp[1];
-    mean[2] = mp[2];
-    if (p.covars != nullptr) {
-        const float *cp = p.covars + ((size_t)b * p.N + g) * 6;
-        covar.m[0][0] = cp[0];
-        covar.m[0][1] = cp[1];
-        covar.m[0][2] = cp[2];
-        covar.m[1][0] = cp[1];
-        covar.m[1][1] = cp[3];
-        covar.m[1][2] = cp[4];
-        covar.m[2][0] = cp[2];
-        covar.m[2][1] = cp[4];
-        covar.m[2][2] = cp[5];
-    } else {
-        const float *qp = p.quats + ((size_t)b * p.N + g) * 4;
-        const float *sp = p.scales + ((size_t)b * p.N + g) * 3;
-        const float qa[4] = {qp[0], qp[1], qp[2], qp[3]};
-        const float sa[3] = {sp[0], sp[1], sp[2]};
-        covar = covar_from_quat_scale(qa, sa, nullptr);
-    }
-}
-
-// Projects one Gaussian into one camera; follows ProjectionEWA3DGSFused.cu:72-233.
-__device__ inline ProjOut project_one(const ProjParams &p, uint32_t b, uint32_t c, uint32_t g,
-                                      const float mean[3], const M3 &covar) {
-    ProjOut o;
-    o.valid = false;
-    const float *vm = p.viewmats + ((size_t)b * p.C + c) * 16;
-    const float *K = p.Ks + ((size_t)b * p.C + c) * 9;
-    M3 R;
-    R.m[0][0] = vm[0];
-    R.m[0][1] = vm[1];
-    R.m[0][2] = vm[2];
-    R.m[1][0] = vm[4];
-    R.m[1][1] = vm[5];
-    R.m[1][2] = vm[6];
-    R.m[2][0] = vm[8];
-    R.m[2][1] = vm[9];
-    R.m[2][2] = vm[10];
-    const float x = R.m[0][0] * mean[0] + R.m[0][1] * mean[1] + R.m[0][2] * mean[2] + vm[3];
-    const float y = R.m[1][0] * mean[0] + R.m[1][1] * mean[1] + R.m[1][2] * mean[2] + vm[7];
-    const float z = R.m[2][0] * mean[0] + R.m[2][1] * mean[1] + R.m[2][2] * mean[2] + vm[11];
-    if (z < p.near_plane || z > p.far_plane) return o;
-
-    const M3 cov_c = m3_mul_bt(m3_mul(R, covar), R);
-    const float fx = K[0], cx = K[2], fy = K[4], cy = K[5];
-    float s00, s01, s11, mx, my;
-    if (p.camera_model == kOrtho) {
-        jsjt(cov_c, fx, 0.f, fy, 0.f, s00, s01, s11);
-        mx = fx * x + cx;
-        my = fy * y + cy;
-    } else {
-        float lxp, lxn, lyp, lyn;
-        persp_limits(fx, fy, cx, cy, p.W, p.H, lxp, lxn, lyp, lyn);
-        const float rz = 1.f / z;
-        const float rz2 = rz * rz;
-        const float tx = z * fminf(lxp, fmaxf(-lxn, x * rz));
-        const float ty = z * fminf(lyp, fmaxf(-lyn, y * rz));
-        jsjt(cov_c, fx * rz, -fx * tx * rz2, fy * rz, -fy * ty * rz2, s00, s01, s11);
-        mx = fx * x * rz + cx;
-        my = fy * y * rz + cy;
-    }
-    // add_blur (Utils.cuh:424-432)
-    const float det_orig = s00 * s11 - s01 * s01;
-    s00 += p.eps2d;
-    s11 += p.eps2d;
-    const float det = s00 * s11 - s01 * s01;
-    const float comp = sqrtf(fmaxf(kMinCompensation * kMinCompensation, det_orig / det));
-    if (det <= 0.f) return o;
-    const float inv_det = 1.f / det;
-
-    float extend = kGaussianExtend;
-    if (p.opacities != nullptr) {
-        float op = p.opacities[(size_t)b * p.N + g];
-        if (p.calc_comp) op *= comp;
-        if (op < kAlphaThreshold) return o;
-        extend = fminf(kGaussianExtend, sqrtf(2.f * det_logf(op / kAlphaThreshold)));
-    }
-    const float rx = ceilf(extend * sqrtf(s00));
-    const float ry = ceilf(extend * sqrtf(s11));
-    if (rx <= p.radius_clip && ry <= p.radius_clip) return o;
-    if (mx + rx <= 0.f || mx - rx >= (float)p.W || my + ry <= 0.f || my - ry >= (float)p.H) return o;
-
-    o.valid = true;
-    o.rx = (int32_t)rx;
-    o.ry = (int32_t)ry;
-    o.mx = mx;
-    o.my = my;
-    o.depth = z;
-    o.conic[0] = s11 * inv_det;
-    o.conic[1] = -s01 * inv_det;
-    o.conic[2] = s00 * inv_det;
-    o.comp = comp;
-    return o;
-}
 
 __global__ void __launch_bounds__(256) projection_fwd_dense_kernel(ProjParams p, int32_t *radii,
                                                                    float *means2d, float *depths,
@@ -168,11 +54,14 @@ __global__ void __launch_bounds__(256) projection_fwd_dense_kernel(ProjParams p,
     }
 }
 
-// Packed layout, pass 1: number of visible (camera, Gaussian) pairs per block
-// row. The grid is (ceil(N/256), B*C) like ProjectionEWA3DGSPacked.cu; a block's
-// count goes to block_cnts[row * blocks_per_row + col].
+// Packed layout, pass 1: visibility of every (camera, Gaussian) pair. The grid is
+// (ceil(N/256), B*C) like ProjectionEWA3DGSPacked.cu; each warp stores its ballot
+// in vis_bits[(row * gridDim.x + blockIdx.x) * 8 + warp] and each block its count
+// in block_cnts[row * gridDim.x + blockIdx.x]. Pass 2 reuses the stored ballots,
+// so both passes agree on the compacted positions by construction.
 __global__ void __launch_bounds__(256) projection_packed_count_kernel(ProjParams p,
-                                                                      int32_t *block_cnts) {
+                                                                      int32_t *block_cnts,
+                                                                      uint32_t *vis_bits) {
     const uint32_t row = blockIdx.y;
     const uint32_t b = row / p.C, c = row % p.C;
     const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
@@ -183,211 +72,59 @@ __global__ void __launch_bounds__(256) projection_packed_count_kernel(ProjParams
         load_gaussian(p, b, g, mean, covar);
         valid = project_one(p, b, c, g, mean, covar).valid;
     }
+    const size_t block_idx = (size_t)row * gridDim.x + blockIdx.x;
+    const uint32_t ballot = __ballot_sync(0xffffffffu, valid);
+    if ((threadIdx.x & 31) == 0) vis_bits[block_idx * 8 + (threadIdx.x >> 5)] = ballot;
     const int n = __syncthreads_count(valid);
-    if (threadIdx.x == 0) block_cnts[(size_t)row * gridDim.x + blockIdx.x] = n;
+    if (threadIdx.x == 0) block_cnts[block_idx] = n;
+}
+
+// Position of this lane's pair in the packed arrays (valid lanes only), from the
+// pass-1 ballots and the inclusive scan of the block counts.
+__device__ inline int64_t packed_position(const uint32_t *vis_bits, const int64_t *block_accum,
+                                          size_t block_idx, uint32_t &ballot) {
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t *words = vis_bits + block_idx * 8;
+    ballot = words[warp];
+    int64_t off = block_idx == 0 ? 0 : block_accum[block_idx - 1];
+    for (uint32_t w = 0; w < warp; ++w) off += __popc(words[w]);
+    return off + __popc(ballot & ((1u << lane) - 1u));
 }
 
 // Packed layout, pass 2: write the visible pairs at their compacted position.
-// block_accum is the inclusive scan of block_cnts; output order is row-major in
-// (b, c) and then by Gaussian id, matching the reference's BlockScan ordering.
+// Output order is row-major in (b, c) and then by Gaussian id, matching the
+// reference's BlockScan ordering.
 __global__ void __launch_bounds__(256) projection_packed_write_kernel(
-    ProjParams p, const int64_t *block_accum, int64_t nnz, int32_t *indptr, int64_t *batch_ids,
-    int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii, float *means2d, float *depths,
-    float *conics, float *comps) {
-    __shared__ int32_t warp_tot[8];
+    ProjParams p, const uint32_t *vis_bits, const int64_t *block_accum, int64_t nnz,
+    int32_t *indptr, int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids,
+    int32_t *radii, float *means2d, float *depths, float *conics, float *comps) {
     const uint32_t row = blockIdx.y;
     const uint32_t b = row / p.C, c = row % p.C;
     const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
     const size_t block_idx = (size_t)row * gridDim.x + blockIdx.x;
-    ProjOut o;
-    o.valid = false;
-    if (g < p.N) {
-        float mean[3];
-        M3 covar;
-        load_gaussian(p, b, g, mean, covar);
-        o = project_one(p, b, c, g, mean, covar);
-    }
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t ballot = __ballot_sync(0xffffffffu, o.valid);
-    if (lane == 0) warp_tot[warp] = __popc(ballot);
-    __syncthreads();
-    int32_t warp_off = 0;
-    for (uint32_t w = 0; w < warp; ++w) warp_off += warp_tot[w];
-    const int64_t base = block_idx == 0 ? 0 : block_accum[block_idx - 1];
-    const int64_t pos = base + warp_off + __popc(ballot & ((1u << lane) - 1u));
-    // Pass 1 evaluated the same visibility test; the bound only guards the
-    // outputs should the two passes ever disagree.
-    if (o.valid && pos < nnz) {
-        batch_ids[pos] = b;
-        camera_ids[pos] = c;
-        gaussian_ids[pos] = g;
-        radii[pos * 2] = o.rx;
-        radii[pos * 2 + 1] = o.ry;
-        means2d[pos * 2] = o.mx;
-        means2d[pos * 2 + 1] = o.my;
-        depths[pos] = o.depth;
-        conics[pos * 3 + 0] = o.conic[0];
-        conics[pos * 3 + 1] = o.conic[1];
-        conics[pos * 3 + 2] = o.conic[2];
-        if (comps) comps[pos] = o.comp;
-    }
+    uint32_t ballot;
+    const int64_t pos = packed_position(vis_bits, block_accum, block_idx, ballot);
     if (threadIdx.x == 0 && blockIdx.x == 0) {
-        indptr[row] = (int32_t)base;
+        indptr[row] = (int32_t)(block_idx == 0 ? 0 : block_accum[block_idx - 1]);
         if (row == gridDim.y - 1) indptr[gridDim.y] = (int32_t)block_accum[(size_t)gridDim.y * gridDim.x - 1];
     }
-}
-
-// ---------------------------------------------------------------------------
-// Backward
-// ---------------------------------------------------------------------------
-
-struct ProjGrads {
-    float v_mean[3];
-    M3 v_cov;     // dL/dSigma (world)
-    M3 v_R;       // dL/dR of this camera
-    float v_t[3]; // dL/dt of this camera
-};
-
-// VJP of project_one for one (camera, Gaussian) pair: Utils.cuh:417-467 (inverse,
-// blur), 583-660 (pinhole), 502-540 (ortho), 62-112 (world-to-camera).
-__device__ inline void project_one_vjp(const ProjParams &p, uint32_t b, uint32_t c,
-                                       const float mean[3], const M3 &covar, const float conic[3],
-                                       float comp, const float v_m2d[2], float v_depth,
-                                       const float v_conic[3], float v_comp, bool has_vcomp,
-                                       ProjGrads &gr) {
-    // inverse VJP: v_S = -Inv V Inv, V = [[va, vb/2], [vb/2, vc]]
-    const float i00 = conic[0], i01 = conic[1], i11 = conic[2];
-    const float va = v_conic[0], vb = 0.5f * v_conic[1], vc = v_conic[2];
-    // Inv V
-    const float t00 = i00 * va + i01 * vb, t01 = i00 * vb + i01 * vc;
-    const float t10 = i01 * va + i11 * vb, t11 = i01 * vb + i11 * vc;
-    float g00 = -(t00 * i00 + t01 * i01);
-    float g01 = -(t00 * i01 + t01 * i11);
-    float g10 = -(t10 * i00 + t11 * i01);
-    float g11 = -(t10 * i01 + t11 * i11);
-    if (has_vcomp) {
-        const float det_conic = i00 * i11 - i01 * i01;
-        const float v_sqr = v_comp * 0.5f / (comp + 1e-6f);
-        const float omc = 1.f - comp * comp;
-        g00 += v_sqr * (omc * i00 - p.eps2d * det_conic);
-        g01 += v_sqr * (omc * i01);
-        g10 += v_sqr * (omc * i01);
-        g11 += v_sqr * (omc * i11 - p.eps2d * det_conic);
-    }
-
-    const float *vm = p.viewmats + ((size_t)b * p.C + c) * 16;
-    const float *K = p.Ks + ((size_t)b * p.C + c) * 9;
-    M3 R;
-    R.m[0][0] = vm[0];
-    R.m[0][1] = vm[1];
-    R.m[0][2] = vm[2];
-    R.m[1][0] = vm[4];
-    R.m[1][1] = vm[5];
-    R.m[1][2] = vm[6];
-    R.m[2][0] = vm[8];
-    R.m[2][1] = vm[9];
-    R.m[2][2] = vm[10];
-    const float x = R.m[0][0] * mean[0] + R.m[0][1] * mean[1] + R.m[0][2] * mean[2] + vm[3];
-    const float y = R.m[1][0] * mean[0] + R.m[1][1] * mean[1] + R.m[1][2] * mean[2] + vm[7];
-    const float z = R.m[2][0] * mean[0] + R.m[2][1] * mean[1] + R.m[2][2] * mean[2] + vm[11];
-    const M3 RS = m3_mul(R, covar);
-    const M3 cov_c = m3_mul_bt(RS, R);
-    const float fx = K[0], cx = K[2], fy = K[4], cy = K[5];
-
-    float vmc[3] = {0.f, 0.f, 0.f};
-    M3 vcov_c;
-    // J (2x3), v_cov3 += J^T G J
-    float J[2][3];
-    if (p.camera_model == kOrtho) {
-        J[0][0] = fx;
-        J[0][1] = 0.f;
-        J[0][2] = 0.f;
-        J[1][0] = 0.f;
-        J[1][1] = fy;
-        J[1][2] = 0.f;
-    } else {
-        const float rz = 1.f / z;
-        float lxp, lxn, lyp, lyn;
-        persp_limits(fx, fy, cx, cy, p.W, p.H, lxp, lxn, lyp, lyn);
-        const float rz2 = rz * rz;
-        const float tx = z * fminf(lxp, fmaxf(-lxn, x * rz));
-        const float ty = z * fminf(lyp, fmaxf(-lyn, y * rz));
-        J[0][0] = fx * rz;
-        J[0][1] = 0.f;
-        J[0][2] = -fx * tx * rz2;
-        J[1][0] = 0.f;
-        J[1][1] = fy * rz;
-        J[1][2] = -fy * ty * rz2;
-    }
-    // G J (2x3)
-    float GJ[2][3];
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-        GJ[0][j] = g00 * J[0][j] + g01 * J[1][j];
-        GJ[1][j] = g10 * J[0][j] + g11 * J[1][j];
-    }
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) vcov_c.m[i][j] = J[0][i] * GJ[0][j] + J[1][i] * GJ[1][j];
-
-    if (p.camera_model == kOrtho) {
-        vmc[0] += fx * v_m2d[0];
-        vmc[1] += fy * v_m2d[1];
-    } else {
-        const float rz = 1.f / z;
-        const float rz2 = rz * rz;
-        const float rz3 = rz2 * rz;
-        float lxp, lxn, lyp, lyn;
-        persp_limits(fx, fy, cx, cy, p.W, p.H, lxp, lxn, lyp, lyn);
-        const float tx = z * fminf(lxp, fmaxf(-lxn, x * rz));
-        const float ty = z * fminf(lyp, fmaxf(-lyn, y * rz));
-        vmc[0] += fx * rz * v_m2d[0];
-        vmc[1] += fy * rz * v_m2d[1];
-        vmc[2] += -(fx * x * v_m2d[0] + fy * y * v_m2d[1]) * rz2;
-        // v_J = G J S^T + G^T J S; S = cov_c is symmetric so both products use J S
-        float vJ[2][3];
-        // (J S) and (J S^T) rows; S symmetric so both equal
-        float JS[2][3];
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int j = 0; j < 3; ++j)
-                JS[r][j] = J[r][0] * cov_c.m[0][j] + J[r][1] * cov_c.m[1][j] + J[r][2] * cov_c.m[2][j];
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-            vJ[0][j] = g00 * JS[0][j] + g01 * JS[1][j] + g00 * JS[0][j] + g10 * JS[1][j];
-            vJ[1][j] = g10 * JS[0][j] + g11 * JS[1][j] + g01 * JS[0][j] + g11 * JS[1][j];
-        }
-        if (x * rz <= lxp && x * rz >= -lxn) {
-            vmc[0] += -fx * rz2 * vJ[0][2];
-        } else {
-            vmc[2] += -fx * rz3 * vJ[0][2] * tx;
-        }
-        if (y * rz <= lyp && y * rz >= -lyn) {
-            vmc[1] += -fy * rz2 * vJ[1][2];
-        } else {
-            vmc[2] += -fy * rz3 * vJ[1][2] * ty;
-        }
-        vmc[2] += -fx * rz2 * vJ[0][0] - fy * rz2 * vJ[1][1] + 2.f * fx * tx * rz3 * vJ[0][2] +
-                  2.f * fy * ty * rz3 * vJ[1][2];
-    }
-    vmc[2] += v_depth;
-
-    // world-to-camera VJPs
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-        gr.v_t[i] = vmc[i];
-        gr.v_mean[i] = R.m[0][i] * vmc[0] + R.m[1][i] * vmc[1] + R.m[2][i] * vmc[2];
-#pragma unroll
-        for (int j = 0; j < 3; ++j) gr.v_R.m[i][j] = vmc[i] * mean[j];
-    }
-    // v_R += G R S^T + G^T R S ; v_S = R^T G R   (G = vcov_c)
-    const M3 GRS = m3_mul(vcov_c, RS);                 // G (R S)
-    const M3 GtRS = m3_mul(m3_transpose(vcov_c), RS);  // G^T (R S)
-    // S symmetric: R S^T = R S
-    gr.v_R = m3_add(gr.v_R, m3_add(GRS, GtRS));
-    gr.v_cov = m3_mul(m3_mul_at(R, vcov_c), R);
+    if (!((ballot >> (threadIdx.x & 31)) & 1u) || g >= p.N || pos >= nnz) return;
+    float mean[3];
+    M3 covar;
+    load_gaussian(p, b, g, mean, covar);
+    const ProjOut o = project_one(p, b, c, g, mean, covar, true);
+    batch_ids[pos] = b;
+    camera_ids[pos] = c;
+    gaussian_ids[pos] = g;
+    radii[pos * 2] = o.rx;
+    radii[pos * 2 + 1] = o.ry;
+    means2d[pos * 2] = o.mx;
+    means2d[pos * 2 + 1] = o.my;
+    depths[pos] = o.depth;
+    conics[pos * 3 + 0] = o.conic[0];
+    conics[pos * 3 + 1] = o.conic[1];
+    conics[pos * 3 + 2] = o.conic[2];
+    if (comps) comps[pos] = o.comp;
 }
 
 struct ProjBwdParams {
@@ -675,9 +412,9 @@ extern "C" int gsb_projection_fused_fwd(int B, int C, int N, const float *means,
                                         float *means2d, float *depths, float *conics,
                                         float *compensations, cudaStream_t stream) {
     if (int e = check_camera_model(camera_model)) return e;
+    if ((size_t)B * N == 0 || C == 0) return kOk;
     if (covars == nullptr && (quats == nullptr || scales == nullptr))
         return set_error(kErrInvalidArgument, "covars or (quats, scales) is required");
-    if ((size_t)B * N == 0 || C == 0) return kOk;
     ProjParams p = make_params(B, C, N, means, covars, quats, scales, opacities, viewmats, Ks, width,
                                height, eps2d, near_plane, far_plane, radius_clip,
                                calc_compensations, camera_model);
@@ -696,14 +433,15 @@ extern "C" int gsb_projection_packed_count(int B, int C, int N, const float *mea
                                            int height, float eps2d, float near_plane,
                                            float far_plane, float radius_clip,
                                            int calc_compensations, int camera_model,
-                                           int32_t *block_cnts, cudaStream_t stream) {
+                                           int32_t *block_cnts, uint32_t *vis_bits,
+                                           cudaStream_t stream) {
     if (int e = check_camera_model(camera_model)) return e;
     if ((size_t)B * C == 0 || N == 0) return kOk;
     ProjParams p = make_params(B, C, N, means, covars, quats, scales, opacities, viewmats, Ks, width,
                                height, eps2d, near_plane, far_plane, radius_clip,
                                calc_compensations, camera_model);
     dim3 grid((N + 255) / 256, B * C);
-    projection_packed_count_kernel<<<grid, 256, 0, stream>>>(p, block_cnts);
+    projection_packed_count_kernel<<<grid, 256, 0, stream>>>(p, block_cnts, vis_bits);
     return check_launch("projection_packed_count_kernel");
 }
 
@@ -711,8 +449,8 @@ extern "C" int gsb_projection_packed_write(
     int B, int C, int N, const float *means, const float *covars, const float *quats,
     const float *scales, const float *opacities, const float *viewmats, const float *Ks, int width,
     int height, float eps2d, float near_plane, float far_plane, float radius_clip,
-    int calc_compensations, int camera_model, const int64_t *block_accum, long long nnz,
-    int32_t *indptr, int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids,
+    int calc_compensations, int camera_model, const uint32_t *vis_bits,
+    const int64_t *block_accum, long long nnz, int32_t *indptr, int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids,
     int32_t *radii, float *means2d, float *depths, float *conics, float *compensations,
     cudaStream_t stream) {
     if (int e = check_camera_model(camera_model)) return e;
@@ -722,7 +460,7 @@ extern "C" int gsb_projection_packed_write(
                                calc_compensations, camera_model);
     dim3 grid((N + 255) / 256, B * C);
     projection_packed_write_kernel<<<grid, 256, 0, stream>>>(
-        p, block_accum, nnz, indptr, batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
+        p, vis_bits, block_accum, nnz, indptr, batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
         calc_compensations ? compensations : nullptr);
     return check_launch("projection_packed_write_kernel");
 }

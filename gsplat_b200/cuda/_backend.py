@@ -51,12 +51,27 @@ SIGNATURES = {
         [I32, I32, I32, P, P, P, P, P, P, I32, I32, F32, I32, P, P, P, P, P, P, P, P, P, P, P, P, P],
     ),
     "gsb_projection_packed_blocks": (I32, [I32]),
-    "gsb_projection_packed_count": (I32, _PROJ_COMMON + [P, P]),
-    "gsb_projection_packed_write": (I32, _PROJ_COMMON + [P, I64, P, P, P, P, P, P, P, P, P, P]),
+    "gsb_projection_packed_count": (I32, _PROJ_COMMON + [P, P, P]),
+    "gsb_projection_packed_write": (I32, _PROJ_COMMON + [P, P, I64, P, P, P, P, P, P, P, P, P, P]),
     "gsb_projection_packed_bwd": (
         I32,
         [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, F32, I32, P, P, P, P, P, P, P, P, P, I32,
          P, P, P, P, P, P],
+    ),
+    "gsb_projection_sh_dense_fwd": (
+        I32,
+        [I32, I32, I32, P, P, P, P, P, I32, I32, P, P, I32, I32, F32, F32, F32, F32, I32, I32,
+         P, P, P, P, P, P, P, P],
+    ),
+    "gsb_projection_sh_packed_write": (
+        I32,
+        [I32, I32, I32, P, P, P, P, P, I32, I32, P, P, I32, I32, F32, F32, F32, F32, I32, I32,
+         P, P, I64, P, P, P, P, P, P, P, P, P, P, P, P, P],
+    ),
+    "gsb_projection_sh_bwd": (
+        I32,
+        [I32, I32, I32, I32, P, P, P, P, P, I32, I32, P, P, I32, I32, F32, I32, I32,
+         P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
     ),
     "gsb_spherical_harmonics_fwd": (I32, [I32, I64, I32, P, P, P, P, P]),
     "gsb_spherical_harmonics_bwd": (I32, [I32, I64, I32, P, P, P, P, P, P, P]),

@@ -319,7 +319,8 @@ class _FullyFusedProjectionPacked(torch.autograd.Function):
             stream = stream_of(means)
             nblocks = _B.lib().gsb_projection_packed_blocks(N)
             block_cnts = torch.empty(B * C * nblocks, dtype=torch.int32, device=dev)
-            call("gsb_projection_packed_count", *common, ptr(block_cnts), stream)
+            vis_bits = torch.empty(B * C * nblocks * 8, dtype=torch.int32, device=dev)
+            call("gsb_projection_packed_count", *common, ptr(block_cnts), ptr(vis_bits), stream)
             block_accum = _scan_i32(block_cnts)
             nnz = int(block_accum[-1].item()) if block_accum.numel() > 0 else 0
             indptr = torch.zeros(B * C + 1, dtype=torch.int32, device=dev)
@@ -332,7 +333,8 @@ class _FullyFusedProjectionPacked(torch.autograd.Function):
             conics = torch.empty((nnz, 3), dtype=means.dtype, device=dev)
             comps = torch.zeros(nnz, dtype=means.dtype, device=dev) if calc_compensations else None
             if block_accum.numel() > 0:
-                call("gsb_projection_packed_write", *common, ptr(block_accum), nnz, ptr(indptr),
+                call("gsb_projection_packed_write", *common, ptr(vis_bits), ptr(block_accum), nnz,
+                     ptr(indptr),
                      ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids), ptr(radii), ptr(means2d),
                      ptr(depths), ptr(conics), ptr(comps), stream)
         ctx.save_for_backward(batch_ids, camera_ids, gaussian_ids, means, covars, quats, scales,
@@ -553,7 +555,15 @@ def rasterize_to_pixels(
         assert colors.shape == image_dims + (N, channels), colors.shape
         assert opacities.shape == image_dims + (N,), opacities.shape
     if backgrounds is not None:
-        assert backgrounds.shape == image_dims + (channels,), backgrounds.shape
+        if packed:
+            # one background per image (isect_offsets' leading dims), or one
+            # shared by all images as in the reference's packed check
+            img_dims = isect_offsets.shape[:-2]
+            if backgrounds.shape == (channels,):
+                backgrounds = backgrounds.expand(img_dims + (channels,))
+            assert backgrounds.shape == img_dims + (channels,), backgrounds.shape
+        else:
+            assert backgrounds.shape == image_dims + (channels,), backgrounds.shape
         backgrounds = backgrounds.contiguous()
     if masks is not None:
         assert masks.shape == isect_offsets.shape, masks.shape
@@ -631,3 +641,158 @@ class _RasterizeToPixels(torch.autograd.Function):
             v_backgrounds = (v_render_colors * (1.0 - render_alphas).float()).sum(dim=(-3, -2))
         return (v_means2d, v_conics, v_colors, v_opacities, v_backgrounds,
                 None, None, None, None, None, None, None)
+
+
+# ---------------------------------------------------------------------------
+# Fused projection + SH (used by rasterization())
+# ---------------------------------------------------------------------------
+def fully_fused_projection_sh(
+    means: Tensor,  # [..., N, 3]
+    quats: Tensor,  # [..., N, 4]
+    scales: Tensor,  # [..., N, 3]
+    opacities: Tensor,  # [..., N]
+    sh_coeffs: Tensor,  # [..., N, K, 3]
+    sh_degree: int,
+    viewmats: Tensor,  # [..., C, 4, 4]
+    Ks: Tensor,  # [..., C, 3, 3]
+    width: int,
+    height: int,
+    eps2d: float = 0.3,
+    near_plane: float = 0.01,
+    far_plane: float = 1e10,
+    radius_clip: float = 0.0,
+    packed: bool = False,
+    calc_compensations: bool = False,
+    camera_model: CameraModel = "pinhole",
+) -> Tuple[Tensor, ...]:
+    """Projection, view-dependent SH colour and opacity compensation in one op.
+
+    Equivalent to fully_fused_projection(..., opacities=opacities) followed by
+    colors = clamp_min(spherical_harmonics(sh_degree, normalize(means - campos),
+    coeffs) + 0.5, 0) and opacities * compensations, as the reference's
+    rasterization() computes them (gsplat/rendering.py:749-872). Returns the
+    projection outputs followed by (colors, opacities): dense
+    (radii, means2d, depths, conics, compensations, colors, opacities) or packed
+    (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
+    compensations, colors, opacities). Gradients flow to means, quats, scales,
+    opacities and sh_coeffs (not to viewmats).
+    """
+    batch_dims = means.shape[:-2]
+    N = means.shape[-2]
+    C = viewmats.shape[-3]
+    assert means.shape == batch_dims + (N, 3), means.shape
+    assert quats.shape == batch_dims + (N, 4), quats.shape
+    assert scales.shape == batch_dims + (N, 3), scales.shape
+    assert opacities.shape == batch_dims + (N,), opacities.shape
+    assert sh_coeffs.shape[:-2] == batch_dims + (N,) and sh_coeffs.shape[-1] == 3, sh_coeffs.shape
+    assert (sh_degree + 1) ** 2 <= sh_coeffs.shape[-2], sh_coeffs.shape
+    assert viewmats.shape == batch_dims + (C, 4, 4), viewmats.shape
+    assert Ks.shape == batch_dims + (C, 3, 3), Ks.shape
+    cam = _camera_id(camera_model)
+    return _FullyFusedProjectionSH.apply(
+        means.contiguous(), quats.contiguous(), scales.contiguous(), opacities.contiguous(),
+        sh_coeffs.contiguous(), sh_degree, viewmats.contiguous(), Ks.contiguous(), width, height,
+        eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, cam)
+
+
+class _FullyFusedProjectionSH(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, quats, scales, opacities, sh, sh_degree, viewmats, Ks, width, height,
+                eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, camera_model):
+        for name, t in (("means", means), ("quats", quats), ("scales", scales),
+                        ("opacities", opacities), ("sh_coeffs", sh), ("viewmats", viewmats),
+                        ("Ks", Ks)):
+            check_cuda(name, t)
+        batch_dims = means.shape[:-2]
+        N = means.shape[-2]
+        C = viewmats.shape[-3]
+        B = math.prod(batch_dims)
+        K = sh.shape[-2]
+        dev = means.device
+        f32 = means.dtype
+        shared = (B, C, N, ptr(means), ptr(quats), ptr(scales), ptr(opacities), ptr(sh), K,
+                  sh_degree, ptr(viewmats), ptr(Ks), width, height, eps2d, near_plane, far_plane,
+                  radius_clip, int(calc_compensations), camera_model)
+        with torch.cuda.device(dev):
+            stream = stream_of(means)
+            if not packed:
+                radii = torch.empty(batch_dims + (C, N, 2), dtype=torch.int32, device=dev)
+                means2d = torch.empty(batch_dims + (C, N, 2), dtype=f32, device=dev)
+                depths = torch.empty(batch_dims + (C, N), dtype=f32, device=dev)
+                conics = torch.empty(batch_dims + (C, N, 3), dtype=f32, device=dev)
+                comps = torch.empty(batch_dims + (C, N), dtype=f32, device=dev) if calc_compensations else None
+                colors = torch.empty(batch_dims + (C, N, 3), dtype=f32, device=dev)
+                opac_out = torch.empty(batch_dims + (C, N), dtype=f32, device=dev)
+                call("gsb_projection_sh_dense_fwd", *shared, ptr(radii), ptr(means2d), ptr(depths),
+                     ptr(conics), ptr(comps), ptr(colors), ptr(opac_out), stream)
+                pair_index = None
+                outs = (radii, means2d, depths, conics, comps, colors, opac_out)
+            else:
+                nblocks = _B.lib().gsb_projection_packed_blocks(N)
+                block_cnts = torch.empty(B * C * nblocks, dtype=torch.int32, device=dev)
+                vis_bits = torch.empty(B * C * nblocks * 8, dtype=torch.int32, device=dev)
+                call("gsb_projection_packed_count", B, C, N, ptr(means), None, ptr(quats),
+                     ptr(scales), ptr(opacities), ptr(viewmats), ptr(Ks), width, height, eps2d,
+                     near_plane, far_plane, radius_clip, int(calc_compensations), camera_model,
+                     ptr(block_cnts), ptr(vis_bits), stream)
+                block_accum = _scan_i32(block_cnts)
+                nnz = int(block_accum[-1].item()) if block_accum.numel() > 0 else 0
+                indptr = torch.zeros(B * C + 1, dtype=torch.int32, device=dev)
+                batch_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+                camera_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+                gaussian_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
+                radii = torch.empty((nnz, 2), dtype=torch.int32, device=dev)
+                means2d = torch.empty((nnz, 2), dtype=f32, device=dev)
+                depths = torch.empty(nnz, dtype=f32, device=dev)
+                conics = torch.empty((nnz, 3), dtype=f32, device=dev)
+                comps = torch.empty(nnz, dtype=f32, device=dev) if calc_compensations else None
+                colors = torch.empty((nnz, 3), dtype=f32, device=dev)
+                opac_out = torch.empty(nnz, dtype=f32, device=dev)
+                pair_index = torch.empty(B * C * N, dtype=torch.int32, device=dev)
+                if block_accum.numel() > 0:
+                    call("gsb_projection_sh_packed_write", *shared, ptr(vis_bits), ptr(block_accum),
+                         nnz, ptr(indptr), ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids),
+                         ptr(radii), ptr(means2d), ptr(depths), ptr(conics), ptr(comps),
+                         ptr(colors), ptr(opac_out), ptr(pair_index), stream)
+                outs = (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
+                        comps, colors, opac_out)
+                ctx.mark_non_differentiable(batch_ids, camera_ids, gaussian_ids, indptr)
+        ctx.mark_non_differentiable(radii)
+        ctx.save_for_backward(means, quats, scales, opacities, sh, viewmats, Ks, pair_index,
+                              None if packed else radii, conics, comps)
+        ctx.meta = (B, C, N, K, sh_degree, width, height, eps2d, calc_compensations, camera_model,
+                    packed)
+        return outs
+
+    @staticmethod
+    def backward(ctx, *grads):
+        means, quats, scales, opacities, sh, viewmats, Ks, pair_index, radii, conics, comps = ctx.saved_tensors
+        B, C, N, K, deg, width, height, eps2d, calc, cam, packed = ctx.meta
+        if packed:
+            _, _, _, _, _, v_means2d, v_depths, v_conics, v_comps, v_colors, v_opac = grads
+        else:
+            _, v_means2d, v_depths, v_conics, v_comps, v_colors, v_opac = grads
+
+        def c(t, like):
+            return torch.zeros_like(like) if t is None else t.contiguous()
+
+        v_means2d = c(v_means2d, conics[..., :2])
+        v_depths = c(v_depths, conics[..., 0])
+        v_conics = c(v_conics, conics)
+        v_colors = c(v_colors, conics)
+        v_opac = c(v_opac, conics[..., 0])
+        v_comps = v_comps.contiguous() if (calc and v_comps is not None) else None
+        v_means = torch.empty_like(means)
+        v_quats = torch.empty_like(quats)
+        v_scales = torch.empty_like(scales)
+        v_opacities = torch.empty_like(opacities)
+        v_sh = torch.empty_like(sh)
+        with torch.cuda.device(means.device):
+            call("gsb_projection_sh_bwd", B, C, N, int(packed), ptr(means), ptr(quats), ptr(scales),
+                 ptr(opacities), ptr(sh), K, deg, ptr(viewmats), ptr(Ks), width, height, eps2d,
+                 int(calc), cam, ptr(pair_index), ptr(radii), ptr(conics), ptr(comps),
+                 ptr(v_means2d), ptr(v_depths), ptr(v_conics), ptr(v_comps), ptr(v_colors),
+                 ptr(v_opac), ptr(v_means), ptr(v_quats), ptr(v_scales), ptr(v_opacities),
+                 ptr(v_sh), stream_of(means))
+        return (v_means, v_quats, v_scales, v_opacities, v_sh, None, None, None, None, None, None,
+                None, None, None, None, None, None)

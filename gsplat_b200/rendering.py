@@ -24,6 +24,7 @@ from typing_extensions import Literal
 
 from .cuda._wrapper import (
     fully_fused_projection,
+    fully_fused_projection_sh,
     isect_offset_encode,
     isect_tiles,
     rasterize_to_pixels,
@@ -255,25 +256,54 @@ def rasterization(
         viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
         C = len(viewmats)
 
-    proj = fully_fused_projection(
-        means, covars, quats, scales, viewmats, Ks, width, height, eps2d=eps2d, packed=packed,
-        near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
-        sparse_grad=sparse_grad, calc_compensations=(rasterize_mode == "antialiased"),
-        camera_model=camera_model, opacities=opacities)
-
-    if packed:
-        (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
-         compensations) = proj
-        opacities = opacities.reshape(B, N)[batch_ids, gaussian_ids]
-        image_ids = batch_ids * C + camera_ids
+    # One fused kernel for projection + view-dependent SH colour + opacity
+    # compensation when the colours are per-Gaussian SH coefficients; the general
+    # op-by-op path otherwise (per-view colours, covariances, extra signals,
+    # pose gradients).
+    use_fused = (
+        has_color
+        and sh_degree is not None
+        and covars is None
+        and extra_signals is None
+        and colors.dim() == num_batch_dims + 3
+        and colors.shape[-2] <= 64
+        and sh_degree <= 4
+        and camera_model in ("pinhole", "ortho")
+        and not viewmats.requires_grad
+    )
+    compensations = None
+    if use_fused:
+        proj = fully_fused_projection_sh(
+            means, quats, scales, opacities, colors, sh_degree, viewmats, Ks, width, height,
+            eps2d=eps2d, near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
+            packed=packed, calc_compensations=(rasterize_mode == "antialiased"),
+            camera_model=camera_model)
+        if packed:
+            (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
+             _, proj_features, opacities) = proj
+            image_ids = batch_ids * C + camera_ids
+        else:
+            radii, means2d, depths, conics, _, proj_features, opacities = proj
+            indptr, batch_ids, camera_ids, gaussian_ids = None, None, None, None
+            image_ids = None
     else:
-        radii, means2d, depths, conics, compensations = proj
-        opacities = torch.broadcast_to(opacities[..., None, :], batch_dims + (C, N))
-        indptr, batch_ids, camera_ids, gaussian_ids = None, None, None, None
-        image_ids = None
-
-    if compensations is not None:
-        opacities = opacities * compensations
+        proj = fully_fused_projection(
+            means, covars, quats, scales, viewmats, Ks, width, height, eps2d=eps2d, packed=packed,
+            near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
+            sparse_grad=sparse_grad, calc_compensations=(rasterize_mode == "antialiased"),
+            camera_model=camera_model, opacities=opacities)
+        if packed:
+            (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
+             compensations) = proj
+            opacities = opacities.reshape(B, N)[batch_ids, gaussian_ids]
+            image_ids = batch_ids * C + camera_ids
+        else:
+            radii, means2d, depths, conics, compensations = proj
+            opacities = torch.broadcast_to(opacities[..., None, :], batch_dims + (C, N))
+            indptr, batch_ids, camera_ids, gaussian_ids = None, None, None, None
+            image_ids = None
+        if compensations is not None:
+            opacities = opacities * compensations
 
     valid_gaussians = (radii > 0).all(dim=-1)
     meta.update(
@@ -289,20 +319,22 @@ def rasterization(
         }
     )
 
-    colors_sh_degree = sh_degree if has_color else None
-    proj_features = None
-    if colors_sh_degree is None and extra_signals_sh_degree is None:
+    if use_fused:
+        pass
+    elif sh_degree is None and extra_signals_sh_degree is None:
         feature_list = []
         if has_color:
             feature_list.append(colors)
         if extra_signals is not None:
             feature_list.append(extra_signals)
+        proj_features = None
         if feature_list:
             proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
             proj_features = normalize_features_layout(
                 proj_features, batch_dims, C, proj_features.shape[-1:], batch_ids, camera_ids,
                 gaussian_ids)
     else:
+        colors_sh_degree = sh_degree if has_color else None
         dirs = compute_directions(batch_dims, means, viewmats, batch_ids, camera_ids, gaussian_ids,
                                   indptr)
         feature_list = []
@@ -324,6 +356,7 @@ def rasterization(
                                                     masks=valid_gaussians)
                 extra_signals = extra_signals + 0.5
             feature_list.append(extra_signals)
+        proj_features = None
         if feature_list:
             proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
 

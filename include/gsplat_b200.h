@@ -71,10 +71,13 @@ GSB_API int gsb_projection_fused_bwd(int B, int C, int N, const float *means, co
 /* Packed (COO) projection, replaces gsplat::projection_ewa_3dgs_packed_fwd
  * (Projection.cpp:308-460), as a two-call protocol equal to the reference's
  * count pass + cumsum + .item() + write pass:
- *   1. gsb_projection_packed_count -> block_cnts int32 [B*C*blocks], blocks =
+ *   1. gsb_projection_packed_count -> block_cnts int32 [B*C*blocks] and the
+ *      visibility ballots vis_bits uint32 [B*C*blocks*8], blocks =
  *      gsb_projection_packed_blocks(N);
  *   2. gsb_inclusive_scan_i32(block_cnts) -> block_accum int64; nnz = last entry;
- *   3. gsb_projection_packed_write with nnz, outputs of length nnz and indptr [B*C+1].
+ *   3. gsb_projection_packed_write with the same vis_bits, nnz, outputs of
+ *      length nnz and indptr [B*C+1]. Pass 2 places exactly the pairs pass 1
+ *      marked, so the two passes cannot disagree.
  * Pairs are ordered by (batch, camera) then Gaussian id. */
 GSB_API int gsb_projection_packed_blocks(int N);
 GSB_API int gsb_projection_packed_count(int B, int C, int N, const float *means, const float *covars,
@@ -82,13 +85,14 @@ GSB_API int gsb_projection_packed_count(int B, int C, int N, const float *means,
                                 const float *viewmats, const float *Ks, int width, int height,
                                 float eps2d, float near_plane, float far_plane, float radius_clip,
                                 int calc_compensations, int camera_model, int32_t *block_cnts,
-                                cudaStream_t stream);
+                                uint32_t *vis_bits, cudaStream_t stream);
 GSB_API int gsb_projection_packed_write(int B, int C, int N, const float *means, const float *covars,
                                 const float *quats, const float *scales, const float *opacities,
                                 const float *viewmats, const float *Ks, int width, int height,
                                 float eps2d, float near_plane, float far_plane, float radius_clip,
                                 int calc_compensations, int camera_model,
-                                const int64_t *block_accum, long long nnz, int32_t *indptr,
+                                const uint32_t *vis_bits, const int64_t *block_accum,
+                                long long nnz, int32_t *indptr,
                                 int64_t *batch_ids,
                                 int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii,
                                 float *means2d, float *depths, float *conics,
@@ -108,6 +112,47 @@ GSB_API int gsb_projection_packed_bwd(int B, int C, int N, int nnz, const float 
                               const float *v_conics, const float *v_compensations,
                               int sparse_grad, float *v_means, float *v_covars, float *v_quats,
                               float *v_scales, float *v_viewmats, cudaStream_t stream);
+
+/* --- Fused projection + SH (no reference counterpart as one op) -----------
+ * The reference's rasterization() runs projection, view directions, SH and the
+ * colour clamp as separate ops (gsplat/rendering.py:749-872). These entry points
+ * do all of it per (camera, Gaussian): besides the projection outputs they write
+ * colors = max(SH(normalize(mean - campos)) + 0.5, 0) [.,3] and opacities_out =
+ * opacities * compensations (antialiased) or opacities [.]. sh is the
+ * per-Gaussian coefficient tensor [B,N,K,3] (K <= 64, degree <= 4).
+ * Packed: pass 1 is gsb_projection_packed_count; pair_index int32 [B*C*N]
+ * (optional) receives each pair's packed position or -1 for the backward. */
+GSB_API int gsb_projection_sh_dense_fwd(int B, int C, int N, const float *means,
+                                        const float *quats, const float *scales,
+                                        const float *opacities, const float *sh, int K,
+                                        int sh_degree, const float *viewmats, const float *Ks,
+                                        int width, int height, float eps2d, float near_plane,
+                                        float far_plane, float radius_clip, int calc_compensations,
+                                        int camera_model, int32_t *radii, float *means2d,
+                                        float *depths, float *conics, float *compensations,
+                                        float *colors, float *opacities_out, cudaStream_t stream);
+GSB_API int gsb_projection_sh_packed_write(
+    int B, int C, int N, const float *means, const float *quats, const float *scales,
+    const float *opacities, const float *sh, int K, int sh_degree, const float *viewmats,
+    const float *Ks, int width, int height, float eps2d, float near_plane, float far_plane,
+    float radius_clip, int calc_compensations, int camera_model, const uint32_t *vis_bits,
+    const int64_t *block_accum, long long nnz, int32_t *indptr, int64_t *batch_ids,
+    int64_t *camera_ids, int64_t *gaussian_ids, int32_t *radii, float *means2d, float *depths,
+    float *conics, float *compensations, float *colors, float *opacities_out, int32_t *pair_index,
+    cudaStream_t stream);
+/* Backward of both layouts. Writes every row of v_means [B,N,3], v_quats
+ * [B,N,4], v_scales [B,N,3], v_opacities [B,N] and v_sh [B,N,K,3] (no
+ * pre-zeroing). packed: pair_index from the forward; dense: radii [B,C,N,2].
+ * Upstream gradients are indexed like the forward outputs. */
+GSB_API int gsb_projection_sh_bwd(
+    int B, int C, int N, int packed, const float *means, const float *quats, const float *scales,
+    const float *opacities, const float *sh, int K, int sh_degree, const float *viewmats,
+    const float *Ks, int width, int height, float eps2d, int calc_compensations, int camera_model,
+    const int32_t *pair_index, const int32_t *radii, const float *conics,
+    const float *compensations, const float *v_means2d, const float *v_depths,
+    const float *v_conics, const float *v_compensations, const float *v_colors,
+    const float *v_opacities_out, float *v_means, float *v_quats, float *v_scales,
+    float *v_opacities, float *v_sh, cudaStream_t stream);
 
 /* --- Spherical harmonics --------------------------------------------------
  * Replaces gsplat::spherical_harmonics_fwd / _bwd

@@ -173,9 +173,17 @@ def test_projection_packed_backward_equals_dense():
         viewmats = d["viewmats"].clone().requires_grad_(True)
         out = gsb().fully_fused_projection(means, None, quats, scales, viewmats, d["Ks"], d["width"],
                                            d["height"], packed=packed, opacities=d["opacities"])
-        m2, dep, con = (out[5], out[6], out[7]) if packed else (out[1], out[2], out[3])
-        w = torch.linspace(0.5, 1.5, m2.numel(), device=DEV).reshape(m2.shape)
-        loss = (m2 * w).sum() + dep.sum() + (con * 0.1).sum()
+        if packed:
+            m2, dep, con = out[5], out[6], out[7]
+            cam, gid = out[1], out[2]
+        else:
+            m2, dep, con = out[1], out[2], out[3]
+            valid = (out[0] > 0).all(-1)
+            cam, gid = torch.nonzero(valid, as_tuple=True)
+            m2, dep, con = m2[valid], dep[valid], con[valid]
+        # the same per-(camera, Gaussian) weights in both layouts
+        w = (1.0 + 0.001 * gid.float() + 0.1 * cam.float())[:, None]
+        loss = (m2 * w).sum() + (dep * w[:, 0]).sum() + (con * 0.1 * w).sum()
         grads.append(torch.autograd.grad(loss, (means, quats, scales, viewmats)))
     for a, b, name in zip(grads[0], grads[1], ("means", "quats", "scales", "viewmats")):
         assert_close(b, a, 1e-5, 1e-5, name=name)

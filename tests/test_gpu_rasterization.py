@@ -1,0 +1,207 @@
+"""End-to-end parity of rasterization() (forward + backward to the Gaussian
+parameters) against the CPU oracle pipeline, and of the fused projection+SH op
+against the op-by-op composition. Mirrors the reference's
+tests/test_rasterization.py (rasterization() vs _rasterization() over packed /
+render_mode / SH variants).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import _data
+from tests._compare import as_np, assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def gsb():
+    import gsplat_b200
+
+    return gsplat_b200
+
+
+def leaf(d):
+    out = {}
+    for k in ("means", "quats", "scales", "opacities", "sh"):
+        out[k] = d[k].detach().clone().to(DEV).requires_grad_(True)
+    return out
+
+
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("calc", [False, True])
+def test_fused_projection_sh_matches_composition(packed, calc):
+    from gsplat_b200.cuda._wrapper import fully_fused_projection_sh
+    from gsplat_b200.rendering import compute_directions
+
+    d = _data.scene(5000, seed=21, C=3, width=300, height=200, fx=250.0)
+    L1, L2 = leaf(d), leaf(d)
+    vm, K = d["viewmats"].to(DEV), d["Ks"].to(DEV)
+    W, H = d["width"], d["height"]
+    out = fully_fused_projection_sh(L1["means"], L1["quats"], L1["scales"], L1["opacities"],
+                                    L1["sh"], 3, vm, K, W, H, packed=packed,
+                                    calc_compensations=calc)
+    ref = gsb().fully_fused_projection(L2["means"], None, L2["quats"], L2["scales"], vm, K, W, H,
+                                       packed=packed, calc_compensations=calc,
+                                       opacities=L2["opacities"])
+    if packed:
+        bids, cids, gids = ref[0], ref[1], ref[2]
+        radii, m2, dep, con, comp = ref[4:9]
+        dirs = compute_directions((), L2["means"], vm, bids, cids, gids)
+        coeffs = L2["sh"][gids]
+        op = L2["opacities"][gids]
+        f_m2, f_dep, f_con, f_col, f_op = out[5], out[6], out[7], out[9], out[10]
+        assert torch.equal(out[2], gids) and torch.equal(out[1], cids)
+        mask = None
+    else:
+        radii, m2, dep, con, comp = ref
+        dirs = compute_directions((), L2["means"], vm)
+        coeffs = L2["sh"][None].expand(3, -1, -1, -1)
+        op = L2["opacities"][None].expand(3, -1)
+        f_m2, f_dep, f_con, f_col, f_op = out[1], out[2], out[3], out[5], out[6]
+        mask = (radii > 0).all(-1)
+    col = torch.clamp_min(gsb().spherical_harmonics(3, dirs, coeffs, masks=mask) + 0.5, 0.0)
+    if calc:
+        op = op * comp
+    sel = mask if mask is not None else slice(None)
+    assert torch.equal(out[0] if not packed else out[4], radii)
+    assert_close(f_m2[sel], m2[sel], 1e-6, 1e-5, name="means2d")
+    assert_close(f_con[sel], con[sel], 1e-6, 1e-6, name="conics")
+    assert_close(f_col[sel], col[sel], 1e-5, 1e-6, name="colors")
+    assert_close(f_op[sel], op[sel], 1e-6, 1e-7, name="opacities")
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    w = [torch.randn(t.shape, device=DEV, generator=gen) for t in (m2, dep, con, col, op)]
+    if mask is not None:
+        w = [x * (mask[..., None] if x.dim() > mask.dim() else mask) for x in w]
+    l1 = sum((a * b).sum() for a, b in zip((f_m2, f_dep, f_con, f_col, f_op), w))
+    l2 = sum((a * b).sum() for a, b in zip((m2, dep, con, col, op), w))
+    g1 = torch.autograd.grad(l1, [L1[k] for k in ("means", "quats", "scales", "opacities", "sh")])
+    g2 = torch.autograd.grad(l2, [L2[k] for k in ("means", "quats", "scales", "opacities", "sh")])
+    for a, b, name in zip(g1, g2, ("means", "quats", "scales", "opacities", "sh")):
+        assert_close(a, b, 1e-4, 1e-5, name=name)
+
+
+def oracle_pipeline(d, W, H, tile_size, calc, depth_channel, v_fn):
+    """The reference algorithm on the CPU: projection -> SH -> AccuTile -> sort ->
+    offsets -> rasterize, then the chain of backward passes to the parameters."""
+    n = lambda t: t.detach().cpu().numpy()
+    means, quats, scales, opac, sh = n(d["means"]), n(d["quats"]), n(d["scales"]), n(d["opacities"]), n(d["sh"])
+    vm, K = n(d["viewmats"]), n(d["Ks"])
+    C = vm.shape[0]
+    N = means.shape[0]
+    radii, m2, dep, con, comp = O.projection_fwd(means, None, quats, scales, opac, vm, K, W, H,
+                                                 calc_compensations=calc)
+    valid = (radii > 0).all(-1)
+    campos = -np.einsum("cji,cj->ci", vm[:, :3, :3], vm[:, :3, 3])
+    dirs = means[None] - campos[:, None]
+    coeffs = np.broadcast_to(sh[None], (C,) + sh.shape)
+    raw = O.sh_fwd(3, dirs, coeffs, valid)
+    colors = np.maximum(raw + 0.5, 0.0)
+    op_eff = opac[None] * (comp if calc else 1.0)
+    feats = np.concatenate([colors, dep[..., None]], -1) if depth_channel else colors
+    tw, th = math.ceil(W / tile_size), math.ceil(H / tile_size)
+    _, keys, fids = O.isect_tiles(m2, radii, dep, tile_size, tw, th, conics=con, opacities=op_eff)
+    offsets = O.isect_offset_encode(keys, C, tw, th)
+    rc, ra, last = O.raster_fwd(m2, con, feats, op_eff, W, H, tile_size, offsets, fids)
+    vrc, vra = v_fn(rc, ra)
+    v_m2, v_con, v_feat, v_op, _ = O.raster_bwd(m2, con, feats, op_eff, W, H, tile_size, offsets,
+                                                fids, ra, last, vrc, vra)
+    v_col = v_feat[..., :3] * (raw + 0.5 >= 0)
+    v_dep = v_feat[..., 3] if depth_channel else np.zeros_like(dep)
+    v_coeffs, v_dirs = O.sh_bwd(3, dirs, coeffs, v_col, valid)
+    v_opac = (v_op * (comp if calc else 1.0)).sum(0)
+    v_comp = v_op * opac[None] if calc else None
+    v_means, _, v_quats, v_scales, _ = O.projection_bwd(
+        means, None, quats, scales, vm, K, W, H, 0.3, radii, con, comp if calc else None,
+        v_m2 * valid[..., None], v_dep * valid, v_con * valid[..., None],
+        v_comp * valid if calc else None)
+    v_means = v_means + (v_dirs * valid[..., None]).sum(0)
+    return dict(render=rc, alpha=ra, v_means=v_means, v_quats=v_quats, v_scales=v_scales,
+                v_opacities=v_opac, v_sh=(v_coeffs * valid[..., None, None]).sum(0))
+
+
+@pytest.mark.parametrize("packed", [True, False])
+@pytest.mark.parametrize("mode", ["RGB", "RGB+ED"])
+@pytest.mark.parametrize("aa", [False, True])
+def test_rasterization_end_to_end_vs_oracle(packed, mode, aa):
+    d = _data.scene(8000, seed=31, C=2, width=160, height=120, fx=150.0)
+    d["scales"] = d["scales"] * 1.5
+    W, H = d["width"], d["height"]
+    L = leaf(d)
+    vm, K = d["viewmats"].to(DEV), d["Ks"].to(DEV)
+    rc, ra, meta = gsb().rasterization(L["means"], L["quats"], L["scales"], L["opacities"], L["sh"],
+                                       vm, K, W, H, sh_degree=3, packed=packed, render_mode=mode,
+                                       rasterize_mode="antialiased" if aa else "classic")
+    gen = np.random.default_rng(7)
+    G = gen.standard_normal((2, H, W, 4 if mode == "RGB+ED" else 3)).astype(np.float32)
+    Ga = gen.standard_normal((2, H, W, 1)).astype(np.float32)
+    depth = mode == "RGB+ED"
+
+    def v_fn(raw_rc, raw_ra):
+        # upstream gradients of L = sum(render * G) + sum(alpha * Ga) with respect
+        # to the rasterizer's raw outputs; for "ED" the depth channel is
+        # accumulated depth / max(alpha, 1e-10) (reference rendering.py:1257-1268)
+        if not depth:
+            return G, Ga
+        a = np.maximum(raw_ra, 1e-10)
+        vrc = G.copy()
+        vrc[..., 3:4] = G[..., 3:4] / a
+        vra = Ga + np.where(raw_ra > 1e-10, -G[..., 3:4] * raw_rc[..., 3:4] / a ** 2, 0.0)
+        return vrc, vra.astype(np.float32)
+
+    e = oracle_pipeline(d, W, H, 16, aa, depth, v_fn)
+    exp_render = e["render"].copy()
+    if depth:
+        exp_render[..., 3:4] = exp_render[..., 3:4] / np.maximum(e["alpha"], 1e-10)
+    assert_close(ra, e["alpha"], 1e-4, 1e-5, max_bad_frac=1e-3, name="alphas")
+    assert_close(rc[..., :3], exp_render[..., :3], 1e-4, 1e-5, max_bad_frac=1e-3, name="colors")
+    if depth:
+        good = e["alpha"][..., 0] > 0.05
+        assert_close(rc[..., 3][torch.from_numpy(good).to(DEV)], exp_render[..., 3][good], 1e-3, 1e-4,
+                     max_bad_frac=1e-3, name="expected depth")
+    loss = (rc * torch.from_numpy(G).to(DEV)).sum() + (ra * torch.from_numpy(Ga).to(DEV)).sum()
+    grads = torch.autograd.grad(loss, [L[k] for k in ("means", "quats", "scales", "opacities", "sh")])
+    for g, k in zip(grads, ("v_means", "v_quats", "v_scales", "v_opacities", "v_sh")):
+        ref = e[k]
+        scale = np.abs(ref).max() + 1e-12
+        # float32 GPU chain vs float64-accumulated oracle chain; atol relative to
+        # the gradient's magnitude, and a few Gaussians may sit on an alpha
+        # threshold decision that one side takes and the other does not
+        assert_close(g, ref, 2e-3, 1e-4 * scale, max_bad_frac=2e-3, name=k)
+
+
+def test_rasterization_meta_and_absgrad():
+    d = _data.scene(3000, seed=5, C=2, width=128, height=96, fx=120.0)
+    L = leaf(d)
+    vm, K = d["viewmats"].to(DEV), d["Ks"].to(DEV)
+    rc, ra, meta = gsb().rasterization(L["means"], L["quats"], L["scales"], L["opacities"], L["sh"],
+                                       vm, K, 128, 96, sh_degree=3, packed=False, absgrad=True)
+    for key in ("camera_ids", "gaussian_ids", "radii", "means2d", "depths", "conics", "opacities",
+                "tile_width", "tile_height", "tiles_per_gauss", "isect_ids", "flatten_ids",
+                "isect_offsets", "width", "height", "tile_size", "n_batches", "n_cameras"):
+        assert key in meta, key
+    meta["means2d"].retain_grad()
+    rc.sum().backward()
+    g = meta["means2d"].grad
+    assert g is not None and g.shape == meta["means2d"].shape
+    assert meta["means2d"].absgrad.shape == g.shape
+    assert (meta["means2d"].absgrad >= g.abs() - 1e-6).all()
+
+
+def test_rasterization_post_activation_colors_and_backgrounds():
+    """colors given as [C, N, D] features (sh_degree=None), with backgrounds."""
+    d = _data.scene(3000, seed=6, C=2, width=96, height=64, fx=100.0)
+    L = leaf(d)
+    vm, K = d["viewmats"].to(DEV), d["Ks"].to(DEV)
+    feats = torch.rand((2, 3000, 5), device=DEV)
+    bg = torch.rand((2, 5), device=DEV)
+    rc, ra, meta = gsb().rasterization(L["means"], L["quats"], L["scales"], L["opacities"], feats,
+                                       vm, K, 96, 64, packed=False, backgrounds=bg)
+    er, ea, _ = O.raster_fwd(as_np(meta["means2d"]), as_np(meta["conics"]), as_np(feats),
+                             as_np(meta["opacities"]), 96, 64, 16, as_np(meta["isect_offsets"]),
+                             as_np(meta["flatten_ids"]), backgrounds=as_np(bg))
+    assert_close(rc, er, 1e-4, 1e-5, max_bad_frac=1e-3, name="render")
