@@ -18,8 +18,11 @@
 //    The box is inflated by 1% plus half a pixel; outside it alpha is below the
 //    threshold by more than the rounding of the exp evaluation.
 //  * Backward threads own PPT pixels each: the per-splat gradient is summed over
-//    those pixels in registers before the warp butterfly, so the shuffle cost
-//    per (pixel, splat) pair drops by PPT. One lane then issues the atomics.
+//    those pixels in registers first. The CDIM + 8 per-splat sums are then
+//    reduced over the warp by recursive halving (each butterfly step exchanges
+//    half of the remaining values), about 16 shuffles instead of 5 per value,
+//    and the finished sums land in different lanes, which issue their atomics
+//    in parallel.
 //  * Channel counts are processed in chunks of at most 32 (kernels are
 //    instantiated for 1-8, 16 and 32 channels) with strided colour access, so no
 //    padding copies are made.
@@ -293,6 +296,85 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
+
+// Warp reduction of V values (V a power of two <= 32) by recursive halving: at
+// each butterfly step a lane keeps one half of its values and sends the other
+// half, so V values cost V - 1 + (5 - log2 V) shuffles instead of 5 V. On return
+// the lane holds the complete sum of value `idx`; `writer` marks one lane per
+// value. Used for the per-splat gradient sums of the backward pass.
+template <int V> struct Log2 { static constexpr int value = 1 + Log2<V / 2>::value; };
+template <> struct Log2<1> { static constexpr int value = 0; };
+
+template <int V>
+__device__ __forceinline__ float halving_reduce(float *v, int lane, int &idx, bool &writer) {
+    constexpr int L = Log2<V>::value;
+#pragma unroll
+    for (int s = 0; s < L; ++s) {
+        const int mask = 16 >> s;
+        const int half = V >> (s + 1);
+        const bool upper = (lane & mask) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int mask = 16 >> L; mask > 0; mask >>= 1) r += __shfl_xor_sync(0xffffffffu, r, mask);
+    idx = (lane >> (5 - L)) & (V - 1);
+    writer = (lane & ((1 << (5 - L)) - 1)) == 0;
+    return r;
+}
+
+template <int N> struct Pow2Ceil {
+    static constexpr int value = N <= 1 ? 1 : 2 * Pow2Ceil<(N + 1) / 2>::value;
+};
+template <> struct Pow2Ceil<1> { static constexpr int value = 1; };
+
+// Per-splat gradient slots: [0, CDIM) colour, then conic a, b, c, mean x, y,
+// opacity, |mean x|, |mean y|.
+template <int CDIM>
+__device__ __forceinline__ float *grad_slot(const RasterParams &p, int j, int32_t g) {
+    if (j < CDIM) return p.v_colors + (size_t)g * p.cstride + p.coff + j;
+    j -= CDIM;
+    if (j < 3) return p.v_conics + (size_t)g * 3 + j;
+    if (j < 5) return p.v_means2d + (size_t)g * 2 + (j - 3);
+    if (j == 5) return p.v_opacities + g;
+    return p.v_means2d_abs ? p.v_means2d_abs + (size_t)g * 2 + (j - 6) : nullptr;
+}
+
+// Reduces the NV slots over the warp and adds them to the splat's gradients, one
+// atomic per slot issued by different lanes.
+template <int CDIM, int NV>
+__device__ __forceinline__ void flush_splat_grads(const RasterParams &p, float *acc, int lane,
+                                                  int32_t g) {
+    constexpr int FIRST = NV < 32 ? NV : 32;
+    constexpr int V1 = Pow2Ceil<FIRST>::value;
+    float v1[V1];
+#pragma unroll
+    for (int i = 0; i < V1; ++i) v1[i] = i < FIRST ? acc[i] : 0.f;
+    int idx;
+    bool writer;
+    float r = halving_reduce<V1>(v1, lane, idx, writer);
+    if (writer && idx < FIRST) {
+        float *dst = grad_slot<CDIM>(p, idx, g);
+        if (dst) atomicAdd(dst, r);
+    }
+    if constexpr (NV > 32) {
+        constexpr int REST = NV - 32;
+        constexpr int V2 = Pow2Ceil<REST>::value;
+        float v2[V2];
+#pragma unroll
+        for (int i = 0; i < V2; ++i) v2[i] = i < REST ? acc[32 + i] : 0.f;
+        r = halving_reduce<V2>(v2, lane, idx, writer);
+        if (writer && idx < REST) {
+            float *dst = grad_slot<CDIM>(p, 32 + idx, g);
+            if (dst) atomicAdd(dst, r);
+        }
+    }
+}
 template <int CDIM, int PPT>
 __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -383,11 +465,10 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
             float col[CDIM];
 #pragma unroll
             for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
-            float g_rgb[CDIM];
+            constexpr int NV = CDIM + 8;
+            float acc[NV];
 #pragma unroll
-            for (int c = 0; c < CDIM; ++c) g_rgb[c] = 0.f;
-            float g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_x = 0.f, g_y = 0.f, g_o = 0.f, g_ax = 0.f,
-                  g_ay = 0.f;
+            for (int j = 0; j < NV; ++j) acc[j] = 0.f;
             bool any = false;
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
@@ -401,56 +482,29 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
                 float v_alpha = 0.f;
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) {
-                    g_rgb[c] += fac * vc[k][c];
+                    acc[c] += fac * vc[k][c];
                     v_alpha += (col[c] * T[k] - buf[k][c] * ra) * vc[k][c];
                 }
                 v_alpha += Tf[k] * ra * va[k];
                 if (bg) v_alpha += -Tf[k] * ra * bgd[k];
                 if (r.o * e.vis <= kMaxAlpha) {
                     const float v_sigma = -r.o * e.vis * v_alpha;
-                    g_ca += 0.5f * v_sigma * e.dx * e.dx;
-                    g_cb += v_sigma * e.dx * e.dy;
-                    g_cc += 0.5f * v_sigma * e.dy * e.dy;
+                    acc[CDIM + 0] += 0.5f * v_sigma * e.dx * e.dx;
+                    acc[CDIM + 1] += v_sigma * e.dx * e.dy;
+                    acc[CDIM + 2] += 0.5f * v_sigma * e.dy * e.dy;
                     const float gx = v_sigma * (r.a * e.dx + r.b * e.dy);
                     const float gy = v_sigma * (r.b * e.dx + r.c * e.dy);
-                    g_x += gx;
-                    g_y += gy;
-                    g_ax += fabsf(gx);
-                    g_ay += fabsf(gy);
-                    g_o += e.vis * v_alpha;
+                    acc[CDIM + 3] += gx;
+                    acc[CDIM + 4] += gy;
+                    acc[CDIM + 5] += e.vis * v_alpha;
+                    acc[CDIM + 6] += fabsf(gx);
+                    acc[CDIM + 7] += fabsf(gy);
                 }
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) buf[k][c] += col[c] * fac;
             }
             if (!__any_sync(0xffffffffu, any)) continue;
-#pragma unroll
-            for (int c = 0; c < CDIM; ++c) g_rgb[c] = warp_sum(g_rgb[c]);
-            g_ca = warp_sum(g_ca);
-            g_cb = warp_sum(g_cb);
-            g_cc = warp_sum(g_cc);
-            g_x = warp_sum(g_x);
-            g_y = warp_sum(g_y);
-            g_o = warp_sum(g_o);
-            if (p.v_means2d_abs) {
-                g_ax = warp_sum(g_ax);
-                g_ay = warp_sum(g_ay);
-            }
-            if (lane == 0) {
-                const int32_t g = s.ids[i];
-                float *vcol = p.v_colors + (size_t)g * p.cstride + p.coff;
-#pragma unroll
-                for (int c = 0; c < CDIM; ++c) atomicAdd(vcol + c, g_rgb[c]);
-                atomicAdd(p.v_conics + (size_t)g * 3 + 0, g_ca);
-                atomicAdd(p.v_conics + (size_t)g * 3 + 1, g_cb);
-                atomicAdd(p.v_conics + (size_t)g * 3 + 2, g_cc);
-                atomicAdd(p.v_means2d + (size_t)g * 2 + 0, g_x);
-                atomicAdd(p.v_means2d + (size_t)g * 2 + 1, g_y);
-                atomicAdd(p.v_opacities + g, g_o);
-                if (p.v_means2d_abs) {
-                    atomicAdd(p.v_means2d_abs + (size_t)g * 2 + 0, g_ax);
-                    atomicAdd(p.v_means2d_abs + (size_t)g * 2 + 1, g_ay);
-                }
-            }
+            flush_splat_grads<CDIM, NV>(p, acc, lane, s.ids[i]);
         }
     }
 }
@@ -481,7 +535,11 @@ static int launch_fwd(const RasterParams &p, cudaStream_t stream) {
 // Pixels per backward thread: enough to amortise the warp reduction, few enough
 // that the per-pixel state (transmittance, colour buffer, upstream gradient)
 // stays in registers.
+#ifdef GSB_BWD_PPT
+template <int CDIM> constexpr int bwd_ppt() { return CDIM <= 4 ? GSB_BWD_PPT : (CDIM <= 8 ? 2 : 1); }
+#else
 template <int CDIM> constexpr int bwd_ppt() { return CDIM <= 4 ? 4 : (CDIM <= 8 ? 2 : 1); }
+#endif
 
 template <int CDIM>
 static int launch_bwd(const RasterParams &p, cudaStream_t stream) {

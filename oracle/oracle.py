@@ -147,6 +147,9 @@ def isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, coni
         iid = np.ascontiguousarray(image_ids, np.int64)
     if (conics is None) != (opacities is None):
         conics, opacities = None, None
+    assert means2d.size == 2 * n and radii.size == 2 * n and depths.size == n
+    if conics is not None:
+        assert conics.size == 3 * n and opacities.size == n, (conics.shape, opacities.shape)
     tpg = np.zeros(depths.shape, np.int32)
     lib().ora_isect_count(n, _p(means2d), _p(radii), _p(conics), _p(opacities), tile_size,
                           tile_width, tile_height, _p(tpg))
@@ -170,6 +173,13 @@ def isect_offset_encode(isect_ids, n_images, tile_width, tile_height):
     return out
 
 
+def _check_splats(means2d, conics, colors, opacities, fids):
+    n = means2d.size // 2
+    assert conics.size == 3 * n and opacities.size == n and colors.size == n * colors.shape[-1], (
+        means2d.shape, conics.shape, colors.shape, opacities.shape)
+    assert fids.size == 0 or (0 <= fids.min() and fids.max() < n)
+
+
 def raster_fwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, flatten_ids,
                backgrounds=None, masks=None):
     means2d, conics, colors, opacities, backgrounds = map(
@@ -181,6 +191,7 @@ def raster_fwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, fla
     I = int(np.prod(idims)) if idims else 1
     th, tw = offsets.shape[-2:]
     CH = colors.shape[-1]
+    _check_splats(means2d, conics, colors, opacities, fids)
     renders = np.zeros(idims + (H, W, CH), np.float32)
     alphas = np.zeros(idims + (H, W, 1), np.float32)
     last = np.zeros(idims + (H, W), np.int32)
@@ -204,6 +215,7 @@ def raster_bwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, fla
     I = int(np.prod(idims)) if idims else 1
     th, tw = offsets.shape[-2:]
     CH = colors.shape[-1]
+    _check_splats(means2d, conics, colors, opacities, fids)
     n_splats = opacities.size
     v_m2d = np.zeros(means2d.shape, np.float32)
     v_abs = np.zeros(means2d.shape, np.float32) if absgrad else None

@@ -186,7 +186,8 @@ def test_projection_packed_backward_equals_dense():
         loss = (m2 * w).sum() + (dep * w[:, 0]).sum() + (con * 0.1 * w).sum()
         grads.append(torch.autograd.grad(loss, (means, quats, scales, viewmats)))
     for a, b, name in zip(grads[0], grads[1], ("means", "quats", "scales", "viewmats")):
-        assert_close(b, a, 1e-5, 1e-5, name=name)
+        # two fp32 summation orders (per-pair atomics vs per-Gaussian sums)
+        assert_close(b, a, 1e-3, 1e-5, name=name)
 
 
 def test_projection_empty_and_culled():
