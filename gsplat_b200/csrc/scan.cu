@@ -6,6 +6,8 @@
 // inter-block waiting: per-tile sums, a single-block scan of the tile sums, and a
 // final pass that rescans each tile and adds its base. Each tile is 2048 values
 // (256 threads x 8); the input is read twice, the output written once.
+#include <mutex>
+
 #include "common.cuh"
 #include "gsb_internal.h"
 #include "gsb_scan.cuh"
@@ -119,7 +121,73 @@ int inclusive_scan_i32_i64(const int32_t *in, int64_t *out, size_t n, void *scra
     return check_launch("inclusive_scan_i32_i64");
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant
+//
+// Some callers cannot allocate device memory at the point where they need a
+// prefix sum: code that runs inside a host application which owns every device
+// allocation itself (a rendering engine or plugin host with a fixed, pre-reserved
+// memory budget), or code called from an allocator's own callbacks, where a
+// cudaMalloc would re-enter the allocator. For them the tile sums live in a
+// file-scope device array instead of a caller-provided buffer.
+//
+// The array holds kNoAllocMaxTiles tile sums, i.e. inputs of up to
+// kNoAllocMaxTiles * kScanTile = 2^27 values; every GPU that loads this library
+// keeps the 512 KiB for the life of the process. Every call on a device shares
+// the one array and leaves its tile sums behind; nothing in it needs to start at
+// zero (each call writes the sums of all its tiles before reading them), but two
+// calls that overlap on the GPU (different streams, no ordering) race on it.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocMaxTiles = 65536;
+constexpr long long kNoAllocMaxN = (long long)kNoAllocMaxTiles * kScanTile;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) int64_t g_noalloc_tile_sums[kNoAllocMaxTiles];
+
+static std::mutex g_noalloc_mutex;
+static void *g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_tile_sums on the current device. In host code the
+// symbol is only a host-side stand-in, so the address is looked up once per
+// device with that device current and cached.
+static int noalloc_scratch(void **addr) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return set_error(kErrLaunch, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return set_error(kErrUnsupported, "device %d beyond the %d supported by the allocation-free scan", dev,
+                         kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_tile_sums);
+        if (e != cudaSuccess)
+            return set_error(kErrLaunch, "cudaGetSymbolAddress(g_noalloc_tile_sums) failed: %s",
+                             cudaGetErrorString(e));
+        g_noalloc_addr[dev] = p;
+    }
+    *addr = g_noalloc_addr[dev];
+    return kOk;
+}
+
 } // namespace gsb
+
+extern "C" int gsb_inclusive_scan_i32_noalloc(const int32_t *in, int64_t *out, long long n,
+                                              cudaStream_t stream) {
+    using namespace gsb;
+    if (n < 0) return set_error(kErrInvalidArgument, "negative length");
+    if (n > kNoAllocMaxN)
+        return set_error(kErrInvalidArgument,
+                         "gsb_inclusive_scan_i32_noalloc: n = %lld exceeds the maximum of %lld values "
+                         "held by its static scratch; use gsb_inclusive_scan_i32 with a caller buffer",
+                         n, kNoAllocMaxN);
+    if (n == 0) return kOk;
+    void *scratch = nullptr;
+    if (int e = noalloc_scratch(&scratch)) return e;
+    return inclusive_scan_i32_i64(in, out, (size_t)n, scratch, kNoAllocMaxTiles * sizeof(int64_t),
+                                  stream);
+}
 
 extern "C" size_t gsb_scan_scratch_bytes(long long n) { return gsb::scan_scratch_bytes((size_t)n); }
 

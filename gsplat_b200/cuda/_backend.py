@@ -77,6 +77,7 @@ SIGNATURES = {
     "gsb_spherical_harmonics_bwd": (I32, [I32, I64, I32, P, P, P, P, P, P, P]),
     "gsb_scan_scratch_bytes": (SZ, [I64]),
     "gsb_inclusive_scan_i32": (I32, [P, P, I64, P, SZ, P]),
+    "gsb_inclusive_scan_i32_noalloc": (I32, [P, P, I64, P]),
     "gsb_isect_key_bits": (I32, [I32, I32, I32]),
     "gsb_isect_count": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, P, P]),
     "gsb_isect_emit": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, P, P, P, P]),

@@ -174,6 +174,19 @@ GSB_API size_t gsb_scan_scratch_bytes(long long n);
 GSB_API int gsb_inclusive_scan_i32(const int32_t *in, int64_t *out, long long n, void *scratch,
                            size_t scratch_bytes, cudaStream_t stream);
 
+/* Allocation-free inclusive scan. No counterpart in the reference: it exists for
+ * callers that may not allocate device memory where they need the scan, e.g.
+ * code running inside a host application that owns all device memory itself, or
+ * inside an allocator's callbacks. Same result as gsb_inclusive_scan_i32, but the
+ * scratch is a static 512 KiB device array inside this library (held on every
+ * GPU that loads it), so n is limited to 2^27 values; larger n returns -1 with a
+ * message. The library itself calls no cudaMalloc/cudaFree here. The first call
+ * on a device looks the array's device address up (cudaGetSymbolAddress), so make
+ * that first call before any stream capture. All calls on a device share the
+ * array: calls that overlap on the GPU (unordered streams) race on it. */
+GSB_API int gsb_inclusive_scan_i32_noalloc(const int32_t *in, int64_t *out, long long n,
+                                           cudaStream_t stream);
+
 /* --- Tile intersection ----------------------------------------------------
  * Replaces gsplat::intersect_tile (Intersect.cpp:33-176) as count -> scan ->
  * emit -> sort. Dense: means2d [I,N,2], radii [I,N,2], depths [I,N] (packed=0).
