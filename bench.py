@@ -145,6 +145,175 @@ def train_step(params, opt, viewmat, K, W, H, G, Ga, distributed=False):
     return loss, meta
 
 
+FLOP_PER_PAIR = {"fwd": 26, "bwd": 68}  # CDIM = 3 (20 + 2 C and 50 + 6 C)
+
+
+def cpu_scene(n, seed):
+    """config-1 scene as float32 numpy arrays (same seeds as the GPU run)."""
+    from tests import _data
+
+    d = _data.config1(N=n, seed=seed)
+    out = {k: (v.numpy() if hasattr(v, "numpy") else v) for k, v in d.items()}
+    rng = __import__("numpy").random.default_rng(100 + seed)
+    out["G"] = rng.standard_normal((1, d["height"], d["width"], 3)).astype("float32")
+    out["Ga"] = rng.standard_normal((1, d["height"], d["width"], 1)).astype("float32")
+    return out
+
+
+def cpu_reference_step(sc, tile_row_stride=8):
+    """One training step of the reference algorithm on the host cores (the CPU
+    restatement in oracle/, OpenMP over all cores): projection, SH, AccuTile
+    intersection + sort + offsets, rasterize forward/backward, the backward chain
+    and the selective Adam update of every parameter. The rasterizer runs on every
+    `tile_row_stride`-th row of tiles (a bounded, representative sample) and its
+    time is scaled to the full image. Returns (seconds for a full step, detail)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    W, H = sc["width"], sc["height"]
+    ts = 16
+    tw, th = -(-W // ts), -(-H // ts)
+    t = {}
+    t0 = time.perf_counter()
+    means, quats, scales, opac, sh = sc["means"], sc["quats"], sc["scales"], sc["opacities"], sc["sh"]
+    vm, K = sc["viewmats"], sc["Ks"]
+    radii, m2, dep, con, _ = O.projection_fwd(means, None, quats, scales, opac, vm, K, W, H,
+                                              far_plane=100.0)
+    valid = (radii > 0).all(-1)
+    campos = -np.einsum("cji,cj->ci", vm[:, :3, :3], vm[:, :3, 3])
+    dirs = means[None] - campos[:, None]
+    coeffs = sh[None]
+    raw = O.sh_fwd(3, dirs, coeffs, valid)
+    colors = np.maximum(raw + 0.5, 0.0).astype(np.float32)
+    op_eff = np.ascontiguousarray(opac[None])
+    t["projection+sh"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    _, keys, fids = O.isect_tiles(m2, radii, dep, ts, tw, th, conics=con, opacities=op_eff)
+    offsets = O.isect_offset_encode(keys, 1, tw, th)
+    t["isect+sort+offsets"] = time.perf_counter() - t0
+    rows = np.arange(th) % tile_row_stride == 0
+    masks = np.repeat(rows[:, None], tw, axis=1)[None]
+    scale = masks.size / masks.sum()
+    t0 = time.perf_counter()
+    rc, ra, last = O.raster_fwd(m2, con, colors, op_eff, W, H, ts, offsets, fids, masks=masks)
+    t["raster_fwd"] = (time.perf_counter() - t0) * scale
+    t0 = time.perf_counter()
+    v_m2, v_con, v_col, v_op, _ = O.raster_bwd(m2, con, colors, op_eff, W, H, ts, offsets, fids,
+                                               ra, last, sc["G"], sc["Ga"], masks=masks)
+    t["raster_bwd"] = (time.perf_counter() - t0) * scale
+    t0 = time.perf_counter()
+    v_col = v_col * (raw + 0.5 >= 0)
+    v_coeffs, v_dirs = O.sh_bwd(3, dirs, coeffs, v_col, valid)
+    v_means, _, v_quats, v_scales, _ = O.projection_bwd(
+        means, None, quats, scales, vm, K, W, H, 0.3, radii, con, None, v_m2 * valid[..., None],
+        np.zeros_like(dep), v_con * valid[..., None], None, viewmats_grad=False)
+    v_means = v_means + v_dirs[0] * valid[0][:, None]
+    t["backward chain"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    vis = valid[0].astype(np.uint8)
+    for p, g, lr in ((means, v_means, LRS["means"]), (quats, v_quats, LRS["quats"]),
+                     (scales, v_scales, LRS["scales"]), (opac, v_op[0], LRS["opacities"]),
+                     (sh, v_coeffs[0], LRS["sh"])):
+        st = sc.setdefault("adam_state", {})
+        m, v = st.setdefault(id(p), (np.zeros_like(p), np.zeros_like(p)))
+        O.adam(p, g, m, v, vis, lr, 0.9, 0.999, 1e-15)
+    t["adam"] = time.perf_counter() - t0
+    return sum(t.values()), {k: round(v * 1e3, 2) for k, v in t.items()}
+
+
+def run_reference(args):
+    """`--impl reference`: the reference algorithm timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sc = cpu_scene(args.n, 1)
+    W, H = sc["width"], sc["height"]
+    for _ in range(args.warmup):
+        cpu_reference_step(sc)
+    times, detail = [], None
+    for _ in range(args.steps):
+        dt, detail = cpu_reference_step(sc)
+        times.append(dt)
+    ms = 1e3 * sum(times) / len(times)
+    value = (W * H / 1e6) / (ms / 1e3)
+    cores = os.cpu_count()
+    sample = ("config 1 (1M Gaussians, 1297x840): projection, SH, isect, sort, backward chain and "
+              "Adam on the full scene; rasterizer forward/backward on every 8th tile row, scaled x8")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "MPix/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded config-1 distributions)",
+        "config": {"workload": "config1: 1M Gaussians, 1297x840 pinhole fx=fy=1150, SH deg 3, "
+                               "fwd+bwd+SelectiveAdam", "stages_ms": detail},
+        "cpu_baseline": {"value": value, "unit": "MPix/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "MPix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def fp32_peak_tflops(dev):
+    """Measured FP32 FMA throughput of this GPU (gsb_fp32_fma_probe)."""
+    import torch
+
+    from gsplat_b200.cuda import _backend
+
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks, threads, iters = sms * 8, 256, 4096
+    out = torch.empty(blocks * threads, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(3):
+        _backend.call("gsb_fp32_fma_probe", out.data_ptr(), blocks, threads, iters, stream)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    reps = 10
+    for _ in range(reps):
+        _backend.call("gsb_fp32_fma_probe", out.data_ptr(), blocks, threads, iters, stream)
+    b.record()
+    torch.cuda.synchronize(dev)
+    sec = a.elapsed_time(b) / 1e3 / reps
+    return blocks * threads * iters * 16 / sec / 1e12
+
+
+def contributing_pairs(meta, W, H, dev):
+    """Number of (pixel, splat) pairs that contribute to the image (alpha >= 1/255
+    before each pixel's transmittance cut-off): the algorithmic work unit of both
+    rasterizer kernels."""
+    import torch
+
+    from gsplat_b200.cuda import _backend
+
+    offsets = meta["isect_offsets"].contiguous()
+    fids = meta["flatten_ids"]
+    n = meta["means2d"].shape[0]
+    ones = torch.zeros((n, 1), device=dev)
+    I = int(offsets.numel() // (offsets.shape[-1] * offsets.shape[-2]))
+    th, tw = offsets.shape[-2:]
+    renders = torch.empty((I, H, W, 1), device=dev)
+    alphas = torch.empty((I, H, W, 1), device=dev)
+    last = torch.empty((I, H, W), dtype=torch.int32, device=dev)
+    counts = torch.empty((I, H, W), dtype=torch.int32, device=dev)
+    _backend.call("gsb_rasterize_fwd_counted", I, 1, meta["means2d"].data_ptr(),
+                  meta["conics"].data_ptr(), ones.data_ptr(), meta["opacities"].data_ptr(), None, None,
+                  W, H, meta["tile_size"], tw, th, offsets.data_ptr(), fids.data_ptr(), fids.numel(),
+                  renders.data_ptr(), alphas.data_ptr(), last.data_ptr(), counts.data_ptr(),
+                  torch.cuda.current_stream(dev).cuda_stream)
+    return int(counts.sum().item())
+
+
+def ncu_traffic(name):
+    """DRAM bytes per launch recorded in profiles/<name>.md (line 'dram_bytes_per_launch: N')."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
 def run_gsb(args):
     import torch
     import torch.distributed as dist
@@ -183,7 +352,7 @@ def run_gsb(args):
     barrier()
 
     # device-timed region: K full steps, inputs resident in HBM
-    _backend.timing = {} if args.profile_ops or rank == 0 else None
+    _backend.timing = {}
     sampler = ClockSampler(local)
     with sampler:
         start = torch.cuda.Event(enable_timing=True)
@@ -244,6 +413,31 @@ def run_gsb(args):
         e2e = {"value": mpix / (ems / 1e3), "unit": "MPix/s", "ms_per_step": ems,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4}
 
+    roofline = None
+    cpu_baseline = None
+    if rank == 0 and ops.get("gsb_rasterize_bwd"):
+        pairs = contributing_pairs(meta, W, H, dev)
+        peak = fp32_peak_tflops(dev)
+        t_bwd = ops["gsb_rasterize_bwd"]["ms_per_step"] / 1e3
+        achieved = FLOP_PER_PAIR["bwd"] * pairs / t_bwd / 1e12
+        roofline = {"kernel": "raster_bwd_kernel<3,4>", "bound": "fp32", "achieved": achieved,
+                    "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "traffic": ncu_traffic("raster_bwd_config1"),
+                    "peak_source": "measured FP32 FMA probe (gsb_fp32_fma_probe) on this GPU",
+                    "algorithmic": f"{FLOP_PER_PAIR['bwd']} FLOP per contributing (pixel, splat) pair; "
+                                   f"{pairs} pairs per launch",
+                    "fwd": {"achieved": FLOP_PER_PAIR["fwd"] * pairs /
+                            (ops["gsb_rasterize_fwd"]["ms_per_step"] / 1e3) / 1e12,
+                            "unit": "TFLOP/s"}}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sc = cpu_scene(args.n, 1)
+        cpu_reference_step(sc)
+        dt, detail = cpu_reference_step(sc)
+        cpu_baseline = {"value": (W * H / 1e6) / dt, "unit": "MPix/s", "cores": os.cpu_count(),
+                        "kind": "port", "ms_per_step": dt * 1e3, "stages_ms": detail,
+                        "sample": "config 1 step of the CPU restatement (oracle/): full projection, SH, "
+                                  "isect, sort, backward chain, Adam; rasterizer on every 8th tile row "
+                                  "scaled x8"}
     n_isects = int(meta["isect_ids"].numel()) if "isect_ids" in meta else None
     nnz = int(meta["gaussian_ids"].numel()) if meta.get("gaussian_ids") is not None else None
     launches = sum(v["launch_calls"] for v in ops.values()) if ops else None
@@ -269,6 +463,9 @@ def run_gsb(args):
                    "visible_splats": nnz, "n_isects": n_isects},
         "clocks": sampler.summary(),
         "e2e": e2e,
+        "roofline": roofline,
+        "cpu_baseline": cpu_baseline,
+        "gpu_launches": launches,
         "ops": ops,
         "host_issue_ms_per_step": host_ms,
     }
@@ -282,10 +479,7 @@ def run_gsb(args):
 def main():
     args = parse()
     if args.impl == "reference":
-        rank = int(os.environ.get("RANK", "0"))
-        if rank != 0:
-            return
-        print(json.dumps({"impl": "reference", "unavailable": "CPU reference arm not implemented yet"}))
+        run_reference(args)
         return
     run_gsb(args)
 

@@ -45,6 +45,7 @@ struct RasterParams {
     float *renders; // [I, H, W, cstride]
     float *alphas;  // [I, H, W]
     int32_t *last_ids;
+    int32_t *pair_counts; // optional [I, H, W]: splats that contributed to each pixel
     bool write_alpha;
     // backward inputs / outputs
     const float *v_renders, *v_alphas;
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     const uint32_t tpix = p.tile_size * p.tile_size;
 
     float px[PPT], py[PPT], T[PPT], out[PPT][CDIM];
-    int32_t cur[PPT];
+    int32_t cur[PPT], npairs[PPT];
     bool inside[PPT], done[PPT];
     uint32_t pid[PPT];
     bool has = false;
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
         pid[k] = i * p.W + j;
         T[k] = 1.f;
         cur[k] = 0;
+        npairs[k] = 0;
         done[k] = !inside[k];
 #pragma unroll
         for (int c = 0; c < CDIM; ++c) out[k][c] = 0.f;
@@ -264,6 +266,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
 #pragma unroll
                     for (int c = 0; c < CDIM; ++c) out[k][c] += s.colors[i * CDIM + c] * w;
                     cur[k] = bstart + i;
+                    ++npairs[k];
                     T[k] = next_T;
                 }
             }
@@ -281,6 +284,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
             if (p.write_alpha) {
                 p.alphas[pix] = 0.f;
                 p.last_ids[pix] = 0;
+                if (p.pair_counts) p.pair_counts[pix] = 0;
             }
             continue;
         }
@@ -289,6 +293,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
         if (p.write_alpha) {
             p.alphas[pix] = 1.f - T[k];
             p.last_ids[pix] = cur[k];
+            if (p.pair_counts) p.pair_counts[pix] = npairs[k];
         }
     }
 }
@@ -603,13 +608,12 @@ static int check_raster_args(int I, int W, int H, int tile_size, int tile_w, int
 
 using namespace gsb;
 
-extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, const float *conics,
-                                 const float *colors, const float *opacities,
-                                 const float *backgrounds, const bool *masks, int width, int height,
-                                 int tile_size, int tile_width, int tile_height,
-                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
-                                 long long n_isects, float *renders, float *alphas,
-                                 int32_t *last_ids, cudaStream_t stream) {
+static int rasterize_fwd(int I, int channels, const float *means2d, const float *conics,
+                         const float *colors, const float *opacities, const float *backgrounds,
+                         const bool *masks, int width, int height, int tile_size, int tile_width,
+                         int tile_height, const int32_t *tile_offsets, const int32_t *flatten_ids,
+                         long long n_isects, float *renders, float *alphas, int32_t *last_ids,
+                         int32_t *pair_counts, cudaStream_t stream) {
     if (int e = check_raster_args(I, width, height, tile_size, tile_width, tile_height, channels)) return e;
     if (I == 0 || width == 0 || height == 0) return kOk;
     RasterParams p = {};
@@ -632,6 +636,7 @@ extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, cons
     p.renders = renders;
     p.alphas = alphas;
     p.last_ids = last_ids;
+    p.pair_counts = pair_counts;
     int coff = 0;
     while (coff < channels) {
         const int n = next_chunk(channels - coff);
@@ -641,6 +646,32 @@ extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, cons
         coff += n;
     }
     return kOk;
+}
+
+extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, float *renders, float *alphas,
+                                 int32_t *last_ids, cudaStream_t stream) {
+    return rasterize_fwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
+                         height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
+                         n_isects, renders, alphas, last_ids, nullptr, stream);
+}
+
+extern "C" int gsb_rasterize_fwd_counted(int I, int channels, const float *means2d,
+                                         const float *conics, const float *colors,
+                                         const float *opacities, const float *backgrounds,
+                                         const bool *masks, int width, int height, int tile_size,
+                                         int tile_width, int tile_height,
+                                         const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                         long long n_isects, float *renders, float *alphas,
+                                         int32_t *last_ids, int32_t *pair_counts,
+                                         cudaStream_t stream) {
+    return rasterize_fwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
+                         height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
+                         n_isects, renders, alphas, last_ids, pair_counts, stream);
 }
 
 extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, const float *conics,

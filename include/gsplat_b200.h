@@ -234,6 +234,19 @@ GSB_API int gsb_rasterize_fwd(int I, int channels, const float *means2d, const f
                       long long n_isects, float *renders, float *alphas, int32_t *last_ids,
                       cudaStream_t stream);
 
+/* Same as gsb_rasterize_fwd and additionally writes pair_counts int32 [I,H,W], the
+ * number of splats that contributed to each pixel (alpha >= 1/255 before the
+ * transmittance cut-off). No reference counterpart; used to count the
+ * algorithmic work of the rasterizer for its roofline. */
+GSB_API int gsb_rasterize_fwd_counted(int I, int channels, const float *means2d,
+                                      const float *conics, const float *colors,
+                                      const float *opacities, const float *backgrounds,
+                                      const bool *masks, int width, int height, int tile_size,
+                                      int tile_width, int tile_height, const int32_t *tile_offsets,
+                                      const int32_t *flatten_ids, long long n_isects,
+                                      float *renders, float *alphas, int32_t *last_ids,
+                                      int32_t *pair_counts, cudaStream_t stream);
+
 /* Replaces gsplat::rasterize_to_pixels_3dgs_bwd (Rasterization.cpp:121-214).
  * v_means2d, v_conics, v_colors, v_opacities and v_means2d_abs (optional,
  * absgrad) are accumulated: zero-initialise them. */
@@ -268,6 +281,12 @@ GSB_API int gsb_adam(float *param, const float *grad, float *exp_avg, float *exp
              float eps, cudaStream_t stream);
 GSB_API int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bool *valid, float b1,
                    float b2, cudaStream_t stream);
+
+/* --- Measurement ----------------------------------------------------------
+ * FP32 FMA throughput probe (no reference counterpart): blocks x threads threads
+ * each run 8 independent FMA chains of iters steps and write one float to out
+ * [blocks*threads]; FLOPs = blocks * threads * iters * 16. Time it with events. */
+GSB_API int gsb_fp32_fma_probe(float *out, int blocks, int threads, int iters, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,133 @@
+"""Host logic of the Gaussian-sharded multi-GPU mode on CPU: the collectives of
+gsplat_b200.distributed run on gloo with world size 2 (the reference's own test,
+tests/_test_distributed.py, needs GPUs). Values and gradients are checked
+against what each rank must receive.
+"""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, fn, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        fn(rank, world)
+        q.put((rank, None))
+    except Exception:  # report to the parent
+        q.put((rank, traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+def run(fn, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    errors = [e for _, e in results if e]
+    assert not errors, errors[0]
+
+
+def _collectives(rank, world):
+    from gsplat_b200.distributed import (all_gather_int32, all_gather_tensor_list, all_to_all_int32,
+                                         all_to_all_tensor_list)
+
+    dev = torch.device("cpu")
+    assert all_gather_int32(world, 10 + rank, device=dev) == [10, 11]
+    assert all_to_all_int32(world, [rank * 10 + 1, rank * 10 + 2], device=dev) == [1 + rank, 11 + rank]
+    a = torch.full((2, 3), float(rank))
+    b = torch.full((2,), float(rank + 5))
+    ga, gb = all_gather_tensor_list(world, [a, b])
+    assert ga.shape == (4, 3) and gb.shape == (4,)
+    assert ga[:2].eq(0).all() and ga[2:].eq(1).all() and gb[:2].eq(5).all() and gb[2:].eq(6).all()
+    # uneven all-to-all with autograd: rank 0 sends 1 row to itself and 2 to rank 1,
+    # rank 1 sends 3 rows to rank 0 and 1 to itself
+    splits = [1, 2] if rank == 0 else [3, 1]
+    n = sum(splits)
+    x = (torch.arange(n, dtype=torch.float32) + 100 * rank).reshape(n, 1).repeat(1, 2)
+    x.requires_grad_(True)
+    y = torch.arange(n, dtype=torch.int64) + 1000 * rank
+    out_x, out_y = all_to_all_tensor_list(world, [x, y], splits)
+    if rank == 0:
+        assert out_x[:, 0].tolist() == [0.0, 100.0, 101.0, 102.0]
+        assert out_y.tolist() == [0, 1000, 1001, 1002]
+    else:
+        assert out_x[:, 0].tolist() == [1.0, 2.0, 103.0]
+        assert out_y.tolist() == [1, 2, 1003]
+    w = torch.arange(out_x.shape[0], dtype=torch.float32)[:, None] + 1.0
+    (out_x * w).sum().backward()
+    # each row's gradient is the weight of the position it landed at on its destination
+    if rank == 0:
+        assert x.grad[:, 0].tolist() == [1.0, 1.0, 2.0]
+    else:
+        assert x.grad[:, 0].tolist() == [2.0, 3.0, 4.0, 3.0]
+
+
+def test_collectives_world2_gloo():
+    run(_collectives)
+
+
+def _single_rank_shortcuts(rank, world):
+    from gsplat_b200.distributed import all_gather_tensor_list, all_to_all_tensor_list
+
+    t = torch.ones(3, 2)
+    assert all_gather_tensor_list(1, [t])[0] is t
+    assert all_to_all_tensor_list(1, [t], [3])[0] is t
+
+
+def test_world1_is_identity():
+    run(_single_rank_shortcuts, world=1)
+
+
+def _raising_rank(rank, world):
+    """A rank that fails between steps: the other one sees its collective fail
+    within the process-group timeout instead of hanging."""
+    import datetime
+
+    from gsplat_b200.distributed import all_gather_int32
+
+    if rank == 1:
+        raise RuntimeError("rank 1 leaves")
+    try:
+        dist.monitored_barrier(timeout=datetime.timedelta(seconds=5))
+    except RuntimeError as e:
+        assert "1" in str(e)
+        return
+    raise AssertionError("the surviving rank did not notice")
+
+
+def test_failed_rank_is_detected_on_host():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, _raising_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] is not None and "rank 1 leaves" in results[1]
+    assert results[0] is None, results[0]
