@@ -29,6 +29,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd+Adam ms/iter at 1M Gaussians 1297x840; MPix/s at 1/2/4/8 GPUs"
+GRAD_BANK = 4
 LRS = {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacities": 5e-2, "sh": 2.5e-3}
 
 
@@ -46,33 +47,76 @@ def parse():
     return ap.parse_args()
 
 
+# Child process that reads the GPU's SM clock, power and clock-event reasons
+# through NVML (the library nvidia-smi queries) every PERIOD seconds and prints
+# one timestamped line per sample. A separate process keeps the sampling off the
+# benchmark's Python thread. Only reads: it changes no setting.
+_SAMPLER_CHILD = r"""
+import sys, time
+import pynvml as N
+N.nvmlInit()
+key, period = sys.argv[1], float(sys.argv[2])
+h = N.nvmlDeviceGetHandleByUUID(key) if key.startswith("GPU-") else N.nvmlDeviceGetHandleByIndex(int(key))
+mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or N.nvmlDeviceGetCurrentClocksThrottleReasons
+while True:
+    t = time.time()
+    sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+    r = reasons(h)
+    p = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+    sys.stdout.write(f"{t:.4f},{sm},{mx},{p:.1f},{r}\n")
+    sys.stdout.flush()
+    time.sleep(period)
+"""
+
+# NVML clock-event reason bits (nvml.h) with nvidia-smi's names
+_REASON_BITS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+    """Samples SM clocks and clock-event (throttle) reasons while the benchmark
+    runs: started before the warm-up, confirmed running (first sample received)
+    before returning, and summarised over the samples taken inside a given host
+    time window (the timed region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD = 0.01
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, device):
+        import torch
+
+        props = torch.cuda.get_device_properties(device)
+        uuid = str(getattr(props, "uuid", ""))
+        self.key = uuid if uuid.startswith("GPU-") else ("GPU-" + uuid if uuid else str(device.index or 0))
+        self.samples = []  # (time, sm_mhz, max_mhz, watts, reasons bitmask)
         self.proc = None
-        self.lines = []
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, self.key, str(self.PERIOD)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+        except OSError as e:
+            self.error = str(e)
+            return self
+        self.ready = threading.Event()
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        if not self.ready.wait(timeout=30):
+            self.error = "no sample within 30 s"
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = line.strip().split(",")
+            if len(parts) == 5:
+                try:
+                    self.samples.append((float(parts[0]), float(parts[1]), float(parts[2]), float(parts[3]),
+                                         int(parts[4])))
+                except ValueError:
+                    continue
+                self.ready.set()
+        self.ready.set()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -81,34 +125,41 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            if not self.samples and self.error is None:
+                self.error = (self.proc.stderr.read() or "sampler exited").strip().splitlines()[-1:]
 
-    def summary(self):
-        mhz, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                mhz.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not mhz:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(mhz)}
+    def summary(self, t0, t1):
+        """Median SM clock and the union of active reasons over the samples taken
+        between host times t0 and t1."""
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": "nvml", "error": self.error}
+        mask = 0
+        for s in inside:
+            mask |= s[4]
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": inside[-1][2],
+                "power_w": statistics.median(s[3] for s in inside),
+                "reasons": sorted(n for b, n in _REASON_BITS.items() if mask & b),
+                "samples": len(inside), "source": "nvml", "window_s": round(t1 - t0, 4)}
 
 
-def make_params(n, seed, dev):
+def make_params(n, seed, dev, rank=0, world=1):
+    """config-1 Gaussians of one rank. With several ranks the shards sit side by
+    side along x (12 units apart) and each rank's camera looks at its own shard,
+    so every GPU renders one config-1 view of a scene that grows with the job
+    (weak scaling); splats near the frustum edges still cross ranks through the
+    all-to-all."""
     import torch
 
     from tests import _data
 
     d = _data.config1(N=n, seed=seed)
+    shift = 12.0 * (rank - (world - 1) / 2.0)
+    if world > 1:
+        d["means"][:, 0] += shift
+        d["viewmats"] = d["viewmats"].clone()
+        d["viewmats"][:, 0, 3] = -shift
     params = {
         "means": d["means"],
         "scales": torch.log(d["scales"]),
@@ -332,39 +383,53 @@ def run_gsb(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
-    params, d = make_params(args.n, 1 + rank, dev)
+    params, d = make_params(args.n, 1 + rank, dev, rank, world)
     W, H = d["width"], d["height"]
     viewmat = d["viewmats"].to(dev)
     K = d["Ks"].to(dev)
     opt = gsplat_b200.SelectiveAdam([{"params": [p], "lr": LRS[k], "name": k} for k, p in params.items()],
                                     eps=1e-15, betas=(0.9, 0.999))
+    # Upstream image gradients: a bank of independent N(0,1) images cycled step by
+    # step, so the Adam moments average out as in training and the scene (hence
+    # the per-step work) stays stationary over the timed steps; a single fixed
+    # gradient image would push every parameter the same way at full learning
+    # rate and drift the workload.
     g = torch.Generator(device=dev).manual_seed(100 + rank)
-    G = torch.randn((1, H, W, 3), device=dev, generator=g)
-    Ga = torch.randn((1, H, W, 1), device=dev, generator=g)
+    bank = [(torch.randn((1, H, W, 3), device=dev, generator=g),
+             torch.randn((1, H, W, 1), device=dev, generator=g)) for _ in range(GRAD_BANK)]
+    step_no = [0]
+
+    def grads():
+        G, Ga = bank[step_no[0] % GRAD_BANK]
+        step_no[0] += 1
+        return G, Ga
 
     def barrier():
         if distributed:
             dist.barrier()
         torch.cuda.synchronize()
 
+    sampler = ClockSampler(dev)
+    sampler.__enter__()
     for _ in range(args.warmup):
-        train_step(params, opt, viewmat, K, W, H, G, Ga, distributed)
+        train_step(params, opt, viewmat, K, W, H, *grads(), distributed)
     barrier()
 
     # device-timed region: K full steps, inputs resident in HBM
     _backend.timing = {}
-    sampler = ClockSampler(local)
-    with sampler:
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        barrier()
-        wall0 = time.perf_counter()
-        start.record()
-        for _ in range(args.steps):
-            loss, meta = train_step(params, opt, viewmat, K, W, H, G, Ga, distributed)
-        end.record()
-        host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
-        barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    wall0 = time.perf_counter()
+    clock0 = time.time()
+    start.record()
+    for _ in range(args.steps):
+        loss, meta = train_step(params, opt, viewmat, K, W, H, *grads(), distributed)
+    end.record()
+    host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
+    barrier()
+    clock1 = time.time()
+    sampler.__exit__(None, None, None)
     ms = start.elapsed_time(end) / args.steps
     timing = _backend.timing
     _backend.timing = None
@@ -389,14 +454,14 @@ def run_gsb(args):
     if not args.no_e2e:
         hv = viewmat.cpu().pin_memory()
         hK = K.cpu().pin_memory()
-        hG = G.cpu().pin_memory()
-        hGa = Ga.cpu().pin_memory()
-        h2d = hv.numel() * 4 + hK.numel() * 4 + hG.numel() * 4 + hGa.numel() * 4
+        hbank = [(G_.cpu().pin_memory(), Ga_.cpu().pin_memory()) for G_, Ga_ in bank]
+        h2d = hv.numel() * 4 + hK.numel() * 4 + hbank[0][0].numel() * 4 + hbank[0][1].numel() * 4
         barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        for _ in range(args.steps):
+        for it in range(args.steps):
+            hG, hGa = hbank[it % GRAD_BANK]
             dv = hv.to(dev, non_blocking=True)
             dK = hK.to(dev, non_blocking=True)
             dG = hG.to(dev, non_blocking=True)
@@ -461,7 +526,7 @@ def run_gsb(args):
                    "parallelism": f"gaussian-sharded x{world}" if distributed else "single",
                    "l2": "inputs larger than L2 (params + Adam state ~700 MB)",
                    "visible_splats": nnz, "n_isects": n_isects},
-        "clocks": sampler.summary(),
+        "clocks": sampler.summary(clock0, clock1),
         "e2e": e2e,
         "roofline": roofline,
         "cpu_baseline": cpu_baseline,

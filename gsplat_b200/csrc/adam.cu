@@ -33,44 +33,79 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
     p += -lr * m / (sqrtf(v) + eps);
 }
 
+#ifndef GSB_ADAM_VEC
+#define GSB_ADAM_VEC 1
+#endif
+constexpr int kAdamVec = GSB_ADAM_VEC; // float4 (or scalar) items per thread, kAdamThreads apart
+
+// Visibility of the rows of elements e .. e+3 with one integer division.
+__device__ __forceinline__ void rows_visible(const bool *valid, uint32_t e, uint32_t D, bool vis[4]) {
+    if (valid == nullptr) {
+        vis[0] = vis[1] = vis[2] = vis[3] = true;
+        return;
+    }
+    const uint32_t r0 = e / D;
+    const uint32_t rem = e - r0 * D;
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t rr = rem + j;
+        const uint32_t row = r0 + (rr >= D) + (rr >= 2 * D) + (rr >= 3 * D);
+        vis[j] = valid[row];
+    }
+}
+
 __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
     int gi = 0;
     while (gi + 1 < B.n_groups && (long long)blockIdx.x >= B.block_start[gi + 1]) ++gi;
     const GsbAdamGroup &G = B.g[gi];
-    const long long local_block = (long long)blockIdx.x - B.block_start[gi];
-    const long long t = local_block * kAdamThreads + threadIdx.x;
-    const int D = G.D;
+    const uint32_t local_block = (uint32_t)((long long)blockIdx.x - B.block_start[gi]);
+    const uint32_t D = (uint32_t)G.D;
+    const uint32_t numel = (uint32_t)G.numel;
+    const float lr = G.lr, eps = G.eps, b1 = B.b1, b2 = B.b2;
     if (B.vec[gi]) {
-        const long long e0 = t * 4;
-        if (e0 >= G.numel) return;
-        bool vis[4];
-        bool anyv = false;
+        float4 p[kAdamVec], g[kAdamVec], m[kAdamVec], v[kAdamVec];
+        bool vis[kAdamVec][4], act[kAdamVec];
+        // issue every load of this thread before any arithmetic
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            vis[j] = B.valid == nullptr || B.valid[(e0 + j) / D];
-            anyv |= vis[j];
+        for (int it = 0; it < kAdamVec; ++it) {
+            const uint32_t e0 = ((local_block * kAdamVec + it) * kAdamThreads + threadIdx.x) * 4u;
+            act[it] = e0 < numel;
+            if (act[it]) {
+                rows_visible(B.valid, e0, D, vis[it]);
+                act[it] = vis[it][0] | vis[it][1] | vis[it][2] | vis[it][3];
+            }
+            if (act[it]) {
+                p[it] = *reinterpret_cast<const float4 *>(G.param + e0);
+                g[it] = *reinterpret_cast<const float4 *>(G.grad + e0);
+                m[it] = *reinterpret_cast<const float4 *>(G.exp_avg + e0);
+                v[it] = *reinterpret_cast<const float4 *>(G.exp_avg_sq + e0);
+            }
         }
-        if (!anyv) return;
-        float4 p = *reinterpret_cast<float4 *>(G.param + e0);
-        const float4 g = *reinterpret_cast<const float4 *>(G.grad + e0);
-        float4 m = *reinterpret_cast<float4 *>(G.exp_avg + e0);
-        float4 v = *reinterpret_cast<float4 *>(G.exp_avg_sq + e0);
-        float pp[4] = {p.x, p.y, p.z, p.w}, gg[4] = {g.x, g.y, g.z, g.w};
-        float mm[4] = {m.x, m.y, m.z, m.w}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (vis[j]) adam_elem(pp[j], gg[j], mm[j], vv[j], G.lr, B.b1, B.b2, G.eps);
-        *reinterpret_cast<float4 *>(G.param + e0) = make_float4(pp[0], pp[1], pp[2], pp[3]);
-        *reinterpret_cast<float4 *>(G.exp_avg + e0) = make_float4(mm[0], mm[1], mm[2], mm[3]);
-        *reinterpret_cast<float4 *>(G.exp_avg_sq + e0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        for (int it = 0; it < kAdamVec; ++it) {
+            if (!act[it]) continue;
+            const uint32_t e0 = ((local_block * kAdamVec + it) * kAdamThreads + threadIdx.x) * 4u;
+            float pp[4] = {p[it].x, p[it].y, p[it].z, p[it].w}, gg[4] = {g[it].x, g[it].y, g[it].z, g[it].w};
+            float mm[4] = {m[it].x, m[it].y, m[it].z, m[it].w}, vv[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (vis[it][j]) adam_elem(pp[j], gg[j], mm[j], vv[j], lr, b1, b2, eps);
+            *reinterpret_cast<float4 *>(G.param + e0) = make_float4(pp[0], pp[1], pp[2], pp[3]);
+            *reinterpret_cast<float4 *>(G.exp_avg + e0) = make_float4(mm[0], mm[1], mm[2], mm[3]);
+            *reinterpret_cast<float4 *>(G.exp_avg_sq + e0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        }
     } else {
-        if (t >= G.numel) return;
-        if (B.valid != nullptr && !B.valid[t / D]) return;
-        float p = G.param[t], m = G.exp_avg[t], v = G.exp_avg_sq[t];
-        adam_elem(p, G.grad[t], m, v, G.lr, B.b1, B.b2, G.eps);
-        G.param[t] = p;
-        G.exp_avg[t] = m;
-        G.exp_avg_sq[t] = v;
+#pragma unroll
+        for (int it = 0; it < kAdamVec; ++it) {
+            const uint32_t t = (local_block * kAdamVec + it) * kAdamThreads + threadIdx.x;
+            if (t >= numel) continue;
+            if (B.valid != nullptr && !B.valid[t / D]) continue;
+            float p = G.param[t], m = G.exp_avg[t], v = G.exp_avg_sq[t];
+            adam_elem(p, G.grad[t], m, v, lr, b1, b2, eps);
+            G.param[t] = p;
+            G.exp_avg[t] = m;
+            G.exp_avg_sq[t] = v;
+        }
     }
 }
 
@@ -99,8 +134,10 @@ extern "C" int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bo
                              aligned16(g.exp_avg) && aligned16(g.exp_avg_sq);
             B.vec[n] = vec ? 1 : 0;
             B.block_start[n] = blocks;
+            if (g.numel >= (1ll << 31))
+                return set_error(kErrInvalidArgument, "adam: group %d has more than 2^31 elements", done + n);
             const long long items = vec ? g.numel / 4 : g.numel;
-            blocks += (items + kAdamThreads - 1) / kAdamThreads;
+            blocks += (items + (long long)kAdamThreads * kAdamVec - 1) / ((long long)kAdamThreads * kAdamVec);
         }
         B.block_start[n] = blocks;
         B.n_groups = n;

@@ -25,6 +25,7 @@ struct FusedParams {
     ProjParams p;
     const float *sh; // [B, N, K, 3]
     uint32_t K;
+    bool sh_vec; // rows of sh are 16-byte aligned (K*3 % 4 == 0, aligned base)
 };
 
 __device__ __forceinline__ void campos_of(const float *vm, float cp[3]) {
@@ -33,19 +34,42 @@ __device__ __forceinline__ void campos_of(const float *vm, float cp[3]) {
     for (int j = 0; j < 3; ++j) cp[j] = -(vm[0 * 4 + j] * vm[3] + vm[1 * 4 + j] * vm[7] + vm[2 * 4 + j] * vm[11]);
 }
 
+// Loads the first (D+1)^2 coefficient rows of one Gaussian; with `vec` the row
+// starts 16-byte aligned and is read with 128-bit loads (all issued up front).
+template <int D>
+__device__ __forceinline__ void load_coefs(const float *coef, bool vec, float *c) {
+    constexpr int NC = (D + 1) * (D + 1) * 3;
+    if (vec && NC % 4 == 0) {
+        const float4 *c4 = reinterpret_cast<const float4 *>(coef);
+#pragma unroll
+        for (int i = 0; i < NC / 4; ++i) {
+            const float4 v = __ldg(c4 + i);
+            c[4 * i + 0] = v.x;
+            c[4 * i + 1] = v.y;
+            c[4 * i + 2] = v.z;
+            c[4 * i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NC; ++i) c[i] = __ldg(coef + i);
+    }
+}
+
 // SH colour of one (camera, Gaussian) pair; returns the pre-clamp value in raw[].
 template <int D>
-__device__ __forceinline__ void sh_color(const float *coef, const float dir[3], float raw[3]) {
+__device__ __forceinline__ void sh_color(const float *coef, bool vec, const float dir[3], float raw[3]) {
     constexpr int NB = (D + 1) * (D + 1);
+    float c[NB * 3];
+    load_coefs<D>(coef, vec, c);
     const float inv = rsqrtf(dir[0] * dir[0] + dir[1] * dir[1] + dir[2] * dir[2]);
     float Y[NB];
     sh_eval<D>(dir[0] * inv, dir[1] * inv, dir[2] * inv, Y);
     raw[0] = raw[1] = raw[2] = 0.f;
 #pragma unroll
     for (int k = 0; k < NB; ++k) {
-        raw[0] += Y[k] * coef[k * 3 + 0];
-        raw[1] += Y[k] * coef[k * 3 + 1];
-        raw[2] += Y[k] * coef[k * 3 + 2];
+        raw[0] += Y[k] * c[k * 3 + 0];
+        raw[1] += Y[k] * c[k * 3 + 1];
+        raw[2] += Y[k] * c[k * 3 + 2];
     }
 }
 
@@ -86,7 +110,7 @@ __global__ void __launch_bounds__(256) fused_packed_write_kernel(
     campos_of(vm, cp);
     const float dir[3] = {mean[0] - cp[0], mean[1] - cp[1], mean[2] - cp[2]};
     float raw[3];
-    sh_color<D>(f.sh + ((size_t)b * p.N + g) * f.K * 3, dir, raw);
+    sh_color<D>(f.sh + ((size_t)b * p.N + g) * f.K * 3, f.sh_vec, dir, raw);
     const float op = p.opacities[(size_t)b * p.N + g];
     batch_ids[pos] = b;
     camera_ids[pos] = c;
@@ -132,7 +156,7 @@ __global__ void __launch_bounds__(256) fused_dense_fwd_kernel(FusedParams f, int
             float cp[3];
             campos_of(vm, cp);
             const float dir[3] = {mean[0] - cp[0], mean[1] - cp[1], mean[2] - cp[2]};
-            sh_color<D>(coef, dir, raw);
+            sh_color<D>(coef, f.sh_vec, dir, raw);
         }
         radii[idx * 2] = o.valid ? o.rx : 0;
         radii[idx * 2 + 1] = o.valid ? o.ry : 0;
@@ -166,18 +190,21 @@ struct FusedBwdParams {
 constexpr int kFusedBwdThreads = 128;
 
 template <int D>
-__global__ void __launch_bounds__(kFusedBwdThreads) fused_bwd_kernel(FusedBwdParams q) {
+__global__ void __launch_bounds__(kFusedBwdThreads, 5) fused_bwd_kernel(FusedBwdParams q) {
     constexpr int NB = (D + 1) * (D + 1);
-    extern __shared__ float s_vsh[]; // [kFusedBwdThreads, K*3] staging for coalesced stores
+    // v_sh rows are accumulated in shared memory (row stride K*3 rounded up to an
+    // odd count, so the lanes of a warp hit distinct banks) and stored to HBM
+    // with coalesced writes at the end.
+    extern __shared__ float s_vsh[];
     const ProjParams &p = q.f.p;
     const uint32_t K3 = q.f.K * 3;
+    const uint32_t stride = K3 | 1u;
     const size_t first = (size_t)blockIdx.x * kFusedBwdThreads;
     const uint32_t tid = threadIdx.x;
     const size_t gi = first + tid; // flattened (b, g)
     const bool in_range = gi < (size_t)p.B * p.N;
-    float vsh[NB * 3];
-#pragma unroll
-    for (int k = 0; k < NB * 3; ++k) vsh[k] = 0.f;
+    float *vsh = s_vsh + (size_t)tid * stride;
+    for (uint32_t k = 0; k < K3; ++k) vsh[k] = 0.f;
     float v_mean[3] = {0.f, 0.f, 0.f}, v_op = 0.f;
     float v_q[4] = {0.f, 0.f, 0.f, 0.f}, v_s[3] = {0.f, 0.f, 0.f};
     if (in_range) {
@@ -291,16 +318,14 @@ __global__ void __launch_bounds__(kFusedBwdThreads) fused_bwd_kernel(FusedBwdPar
         q.v_scales[gi * 3 + 2] = v_s[2];
         q.v_opacities[gi] = v_op;
     }
-    // v_sh rows through shared memory so the [N, K, 3] stores are coalesced.
-    float *row = s_vsh + (size_t)tid * K3;
-#pragma unroll
-    for (int k = 0; k < NB * 3; ++k) row[k] = vsh[k];
-    for (uint32_t k = NB * 3; k < K3; ++k) row[k] = 0.f;
     __syncthreads();
     const size_t total = (size_t)p.B * p.N;
     const size_t count = (total - first) < kFusedBwdThreads ? (total - first) : kFusedBwdThreads;
     float *dst = q.v_sh + first * K3;
-    for (size_t i = tid; i < count * K3; i += kFusedBwdThreads) dst[i] = s_vsh[i];
+    for (size_t i = tid; i < count * K3; i += kFusedBwdThreads) {
+        const size_t r = i / K3;
+        dst[i] = s_vsh[r * stride + (i - r * K3)];
+    }
 }
 
 template <int D> static void launch_dense_fwd(const FusedParams &f, int32_t *radii, float *means2d,
@@ -325,7 +350,7 @@ static void launch_packed_write(const FusedParams &f, const uint32_t *vis, const
 
 template <int D> static void launch_bwd(const FusedBwdParams &q, cudaStream_t s) {
     const uint32_t n = q.f.p.B * q.f.p.N;
-    const size_t smem = (size_t)kFusedBwdThreads * q.f.K * 3 * sizeof(float);
+    const size_t smem = (size_t)kFusedBwdThreads * ((q.f.K * 3) | 1u) * sizeof(float);
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(fused_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     fused_bwd_kernel<D><<<(n + kFusedBwdThreads - 1) / kFusedBwdThreads, kFusedBwdThreads, smem, s>>>(q);
@@ -371,6 +396,7 @@ static FusedParams make_fused(int B, int C, int N, const float *means, const flo
     p.camera_model = camera_model;
     f.sh = sh;
     f.K = K;
+    f.sh_vec = (K * 3) % 4 == 0 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0;
     return f;
 }
 

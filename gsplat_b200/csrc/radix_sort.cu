@@ -7,12 +7,12 @@
 // reports which pair holds the result.
 //
 // Each pass over 8 bits is three launches:
-//   1. upsweep:   per-tile digit histograms (tile = 4096 keys), digit-major
+//   1. upsweep:   per-tile digit histograms (tile = 2048 keys), digit-major
 //   2. scan:      inclusive scan of the [256 x tiles] histogram (scan.cu)
 //   3. downsweep: stable in-tile ranking with warp match/popc, a local sort of
 //                 the tile in shared memory, then coalesced runs written out.
 // Ranking order inside a tile is (warp, round, lane) and each warp owns a
-// contiguous 512-key slice, so the pass is stable.
+// contiguous 256-key slice, so the pass is stable.
 #include "common.cuh"
 #include "gsb_internal.h"
 #include "gsb_scan.cuh"
@@ -21,7 +21,7 @@ namespace gsb {
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 16; // per lane
+constexpr int kSortItems = 8; // per lane
 constexpr int kSortTile = kSortThreads * kSortItems;
 constexpr int kWarpSlice = 32 * kSortItems;
 constexpr int kRadix = 256;

@@ -53,9 +53,11 @@ struct RasterParams {
     bool first_chunk;
 };
 
+// Staged splat: mean, opacity, conic and sig_max = ln(255 o), the largest sigma
+// at which alpha = o exp(-sigma) still reaches 1/255.
 struct __align__(16) SplatRec {
     float x, y, o, a;
-    float b, c, pad0, pad1;
+    float b, c, sig_max, pad1;
 };
 
 struct RasterSmem {
@@ -103,7 +105,7 @@ __device__ __forceinline__ void stage_splat(const RasterParams &p, const RasterS
     r.a = a;
     r.b = b;
     r.c = c;
-    r.pad0 = 0.f;
+    r.sig_max = o > 0.f ? __logf(o * 255.f) : -1.f;
     r.pad1 = 0.f;
     s.recs[i] = r;
     const float *cp = p.colors + (size_t)g * p.cstride + p.coff;
@@ -155,9 +157,15 @@ __device__ __forceinline__ bool box_hits(const float4 &bx, const WarpRect &r) {
 }
 
 // Shared per-pair evaluation: identical in forward and backward so both make the
-// same decisions.
+// same decisions. A pair contributes when sigma >= 0 and alpha = min(0.99,
+// o exp(-sigma)) >= 1/255 (reference RasterizeToPixels3DGSFwd.cu:170-176). The
+// cheap test sigma > sig_max = ln(255 o) rejects almost every non-contributing
+// pair before the exponential; it is equivalent to alpha < 1/255 up to the
+// rounding of the two transcendental evaluations, and the exact alpha test is
+// still applied to the pairs that pass it.
 struct PairEval {
     float dx, dy, sigma, vis, alpha;
+    bool keep;
 };
 
 __device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float py) {
@@ -165,16 +173,21 @@ __device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float
     e.dx = r.x - px;
     e.dy = r.y - py;
     e.sigma = 0.5f * (r.a * e.dx * e.dx + r.c * e.dy * e.dy) + r.b * e.dx * e.dy;
-    e.vis = __expf(-e.sigma);
-    e.alpha = fminf(kMaxAlpha, r.o * e.vis);
+    e.keep = e.sigma >= 0.f && e.sigma <= r.sig_max;
+    if (e.keep) {
+        e.vis = __expf(-e.sigma);
+        e.alpha = fminf(kMaxAlpha, r.o * e.vis);
+        e.keep = e.alpha >= kAlphaThreshold;
+    }
     return e;
 }
 
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
-template <int CDIM, int PPT>
+template <int CDIM, int BX, int BY>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
+    constexpr int PPT = BX * BY;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int nwarps = blockDim.x >> 5;
     const RasterSmem s = carve<CDIM>(smem_raw);
@@ -182,7 +195,6 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     const uint32_t tile = blockIdx.x;
     const uint32_t tx0 = (tile % p.tile_w) * p.tile_size, ty0 = (tile / p.tile_w) * p.tile_size;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t tpix = p.tile_size * p.tile_size;
 
     float px[PPT], py[PPT], T[PPT], out[PPT][CDIM];
     int32_t cur[PPT], npairs[PPT];
@@ -192,9 +204,11 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
-        const uint32_t q = threadIdx.x * PPT + k;
-        const uint32_t i = ty0 + q / p.tile_size, j = tx0 + q % p.tile_size;
-        inside[k] = q < tpix && i < p.H && j < p.W;
+        // thread owns a BX x BY block of pixels; blocks are laid out row-major
+        const uint32_t tpr = p.tile_size / BX;
+        const uint32_t ly = (threadIdx.x / tpr) * BY + k / BX, lx = (threadIdx.x % tpr) * BX + k % BX;
+        const uint32_t i = ty0 + ly, j = tx0 + lx;
+        inside[k] = ly < p.tile_size && i < p.H && j < p.W;
         px[k] = (float)j + 0.5f;
         py[k] = (float)i + 0.5f;
         pid[k] = i * p.W + j;
@@ -256,7 +270,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
                 for (int k = 0; k < PPT; ++k) {
                     if (done[k]) continue;
                     const PairEval e = eval_pair(r, px[k], py[k]);
-                    if (e.sigma < 0.f || e.alpha < kAlphaThreshold) continue;
+                    if (!e.keep) continue;
                     const float next_T = T[k] * (1.f - e.alpha);
                     if (next_T <= kTransmittanceThreshold) {
                         done[k] = true;
@@ -380,8 +394,13 @@ __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, float *
         }
     }
 }
-template <int CDIM, int PPT>
-__global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
+#ifndef GSB_BWD_MINB
+#define GSB_BWD_MINB 10
+#endif
+template <int CDIM, int BX, int BY>
+__global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB : 1))
+    raster_bwd_kernel(RasterParams p) {
+    constexpr int PPT = BX * BY;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const RasterSmem s = carve<CDIM>(smem_raw);
     const uint32_t image = blockIdx.y;
@@ -390,7 +409,6 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
     if (p.masks != nullptr && !p.masks[tile_flat]) return;
     const uint32_t tx0 = (tile % p.tile_w) * p.tile_size, ty0 = (tile / p.tile_w) * p.tile_size;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t tpix = p.tile_size * p.tile_size;
     const size_t img_pix = (size_t)image * p.H * p.W;
     const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
 
@@ -402,9 +420,11 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
     float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
-        const uint32_t q = threadIdx.x * PPT + k;
-        const uint32_t i = ty0 + q / p.tile_size, j = tx0 + q % p.tile_size;
-        inside[k] = q < tpix && i < p.H && j < p.W;
+        // thread owns a BX x BY block of pixels; blocks are laid out row-major
+        const uint32_t tpr = p.tile_size / BX;
+        const uint32_t ly = (threadIdx.x / tpr) * BY + k / BX, lx = (threadIdx.x % tpr) * BX + k % BX;
+        const uint32_t i = ty0 + ly, j = tx0 + lx;
+        inside[k] = ly < p.tile_size && i < p.H && j < p.W;
         px[k] = (float)j + 0.5f;
         py[k] = (float)i + 0.5f;
         const size_t pix = img_pix + (inside[k] ? i * p.W + j : 0);
@@ -466,20 +486,20 @@ __global__ void __launch_bounds__(256) raster_bwd_kernel(RasterParams p) {
         for (int li = 0; li < cnt; ++li) {
             const int i = mylist[li];
             const int32_t gidx = bend - i;
-            const SplatRec r = s.recs[i];
-            float col[CDIM];
-#pragma unroll
-            for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
             constexpr int NV = CDIM + 8;
             float acc[NV];
 #pragma unroll
             for (int j = 0; j < NV; ++j) acc[j] = 0.f;
             bool any = false;
+            const SplatRec r = s.recs[i];
+            float col[CDIM];
+#pragma unroll
+            for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
                 if (!inside[k] || gidx > bin_final[k]) continue;
                 const PairEval e = eval_pair(r, px[k], py[k]);
-                if (e.sigma < 0.f || e.alpha < kAlphaThreshold) continue;
+                if (!e.keep) continue;
                 any = true;
                 const float ra = 1.f / fmaxf(kMinOneMinusAlpha, 1.f - e.alpha);
                 T[k] *= ra;
@@ -524,46 +544,53 @@ static int threads_for(uint32_t tile_size, int ppt) {
     return (int)t;
 }
 
-template <int CDIM>
-static int launch_fwd(const RasterParams &p, cudaStream_t stream) {
-    const int ppt = 1;
-    const int nt = threads_for(p.tile_size, ppt);
+template <int CDIM, int BX, int BY>
+static int launch_variant(bool fwd, const RasterParams &p, cudaStream_t stream) {
+    const int nt = threads_for(p.tile_size, BX * BY);
     if (nt > 256) return set_error(kErrUnsupported, "tile_size %u too large", p.tile_size);
     const size_t smem = raster_smem_bytes<CDIM>(nt / 32);
-    auto kern = raster_fwd_kernel<CDIM, 1>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     dim3 grid(p.tile_w * p.tile_h, p.I);
+    if (fwd) {
+        auto kern = raster_fwd_kernel<CDIM, BX, BY>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, nt, smem, stream>>>(p);
+        return check_launch("raster_fwd_kernel");
+    }
+    auto kern = raster_bwd_kernel<CDIM, BX, BY>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<grid, nt, smem, stream>>>(p);
-    return check_launch("raster_fwd_kernel");
+    return check_launch("raster_bwd_kernel");
 }
 
-// Pixels per backward thread: enough to amortise the warp reduction, few enough
-// that the per-pixel state (transmittance, colour buffer, upstream gradient)
-// stays in registers.
-#ifdef GSB_BWD_PPT
-template <int CDIM> constexpr int bwd_ppt() { return CDIM <= 4 ? GSB_BWD_PPT : (CDIM <= 8 ? 2 : 1); }
-#else
-template <int CDIM> constexpr int bwd_ppt() { return CDIM <= 4 ? 4 : (CDIM <= 8 ? 2 : 1); }
+// Pixel blocks per thread (BX x BY). Backward: enough pixels per thread to
+// amortise the warp reduction, few enough that the per-pixel state
+// (transmittance, colour buffer, upstream gradient) stays in registers. Both
+// need the tile size to be a multiple of the block; other tile sizes use 1x1.
+#ifndef GSB_FWD_BX
+#define GSB_FWD_BX 2
+#define GSB_FWD_BY 1
+#endif
+#ifndef GSB_BWD_BX
+#define GSB_BWD_BX 4
+#define GSB_BWD_BY 1
 #endif
 
 template <int CDIM>
+static int launch_fwd(const RasterParams &p, cudaStream_t stream) {
+    constexpr int BX = GSB_FWD_BX, BY = GSB_FWD_BY;
+    if (p.tile_size % BX == 0 && p.tile_size % BY == 0 && p.tile_size >= 8)
+        return launch_variant<CDIM, BX, BY>(true, p, stream);
+    return launch_variant<CDIM, 1, 1>(true, p, stream);
+}
+
+template <int CDIM>
 static int launch_bwd(const RasterParams &p, cudaStream_t stream) {
-    constexpr int kPPT = bwd_ppt<CDIM>();
-    const bool multi = p.tile_size % kPPT == 0 && p.tile_size >= 8;
-    const int nt = threads_for(p.tile_size, multi ? kPPT : 1);
-    if (nt > 256) return set_error(kErrUnsupported, "tile_size %u too large", p.tile_size);
-    const size_t smem = raster_smem_bytes<CDIM>(nt / 32);
-    dim3 grid(p.tile_w * p.tile_h, p.I);
-    if (multi) {
-        auto kern = raster_bwd_kernel<CDIM, kPPT>;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, nt, smem, stream>>>(p);
-    } else {
-        auto kern = raster_bwd_kernel<CDIM, 1>;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, nt, smem, stream>>>(p);
-    }
-    return check_launch("raster_bwd_kernel");
+    constexpr int BX = CDIM <= 4 ? GSB_BWD_BX : (CDIM <= 8 ? 2 : 1);
+    constexpr int BY = CDIM <= 4 ? GSB_BWD_BY : 1;
+    static_assert(BX * BY <= 8, "pixels per thread");
+    if (p.tile_size % BX == 0 && p.tile_size % BY == 0 && p.tile_size >= 8)
+        return launch_variant<CDIM, BX, BY>(false, p, stream);
+    return launch_variant<CDIM, 1, 1>(false, p, stream);
 }
 
 template <bool FWD> static int dispatch(int cdim, const RasterParams &p, cudaStream_t s) {
