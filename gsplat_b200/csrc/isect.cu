@@ -12,6 +12,7 @@
 // portable logarithm accurate to ~1 ulp, as documented in detmath.h.
 #include "common.cuh"
 #include "gsb_internal.h"
+#include "gsb_scan.cuh"
 
 namespace gsb {
 
@@ -68,9 +69,9 @@ __device__ __forceinline__ LinePair ellipse_line(float A, float B, float C, floa
 
 // AccuTile sweep (IntersectTile.cu:54-126 and 195-253). Returns the number of
 // tiles; emits them when `sink` is non-null.
-template <bool EMIT>
+template <bool EMIT, class Sink>
 __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, float B, float C,
-                             float opacity, EmitSink *sink) {
+                             float opacity, Sink *sink) {
     const float disc = DET_SUB(DET_MUL(B, B), DET_MUL(A, C));
     const float t = det_fmin(kGaussianExtend * kGaussianExtend,
                              DET_MUL(2.0f, det_logf(DET_DIV(opacity, kAlphaThreshold))));
@@ -129,9 +130,9 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
     return count;
 }
 
-template <bool EMIT>
+template <bool EMIT, class Sink>
 __device__ uint32_t aabb_tiles(const IsectParams &p, float mx, float my, int32_t rx, int32_t ry,
-                               EmitSink *sink) {
+                               Sink *sink) {
     const float ts = (float)p.tile_size;
     const float trx = DET_DIV((float)rx, ts), try_ = DET_DIV((float)ry, ts);
     const float tx = DET_DIV(mx, ts), ty = DET_DIV(my, ts);
@@ -147,23 +148,23 @@ __device__ uint32_t aabb_tiles(const IsectParams &p, float mx, float my, int32_t
     return (uint32_t)((y1 - y0) * (x1 - x0));
 }
 
-template <bool EMIT>
-__device__ __forceinline__ uint32_t splat_tiles(const IsectParams &p, uint32_t idx, EmitSink *sink) {
+template <bool EMIT, class Sink = EmitSink>
+__device__ __forceinline__ uint32_t splat_tiles(const IsectParams &p, uint32_t idx, Sink *sink) {
     const int32_t rx = p.radii[(size_t)idx * 2], ry = p.radii[(size_t)idx * 2 + 1];
     if (rx <= 0 || ry <= 0) return 0;
     const float mx = p.means2d[(size_t)idx * 2], my = p.means2d[(size_t)idx * 2 + 1];
     if (p.conics != nullptr && p.opacities != nullptr) {
-        return accutile<EMIT>(p, mx, my, p.conics[(size_t)idx * 3], p.conics[(size_t)idx * 3 + 1],
-                              p.conics[(size_t)idx * 3 + 2], p.opacities[idx], sink);
+        return accutile<EMIT, Sink>(p, mx, my, p.conics[(size_t)idx * 3], p.conics[(size_t)idx * 3 + 1],
+                                    p.conics[(size_t)idx * 3 + 2], p.opacities[idx], sink);
     }
-    return aabb_tiles<EMIT>(p, mx, my, rx, ry, sink);
+    return aabb_tiles<EMIT, Sink>(p, mx, my, rx, ry, sink);
 }
 
 __global__ void __launch_bounds__(256) isect_count_kernel(IsectParams p, int32_t *tiles_per_gauss) {
     const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t n = p.packed ? p.nnz : p.I * p.N;
     if (idx >= n) return;
-    tiles_per_gauss[idx] = (int32_t)splat_tiles<false>(p, idx, nullptr);
+    tiles_per_gauss[idx] = (int32_t)splat_tiles<false, EmitSink>(p, idx, nullptr);
 }
 
 __global__ void __launch_bounds__(256) isect_emit_kernel(IsectParams p, const int64_t *cum_tiles,
@@ -213,6 +214,336 @@ __global__ void __launch_bounds__(256) isect_offsets_kernel(const int64_t *__res
 __global__ void fill_i32_kernel(int32_t *p, uint32_t n, int32_t v) {
     const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
     if (k < n) p[k] = v;
+}
+
+// ---------------------------------------------------------------------------
+// Tile-bucket pipeline for the sorted intersection list.
+//
+// The reference sorts all keys with one global stable radix sort
+// (Intersect.cpp:140-170, cub::DeviceRadixSort::SortPairs). Inside one
+// (image, tile) bucket the keys differ only in their depth bits, and the emit
+// order of a bucket's entries is by increasing splat index (every splat emits a
+// given tile at most once, and splats emit in index order). A stable sort by
+// depth inside a bucket is therefore the same as a sort by the unique pair
+// (depth bits, splat index). The pipeline:
+//   1. count: every splat's tile count, and per bucket the entries of each
+//      "shard" of splats (below);
+//   2. offsets: exclusive scan over (bucket, shard) in bucket-major order,
+//      giving each shard's first slot and each bucket's start -- exactly the
+//      offsets array of isect_offset_encode -- and the largest bucket;
+//   3. emit: every entry (depth bits, splat index) goes to the next free slot
+//      of its (bucket, shard), in arbitrary order inside the shard;
+//   4. sort: each bucket is sorted on chip by (depth bits, splat index), and
+//      the final 64-bit keys and flatten ids are written.
+// The output is bit-identical to the global stable sort of the emitted keys.
+//
+// Shards. With few buckets (the usual case: one image has a few thousand
+// tiles) the splats are cut into G contiguous ranges, one per CTA, and each CTA
+// counts and places its entries through a histogram / cursor array of all
+// buckets in its shared memory: no global atomics. With more buckets than fit
+// in shared memory, 16 shards per bucket live in global memory and splat idx
+// uses shard idx % 16, so that the hottest buckets do not serialise their
+// atomics on one address.
+// ---------------------------------------------------------------------------
+constexpr int kBucketShards = GSB_ISECT_BUCKET_SHARDS; // global-memory path
+static_assert((kBucketShards & (kBucketShards - 1)) == 0, "shards: power of two");
+constexpr uint32_t kCtaBucketMax = 24576; // buckets of the shared-memory path (96 KiB)
+#ifndef GSB_CTA_THREADS
+#define GSB_CTA_THREADS 1024
+#define GSB_CTAS_PER_SM 1
+#endif
+constexpr int kCtaThreads = GSB_CTA_THREADS;
+
+struct BucketPlan {
+    bool cta;       // shared-memory histograms, one CTA per contiguous splat range
+    uint32_t shards; // counters per bucket: G CTAs, or kBucketShards
+};
+
+static BucketPlan bucket_plan(uint64_t n_buckets, int num_sms) {
+    BucketPlan pl;
+    pl.cta = n_buckets > 0 && n_buckets <= kCtaBucketMax;
+    if (!pl.cta) {
+        pl.shards = kBucketShards;
+        return pl;
+    }
+    // one 1024-thread CTA per SM, fewer when the (bucket x CTA) counter matrix would pass
+    // ~4M entries
+    uint64_t g = (uint64_t)GSB_CTAS_PER_SM * (uint64_t)(num_sms > 0 ? num_sms : 148);
+    const uint64_t cap = (4ull << 20) / n_buckets;
+    if (g > cap) g = cap < 32 ? 32 : cap;
+    pl.shards = (uint32_t)g;
+    return pl;
+}
+
+static int device_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+    return sms;
+}
+
+struct CountSink {
+    int32_t *counts; // [I * n_tiles * kBucketShards]
+    int64_t base;    // image * n_tiles
+    int32_t shard;
+    __device__ __forceinline__ void put(int64_t tile_id) {
+        atomicAdd(counts + (base + tile_id) * kBucketShards + shard, 1);
+    }
+};
+
+struct SmemCountSink {
+    int32_t *hist; // shared memory, one counter per bucket
+    int64_t base;
+    __device__ __forceinline__ void put(int64_t tile_id) { atomicAdd(hist + base + tile_id, 1); }
+};
+
+// Places one entry at the slot returned by an atomic increment of its cursor
+// (global or shared memory). The bound keeps the slot inside the arrays.
+struct BucketSink {
+    uint32_t *depth_out;
+    int32_t *id_out;
+    int32_t *cursor;
+    int64_t base;   // first cursor of the splat's image
+    int32_t stride; // cursors per bucket in `cursor`
+    int32_t shard;
+    uint32_t limit; // n_isects
+    uint32_t depth_bits;
+    int32_t flat_id;
+    __device__ __forceinline__ void put(int64_t tile_id) {
+        const uint32_t pos = (uint32_t)atomicAdd(cursor + (base + tile_id) * stride + shard, 1);
+        if (pos < limit) {
+            depth_out[pos] = depth_bits;
+            id_out[pos] = flat_id;
+        }
+    }
+};
+
+__device__ __forceinline__ int64_t splat_image(const IsectParams &p, uint32_t idx) {
+    return p.packed ? p.image_ids[idx] : (int64_t)(idx / p.N);
+}
+
+__device__ __forceinline__ uint32_t n_splats(const IsectParams &p) { return p.packed ? p.nnz : p.I * p.N; }
+
+// global-memory shards
+__global__ void __launch_bounds__(256) isect_count_tiles_kernel(IsectParams p, int32_t *tiles_per_gauss,
+                                                                int32_t *shard_counts) {
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_splats(p)) return;
+    CountSink sink;
+    sink.counts = shard_counts;
+    sink.base = splat_image(p, idx) * (int64_t)p.tile_width * p.tile_height;
+    sink.shard = (int32_t)(idx & (kBucketShards - 1));
+    tiles_per_gauss[idx] = (int32_t)splat_tiles<true, CountSink>(p, idx, &sink);
+}
+
+// shared-memory shards: CTA c counts splats [c chunk, (c + 1) chunk) and writes
+// its histogram to column c of the bucket-major (bucket x G) matrix
+__global__ void __launch_bounds__(kCtaThreads) isect_count_cta_kernel(IsectParams p, uint32_t n_buckets,
+                                                                      int32_t *tiles_per_gauss,
+                                                                      int32_t *matrix) {
+    extern __shared__ int32_t hist[];
+    for (uint32_t b = threadIdx.x; b < n_buckets; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    const uint32_t n = n_splats(p), G = gridDim.x;
+    const uint32_t chunk = (n + G - 1) / G;
+    const uint32_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    const int64_t n_tiles = (int64_t)p.tile_width * p.tile_height;
+    for (uint32_t idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
+        SmemCountSink sink;
+        sink.hist = hist;
+        sink.base = splat_image(p, idx) * n_tiles;
+        tiles_per_gauss[idx] = (int32_t)splat_tiles<true, SmemCountSink>(p, idx, &sink);
+    }
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < n_buckets; b += blockDim.x) matrix[(size_t)b * G + blockIdx.x] = hist[b];
+}
+
+// cursor[k] = first slot of (bucket, shard) k = exclusive scan of the counts
+__global__ void __launch_bounds__(256) shard_bases_kernel(const int64_t *__restrict__ incl, uint32_t n,
+                                                          int32_t *__restrict__ cursor) {
+    const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k < n) cursor[k] = k == 0 ? 0 : (int32_t)incl[k - 1];
+}
+
+// Bucket b occupies [incl[b S - 1], incl[b S + S - 1]).
+// totals[0] = number of entries (-1 when it does not fit int32, like every
+// offset here), totals[1] = largest bucket.
+__global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__restrict__ incl, uint32_t n_buckets,
+                                                            uint32_t shards, int32_t *__restrict__ starts,
+                                                            int32_t *__restrict__ sizes, int32_t *totals) {
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    int32_t c = 0;
+    if (b < n_buckets) {
+        const size_t s0 = (size_t)b * shards;
+        const int64_t first = s0 == 0 ? 0 : incl[s0 - 1];
+        starts[b] = (int32_t)first;
+        c = (int32_t)(incl[s0 + shards - 1] - first);
+        sizes[b] = c;
+    }
+    if (b == n_buckets - 1) {
+        const int64_t total = incl[(size_t)n_buckets * shards - 1];
+        totals[0] = total > 0x7fffffffll ? -1 : (int32_t)total;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c = max(c, __shfl_xor_sync(0xffffffffu, c, o));
+    if ((threadIdx.x & 31) == 0 && c > 0) atomicMax(totals + 1, c);
+}
+
+__global__ void __launch_bounds__(256) isect_bucket_emit_kernel(IsectParams p, uint32_t n_isects,
+                                                                int32_t *cursor, uint32_t *depth_out,
+                                                                int32_t *id_out) {
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_splats(p)) return;
+    BucketSink sink;
+    sink.depth_out = depth_out;
+    sink.id_out = id_out;
+    sink.cursor = cursor;
+    sink.base = splat_image(p, idx) * (int64_t)p.tile_width * p.tile_height;
+    sink.stride = kBucketShards;
+    sink.shard = (int32_t)(idx & (kBucketShards - 1));
+    sink.limit = n_isects;
+    sink.depth_bits = det_f2u(p.depths[idx]);
+    sink.flat_id = (int32_t)idx;
+    splat_tiles<true, BucketSink>(p, idx, &sink);
+}
+
+__global__ void __launch_bounds__(kCtaThreads) isect_emit_cta_kernel(IsectParams p, uint32_t n_buckets,
+                                                                     uint32_t n_isects, const int32_t *cursor,
+                                                                     uint32_t *depth_out, int32_t *id_out) {
+    extern __shared__ int32_t cur[];
+    const uint32_t n = n_splats(p), G = gridDim.x;
+    for (uint32_t b = threadIdx.x; b < n_buckets; b += blockDim.x) cur[b] = cursor[(size_t)b * G + blockIdx.x];
+    __syncthreads();
+    const uint32_t chunk = (n + G - 1) / G;
+    const uint32_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    const int64_t n_tiles = (int64_t)p.tile_width * p.tile_height;
+    for (uint32_t idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
+        BucketSink sink;
+        sink.depth_out = depth_out;
+        sink.id_out = id_out;
+        sink.cursor = cur;
+        sink.base = splat_image(p, idx) * n_tiles;
+        sink.stride = 1;
+        sink.shard = 0;
+        sink.limit = n_isects;
+        sink.depth_bits = det_f2u(p.depths[idx]);
+        sink.flat_id = (int32_t)idx;
+        splat_tiles<true, BucketSink>(p, idx, &sink);
+    }
+}
+
+constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (128 KiB of shared memory)
+
+
+// Bitonic compare-exchange of entries held in registers. Entry index i =
+// threadIdx.x * E + e (blocked: thread t owns E consecutive entries); the
+// network stage (k, j) pairs i with i ^ j, ascending where (i & k) == 0.
+//   j <  E       : both entries are in the same thread (register exchange);
+//   j <  32 E    : the partner is lane ^ (j / E) of the same warp (shuffle);
+//   j >= 32 E    : the partner is in another warp; these stages run on the
+//                  shared-memory copy between two block barriers.
+template <int E> struct BitonicRegs {
+    uint64_t v[E];
+
+    template <int J> __device__ __forceinline__ void reg_stage(uint32_t base, uint32_t k) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            if (e & J) continue;
+            const uint64_t a = v[e], b = v[e + J];
+            const bool asc = ((base + e) & k) == 0;
+            const bool swap = (a > b) == asc;
+            v[e] = swap ? b : a;
+            v[e + J] = swap ? a : b;
+        }
+    }
+
+    __device__ __forceinline__ void shfl_stage(uint32_t base, uint32_t k, uint32_t j) {
+        const int lane_mask = (int)(j / E);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const uint64_t other = __shfl_xor_sync(0xffffffffu, v[e], lane_mask);
+            const uint32_t i = base + e;
+            const bool keep_min = (((i & j) == 0) == ((i & k) == 0));
+            const bool other_smaller = other < v[e];
+            v[e] = (other_smaller == keep_min) ? other : v[e];
+        }
+    }
+};
+
+// One CTA per bucket: entries packed as (depth bits << 32 | splat index),
+// padded with all-ones to a power of two, sorted ascending.
+template <int E>
+__global__ void __launch_bounds__(1024)
+    bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
+                       const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
+                       uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
+                       int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
+    extern __shared__ __align__(16) uint64_t sk[];
+    const uint32_t b = blockIdx.x;
+    const int n = sizes[b];
+    if (n <= lo_size || n > hi_size) return; // another size class
+    const int start = starts[b];
+    const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
+    if (n == 1) {
+        if (threadIdx.x == 0) {
+            keys_out[start] = hi | (int64_t)depth_in[start];
+            ids_out[start] = id_in[start];
+        }
+        return;
+    }
+    uint32_t npad = 2;
+    while (npad < (uint32_t)n) npad <<= 1;
+    const uint32_t base = threadIdx.x * E;
+    BitonicRegs<E> r;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const uint32_t i = base + e;
+        r.v[e] = i < (uint32_t)n ? ((uint64_t)depth_in[start + i] << 32) | (uint32_t)id_in[start + i] : ~0ull;
+    }
+    const uint32_t nthreads = blockDim.x;
+    // warps whose entries all lie beyond npad (a bucket smaller than the largest)
+    // hold padding only; they join the block barriers and nothing else
+    const bool warp_active = (threadIdx.x & ~31u) * E < npad;
+    for (uint32_t k = 2; k <= npad; k <<= 1) {
+        uint32_t j = k >> 1;
+        if (j >= 32u * E) {
+            // cross-warp stages through shared memory
+#pragma unroll
+            for (int e = 0; e < E; ++e) sk[base + e] = r.v[e];
+            __syncthreads();
+            for (; j >= 32u * E; j >>= 1) {
+                uint32_t lj = 31 - __clz(j);
+                for (uint32_t q = threadIdx.x; q < npad / 2; q += nthreads) {
+                    const uint32_t i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
+                    const uint64_t a = sk[i], c = sk[i + j];
+                    const bool asc = (i & k) == 0;
+                    if ((a > c) == asc) {
+                        sk[i] = c;
+                        sk[i + j] = a;
+                    }
+                }
+                __syncthreads();
+            }
+#pragma unroll
+            for (int e = 0; e < E; ++e) r.v[e] = sk[base + e];
+            __syncthreads(); // the copy is reused by the next k
+        }
+        if (!warp_active) continue; // only padding: nothing to exchange
+        for (; j >= (uint32_t)E; j >>= 1) r.shfl_stage(base, k, j);
+        // j = min(k / 2, E / 2): the in-thread stages, unrolled with constant distances
+        if (E >= 16 && j >= 8) r.template reg_stage<(E >= 16 ? 8 : 1)>(base, k);
+        if (E >= 8 && j >= 4) r.template reg_stage<(E >= 8 ? 4 : 1)>(base, k);
+        if (j >= 2) r.template reg_stage<2>(base, k);
+        r.template reg_stage<1>(base, k);
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const uint32_t i = base + e;
+        if (i < (uint32_t)n) {
+            keys_out[start + i] = hi | (int64_t)(r.v[e] >> 32);
+            ids_out[start + i] = (int32_t)(uint32_t)r.v[e];
+        }
+    }
 }
 
 static uint32_t bit_length(uint64_t v) {
@@ -311,4 +642,144 @@ extern "C" int gsb_isect_offset_encode(const int64_t *isect_ids, long long n_ise
     isect_offsets_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
         isect_ids, (uint32_t)n_isects, n_tiles, bit_length(n_tiles), (uint32_t)total, offsets);
     return check_launch("isect_offsets_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Tile-bucket pipeline entry points
+// ---------------------------------------------------------------------------
+extern "C" int gsb_isect_bucket_shards(int I, int tile_width, int tile_height) {
+    if (I <= 0 || tile_width <= 0 || tile_height <= 0) return kBucketShards;
+    return (int)bucket_plan((uint64_t)I * tile_width * tile_height, device_sms()).shards;
+}
+
+static int set_cta_smem(const void *kern, size_t smem) {
+    if (smem <= 48 * 1024) return kOk;
+    cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce));
+    return kOk;
+}
+
+extern "C" int gsb_isect_count_tiles(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                                     const float *means2d, const int32_t *radii, const float *depths,
+                                     const float *conics, const float *opacities, int tile_size,
+                                     int tile_width, int tile_height, int32_t *tiles_per_gauss,
+                                     int32_t *shard_counts, cudaStream_t stream) {
+    IsectParams p;
+    if (int e = make_isect_params(p, packed, I, N, nnz, image_ids, means2d, radii, depths, conics,
+                                  opacities, tile_size, tile_width, tile_height))
+        return e;
+    const uint64_t n_buckets = (uint64_t)I * tile_width * tile_height;
+    const size_t n = packed ? (size_t)nnz : (size_t)I * N;
+    if (n > 0x7fffffffu) return set_error(kErrInvalidArgument, "too many splats: %zu", n);
+    const BucketPlan pl = bucket_plan(n_buckets, device_sms());
+    if (pl.cta) {
+        // every matrix entry is written, also with no splats
+        const size_t smem = n_buckets * sizeof(int32_t);
+        if (int e = set_cta_smem((const void *)isect_count_cta_kernel, smem)) return e;
+        isect_count_cta_kernel<<<pl.shards, kCtaThreads, smem, stream>>>(p, (uint32_t)n_buckets,
+                                                                         tiles_per_gauss, shard_counts);
+        return check_launch("isect_count_cta_kernel");
+    }
+    if (n_buckets > 0) {
+        cudaError_t ce = cudaMemsetAsync(shard_counts, 0, n_buckets * kBucketShards * sizeof(int32_t), stream);
+        if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
+    }
+    if (n == 0) return kOk;
+    isect_count_tiles_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(p, tiles_per_gauss,
+                                                                              shard_counts);
+    return check_launch("isect_count_tiles_kernel");
+}
+
+extern "C" size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, int shards) {
+    const size_t n = (n_buckets > 0 ? (size_t)n_buckets : 1) * (size_t)(shards > 0 ? shards : 1);
+    return ((n * sizeof(int64_t) + 255) / 256) * 256 + scan_scratch_bytes(n);
+}
+
+extern "C" int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
+                                        int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
+                                        int32_t *totals, void *scratch, size_t scratch_bytes,
+                                        cudaStream_t stream) {
+    if (shards <= 0 || n_buckets < 0 || n_buckets > 0x7fffffffll / shards)
+        return set_error(kErrInvalidArgument, "bad bucket count %lld x %d shards", n_buckets, shards);
+    cudaError_t ce = cudaMemsetAsync(totals, 0, 2 * sizeof(int32_t), stream);
+    if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
+    if (n_buckets == 0) return kOk;
+    if (scratch_bytes < gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards))
+        return set_error(kErrInvalidArgument, "bucket offsets scratch too small");
+    const size_t n_shards = (size_t)n_buckets * shards;
+    int64_t *incl = static_cast<int64_t *>(scratch);
+    const size_t incl_bytes = ((n_shards * sizeof(int64_t) + 255) / 256) * 256;
+    void *scan_scratch = static_cast<char *>(scratch) + incl_bytes;
+    if (int e = inclusive_scan_i32_i64(shard_counts, incl, n_shards, scan_scratch, scratch_bytes - incl_bytes,
+                                       stream))
+        return e;
+    shard_bases_kernel<<<(unsigned)((n_shards + 255) / 256), 256, 0, stream>>>(incl, (uint32_t)n_shards, cursor);
+    bucket_starts_kernel<<<(unsigned)((n_buckets + 255) / 256), 256, 0, stream>>>(
+        incl, (uint32_t)n_buckets, (uint32_t)shards, offsets, bucket_sizes, totals);
+    return check_launch("bucket_starts_kernel");
+}
+
+extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                                     const float *means2d, const int32_t *radii, const float *depths,
+                                     const float *conics, const float *opacities, int tile_size,
+                                     int tile_width, int tile_height, long long n_isects, int32_t *cursor,
+                                     uint32_t *bucket_depths, int32_t *bucket_ids, cudaStream_t stream) {
+    IsectParams p;
+    if (int e = make_isect_params(p, packed, I, N, nnz, image_ids, means2d, radii, depths, conics,
+                                  opacities, tile_size, tile_width, tile_height))
+        return e;
+    if (n_isects < 0 || n_isects > 0x7fffffffll)
+        return set_error(kErrInvalidArgument, "bad intersection count %lld", n_isects);
+    const size_t n = packed ? (size_t)nnz : (size_t)I * N;
+    if (n == 0 || n_isects == 0) return kOk;
+    const uint64_t n_buckets = (uint64_t)I * tile_width * tile_height;
+    const BucketPlan pl = bucket_plan(n_buckets, device_sms());
+    if (pl.cta) {
+        const size_t smem = n_buckets * sizeof(int32_t);
+        if (int e = set_cta_smem((const void *)isect_emit_cta_kernel, smem)) return e;
+        isect_emit_cta_kernel<<<pl.shards, kCtaThreads, smem, stream>>>(
+            p, (uint32_t)n_buckets, (uint32_t)n_isects, cursor, bucket_depths, bucket_ids);
+        return check_launch("isect_emit_cta_kernel");
+    }
+    isect_bucket_emit_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        p, (uint32_t)n_isects, cursor, bucket_depths, bucket_ids);
+    return check_launch("isect_bucket_emit_kernel");
+}
+
+extern "C" int gsb_isect_bucket_sort_max(void) { return kBucketSortMax; }
+
+extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
+                                     const int32_t *bucket_sizes, int max_count,
+                                     const uint32_t *bucket_depths, const int32_t *bucket_ids,
+                                     int64_t *isect_ids, int32_t *flatten_ids, cudaStream_t stream) {
+    const uint64_t n_tiles = (uint64_t)tile_width * (uint64_t)tile_height;
+    const uint64_t n_buckets = (uint64_t)I * n_tiles;
+    if (max_count > kBucketSortMax)
+        return set_error(kErrUnsupported, "bucket of %d entries exceeds the on-chip sort (%d)", max_count,
+                         kBucketSortMax);
+    if (n_buckets == 0 || max_count <= 0) return kOk;
+    if (n_buckets > 0x7fffffffull) return set_error(kErrInvalidArgument, "too many buckets");
+    const uint32_t tb = bit_length(n_tiles);
+    const unsigned grid = (unsigned)n_buckets;
+    // size classes (0, 1024], (1024, 4096], (4096, 16384], one launch each, sized
+    // for the largest bucket of the class; a CTA whose bucket is in another
+    // class returns at once
+    int lo = 0;
+    for (int hi : {1024, 4096, kBucketSortMax}) {
+        if (max_count > lo) {
+            const int cap = hi < max_count ? hi : max_count;
+            int npad = 2;
+            while (npad < cap) npad <<= 1;
+            const int E = hi <= 4096 ? 4 : 16;
+            const int threads = npad / E < 32 ? 32 : npad / E;
+            const size_t smem = (size_t)threads * E * sizeof(uint64_t);
+            auto kern = E == 4 ? bucket_sort_kernel<4> : bucket_sort_kernel<16>;
+            if (int e = set_cta_smem((const void *)kern, smem)) return e;
+            kern<<<grid, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
+                                                  (uint32_t)n_tiles, tb, lo, hi, isect_ids, flatten_ids);
+            if (int e = check_launch("bucket_sort_kernel")) return e;
+        }
+        lo = hi;
+    }
+    return kOk;
 }

@@ -427,8 +427,37 @@ def isect_tiles(
     Returns (tiles_per_gauss int32, isect_ids int64 [n_isects], flatten_ids int32
     [n_isects]); with ``sort`` the pairs are ordered exactly like a stable sort of
     isect_ids. ``segmented`` gives the same result (the keys of each image are
-    already contiguous), so the single global sort is used for both.
+    already contiguous), so one code path serves both.
     """
+    if packed:
+        assert gaussian_ids is not None, "gaussian_ids is required if packed is True"
+    tiles_per_gauss, isect_ids, flatten_ids, _ = _isect_tiles(
+        means2d, radii, depths, tile_size, tile_width, tile_height, sort, packed, n_images, image_ids,
+        conics, opacities)
+    return tiles_per_gauss, isect_ids, flatten_ids
+
+
+@torch.no_grad()
+def isect_tiles_with_offsets(means2d, radii, depths, tile_size, tile_width, tile_height, packed=False,
+                             n_images=None, image_ids=None, gaussian_ids=None, conics=None, opacities=None):
+    """isect_tiles(sort=True) followed by isect_offset_encode, as used by
+    rasterization(): returns (tiles_per_gauss, isect_ids, flatten_ids, offsets
+    [I, th, tw]). The tile-bucket sort produces the offsets on the way."""
+    if packed:
+        assert gaussian_ids is not None, "gaussian_ids is required if packed is True"
+    tiles_per_gauss, isect_ids, flatten_ids, offsets = _isect_tiles(
+        means2d, radii, depths, tile_size, tile_width, tile_height, True, packed, n_images, image_ids,
+        conics, opacities)
+    I = n_images if packed else math.prod(means2d.shape[:-2])
+    if offsets is None:
+        offsets = isect_offset_encode(isect_ids, I, tile_width, tile_height)
+    else:
+        offsets = offsets.view(I, tile_height, tile_width)
+    return tiles_per_gauss, isect_ids, flatten_ids, offsets
+
+
+def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sort, packed, n_images,
+                 image_ids, conics, opacities):
     if packed:
         nnz = means2d.size(0)
         assert means2d.shape == (nnz, 2), means2d.shape
@@ -439,7 +468,6 @@ def isect_tiles(
         if opacities is not None:
             assert opacities.shape == (nnz,), opacities.shape
         assert image_ids is not None, "image_ids is required if packed is True"
-        assert gaussian_ids is not None, "gaussian_ids is required if packed is True"
         assert n_images is not None, "n_images is required if packed is True"
         image_ids = image_ids.contiguous()
         I = n_images
@@ -472,24 +500,59 @@ def isect_tiles(
     tiles_per_gauss = torch.empty(depths.shape, dtype=torch.int32, device=dev)
     if (conics is None) != (opacities is None):
         conics, opacities = None, None  # AccuTile needs both; AABB otherwise
+    n_buckets = I * tile_width * tile_height
     with torch.cuda.device(dev):
         stream = stream_of(means2d)
         args = (int(packed), I, N, nnz, ptr(image_ids), ptr(means2d), ptr(radii), ptr(depths),
                 ptr(conics), ptr(opacities), tile_size, tile_width, tile_height)
         if n == 0:
             empty = torch.empty(0, dtype=torch.int64, device=dev)
-            return tiles_per_gauss, empty, torch.empty(0, dtype=torch.int32, device=dev)
-        call("gsb_isect_count", *args, ptr(tiles_per_gauss), stream)
-        cum = _scan_i32(tiles_per_gauss.view(-1))
-        n_isects = int(cum[-1].item())
+            return tiles_per_gauss, empty, torch.empty(0, dtype=torch.int32, device=dev), None
+        if not sort:
+            call("gsb_isect_count", *args, ptr(tiles_per_gauss), stream)
+            cum = _scan_i32(tiles_per_gauss.view(-1))
+            n_isects = int(cum[-1].item())
+            isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
+            flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+            if n_isects:
+                call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
+            return tiles_per_gauss, isect_ids, flatten_ids, None
+
+        # tile-bucket path: counts per splat and per (image, tile) bucket, bucket
+        # offsets, then one host read of (n_isects, largest bucket)
+        shards = _B.lib().gsb_isect_bucket_shards(I, tile_width, tile_height)
+        shard_counts = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
+        call("gsb_isect_count_tiles", *args, ptr(tiles_per_gauss), ptr(shard_counts), stream)
+        offsets = torch.empty(n_buckets, dtype=torch.int32, device=dev)
+        bucket_sizes = torch.empty(n_buckets, dtype=torch.int32, device=dev)
+        cursor = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
+        totals = torch.empty(2, dtype=torch.int32, device=dev)
+        nbytes = _B.lib().gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        call("gsb_isect_bucket_offsets", ptr(shard_counts), n_buckets, shards, ptr(offsets),
+             ptr(bucket_sizes), ptr(cursor), ptr(totals), ptr(scratch), nbytes, stream)
+        n_isects, largest = (int(v) for v in totals.tolist())
+        if n_isects < 0:
+            raise RuntimeError("isect_tiles: more than 2^31 - 1 tile intersections")
         isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
         flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
-        if n_isects:
-            call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
-        if n_isects and sort:
-            isect_ids, flatten_ids = _radix_sort(isect_ids, flatten_ids,
-                                                 _B.lib().gsb_isect_key_bits(I, tile_width, tile_height))
-    return tiles_per_gauss, isect_ids, flatten_ids
+        if n_isects == 0:
+            return tiles_per_gauss, isect_ids, flatten_ids, offsets
+        if largest <= _B.lib().gsb_isect_bucket_sort_max():
+            bucket_depths = torch.empty(n_isects, dtype=torch.int32, device=dev)
+            bucket_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+            call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_depths),
+                 ptr(bucket_ids), stream)
+            call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes),
+                 largest, ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids), ptr(flatten_ids), stream)
+            return tiles_per_gauss, isect_ids, flatten_ids, offsets
+        # a bucket too large for the shared-memory sort: emit in splat order and
+        # sort globally (stable LSD radix sort)
+        cum = _scan_i32(tiles_per_gauss.view(-1))
+        call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
+        isect_ids, flatten_ids = _radix_sort(isect_ids, flatten_ids,
+                                             _B.lib().gsb_isect_key_bits(I, tile_width, tile_height))
+        return tiles_per_gauss, isect_ids, flatten_ids, offsets
 
 
 def _radix_sort(keys: Tensor, vals: Tensor, end_bit: int) -> Tuple[Tensor, Tensor]:

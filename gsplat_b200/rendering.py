@@ -25,8 +25,7 @@ from typing_extensions import Literal
 from .cuda._wrapper import (
     fully_fused_projection,
     fully_fused_projection_sh,
-    isect_offset_encode,
-    isect_tiles,
+    isect_tiles_with_offsets,
     rasterize_to_pixels,
     spherical_harmonics,
 )
@@ -416,11 +415,10 @@ def rasterization(
 
     tile_width = math.ceil(width / float(tile_size))
     tile_height = math.ceil(height / float(tile_size))
-    tiles_per_gauss, isect_ids, flatten_ids = isect_tiles(
-        means2d, radii, depths, tile_size, tile_width, tile_height, segmented=segmented,
-        packed=packed, n_images=I, image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics,
-        opacities=opacities)
-    isect_offsets = isect_offset_encode(isect_ids, I, tile_width, tile_height)
+    # isect_tiles(sort=True, segmented) + isect_offset_encode in one pass
+    tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(
+        means2d, radii, depths, tile_size, tile_width, tile_height, packed=packed, n_images=I,
+        image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics, opacities=opacities)
     isect_offsets = isect_offsets.reshape(batch_dims + (C, tile_height, tile_width))
 
     meta.update(

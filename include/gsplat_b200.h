@@ -221,6 +221,53 @@ GSB_API int gsb_radix_sort_pairs(int64_t *keys, int32_t *vals, int64_t *keys_alt
 GSB_API int gsb_isect_offset_encode(const int64_t *isect_ids, long long n_isects, int I, int tile_width,
                             int tile_height, int32_t *offsets, cudaStream_t stream);
 
+/* --- Tile-bucket path for the sorted intersection list --------------------
+ * Produces the same (isect_ids, flatten_ids, offsets) as gsb_isect_count +
+ * gsb_inclusive_scan_i32 + gsb_isect_emit + gsb_radix_sort_pairs +
+ * gsb_isect_offset_encode -- the reference's intersect_tile(sort=true) followed
+ * by intersect_offset (Intersect.cpp:33-176, 320-337) -- bit for bit, without a
+ * global sort: entries are scattered into their (image, tile) bucket and each
+ * bucket is sorted by (depth bits, splat index) on chip. Buckets are numbered
+ * image * tile_width * tile_height + tile; each bucket has S =
+ * gsb_isect_bucket_shards(I, tile_width, tile_height) counters, one per shard
+ * of splats (contiguous splat ranges handled by one CTA each when the buckets
+ * fit in shared memory, else GSB_ISECT_BUCKET_SHARDS shards idx % 16 in
+ * global memory).
+ *
+ * 1. gsb_isect_count_tiles: tiles_per_gauss as gsb_isect_count, plus
+ *    shard_counts int32 [n_buckets * S] (all written by the call). */
+#define GSB_ISECT_BUCKET_SHARDS 16
+GSB_API int gsb_isect_bucket_shards(int I, int tile_width, int tile_height);
+GSB_API int gsb_isect_count_tiles(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                                  const float *means2d, const int32_t *radii, const float *depths,
+                                  const float *conics, const float *opacities, int tile_size,
+                                  int tile_width, int tile_height, int32_t *tiles_per_gauss,
+                                  int32_t *shard_counts, cudaStream_t stream);
+/* 2. offsets int32 [n_buckets] (= gsb_isect_offset_encode's output),
+ *    bucket_sizes int32 [n_buckets], the emit cursor int32 [n_buckets * S]
+ *    and totals int32 [2] = {n_isects (-1 if above 2^31 - 1), largest bucket},
+ *    all device memory; scratch of gsb_isect_bucket_offsets_scratch_bytes(n_buckets, S). */
+GSB_API size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, int shards);
+GSB_API int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
+                                     int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
+                                     int32_t *totals, void *scratch, size_t scratch_bytes,
+                                     cudaStream_t stream);
+/* 3. Scatter (depth bits, splat index) of every intersection into its bucket
+ *    (unordered inside the bucket); n_isects = totals[0] of step 2. */
+GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
+                                  const float *means2d, const int32_t *radii, const float *depths,
+                                  const float *conics, const float *opacities, int tile_size,
+                                  int tile_width, int tile_height, long long n_isects, int32_t *cursor,
+                                  uint32_t *bucket_depths, int32_t *bucket_ids, cudaStream_t stream);
+/* 4. Sort every bucket and write isect_ids int64 / flatten_ids int32
+ *    [n_isects]. max_count (totals[1] of step 2) must not exceed
+ *    gsb_isect_bucket_sort_max(); larger buckets take the global-sort path. */
+GSB_API int gsb_isect_bucket_sort_max(void);
+GSB_API int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
+                                  const int32_t *bucket_sizes, int max_count, const uint32_t *bucket_depths,
+                                  const int32_t *bucket_ids, int64_t *isect_ids, int32_t *flatten_ids,
+                                  cudaStream_t stream);
+
 /* --- Rasterization --------------------------------------------------------
  * Replaces gsplat::rasterize_to_pixels_3dgs_fwd (Rasterization.cpp:42-119).
  * means2d [.,2], conics [.,3], colors [.,channels], opacities [.] indexed by

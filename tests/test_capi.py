@@ -40,7 +40,7 @@ def test_ctypes_signatures_cover_header():
     assert declared == set(_backend.SIGNATURES), declared ^ set(_backend.SIGNATURES)
     text = open(HEADER).read()
     for name, (_, args) in _backend.SIGNATURES.items():
-        m = re.search(r"\b" + name + r"\s*\(([^;]*)\)\s*;", text, re.S)
+        m = re.search(r"GSB_API[^;(]*\b" + name + r"\s*\(([^;]*)\)\s*;", text, re.S)
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), (name, len(params), len(args))
 
@@ -106,3 +106,15 @@ def test_api_signature_matches_reference():
     assert p == ["means2d", "conics", "colors", "opacities", "image_width", "image_height",
                  "tile_size", "isect_offsets", "flatten_ids", "backgrounds", "masks", "packed",
                  "absgrad"]
+
+
+def test_bucket_shard_plan():
+    """Few buckets: one shard per CTA of the shared-memory path; many buckets:
+    the GSB_ISECT_BUCKET_SHARDS global shards of the header."""
+    from gsplat_b200.cuda import _backend
+
+    text = open(HEADER).read()
+    m = re.search(r"#define GSB_ISECT_BUCKET_SHARDS (\d+)", text)
+    lib = _backend.lib()
+    assert lib.gsb_isect_bucket_shards(1, 2000, 2000) == int(m.group(1))
+    assert lib.gsb_isect_bucket_shards(1, 81, 53) >= 32

@@ -296,6 +296,70 @@ def test_isect_accutile_bit_exact_vs_oracle(packed, tile_size):
     assert (tpg <= tpg_aabb).all()
 
 
+def _entry_points_called(fn):
+    """Runs fn with the backend's call recorder on; returns the entry-point names."""
+    from gsplat_b200.cuda import _backend
+
+    _backend.timing = {}
+    try:
+        out = fn()
+        torch.cuda.synchronize()
+        names = set(_backend.timing)
+    finally:
+        _backend.timing = None
+    return out, names
+
+
+@pytest.mark.parametrize("mode", ["spread", "many_buckets", "cluster_on_chip", "cluster_fallback"])
+def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
+    """Tile-bucket sort against the oracle's stable global sort, with many equal
+    depths (ties are ordered by splat index, as in a stable sort of the emitted
+    keys). The clustered cases pile thousands of splats into two tiles:
+    cluster_on_chip stays within the on-chip bucket sort (16 entries per thread),
+    cluster_fallback exceeds it and must switch to the global radix sort with the
+    same result."""
+    from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
+
+    rng = np.random.default_rng(31 + len(mode))
+    I, W, H = 2, 320, 240
+    ts = 2 if mode == "many_buckets" else 16  # 2 x 160 x 120 buckets: the global-shard path
+    N = {"spread": 6000, "many_buckets": 6000, "cluster_on_chip": 9000, "cluster_fallback": 20000}[mode]
+    tw, th = math.ceil(W / ts), math.ceil(H / ts)
+    if mode.startswith("cluster"):
+        m2 = np.empty((I, N, 2), np.float32)
+        m2[..., 0] = 100.0 + rng.uniform(0, 8, (I, N))
+        m2[..., 1] = 60.0 + rng.uniform(0, 8, (I, N))
+        r = np.full((I, N, 2), 3, np.int32)
+    else:
+        m2 = np.stack([rng.uniform(-20, W + 20, (I, N)), rng.uniform(-20, H + 20, (I, N))], -1)
+        r = rng.integers(0, 6 if mode == "many_buckets" else 40, (I, N, 2)).astype(np.int32)
+    dep = rng.integers(1, 9, (I, N)).astype(np.float32) * 0.5  # 8 distinct depths
+    m2 = m2.astype(np.float32)
+    (tpg, keys, ids, off), names = _entry_points_called(lambda: isect_tiles_with_offsets(
+        torch.from_numpy(m2).to(DEV), torch.from_numpy(r).to(DEV), torch.from_numpy(dep).to(DEV), ts, tw, th))
+    etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th)
+    assert_equal(tpg, etpg, "tiles_per_gauss")
+    assert_equal(keys, ekeys, "isect_ids")
+    assert_equal(ids, eids, "flatten_ids")
+    assert_equal(off, O.isect_offset_encode(ekeys, I, tw, th), "offsets")
+    fallback = mode == "cluster_fallback"
+    assert ("gsb_radix_sort_pairs" in names) == fallback, names
+    assert ("gsb_isect_bucket_sort" in names) != fallback, names
+    largest = np.bincount(ekeys >> 32).max()
+    if fallback:
+        assert largest > gsb_lib().gsb_isect_bucket_sort_max()
+    elif mode == "cluster_on_chip":
+        assert 4096 < largest <= gsb_lib().gsb_isect_bucket_sort_max()
+    shards = gsb_lib().gsb_isect_bucket_shards(I, tw, th)
+    assert (shards == 16) == (mode == "many_buckets"), shards
+
+
+def gsb_lib():
+    from gsplat_b200.cuda import _backend
+
+    return _backend.lib()
+
+
 @pytest.mark.parametrize("n", [1, 4095, 4096, 4097, 300_001])
 def test_radix_sort_stable_vs_numpy(n):
     from gsplat_b200.cuda._wrapper import _radix_sort
