@@ -26,6 +26,9 @@ struct IsectParams {
     const float *conics;    // optional: AccuTile when conics and opacities are given
     const float *opacities; // optional
     uint32_t tile_size, tile_width, tile_height, tile_n_bits;
+    // packed only, optional: the splat count lives in device memory (nnz is then
+    // the capacity of the arrays); lets the caller skip reading it back
+    const int64_t *nnz_device;
 };
 
 struct EmitSink {
@@ -322,7 +325,12 @@ __device__ __forceinline__ int64_t splat_image(const IsectParams &p, uint32_t id
     return p.packed ? p.image_ids[idx] : (int64_t)(idx / p.N);
 }
 
-__device__ __forceinline__ uint32_t n_splats(const IsectParams &p) { return p.packed ? p.nnz : p.I * p.N; }
+__device__ __forceinline__ uint32_t n_splats(const IsectParams &p) {
+    if (!p.packed) return p.I * p.N;
+    if (p.nnz_device == nullptr) return p.nnz;
+    const int64_t n = *p.nnz_device;
+    return n < 0 ? 0u : (n < (int64_t)p.nnz ? (uint32_t)n : p.nnz);
+}
 
 // global-memory shards
 __global__ void __launch_bounds__(256) isect_count_tiles_kernel(IsectParams p, int32_t *tiles_per_gauss,
@@ -367,10 +375,11 @@ __global__ void __launch_bounds__(256) shard_bases_kernel(const int64_t *__restr
 
 // Bucket b occupies [incl[b S - 1], incl[b S + S - 1]).
 // totals[0] = number of entries (-1 when it does not fit int32, like every
-// offset here), totals[1] = largest bucket.
+// offset here), totals[1] = largest bucket, totals[2] = *nnz_device if given.
 __global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__restrict__ incl, uint32_t n_buckets,
                                                             uint32_t shards, int32_t *__restrict__ starts,
-                                                            int32_t *__restrict__ sizes, int32_t *totals) {
+                                                            int32_t *__restrict__ sizes, const int64_t *nnz_device,
+                                                            int32_t *totals) {
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     int32_t c = 0;
     if (b < n_buckets) {
@@ -383,6 +392,10 @@ __global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__res
     if (b == n_buckets - 1) {
         const int64_t total = incl[(size_t)n_buckets * shards - 1];
         totals[0] = total > 0x7fffffffll ? -1 : (int32_t)total;
+        if (nnz_device != nullptr) {
+            const int64_t v = *nnz_device;
+            totals[2] = v > 0x7fffffffll ? -1 : (int32_t)v;
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) c = max(c, __shfl_xor_sync(0xffffffffu, c, o));
@@ -584,6 +597,7 @@ static int make_isect_params(IsectParams &p, int packed, int I, int N, int nnz,
     p.tile_width = tile_width;
     p.tile_height = tile_height;
     p.tile_n_bits = tile_bits;
+    p.nnz_device = nullptr;
     return kOk;
 }
 
@@ -662,12 +676,13 @@ static int set_cta_smem(const void *kern, size_t smem) {
 extern "C" int gsb_isect_count_tiles(int packed, int I, int N, int nnz, const int64_t *image_ids,
                                      const float *means2d, const int32_t *radii, const float *depths,
                                      const float *conics, const float *opacities, int tile_size,
-                                     int tile_width, int tile_height, int32_t *tiles_per_gauss,
-                                     int32_t *shard_counts, cudaStream_t stream) {
+                                     int tile_width, int tile_height, const int64_t *nnz_device,
+                                     int32_t *tiles_per_gauss, int32_t *shard_counts, cudaStream_t stream) {
     IsectParams p;
     if (int e = make_isect_params(p, packed, I, N, nnz, image_ids, means2d, radii, depths, conics,
                                   opacities, tile_size, tile_width, tile_height))
         return e;
+    p.nnz_device = packed ? nnz_device : nullptr;
     const uint64_t n_buckets = (uint64_t)I * tile_width * tile_height;
     const size_t n = packed ? (size_t)nnz : (size_t)I * N;
     if (n > 0x7fffffffu) return set_error(kErrInvalidArgument, "too many splats: %zu", n);
@@ -697,11 +712,11 @@ extern "C" size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, in
 
 extern "C" int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
                                         int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
-                                        int32_t *totals, void *scratch, size_t scratch_bytes,
-                                        cudaStream_t stream) {
+                                        const int64_t *nnz_device, int32_t *totals, void *scratch,
+                                        size_t scratch_bytes, cudaStream_t stream) {
     if (shards <= 0 || n_buckets < 0 || n_buckets > 0x7fffffffll / shards)
         return set_error(kErrInvalidArgument, "bad bucket count %lld x %d shards", n_buckets, shards);
-    cudaError_t ce = cudaMemsetAsync(totals, 0, 2 * sizeof(int32_t), stream);
+    cudaError_t ce = cudaMemsetAsync(totals, 0, 3 * sizeof(int32_t), stream);
     if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
     if (n_buckets == 0) return kOk;
     if (scratch_bytes < gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards))
@@ -715,7 +730,7 @@ extern "C" int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n
         return e;
     shard_bases_kernel<<<(unsigned)((n_shards + 255) / 256), 256, 0, stream>>>(incl, (uint32_t)n_shards, cursor);
     bucket_starts_kernel<<<(unsigned)((n_buckets + 255) / 256), 256, 0, stream>>>(
-        incl, (uint32_t)n_buckets, (uint32_t)shards, offsets, bucket_sizes, totals);
+        incl, (uint32_t)n_buckets, (uint32_t)shards, offsets, bucket_sizes, nnz_device, totals);
     return check_launch("bucket_starts_kernel");
 }
 

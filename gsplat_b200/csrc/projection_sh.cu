@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kFusedBwdThreads, 5) fused_bwd_kernel(FusedBwd
             const float v_m2d[2] = {q.v_means2d[e * 2], q.v_means2d[e * 2 + 1]};
             const float v_conic[3] = {q.v_conics[e * 3], q.v_conics[e * 3 + 1], q.v_conics[e * 3 + 2]};
             ProjGrads gr;
-            project_one_vjp(p, b, c, mean, covar, conic, comp, v_m2d, q.v_depths[e], v_conic, v_comp,
+            project_one_vjp(p, b, c, mean, covar, conic, comp, v_m2d, q.v_depths ? q.v_depths[e] : 0.f, v_conic, v_comp,
                             p.calc_comp, gr);
             v_mean[0] += gr.v_mean[0];
             v_mean[1] += gr.v_mean[1];

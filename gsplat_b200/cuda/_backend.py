@@ -84,10 +84,10 @@ SIGNATURES = {
     "gsb_radix_sort_scratch_bytes": (SZ, [I64]),
     "gsb_radix_sort_pairs": (I32, [P, P, P, P, I64, I32, P, SZ, P]),
     "gsb_isect_offset_encode": (I32, [P, I64, I32, I32, I32, P, P]),
-    "gsb_isect_count_tiles": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, P, P, P]),
+    "gsb_isect_count_tiles": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, P, P, P, P]),
     "gsb_isect_bucket_shards": (I32, [I32, I32, I32]),
     "gsb_isect_bucket_offsets_scratch_bytes": (SZ, [I64, I32]),
-    "gsb_isect_bucket_offsets": (I32, [P, I64, I32, P, P, P, P, P, SZ, P]),
+    "gsb_isect_bucket_offsets": (I32, [P, I64, I32, P, P, P, P, P, P, SZ, P]),
     "gsb_isect_bucket_emit": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, I64, P, P, P, P]),
     "gsb_isect_bucket_sort_max": (I32, []),
     "gsb_isect_bucket_sort": (I32, [I32, I32, I32, P, P, I32, P, P, P, P, P]),

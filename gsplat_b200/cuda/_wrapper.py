@@ -518,41 +518,59 @@ def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sor
                 call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
             return tiles_per_gauss, isect_ids, flatten_ids, None
 
-        # tile-bucket path: counts per splat and per (image, tile) bucket, bucket
-        # offsets, then one host read of (n_isects, largest bucket)
-        shards = _B.lib().gsb_isect_bucket_shards(I, tile_width, tile_height)
-        shard_counts = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
-        call("gsb_isect_count_tiles", *args, ptr(tiles_per_gauss), ptr(shard_counts), stream)
-        offsets = torch.empty(n_buckets, dtype=torch.int32, device=dev)
-        bucket_sizes = torch.empty(n_buckets, dtype=torch.int32, device=dev)
-        cursor = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
-        totals = torch.empty(2, dtype=torch.int32, device=dev)
-        nbytes = _B.lib().gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards)
-        scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        call("gsb_isect_bucket_offsets", ptr(shard_counts), n_buckets, shards, ptr(offsets),
-             ptr(bucket_sizes), ptr(cursor), ptr(totals), ptr(scratch), nbytes, stream)
-        n_isects, largest = (int(v) for v in totals.tolist())
-        if n_isects < 0:
-            raise RuntimeError("isect_tiles: more than 2^31 - 1 tile intersections")
-        isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
-        flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
-        if n_isects == 0:
-            return tiles_per_gauss, isect_ids, flatten_ids, offsets
-        if largest <= _B.lib().gsb_isect_bucket_sort_max():
-            bucket_depths = torch.empty(n_isects, dtype=torch.int32, device=dev)
-            bucket_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
-            call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_depths),
-                 ptr(bucket_ids), stream)
-            call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes),
-                 largest, ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids), ptr(flatten_ids), stream)
-            return tiles_per_gauss, isect_ids, flatten_ids, offsets
-        # a bucket too large for the shared-memory sort: emit in splat order and
-        # sort globally (stable LSD radix sort)
-        cum = _scan_i32(tiles_per_gauss.view(-1))
-        call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
-        isect_ids, flatten_ids = _radix_sort(isect_ids, flatten_ids,
-                                             _B.lib().gsb_isect_key_bits(I, tile_width, tile_height))
+        isect_ids, flatten_ids, offsets, _ = _bucket_isect(args, I, tile_width, tile_height,
+                                                          tiles_per_gauss, dev, stream)
         return tiles_per_gauss, isect_ids, flatten_ids, offsets
+
+
+def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream, nnz_device=None):
+    """Sorted intersections through the tile-bucket path: per-splat and
+    per-(image, tile) counts, bucket offsets, one host read of (n_isects, largest
+    bucket, nnz), bucket emit and on-chip bucket sort. ``args`` are the leading
+    arguments of the isect entry points (packed, I, N, nnz, image_ids, means2d,
+    radii, depths, conics, opacities, tile_size, tile_width, tile_height). With
+    ``nnz_device`` (packed, a device int64 count) the splat arrays have ``nnz``
+    rows of capacity and the actual count is read back with the other sizes.
+    Returns (isect_ids, flatten_ids, offsets int32 [I * th * tw], nnz or None)."""
+    n_buckets = I * tile_width * tile_height
+    shards = _B.lib().gsb_isect_bucket_shards(I, tile_width, tile_height)
+    shard_counts = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
+    call("gsb_isect_count_tiles", *args, ptr(nnz_device), ptr(tiles_per_gauss), ptr(shard_counts), stream)
+    offsets = torch.empty(n_buckets, dtype=torch.int32, device=dev)
+    bucket_sizes = torch.empty(n_buckets, dtype=torch.int32, device=dev)
+    cursor = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
+    totals = torch.empty(3, dtype=torch.int32, device=dev)
+    nbytes = _B.lib().gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    call("gsb_isect_bucket_offsets", ptr(shard_counts), n_buckets, shards, ptr(offsets), ptr(bucket_sizes),
+         ptr(cursor), ptr(nnz_device), ptr(totals), ptr(scratch), nbytes, stream)
+    n_isects, largest, nnz = (int(v) for v in totals.tolist())
+    if n_isects < 0 or nnz < 0:
+        raise RuntimeError("isect_tiles: more than 2^31 - 1 tile intersections or splats")
+    if nnz_device is None:
+        nnz = None
+    else:
+        args = args[:3] + (nnz,) + args[4:]
+    isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
+    flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+    if n_isects == 0:
+        return isect_ids, flatten_ids, offsets, nnz
+    if largest <= _B.lib().gsb_isect_bucket_sort_max():
+        bucket_depths = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        bucket_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_depths), ptr(bucket_ids),
+             stream)
+        call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
+             ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids), ptr(flatten_ids), stream)
+        return isect_ids, flatten_ids, offsets, nnz
+    # a bucket too large for the on-chip sort: emit in splat order and sort
+    # globally (stable LSD radix sort)
+    n_live = tiles_per_gauss.numel() if nnz is None else nnz
+    cum = _scan_i32(tiles_per_gauss.view(-1)[:n_live])
+    call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
+    isect_ids, flatten_ids = _radix_sort(isect_ids, flatten_ids,
+                                         _B.lib().gsb_isect_key_bits(I, tile_width, tile_height))
+    return isect_ids, flatten_ids, offsets, nnz
 
 
 def _radix_sort(keys: Tensor, vals: Tensor, end_bit: int) -> Tuple[Tensor, Tensor]:
@@ -727,6 +745,7 @@ def fully_fused_projection_sh(
     packed: bool = False,
     calc_compensations: bool = False,
     camera_model: CameraModel = "pinhole",
+    isect_tiling: Optional[Tuple[int, int, int]] = None,
 ) -> Tuple[Tensor, ...]:
     """Projection, view-dependent SH colour and opacity compensation in one op.
 
@@ -739,6 +758,13 @@ def fully_fused_projection_sh(
     (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
     compensations, colors, opacities). Gradients flow to means, quats, scales,
     opacities and sh_coeffs (not to viewmats).
+
+    With ``packed`` and ``isect_tiling = (tile_size, tile_width, tile_height)``
+    the op also runs isect_tiles (AccuTile with the conics and the output
+    opacities, sorted) and isect_offset_encode on the projected splats, and
+    appends (tiles_per_gauss, isect_ids, flatten_ids, isect_offsets [B*C, th,
+    tw]). The splat count then travels to the host together with the
+    intersection sizes in one read instead of two.
     """
     batch_dims = means.shape[:-2]
     N = means.shape[-2]
@@ -755,13 +781,15 @@ def fully_fused_projection_sh(
     return _FullyFusedProjectionSH.apply(
         means.contiguous(), quats.contiguous(), scales.contiguous(), opacities.contiguous(),
         sh_coeffs.contiguous(), sh_degree, viewmats.contiguous(), Ks.contiguous(), width, height,
-        eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, cam)
+        eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, cam,
+        isect_tiling if packed else None)
 
 
 class _FullyFusedProjectionSH(torch.autograd.Function):
     @staticmethod
     def forward(ctx, means, quats, scales, opacities, sh, sh_degree, viewmats, Ks, width, height,
-                eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, camera_model):
+                eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, camera_model,
+                isect_tiling):
         for name, t in (("means", means), ("quats", quats), ("scales", scales),
                         ("opacities", opacities), ("sh_coeffs", sh), ("viewmats", viewmats),
                         ("Ks", Ks)):
@@ -799,7 +827,13 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                      near_plane, far_plane, radius_clip, int(calc_compensations), camera_model,
                      ptr(block_cnts), ptr(vis_bits), stream)
                 block_accum = _scan_i32(block_cnts)
-                nnz = int(block_accum[-1].item()) if block_accum.numel() > 0 else 0
+                deferred = isect_tiling is not None and block_accum.numel() > 0
+                if deferred:
+                    # capacity rows; the count stays on the device until the
+                    # intersection sizes are read
+                    nnz = B * C * N
+                else:
+                    nnz = int(block_accum[-1].item()) if block_accum.numel() > 0 else 0
                 indptr = torch.zeros(B * C + 1, dtype=torch.int32, device=dev)
                 batch_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
                 camera_ids = torch.empty(nnz, dtype=torch.int64, device=dev)
@@ -819,8 +853,29 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                          ptr(colors), ptr(opac_out), ptr(pair_index), stream)
                 outs = (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
                         comps, colors, opac_out)
-                ctx.mark_non_differentiable(batch_ids, camera_ids, gaussian_ids, indptr)
-        ctx.mark_non_differentiable(radii)
+                if isect_tiling is not None:
+                    tile_size, tile_width, tile_height = isect_tiling
+                    I = B * C
+                    tiles_per_gauss = torch.empty(nnz, dtype=torch.int32, device=dev)
+                    if nnz == 0:
+                        isect = (torch.empty(0, dtype=torch.int64, device=dev),
+                                 torch.empty(0, dtype=torch.int32, device=dev),
+                                 torch.zeros(I * tile_width * tile_height, dtype=torch.int32, device=dev))
+                    else:
+                        image_ids = camera_ids if B == 1 else batch_ids * C + camera_ids
+                        args = (1, I, 0, nnz, ptr(image_ids), ptr(means2d), ptr(radii), ptr(depths),
+                                ptr(conics), ptr(opac_out), tile_size, tile_width, tile_height)
+                        *isect, nnz = _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss,
+                                                    dev, stream, nnz_device=block_accum[-1:])
+                        outs = tuple(t[:nnz] if t is not None and t is not indptr else t for t in outs)
+                        tiles_per_gauss = tiles_per_gauss[:nnz]
+                    isect_offsets = isect[2].view(I, tile_height, tile_width)
+                    outs = outs + (tiles_per_gauss, isect[0], isect[1], isect_offsets)
+                (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics, comps,
+                 colors, opac_out) = outs[:11]
+                ctx.mark_non_differentiable(batch_ids, camera_ids, gaussian_ids, indptr, radii, *outs[11:])
+        if not packed:
+            ctx.mark_non_differentiable(radii)
         ctx.save_for_backward(means, quats, scales, opacities, sh, viewmats, Ks, pair_index,
                               None if packed else radii, conics, comps)
         ctx.meta = (B, C, N, K, sh_degree, width, height, eps2d, calc_compensations, camera_model,
@@ -832,7 +887,7 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
         means, quats, scales, opacities, sh, viewmats, Ks, pair_index, radii, conics, comps = ctx.saved_tensors
         B, C, N, K, deg, width, height, eps2d, calc, cam, packed = ctx.meta
         if packed:
-            _, _, _, _, _, v_means2d, v_depths, v_conics, v_comps, v_colors, v_opac = grads
+            _, _, _, _, _, v_means2d, v_depths, v_conics, v_comps, v_colors, v_opac = grads[:11]
         else:
             _, v_means2d, v_depths, v_conics, v_comps, v_colors, v_opac = grads
 
@@ -840,7 +895,7 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
             return torch.zeros_like(like) if t is None else t.contiguous()
 
         v_means2d = c(v_means2d, conics[..., :2])
-        v_depths = c(v_depths, conics[..., 0])
+        v_depths = v_depths.contiguous() if v_depths is not None else None  # the kernel reads None as 0
         v_conics = c(v_conics, conics)
         v_colors = c(v_colors, conics)
         v_opac = c(v_opac, conics[..., 0])
@@ -858,4 +913,4 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                  ptr(v_opac), ptr(v_means), ptr(v_quats), ptr(v_scales), ptr(v_opacities),
                  ptr(v_sh), stream_of(means))
         return (v_means, v_quats, v_scales, v_opacities, v_sh, None, None, None, None, None, None,
-                None, None, None, None, None, None)
+                None, None, None, None, None, None, None)

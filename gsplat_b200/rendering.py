@@ -271,16 +271,25 @@ def rasterization(
         and not viewmats.requires_grad
     )
     compensations = None
+    tile_width = math.ceil(width / float(tile_size))
+    tile_height = math.ceil(height / float(tile_size))
+    isect = None  # (tiles_per_gauss, isect_ids, flatten_ids, isect_offsets) when done by the projection
     if use_fused:
+        # packed and not distributed: the projection op also intersects the tiles,
+        # so the splat count and the intersection sizes reach the host in one read
+        fuse_isect = packed and not distributed
         proj = fully_fused_projection_sh(
             means, quats, scales, opacities, colors, sh_degree, viewmats, Ks, width, height,
             eps2d=eps2d, near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
             packed=packed, calc_compensations=(rasterize_mode == "antialiased"),
-            camera_model=camera_model)
+            camera_model=camera_model,
+            isect_tiling=(tile_size, tile_width, tile_height) if fuse_isect else None)
         if packed:
             (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
-             _, proj_features, opacities) = proj
-            image_ids = batch_ids * C + camera_ids
+             _, proj_features, opacities) = proj[:11]
+            if fuse_isect:
+                isect = proj[11:]
+            image_ids = camera_ids if B == 1 else batch_ids * C + camera_ids
         else:
             radii, means2d, depths, conics, _, proj_features, opacities = proj
             indptr, batch_ids, camera_ids, gaussian_ids = None, None, None, None
@@ -304,7 +313,6 @@ def rasterization(
         if compensations is not None:
             opacities = opacities * compensations
 
-    valid_gaussians = (radii > 0).all(dim=-1)
     meta.update(
         {
             "batch_ids": batch_ids,
@@ -342,7 +350,8 @@ def rasterization(
             colors = normalize_features_layout(colors, batch_dims, C, tail, batch_ids, camera_ids,
                                                gaussian_ids)
             if colors_sh_degree is not None:
-                colors = spherical_harmonics(colors_sh_degree, dirs, colors, masks=valid_gaussians)
+                colors = spherical_harmonics(colors_sh_degree, dirs, colors,
+                                             masks=(radii > 0).all(dim=-1))
                 colors = torch.clamp_min(colors + 0.5, 0.0)
             feature_list.append(colors)
         if extra_signals is not None:
@@ -352,7 +361,7 @@ def rasterization(
                                                       camera_ids, gaussian_ids)
             if extra_signals_sh_degree is not None:
                 extra_signals = spherical_harmonics(extra_signals_sh_degree, dirs, extra_signals,
-                                                    masks=valid_gaussians)
+                                                    masks=(radii > 0).all(dim=-1))
                 extra_signals = extra_signals + 0.5
             feature_list.append(extra_signals)
         proj_features = None
@@ -413,12 +422,13 @@ def rasterization(
                 backgrounds = torch.zeros((*batch_dims, C, 1), device=backgrounds.device)
     assert proj_features is not None
 
-    tile_width = math.ceil(width / float(tile_size))
-    tile_height = math.ceil(height / float(tile_size))
-    # isect_tiles(sort=True, segmented) + isect_offset_encode in one pass
-    tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(
-        means2d, radii, depths, tile_size, tile_width, tile_height, packed=packed, n_images=I,
-        image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics, opacities=opacities)
+    if isect is not None:
+        tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect
+    else:
+        # isect_tiles(sort=True, segmented) + isect_offset_encode in one pass
+        tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(
+            means2d, radii, depths, tile_size, tile_width, tile_height, packed=packed, n_images=I,
+            image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics, opacities=opacities)
     isect_offsets = isect_offsets.reshape(batch_dims + (C, tile_height, tile_width))
 
     meta.update(

@@ -143,7 +143,8 @@ GSB_API int gsb_projection_sh_packed_write(
 /* Backward of both layouts. Writes every row of v_means [B,N,3], v_quats
  * [B,N,4], v_scales [B,N,3], v_opacities [B,N] and v_sh [B,N,K,3] (no
  * pre-zeroing). packed: pair_index from the forward; dense: radii [B,C,N,2].
- * Upstream gradients are indexed like the forward outputs. */
+ * Upstream gradients are indexed like the forward outputs; v_depths and
+ * v_compensations may be NULL (no gradient). */
 GSB_API int gsb_projection_sh_bwd(
     int B, int C, int N, int packed, const float *means, const float *quats, const float *scales,
     const float *opacities, const float *sh, int K, int sh_degree, const float *viewmats,
@@ -235,23 +236,28 @@ GSB_API int gsb_isect_offset_encode(const int64_t *isect_ids, long long n_isects
  * global memory).
  *
  * 1. gsb_isect_count_tiles: tiles_per_gauss as gsb_isect_count, plus
- *    shard_counts int32 [n_buckets * S] (all written by the call). */
+ *    shard_counts int32 [n_buckets * S] (all written by the call). Packed
+ *    only: with nnz_device (device int64, may be NULL) the splat count is read
+ *    on the device and nnz is the capacity of the arrays, so the caller need
+ *    not read the count back after the projection. */
 #define GSB_ISECT_BUCKET_SHARDS 16
 GSB_API int gsb_isect_bucket_shards(int I, int tile_width, int tile_height);
 GSB_API int gsb_isect_count_tiles(int packed, int I, int N, int nnz, const int64_t *image_ids,
                                   const float *means2d, const int32_t *radii, const float *depths,
                                   const float *conics, const float *opacities, int tile_size,
-                                  int tile_width, int tile_height, int32_t *tiles_per_gauss,
-                                  int32_t *shard_counts, cudaStream_t stream);
+                                  int tile_width, int tile_height, const int64_t *nnz_device,
+                                  int32_t *tiles_per_gauss, int32_t *shard_counts, cudaStream_t stream);
 /* 2. offsets int32 [n_buckets] (= gsb_isect_offset_encode's output),
  *    bucket_sizes int32 [n_buckets], the emit cursor int32 [n_buckets * S]
- *    and totals int32 [2] = {n_isects (-1 if above 2^31 - 1), largest bucket},
- *    all device memory; scratch of gsb_isect_bucket_offsets_scratch_bytes(n_buckets, S). */
+ *    and totals int32 [3] = {n_isects (-1 if above 2^31 - 1), largest bucket,
+ *    *nnz_device (0 when nnz_device is NULL)}, all device memory, so one copy
+ *    brings every size the host needs; scratch of
+ *    gsb_isect_bucket_offsets_scratch_bytes(n_buckets, S). */
 GSB_API size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, int shards);
 GSB_API int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
                                      int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
-                                     int32_t *totals, void *scratch, size_t scratch_bytes,
-                                     cudaStream_t stream);
+                                     const int64_t *nnz_device, int32_t *totals, void *scratch,
+                                     size_t scratch_bytes, cudaStream_t stream);
 /* 3. Scatter (depth bits, splat index) of every intersection into its bucket
  *    (unordered inside the bucket); n_isects = totals[0] of step 2. */
 GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
