@@ -350,7 +350,22 @@ def contributing_pairs(meta, W, H, dev):
                   W, H, meta["tile_size"], tw, th, offsets.data_ptr(), fids.data_ptr(), fids.numel(),
                   renders.data_ptr(), alphas.data_ptr(), last.data_ptr(), counts.data_ptr(),
                   torch.cuda.current_stream(dev).cuda_stream)
-    return int(counts.sum().item())
+    # pairs a per-pixel rasterizer evaluates in the backward: every entry of the
+    # pixel's tile list up to its last contributor (none when nothing contributed)
+    ts = meta["tile_size"]
+    ys = torch.arange(H, device=dev) // ts
+    xs = torch.arange(W, device=dev) // ts
+    start = offsets.reshape(I, th, tw)[:, ys][:, :, xs].to(torch.int64)  # [I, H, W]
+    walked = torch.where(counts > 0, last.to(torch.int64) - start + 1, torch.zeros_like(start))
+    return int(counts.sum().item()), int(walked.sum().item())
+
+
+def measured_hbm_gbs():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def ncu_traffic(name):
@@ -525,19 +540,31 @@ def run_gsb(args):
     roofline = None
     cpu_baseline = None
     if rank == 0 and ops.get("gsb_rasterize_bwd"):
-        pairs = contributing_pairs(meta, W, H, dev)
+        pairs, walked = contributing_pairs(meta, W, H, dev)
         peak = fp32_peak_tflops(dev)
         t_bwd = ops["gsb_rasterize_bwd"]["ms_per_step"] / 1e3
         achieved = FLOP_PER_PAIR["bwd"] * pairs / t_bwd / 1e12
+        traffic = ncu_traffic("raster_bwd_config1")
         roofline = {"kernel": "raster_bwd_kernel<3,4>", "bound": "fp32", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": ncu_traffic("raster_bwd_config1"),
-                    "peak_source": "measured FP32 FMA probe (gsb_fp32_fma_probe) on this GPU",
+                    "traffic": traffic,
+                    "peak_source": "measured FP32 FMA probe (gsb_fp32_fma_probe) on this GPU; "
+                                   "the kernel is FP32-issue bound (no tensor-core contraction, "
+                                   "DRAM ~1%), so neither MEASURED_PEAKS figure applies",
                     "algorithmic": f"{FLOP_PER_PAIR['bwd']} FLOP per contributing (pixel, splat) pair; "
                                    f"{pairs} pairs per launch",
+                    "walked_pairs": walked,
+                    "walked_note": "(pixel, splat) pairs up to each pixel's last contributor, the unit "
+                                   "a per-pixel rasterizer evaluates; this kernel culls most of them "
+                                   "before any arithmetic, so the contributing pairs are the unit",
                     "fwd": {"achieved": FLOP_PER_PAIR["fwd"] * pairs /
                             (ops["gsb_rasterize_fwd"]["ms_per_step"] / 1e3) / 1e12,
                             "unit": "TFLOP/s"}}
+        hbm_peak = measured_hbm_gbs()
+        if traffic and hbm_peak:
+            gbs = traffic / t_bwd / 1e9
+            roofline["hbm"] = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                               "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
     if rank == 0 and world == 1 and not args.no_cpu:
         sc = cpu_scene(args.n, 1)
         cpu_reference_step(sc)
