@@ -17,17 +17,35 @@
 //    popc), so warps never evaluate splats that cannot touch their pixels.
 //    The box is inflated by 1% plus half a pixel; outside it alpha is below the
 //    threshold by more than the rounding of the exp evaluation.
-//  * Backward threads own PPT pixels each: the per-splat gradient is summed over
-//    those pixels in registers first. The CDIM + 8 per-splat sums are then
-//    reduced over the warp by recursive halving (each butterfly step exchanges
-//    half of the remaining values), about 16 shuffles instead of 5 per value,
-//    and the finished sums land in different lanes, which issue their atomics
-//    in parallel.
+//  * Backward threads own 4 pixels each, interleaved for 16x16 tiles (lane l
+//    owns pixel l of each 8x4 quarter of its warp's 16x8 rows), so a splat that
+//    covers one quarter runs one of the four unrolled per-pixel code blocks.
+//    The per-splat gradient is summed over the thread's pixels in registers
+//    first. The CDIM + 6 (+ 2 with absgrad) per-splat sums are then reduced over
+//    the warp by recursive halving in power-of-two groups (each butterfly step
+//    exchanges half of the remaining values), and the finished sums land in
+//    different lanes, which issue their atomics in parallel.
+//  * The backward recovers T with an approximate reciprocal (__fdividef), as
+//    the reference's default fast-math build does.
 //  * Channel counts are processed in chunks of at most 32 (kernels are
 //    instantiated for 1-8, 16 and 32 channels) with strided colour access, so no
 //    padding copies are made.
 #include "common.cuh"
 #include "gsb_internal.h"
+
+// Compile-time choices of the backward kernel (defaults are the tuned ones).
+#ifndef GSB_BWD_MINB
+#define GSB_BWD_MINB 10
+#endif
+#ifndef GSB_RAST_SPLIT_FLUSH
+#define GSB_RAST_SPLIT_FLUSH 1
+#endif
+#ifndef GSB_RAST_FAST_RCP
+#define GSB_RAST_FAST_RCP 1
+#endif
+#ifndef GSB_RAST_INTERLEAVE
+#define GSB_RAST_INTERLEAVE 1
+#endif
 
 namespace gsb {
 
@@ -364,11 +382,33 @@ __device__ __forceinline__ float *grad_slot(const RasterParams &p, int j, int32_
     return p.v_means2d_abs ? p.v_means2d_abs + (size_t)g * 2 + (j - 6) : nullptr;
 }
 
-// Reduces the NV slots over the warp and adds them to the splat's gradients, one
-// atomic per slot issued by different lanes.
+// Reduces slots [FIRST, FIRST + COUNT) over the warp and adds them to the
+// splat's gradients: the largest power-of-two group by recursive halving, the
+// rest recursively (8 + 1 slots cost fewer instructions than 16 padded ones).
+template <int CDIM, int FIRST, int COUNT>
+__device__ __forceinline__ void flush_range(const RasterParams &p, const float *acc, int lane, int32_t g) {
+    if constexpr (COUNT > 0) {
+        constexpr int V = COUNT >= 32 ? 32 : (COUNT >= 16 ? 16 : (COUNT >= 8 ? 8 : (COUNT >= 4 ? 4 : (COUNT >= 2 ? 2 : 1))));
+        float v[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = acc[FIRST + i];
+        int idx;
+        bool writer;
+        const float r = halving_reduce<V>(v, lane, idx, writer);
+        if (writer) {
+            float *dst = grad_slot<CDIM>(p, FIRST + idx, g);
+            if (dst) atomicAdd(dst, r);
+        }
+        flush_range<CDIM, FIRST + V, COUNT - V>(p, acc, lane, g);
+    }
+}
+
 template <int CDIM, int NV>
-__device__ __forceinline__ void flush_splat_grads(const RasterParams &p, float *acc, int lane,
+__device__ __forceinline__ void flush_splat_grads(const RasterParams &p, const float *acc, int lane,
                                                   int32_t g) {
+#if GSB_RAST_SPLIT_FLUSH
+    flush_range<CDIM, 0, NV>(p, acc, lane, g);
+#else
     constexpr int FIRST = NV < 32 ? NV : 32;
     constexpr int V1 = Pow2Ceil<FIRST>::value;
     float v1[V1];
@@ -393,14 +433,19 @@ __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, float *
             if (dst) atomicAdd(dst, r);
         }
     }
-}
-#ifndef GSB_BWD_MINB
-#define GSB_BWD_MINB 10
 #endif
-template <int CDIM, int BX, int BY>
+}
+
+// ABS: accumulate |v_mean2d| per pair (absgrad). IL: interleaved pixel layout
+// for 16x16 tiles with 4 pixels per thread: warp w covers rows 8w .. 8w + 7 as
+// four 8x4 sub-blocks and lane l owns pixel (l % 8, l / 8) of every sub-block,
+// so a splat that touches one sub-block runs the per-pair code of one of the
+// four unrolled pixel slots instead of all four.
+template <int CDIM, int BX, int BY, bool ABS, bool IL>
 __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB : 1))
     raster_bwd_kernel(RasterParams p) {
     constexpr int PPT = BX * BY;
+    static_assert(!IL || PPT == 4, "interleaved layout: 4 pixels per thread");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const RasterSmem s = carve<CDIM>(smem_raw);
     const uint32_t image = blockIdx.y;
@@ -420,9 +465,16 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB 
     float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
-        // thread owns a BX x BY block of pixels; blocks are laid out row-major
-        const uint32_t tpr = p.tile_size / BX;
-        const uint32_t ly = (threadIdx.x / tpr) * BY + k / BX, lx = (threadIdx.x % tpr) * BX + k % BX;
+        uint32_t ly, lx;
+        if (IL) {
+            ly = warp * 8 + (k >> 1) * 4 + (lane >> 3);
+            lx = (k & 1) * 8 + (lane & 7);
+        } else {
+            // thread owns a BX x BY block of pixels; blocks are laid out row-major
+            const uint32_t tpr = p.tile_size / BX;
+            ly = (threadIdx.x / tpr) * BY + k / BX;
+            lx = (threadIdx.x % tpr) * BX + k % BX;
+        }
         const uint32_t i = ty0 + ly, j = tx0 + lx;
         inside[k] = ly < p.tile_size && i < p.H && j < p.W;
         px[k] = (float)j + 0.5f;
@@ -486,7 +538,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB 
         for (int li = 0; li < cnt; ++li) {
             const int i = mylist[li];
             const int32_t gidx = bend - i;
-            constexpr int NV = CDIM + 8;
+            constexpr int NV = CDIM + (ABS ? 8 : 6);
             float acc[NV];
 #pragma unroll
             for (int j = 0; j < NV; ++j) acc[j] = 0.f;
@@ -501,7 +553,12 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB 
                 const PairEval e = eval_pair(r, px[k], py[k]);
                 if (!e.keep) continue;
                 any = true;
+#if GSB_RAST_FAST_RCP
+                // approximate reciprocal, as the reference's default fast-math build
+                const float ra = __fdividef(1.f, fmaxf(kMinOneMinusAlpha, 1.f - e.alpha));
+#else
                 const float ra = 1.f / fmaxf(kMinOneMinusAlpha, 1.f - e.alpha);
+#endif
                 T[k] *= ra;
                 const float fac = e.alpha * T[k];
                 float v_alpha = 0.f;
@@ -522,8 +579,10 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB 
                     acc[CDIM + 3] += gx;
                     acc[CDIM + 4] += gy;
                     acc[CDIM + 5] += e.vis * v_alpha;
-                    acc[CDIM + 6] += fabsf(gx);
-                    acc[CDIM + 7] += fabsf(gy);
+                    if constexpr (ABS) {
+                        acc[CDIM + 6] += fabsf(gx);
+                        acc[CDIM + 7] += fabsf(gy);
+                    }
                 }
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) buf[k][c] += col[c] * fac;
@@ -556,10 +615,20 @@ static int launch_variant(bool fwd, const RasterParams &p, cudaStream_t stream) 
         kern<<<grid, nt, smem, stream>>>(p);
         return check_launch("raster_fwd_kernel");
     }
-    auto kern = raster_bwd_kernel<CDIM, BX, BY>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, nt, smem, stream>>>(p);
-    return check_launch("raster_bwd_kernel");
+    auto run = [&](auto kern) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, nt, smem, stream>>>(p);
+        return check_launch("raster_bwd_kernel");
+    };
+    constexpr bool kCanInterleave = GSB_RAST_INTERLEAVE && BX * BY == 4;
+    const bool il = kCanInterleave && p.tile_size == 16;
+    const bool abs = p.v_means2d_abs != nullptr;
+    if (il) {
+        return abs ? run(raster_bwd_kernel<CDIM, BX, BY, true, kCanInterleave>)
+                   : run(raster_bwd_kernel<CDIM, BX, BY, false, kCanInterleave>);
+    }
+    return abs ? run(raster_bwd_kernel<CDIM, BX, BY, true, false>)
+               : run(raster_bwd_kernel<CDIM, BX, BY, false, false>);
 }
 
 // Pixel blocks per thread (BX x BY). Backward: enough pixels per thread to
