@@ -20,17 +20,36 @@ constexpr int kAdamThreads = 256;
 struct AdamBatch {
     GsbAdamGroup g[kAdamMaxGroups];
     long long block_start[kAdamMaxGroups + 1]; // first block of each group
+    unsigned long long row_magic[kAdamMaxGroups]; // ceil(2^64 / D), 0 for D = 1
     int n_groups;
     int vec[kAdamMaxGroups]; // 1 when the group uses float4 access
     float b1, b2;
     const bool *valid;
 };
 
+// Row of element e (< 2^32) of a group with D elements per row, without an
+// integer division: division by an invariant integer through a multiply-high
+// (Granlund and Montgomery, PLDI 1994). With M = ceil(2^64 / D) = (2^64 + r) / D,
+// 0 <= r < D, e M / 2^64 = e / D + e r / (D 2^64), and the second term is below
+// 2^-32 < 1 / D, so it never carries e / D past the next integer:
+// floor(e M / 2^64) = floor(e / D).
+__device__ __forceinline__ uint32_t row_of(uint32_t e, unsigned long long magic) {
+    return magic == 0ull ? e : (uint32_t)__umul64hi((unsigned long long)e, magic);
+}
+
+// Hardware square root approximation (the reference's default fast-math build
+// evaluates sqrtf this way; subnormal inputs are kept).
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float y;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v, float lr, float b1,
                                           float b2, float eps) {
     m = b1 * m + (1.f - b1) * g;
     v = b2 * v + (1.f - b2) * g * g;
-    p += -lr * m / (sqrtf(v) + eps);
+    p += -lr * __fdividef(m, sqrt_approx(v) + eps);
 }
 
 #ifndef GSB_ADAM_VEC
@@ -38,13 +57,14 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
 #endif
 constexpr int kAdamVec = GSB_ADAM_VEC; // float4 (or scalar) items per thread, kAdamThreads apart
 
-// Visibility of the rows of elements e .. e+3 with one integer division.
-__device__ __forceinline__ void rows_visible(const bool *valid, uint32_t e, uint32_t D, bool vis[4]) {
+// Visibility of the rows of elements e .. e+3.
+__device__ __forceinline__ void rows_visible(const bool *valid, uint32_t e, uint32_t D,
+                                             unsigned long long magic, bool vis[4]) {
     if (valid == nullptr) {
         vis[0] = vis[1] = vis[2] = vis[3] = true;
         return;
     }
-    const uint32_t r0 = e / D;
+    const uint32_t r0 = row_of(e, magic);
     const uint32_t rem = e - r0 * D;
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
@@ -71,7 +91,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
             const uint32_t e0 = ((local_block * kAdamVec + it) * kAdamThreads + threadIdx.x) * 4u;
             act[it] = e0 < numel;
             if (act[it]) {
-                rows_visible(B.valid, e0, D, vis[it]);
+                rows_visible(B.valid, e0, D, B.row_magic[gi], vis[it]);
                 act[it] = vis[it][0] | vis[it][1] | vis[it][2] | vis[it][3];
             }
             if (act[it]) {
@@ -99,7 +119,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
         for (int it = 0; it < kAdamVec; ++it) {
             const uint32_t t = (local_block * kAdamVec + it) * kAdamThreads + threadIdx.x;
             if (t >= numel) continue;
-            if (B.valid != nullptr && !B.valid[t / D]) continue;
+            if (B.valid != nullptr && !B.valid[row_of(t, B.row_magic[gi])]) continue;
             float p = G.param[t], m = G.exp_avg[t], v = G.exp_avg_sq[t];
             adam_elem(p, G.grad[t], m, v, lr, b1, b2, eps);
             G.param[t] = p;
@@ -130,6 +150,7 @@ extern "C" int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bo
             const GsbAdamGroup &g = groups[done + n];
             if (g.D <= 0 && g.numel > 0) return set_error(kErrInvalidArgument, "group %d has D <= 0", done + n);
             B.g[n] = g;
+            B.row_magic[n] = g.D <= 1 ? 0ull : ~0ull / (unsigned long long)g.D + 1ull;
             const bool vec = (g.numel % 4 == 0) && aligned16(g.param) && aligned16(g.grad) &&
                              aligned16(g.exp_avg) && aligned16(g.exp_avg_sq);
             B.vec[n] = vec ? 1 : 0;
