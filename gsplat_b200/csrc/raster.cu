@@ -47,6 +47,7 @@
 #define GSB_RAST_INTERLEAVE 1
 #endif
 
+
 namespace gsb {
 
 constexpr int kBatch = 256;
@@ -277,6 +278,21 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
                 }
             }
             __syncwarp();
+            // composite one pair (in list order) into pixel k
+            auto apply = [&](int k, const PairEval &e, int i) {
+                if (!e.keep) return;
+                const float next_T = T[k] * (1.f - e.alpha);
+                if (next_T <= kTransmittanceThreshold) {
+                    done[k] = true;
+                    return;
+                }
+                const float w = e.alpha * T[k];
+#pragma unroll
+                for (int c = 0; c < CDIM; ++c) out[k][c] += s.colors[i * CDIM + c] * w;
+                cur[k] = bstart + i;
+                ++npairs[k];
+                T[k] = next_T;
+            };
             for (int li = 0; li < cnt; ++li) {
                 bool stop = true;
 #pragma unroll
@@ -287,21 +303,10 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
 #pragma unroll
                 for (int k = 0; k < PPT; ++k) {
                     if (done[k]) continue;
-                    const PairEval e = eval_pair(r, px[k], py[k]);
-                    if (!e.keep) continue;
-                    const float next_T = T[k] * (1.f - e.alpha);
-                    if (next_T <= kTransmittanceThreshold) {
-                        done[k] = true;
-                        continue;
-                    }
-                    const float w = e.alpha * T[k];
-#pragma unroll
-                    for (int c = 0; c < CDIM; ++c) out[k][c] += s.colors[i * CDIM + c] * w;
-                    cur[k] = bstart + i;
-                    ++npairs[k];
-                    T[k] = next_T;
+                    apply(k, eval_pair(r, px[k], py[k]), i);
                 }
             }
+
         }
     }
     const size_t img_pix = (size_t)image * p.H * p.W;
@@ -442,7 +447,7 @@ __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, const f
 // so a splat that touches one sub-block runs the per-pair code of one of the
 // four unrolled pixel slots instead of all four.
 template <int CDIM, int BX, int BY, bool ABS, bool IL>
-__global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? GSB_BWD_MINB : 1))
+__global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? GSB_BWD_MINB : 8) : 1))
     raster_bwd_kernel(RasterParams p) {
     constexpr int PPT = BX * BY;
     static_assert(!IL || PPT == 4, "interleaved layout: 4 pixels per thread");

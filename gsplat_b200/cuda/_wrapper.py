@@ -703,11 +703,16 @@ class _RasterizeToPixels(torch.autograd.Function):
         channels = colors.shape[-1]
         v_render_colors = v_render_colors.contiguous()
         v_render_alphas = v_render_alphas.contiguous()
-        v_means2d = torch.zeros_like(means2d)
-        v_conics = torch.zeros_like(conics)
-        v_colors = torch.zeros_like(colors)
-        v_opacities = torch.zeros_like(opacities)
-        v_means2d_abs = torch.zeros_like(means2d) if ctx.absgrad else None
+        # the kernel accumulates with atomics: all gradients live in one zeroed
+        # buffer (a single fill)
+        likes = [means2d, conics, colors, opacities] + ([means2d] if ctx.absgrad else [])
+        flat = torch.zeros(sum(t.numel() for t in likes), dtype=means2d.dtype, device=means2d.device)
+        views, off = [], 0
+        for t in likes:
+            views.append(flat[off:off + t.numel()].view(t.shape))
+            off += t.numel()
+        v_means2d, v_conics, v_colors, v_opacities = views[:4]
+        v_means2d_abs = views[4] if ctx.absgrad else None
         with torch.cuda.device(means2d.device):
             call("gsb_rasterize_bwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
                  ptr(opacities), ptr(backgrounds), ptr(masks), ctx.width, ctx.height,
@@ -790,6 +795,9 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
     def forward(ctx, means, quats, scales, opacities, sh, sh_degree, viewmats, Ks, width, height,
                 eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, camera_model,
                 isect_tiling):
+        # outputs without a gradient (ids, radii, depths, intersections) reach the
+        # backward as None instead of zero-filled tensors
+        ctx.set_materialize_grads(False)
         for name, t in (("means", means), ("quats", quats), ("scales", scales),
                         ("opacities", opacities), ("sh_coeffs", sh), ("viewmats", viewmats),
                         ("Ks", Ks)):
