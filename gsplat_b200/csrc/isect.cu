@@ -10,6 +10,8 @@
 // tile sets bit for bit. The reference evaluates the ellipse level set with the
 // hardware approximate logarithm (__logf); this implementation uses det_logf, a
 // portable logarithm accurate to ~1 ulp, as documented in detmath.h.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gsb_internal.h"
 #include "gsb_scan.cuh"
@@ -26,6 +28,10 @@ struct IsectParams {
     const float *conics;    // optional: AccuTile when conics and opacities are given
     const float *opacities; // optional
     uint32_t tile_size, tile_width, tile_height, tile_n_bits;
+    // 1 / tile_size when tile_size is a power of two: x / 2^k and x * 2^-k are
+    // the same correctly rounded value, so the multiplication is bit-identical
+    // to the division (0 otherwise)
+    float inv_tile_pow2;
     // packed only, optional: the splat count lives in device memory (nnz is then
     // the capacity of the arrays); lets the caller skip reading it back
     const int64_t *nnz_device;
@@ -49,6 +55,11 @@ struct EmitSink {
         ++cursor;
     }
 };
+
+// x / tile_size, correctly rounded.
+__device__ __forceinline__ float tile_div(const IsectParams &p, float x) {
+    return p.inv_tile_pow2 != 0.f ? DET_MUL(x, p.inv_tile_pow2) : DET_DIV(x, (float)p.tile_size);
+}
 
 struct LinePair {
     float lo, hi;
@@ -89,10 +100,10 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
     float amax_x = DET_SUB(my, bxc), amax_y = DET_SUB(mx, bya);
     const float ts = (float)p.tile_size;
     const int tw = (int)p.tile_width, th = (int)p.tile_height;
-    int rmin_x = max(0, min(tw, det_f2i_rz(DET_DIV(bmin_x, ts))));
-    int rmin_y = max(0, min(th, det_f2i_rz(DET_DIV(bmin_y, ts))));
-    int rmax_x = max(0, min(tw, det_f2i_rz(DET_ADD(DET_DIV(bmax_x, ts), 1.f))));
-    int rmax_y = max(0, min(th, det_f2i_rz(DET_ADD(DET_DIV(bmax_y, ts), 1.f))));
+    int rmin_x = max(0, min(tw, det_f2i_rz(tile_div(p, bmin_x))));
+    int rmin_y = max(0, min(th, det_f2i_rz(tile_div(p, bmin_y))));
+    int rmax_x = max(0, min(tw, det_f2i_rz(DET_ADD(tile_div(p, bmax_x), 1.f))));
+    int rmax_y = max(0, min(th, det_f2i_rz(DET_ADD(tile_div(p, bmax_y), 1.f))));
     const int y_span = rmax_y - rmin_y, x_span = rmax_x - rmin_x;
     if (y_span * x_span == 0) return 0;
     const bool is_y = y_span < x_span;
@@ -118,8 +129,8 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
                                                                     : det_fmin(cur_lo.lo, cur_hi.lo);
         const float emax = (min_line <= amax_y && amax_y < max_line) ? bmax_y
                                                                     : det_fmax(cur_lo.hi, cur_hi.hi);
-        const int v0 = max(rmin_y, min(rmax_y, det_f2i_rz(DET_DIV(emin, ts))));
-        const int v1 = min(rmax_y, max(rmin_y, det_f2i_rz(DET_ADD(DET_DIV(emax, ts), 1.f))));
+        const int v0 = max(rmin_y, min(rmax_y, det_f2i_rz(tile_div(p, emin))));
+        const int v1 = min(rmax_y, max(rmin_y, det_f2i_rz(DET_ADD(tile_div(p, emax), 1.f))));
         if (v1 > v0) {
             count += (uint32_t)(v1 - v0);
             if (EMIT) {
@@ -137,8 +148,8 @@ template <bool EMIT, class Sink>
 __device__ uint32_t aabb_tiles(const IsectParams &p, float mx, float my, int32_t rx, int32_t ry,
                                Sink *sink) {
     const float ts = (float)p.tile_size;
-    const float trx = DET_DIV((float)rx, ts), try_ = DET_DIV((float)ry, ts);
-    const float tx = DET_DIV(mx, ts), ty = DET_DIV(my, ts);
+    const float trx = tile_div(p, (float)rx), try_ = tile_div(p, (float)ry);
+    const float tx = tile_div(p, mx), ty = tile_div(p, my);
     const int tw = (int)p.tile_width, th = (int)p.tile_height;
     const int x0 = min(max(0, det_f2i_rz(floorf(DET_SUB(tx, trx)))), tw);
     const int y0 = min(max(0, det_f2i_rz(floorf(DET_SUB(ty, try_)))), th);
@@ -255,6 +266,9 @@ constexpr uint32_t kCtaBucketMax = 24576; // buckets of the shared-memory path (
 #define GSB_CTA_THREADS 1024
 #define GSB_CTAS_PER_SM 1
 #endif
+#ifndef GSB_CTA_MINB
+#define GSB_CTA_MINB 1
+#endif
 constexpr int kCtaThreads = GSB_CTA_THREADS;
 
 struct BucketPlan {
@@ -346,7 +360,7 @@ __global__ void __launch_bounds__(256) isect_count_tiles_kernel(IsectParams p, i
 
 // shared-memory shards: CTA c counts splats [c chunk, (c + 1) chunk) and writes
 // its histogram to column c of the bucket-major (bucket x G) matrix
-__global__ void __launch_bounds__(kCtaThreads) isect_count_cta_kernel(IsectParams p, uint32_t n_buckets,
+__global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_count_cta_kernel(IsectParams p, uint32_t n_buckets,
                                                                       int32_t *tiles_per_gauss,
                                                                       int32_t *matrix) {
     extern __shared__ int32_t hist[];
@@ -420,7 +434,7 @@ __global__ void __launch_bounds__(256) isect_bucket_emit_kernel(IsectParams p, u
     splat_tiles<true, BucketSink>(p, idx, &sink);
 }
 
-__global__ void __launch_bounds__(kCtaThreads) isect_emit_cta_kernel(IsectParams p, uint32_t n_buckets,
+__global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kernel(IsectParams p, uint32_t n_buckets,
                                                                      uint32_t n_isects, const int32_t *cursor,
                                                                      uint32_t *depth_out, int32_t *id_out) {
     extern __shared__ int32_t cur[];
@@ -486,16 +500,11 @@ template <int E> struct BitonicRegs {
 // One CTA per bucket: entries packed as (depth bits << 32 | splat index),
 // padded with all-ones to a power of two, sorted ascending.
 template <int E>
-__global__ void __launch_bounds__(1024)
-    bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
-                       const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
-                       uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
-                       int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
-    extern __shared__ __align__(16) uint64_t sk[];
-    const uint32_t b = blockIdx.x;
-    const int n = sizes[b];
-    if (n <= lo_size || n > hi_size) return; // another size class
-    const int start = starts[b];
+__device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n, int start,
+                                                const uint32_t *__restrict__ depth_in,
+                                                const int32_t *__restrict__ id_in, uint32_t n_tiles,
+                                                uint32_t tile_bits, int64_t *__restrict__ keys_out,
+                                                int32_t *__restrict__ ids_out) {
     const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
     if (n == 1) {
         if (threadIdx.x == 0) {
@@ -559,6 +568,24 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+template <int E>
+__global__ void __launch_bounds__(1024)
+    bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
+                       const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
+                       uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
+                       int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
+    extern __shared__ __align__(16) uint64_t sk[];
+    // CTA c sorts buckets c, c + grid, ...: the grid is one CTA per bucket for
+    // the class that holds most buckets, and a few CTAs per SM for the rare
+    // large buckets
+    for (uint32_t b = blockIdx.x; b < n_buckets; b += gridDim.x) {
+        const int n = sizes[b];
+        if (n <= lo_size || n > hi_size) continue; // another size class
+        sort_one_bucket<E>(sk, b, n, starts[b], depth_in, id_in, n_tiles, tile_bits, keys_out, ids_out);
+    }
+}
+
+
 static uint32_t bit_length(uint64_t v) {
     uint32_t b = 0;
     while (v) {
@@ -597,6 +624,7 @@ static int make_isect_params(IsectParams &p, int packed, int I, int N, int nnz,
     p.tile_width = tile_width;
     p.tile_height = tile_height;
     p.tile_n_bits = tile_bits;
+    p.inv_tile_pow2 = (tile_size & (tile_size - 1)) == 0 ? 1.f / (float)tile_size : 0.f;
     p.nnz_device = nullptr;
     return kOk;
 }
@@ -790,8 +818,12 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
             const size_t smem = (size_t)threads * E * sizeof(uint64_t);
             auto kern = E == 4 ? bucket_sort_kernel<4> : bucket_sort_kernel<16>;
             if (int e = set_cta_smem((const void *)kern, smem)) return e;
-            kern<<<grid, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
-                                                  (uint32_t)n_tiles, tb, lo, hi, isect_ids, flatten_ids);
+            // first class: one CTA per bucket; larger (rare) buckets: two CTAs per
+            // SM walking all buckets, instead of launching one CTA per bucket
+            const unsigned g = lo == 0 ? grid : (unsigned)std::min<uint64_t>(n_buckets, 2ull * device_sms());
+            kern<<<g, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
+                                               (uint32_t)n_buckets, (uint32_t)n_tiles, tb, lo, hi, isect_ids,
+                                               flatten_ids);
             if (int e = check_launch("bucket_sort_kernel")) return e;
         }
         lo = hi;

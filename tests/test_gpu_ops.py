@@ -263,7 +263,7 @@ def test_isect_aabb_batch_dims(batch):
 
 
 @pytest.mark.parametrize("packed", [False, True])
-@pytest.mark.parametrize("tile_size", [16, 8])
+@pytest.mark.parametrize("tile_size", [16, 8, 12])
 def test_isect_accutile_bit_exact_vs_oracle(packed, tile_size):
     d = _data.to(_data.scene(20000, seed=8, C=2, width=320, height=240, fx=260.0), DEV)
     out = project(d, packed=packed, calc=True)
