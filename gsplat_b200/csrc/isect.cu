@@ -460,6 +460,9 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
 }
 
 constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (128 KiB of shared memory)
+#ifndef GSB_BUCKET_E
+#define GSB_BUCKET_E 8 // entries per thread up to 4096-entry buckets
+#endif
 
 
 // Bitonic compare-exchange of entries held in registers. Entry index i =
@@ -486,11 +489,12 @@ template <int E> struct BitonicRegs {
 
     __device__ __forceinline__ void shfl_stage(uint32_t base, uint32_t k, uint32_t j) {
         const int lane_mask = (int)(j / E);
+        // base is a multiple of E <= j < k: bits j and k of base + e are those of
+        // base, so every entry of the thread keeps the same side
+        const bool keep_min = (((base & j) == 0) == ((base & k) == 0));
 #pragma unroll
         for (int e = 0; e < E; ++e) {
             const uint64_t other = __shfl_xor_sync(0xffffffffu, v[e], lane_mask);
-            const uint32_t i = base + e;
-            const bool keep_min = (((i & j) == 0) == ((i & k) == 0));
             const bool other_smaller = other < v[e];
             v[e] = (other_smaller == keep_min) ? other : v[e];
         }
@@ -813,10 +817,10 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
             const int cap = hi < max_count ? hi : max_count;
             int npad = 2;
             while (npad < cap) npad <<= 1;
-            const int E = hi <= 4096 ? 4 : 16;
+            const int E = hi <= 4096 ? GSB_BUCKET_E : 16;
             const int threads = npad / E < 32 ? 32 : npad / E;
             const size_t smem = (size_t)threads * E * sizeof(uint64_t);
-            auto kern = E == 4 ? bucket_sort_kernel<4> : bucket_sort_kernel<16>;
+            auto kern = E == 16 ? bucket_sort_kernel<16> : bucket_sort_kernel<GSB_BUCKET_E>;
             if (int e = set_cta_smem((const void *)kern, smem)) return e;
             // first class: one CTA per bucket; larger (rare) buckets: two CTAs per
             // SM walking all buckets, instead of launching one CTA per bucket
