@@ -36,8 +36,8 @@ LRS = {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacities": 5e-2, "sh": 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="gsb", choices=["gsb", "reference"])
     ap.add_argument("--n", type=int, default=1_000_000, help="Gaussians per rank")
     ap.add_argument("--dense", action="store_true", help="packed=False (trainer default)")

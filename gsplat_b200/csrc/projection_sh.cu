@@ -55,6 +55,28 @@ __device__ __forceinline__ void load_coefs(const float *coef, bool vec, float *c
     }
 }
 
+// Calls fn(f, coef[f]) for the (D + 1)^2 * 3 coefficients of one Gaussian in
+// order, reading them with 128-bit loads when the row is 16-byte aligned; the
+// loop is fully unrolled, so f is a compile-time index in fn.
+template <int D, class Fn>
+__device__ __forceinline__ void for_each_coef(const float *coef, bool vec, Fn fn) {
+    constexpr int NC = (D + 1) * (D + 1) * 3;
+    if (vec && NC % 4 == 0) {
+        const float4 *c4 = reinterpret_cast<const float4 *>(coef);
+#pragma unroll
+        for (int i = 0; i < NC / 4; ++i) {
+            const float4 v = __ldg(c4 + i);
+            fn(4 * i + 0, v.x);
+            fn(4 * i + 1, v.y);
+            fn(4 * i + 2, v.z);
+            fn(4 * i + 3, v.w);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NC; ++i) fn(i, __ldg(coef + i));
+    }
+}
+
 // SH colour of one (camera, Gaussian) pair; returns the pre-clamp value in raw[].
 template <int D>
 __device__ __forceinline__ void sh_color(const float *coef, bool vec, const float dir[3], float raw[3]) {
@@ -190,7 +212,11 @@ struct FusedBwdParams {
 constexpr int kFusedBwdThreads = 128;
 
 template <int D>
-__global__ void __launch_bounds__(kFusedBwdThreads, 5) fused_bwd_kernel(FusedBwdParams q) {
+#ifndef GSB_FUSED_BWD_MINB
+#define GSB_FUSED_BWD_MINB 5
+#endif
+__global__ void __launch_bounds__(kFusedBwdThreads, (D >= 4 ? 3 : (D == 1 ? 4 : GSB_FUSED_BWD_MINB)))
+    fused_bwd_kernel(FusedBwdParams q) {
     constexpr int NB = (D + 1) * (D + 1);
     // v_sh rows are accumulated in shared memory (row stride K*3 rounded up to an
     // odd count, so the lanes of a warp hit distinct banks) and stored to HBM
@@ -274,12 +300,8 @@ __global__ void __launch_bounds__(kFusedBwdThreads, 5) fused_bwd_kernel(FusedBwd
             float Y[NB];
             sh_eval<D>(x, y, z, Y);
             float raw[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-            for (int k = 0; k < NB; ++k) {
-                raw[0] += Y[k] * coef[k * 3 + 0];
-                raw[1] += Y[k] * coef[k * 3 + 1];
-                raw[2] += Y[k] * coef[k * 3 + 2];
-            }
+            // coefficient f = 3 k + ch, streamed in 128-bit pieces when aligned
+            for_each_coef<D>(coef, q.f.sh_vec, [&](int f, float cf) { raw[f % 3] += Y[f / 3] * cf; });
             float vc[3];
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) vc[ch] = (raw[ch] + 0.5f >= 0.f) ? q.v_colors[e * 3 + ch] : 0.f;
@@ -292,8 +314,8 @@ __global__ void __launch_bounds__(kFusedBwdThreads, 5) fused_bwd_kernel(FusedBwd
             if (D > 0) {
                 float w[NB];
 #pragma unroll
-                for (int k = 0; k < NB; ++k)
-                    w[k] = coef[k * 3] * vc[0] + coef[k * 3 + 1] * vc[1] + coef[k * 3 + 2] * vc[2];
+                for (int k = 0; k < NB; ++k) w[k] = 0.f;
+                for_each_coef<D>(coef, q.f.sh_vec, [&](int f, float cf) { w[f / 3] += cf * vc[f % 3]; });
                 float gn[3];
                 sh_grad_dot<D>(x, y, z, w, gn);
                 const float dd = gn[0] * x + gn[1] * y + gn[2] * z;
