@@ -462,9 +462,13 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
     const size_t img_pix = (size_t)image * p.H * p.W;
     const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
 
-    float px[PPT], py[PPT], T[PPT], Tf[PPT], buf[PPT][CDIM], vc[PPT][CDIM], va[PPT], bgd[PPT];
+    // Per pixel: T (recovered back to front), the colour buffer, the upstream
+    // colour gradient, tv = T_final (v_alpha - bg . v_colour) (the only way the
+    // final transmittance, the alpha gradient and the background enter the
+    // gradients) and the last contributor (-1 outside the image: every splat
+    // index is larger, so those pixels are skipped).
+    float px[PPT], py[PPT], T[PPT], buf[PPT][CDIM], vc[PPT][CDIM], tv[PPT];
     int32_t bin_final[PPT];
-    bool inside[PPT];
     bool has = false;
     int32_t my_max = -1;
     float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
@@ -481,23 +485,23 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
             lx = (threadIdx.x % tpr) * BX + k % BX;
         }
         const uint32_t i = ty0 + ly, j = tx0 + lx;
-        inside[k] = ly < p.tile_size && i < p.H && j < p.W;
+        const bool inside = ly < p.tile_size && i < p.H && j < p.W;
         px[k] = (float)j + 0.5f;
         py[k] = (float)i + 0.5f;
-        const size_t pix = img_pix + (inside[k] ? i * p.W + j : 0);
-        Tf[k] = inside[k] ? 1.f - p.alphas[pix] : 0.f;
-        T[k] = Tf[k];
-        bin_final[k] = inside[k] ? p.last_ids[pix] : -1;
-        va[k] = (inside[k] && p.first_chunk) ? p.v_alphas[pix] : 0.f;
+        const size_t pix = img_pix + (inside ? i * p.W + j : 0);
+        const float Tf = inside ? 1.f - p.alphas[pix] : 0.f;
+        T[k] = Tf;
+        bin_final[k] = inside ? p.last_ids[pix] : -1;
         float dotbg = 0.f;
 #pragma unroll
         for (int c = 0; c < CDIM; ++c) {
-            vc[k][c] = inside[k] ? p.v_renders[pix * p.cstride + p.coff + c] : 0.f;
+            vc[k][c] = inside ? p.v_renders[pix * p.cstride + p.coff + c] : 0.f;
             buf[k][c] = 0.f;
             if (bg) dotbg += bg[c] * vc[k][c];
         }
-        bgd[k] = dotbg;
-        if (inside[k]) {
+        const float va = (inside && p.first_chunk) ? p.v_alphas[pix] : 0.f;
+        tv[k] = Tf * (va - dotbg);
+        if (inside) {
             has = true;
             my_max = max(my_max, bin_final[k]);
             rx0 = fminf(rx0, px[k]);
@@ -554,7 +558,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
             for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
-                if (!inside[k] || gidx > bin_final[k]) continue;
+                if (gidx > bin_final[k]) continue;
                 const PairEval e = eval_pair(r, px[k], py[k]);
                 if (!e.keep) continue;
                 any = true;
@@ -572,8 +576,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
                     acc[c] += fac * vc[k][c];
                     v_alpha += (col[c] * T[k] - buf[k][c] * ra) * vc[k][c];
                 }
-                v_alpha += Tf[k] * ra * va[k];
-                if (bg) v_alpha += -Tf[k] * ra * bgd[k];
+                v_alpha += ra * tv[k];
                 if (r.o * e.vis <= kMaxAlpha) {
                     const float v_sigma = -r.o * e.vis * v_alpha;
                     acc[CDIM + 0] += 0.5f * v_sigma * e.dx * e.dx;
