@@ -181,5 +181,25 @@ def check_cuda(name: str, t: Optional[torch.Tensor]) -> None:
         raise RuntimeError(f"{name} must be contiguous")
 
 
-def stream_of(t: torch.Tensor):
-    return torch.cuda.current_stream(t.device).cuda_stream
+def stream_of(t: torch.Tensor) -> int:
+    """Raw handle of the current CUDA stream of t's device."""
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
+
+
+class _NoGuard:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_GUARD = _NoGuard()
+
+
+def device_guard(device: torch.device):
+    """torch.cuda.device(device), skipped when that device is already current
+    (the common case: it saves a device switch and restore per call)."""
+    if device.type == "cuda" and device.index == torch.cuda.current_device():
+        return _NO_GUARD
+    return torch.cuda.device(device)

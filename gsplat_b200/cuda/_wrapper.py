@@ -18,7 +18,7 @@ from torch import Tensor
 from typing_extensions import Literal
 
 from . import _backend as _B
-from ._backend import call, check_cuda, ptr, stream_of
+from ._backend import call, check_cuda, device_guard, ptr, stream_of
 
 CameraModel = Literal["pinhole", "ortho", "fisheye", "ftheta", "lidar"]
 _CAMERA_IDS = {"pinhole": 0, "ortho": 1}
@@ -78,7 +78,7 @@ def adam(
         check_cuda(name, t)
     N = param.size(0)
     D = param.numel() // N if N > 0 else 0
-    with torch.cuda.device(param.device):
+    with device_guard(param.device):
         call("gsb_adam", ptr(param), ptr(param_grad), ptr(exp_avg), ptr(exp_avg_sq), ptr(valid),
              N, D, lr, b1, b2, eps, stream_of(param))
 
@@ -97,9 +97,8 @@ def adam_multi(groups, valid: Optional[Tensor], b1: float, b2: float) -> None:
         arr[i] = _B.GsbAdamGroup(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), p.numel(),
                                  p.numel() // N if N > 0 else 1, lr, eps)
     check_cuda("valid", valid)
-    with torch.cuda.device(dev):
-        call("gsb_adam_multi", len(groups), arr, ptr(valid), b1, b2,
-             torch.cuda.current_stream(dev).cuda_stream)
+    with device_guard(dev):
+        call("gsb_adam_multi", len(groups), arr, ptr(valid), b1, b2, stream_of(groups[0][0]))
 
 
 # ---------------------------------------------------------------------------
@@ -134,7 +133,7 @@ class _SphericalHarmonics(torch.autograd.Function):
         n = dirs.numel() // 3
         K = coeffs.shape[-2]
         colors = torch.empty(dirs.shape, dtype=dirs.dtype, device=dirs.device)
-        with torch.cuda.device(dirs.device):
+        with device_guard(dirs.device):
             call("gsb_spherical_harmonics_fwd", sh_degree, n, K, ptr(dirs), ptr(coeffs), ptr(masks),
                  ptr(colors), stream_of(dirs))
         ctx.save_for_backward(dirs, coeffs, masks)
@@ -150,7 +149,7 @@ class _SphericalHarmonics(torch.autograd.Function):
         K = coeffs.shape[-2]
         v_coeffs = torch.empty_like(coeffs)
         v_dirs = torch.empty_like(dirs) if compute_v_dirs else None
-        with torch.cuda.device(dirs.device):
+        with device_guard(dirs.device):
             call("gsb_spherical_harmonics_bwd", ctx.sh_degree, n, K, ptr(dirs), ptr(coeffs),
                  ptr(masks), ptr(v_colors), ptr(v_coeffs), ptr(v_dirs), stream_of(dirs))
         return None, v_dirs, v_coeffs, None
@@ -242,7 +241,7 @@ class _FullyFusedProjection(torch.autograd.Function):
         depths = torch.empty(batch_dims + (C, N), dtype=means.dtype, device=dev)
         conics = torch.empty(batch_dims + (C, N, 3), dtype=means.dtype, device=dev)
         comps = torch.zeros(batch_dims + (C, N), dtype=means.dtype, device=dev) if calc_compensations else None
-        with torch.cuda.device(dev):
+        with device_guard(dev):
             call("gsb_projection_fused_fwd", B, C, N, ptr(means), ptr(covars), ptr(quats),
                  ptr(scales), ptr(opacities), ptr(viewmats), ptr(Ks), width, height, eps2d,
                  near_plane, far_plane, radius_clip, int(calc_compensations), camera_model,
@@ -274,7 +273,7 @@ class _FullyFusedProjection(torch.autograd.Function):
         v_quats = torch.empty_like(quats) if covars is None else None
         v_scales = torch.empty_like(scales) if covars is None else None
         v_viewmats = torch.zeros_like(viewmats) if ctx.needs_input_grad[4] else None
-        with torch.cuda.device(means.device):
+        with device_guard(means.device):
             call("gsb_projection_fused_bwd", B, C, N, ptr(means), ptr(covars), ptr(quats),
                  ptr(scales), ptr(viewmats), ptr(Ks), ctx.width, ctx.height, ctx.eps2d,
                  ctx.camera_model, ptr(radii), ptr(conics), ptr(comps), ptr(v_means2d),
@@ -315,7 +314,7 @@ class _FullyFusedProjectionPacked(torch.autograd.Function):
         common = (B, C, N, ptr(means), ptr(covars), ptr(quats), ptr(scales), ptr(opacities),
                   ptr(viewmats), ptr(Ks), width, height, eps2d, near_plane, far_plane, radius_clip,
                   int(calc_compensations), camera_model)
-        with torch.cuda.device(dev):
+        with device_guard(dev):
             stream = stream_of(means)
             nblocks = _B.lib().gsb_projection_packed_blocks(N)
             block_cnts = torch.empty(B * C * nblocks, dtype=torch.int32, device=dev)
@@ -376,7 +375,7 @@ class _FullyFusedProjectionPacked(torch.autograd.Function):
         v_quats = grad_buf(quats, 4) if covars is None else None
         v_scales = grad_buf(scales, 3) if covars is None else None
         v_viewmats = torch.zeros_like(viewmats) if ctx.needs_input_grad[4] else None
-        with torch.cuda.device(means.device):
+        with device_guard(means.device):
             call("gsb_projection_packed_bwd", B, C, N, nnz, ptr(means), ptr(covars), ptr(quats),
                  ptr(scales), ptr(viewmats), ptr(Ks), ctx.width, ctx.height, ctx.eps2d,
                  ctx.camera_model, ptr(batch_ids), ptr(camera_ids), ptr(gaussian_ids), ptr(conics),
@@ -501,7 +500,7 @@ def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sor
     if (conics is None) != (opacities is None):
         conics, opacities = None, None  # AccuTile needs both; AABB otherwise
     n_buckets = I * tile_width * tile_height
-    with torch.cuda.device(dev):
+    with device_guard(dev):
         stream = stream_of(means2d)
         args = (int(packed), I, N, nnz, ptr(image_ids), ptr(means2d), ptr(radii), ptr(depths),
                 ptr(conics), ptr(opacities), tile_size, tile_width, tile_height)
@@ -592,7 +591,7 @@ def isect_offset_encode(isect_ids: Tensor, n_images: int, tile_width: int, tile_
     check_cuda("isect_ids", isect_ids)
     offsets = torch.empty((n_images, tile_height, tile_width), dtype=torch.int32,
                           device=isect_ids.device)
-    with torch.cuda.device(isect_ids.device):
+    with device_guard(isect_ids.device):
         call("gsb_isect_offset_encode", ptr(isect_ids), isect_ids.numel(), n_images, tile_width,
              tile_height, ptr(offsets), stream_of(isect_ids))
     return offsets
@@ -680,7 +679,7 @@ class _RasterizeToPixels(torch.autograd.Function):
         renders = torch.empty(image_dims + (height, width, channels), dtype=torch.float32, device=dev)
         alphas = torch.empty(image_dims + (height, width, 1), dtype=torch.float32, device=dev)
         last_ids = torch.empty(image_dims + (height, width), dtype=torch.int32, device=dev)
-        with torch.cuda.device(dev):
+        with device_guard(dev):
             call("gsb_rasterize_fwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
                  ptr(opacities), ptr(backgrounds), ptr(masks), width, height, tile_size, tw, th,
                  ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(), ptr(renders),
@@ -713,7 +712,7 @@ class _RasterizeToPixels(torch.autograd.Function):
             off += t.numel()
         v_means2d, v_conics, v_colors, v_opacities = views[:4]
         v_means2d_abs = views[4] if ctx.absgrad else None
-        with torch.cuda.device(means2d.device):
+        with device_guard(means2d.device):
             call("gsb_rasterize_bwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
                  ptr(opacities), ptr(backgrounds), ptr(masks), ctx.width, ctx.height,
                  ctx.tile_size, tw, th, ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(),
@@ -751,6 +750,7 @@ def fully_fused_projection_sh(
     calc_compensations: bool = False,
     camera_model: CameraModel = "pinhole",
     isect_tiling: Optional[Tuple[int, int, int]] = None,
+    defer_count: bool = False,
 ) -> Tuple[Tensor, ...]:
     """Projection, view-dependent SH colour and opacity compensation in one op.
 
@@ -770,6 +770,11 @@ def fully_fused_projection_sh(
     appends (tiles_per_gauss, isect_ids, flatten_ids, isect_offsets [B*C, th,
     tw]). The splat count then travels to the host together with the
     intersection sizes in one read instead of two.
+
+    With ``packed`` and ``defer_count`` (and no ``isect_tiling``) the packed
+    outputs keep B*C*N rows of capacity, their first nnz rows valid, and the
+    device-side count ``nnz`` (int64 [1]) is appended: the caller reads it
+    together with whatever else it needs from the device.
     """
     batch_dims = means.shape[:-2]
     N = means.shape[-2]
@@ -787,14 +792,14 @@ def fully_fused_projection_sh(
         means.contiguous(), quats.contiguous(), scales.contiguous(), opacities.contiguous(),
         sh_coeffs.contiguous(), sh_degree, viewmats.contiguous(), Ks.contiguous(), width, height,
         eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, cam,
-        isect_tiling if packed else None)
+        isect_tiling if packed else None, bool(packed and defer_count and isect_tiling is None))
 
 
 class _FullyFusedProjectionSH(torch.autograd.Function):
     @staticmethod
     def forward(ctx, means, quats, scales, opacities, sh, sh_degree, viewmats, Ks, width, height,
                 eps2d, near_plane, far_plane, radius_clip, packed, calc_compensations, camera_model,
-                isect_tiling):
+                isect_tiling, defer_count):
         # outputs without a gradient (ids, radii, depths, intersections) reach the
         # backward as None instead of zero-filled tensors
         ctx.set_materialize_grads(False)
@@ -812,7 +817,7 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
         shared = (B, C, N, ptr(means), ptr(quats), ptr(scales), ptr(opacities), ptr(sh), K,
                   sh_degree, ptr(viewmats), ptr(Ks), width, height, eps2d, near_plane, far_plane,
                   radius_clip, int(calc_compensations), camera_model)
-        with torch.cuda.device(dev):
+        with device_guard(dev):
             stream = stream_of(means)
             if not packed:
                 radii = torch.empty(batch_dims + (C, N, 2), dtype=torch.int32, device=dev)
@@ -835,7 +840,7 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                      near_plane, far_plane, radius_clip, int(calc_compensations), camera_model,
                      ptr(block_cnts), ptr(vis_bits), stream)
                 block_accum = _scan_i32(block_cnts)
-                deferred = isect_tiling is not None and block_accum.numel() > 0
+                deferred = (isect_tiling is not None or defer_count) and block_accum.numel() > 0
                 if deferred:
                     # capacity rows; the count stays on the device until the
                     # intersection sizes are read
@@ -879,6 +884,9 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                         tiles_per_gauss = tiles_per_gauss[:nnz]
                     isect_offsets = isect[2].view(I, tile_height, tile_width)
                     outs = outs + (tiles_per_gauss, isect[0], isect[1], isect_offsets)
+                elif defer_count:
+                    nnz_dev = block_accum[-1:] if deferred else torch.zeros(1, dtype=torch.int64, device=dev)
+                    outs = outs + (nnz_dev,)
                 (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics, comps,
                  colors, opac_out) = outs[:11]
                 ctx.mark_non_differentiable(batch_ids, camera_ids, gaussian_ids, indptr, radii, *outs[11:])
@@ -913,7 +921,7 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
         v_scales = torch.empty_like(scales)
         v_opacities = torch.empty_like(opacities)
         v_sh = torch.empty_like(sh)
-        with torch.cuda.device(means.device):
+        with device_guard(means.device):
             call("gsb_projection_sh_bwd", B, C, N, int(packed), ptr(means), ptr(quats), ptr(scales),
                  ptr(opacities), ptr(sh), K, deg, ptr(viewmats), ptr(Ks), width, height, eps2d,
                  int(calc), cam, ptr(pair_index), ptr(radii), ptr(conics), ptr(comps),
@@ -921,4 +929,4 @@ class _FullyFusedProjectionSH(torch.autograd.Function):
                  ptr(v_opac), ptr(v_means), ptr(v_quats), ptr(v_scales), ptr(v_opacities),
                  ptr(v_sh), stream_of(means))
         return (v_means, v_quats, v_scales, v_opacities, v_sh, None, None, None, None, None, None,
-                None, None, None, None, None, None, None)
+                None, None, None, None, None, None, None, None)

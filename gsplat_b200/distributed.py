@@ -105,6 +105,68 @@ def all_to_all_tensor_list(world_size: int, tensor_list: List[Tensor], splits: L
     return [o.reshape(-1, *t.shape[1:]) for o, t in zip(out, tensor_list)]
 
 
+class _ExchangeRows(torch.autograd.Function):
+    """One all_to_all_single of a row-packed buffer: float columns (differentiable)
+    followed by int32 columns bit-cast to float32 (not differentiable). The
+    backward sends the float-column gradients back with the splits swapped."""
+
+    @staticmethod
+    def forward(ctx, send_splits, recv_splits, n_float_cols, buf):
+        out = torch.empty((sum(recv_splits), buf.shape[1]), dtype=buf.dtype, device=buf.device)
+        dist.all_to_all_single(out, buf, recv_splits, send_splits)
+        ctx.splits = (send_splits, recv_splits)
+        ctx.nf = n_float_cols
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out):
+        send_splits, recv_splits = ctx.splits
+        g = g_out[:, :ctx.nf].contiguous()
+        g_in = torch.empty((sum(send_splits), ctx.nf), dtype=g.dtype, device=g.device)
+        dist.all_to_all_single(g_in, g, send_splits, recv_splits)
+        pad = g_out.shape[1] - ctx.nf
+        if pad:
+            g_in = torch.cat([g_in, g_in.new_zeros((g_in.shape[0], pad))], dim=1)
+        return None, None, None, g_in
+
+
+def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], send_splits: List[int],
+                  recv_splits: List[int]):
+    """Sends rows [sum(send_splits[:r]), sum(send_splits[:r+1])) of every listed
+    tensor to rank r and receives recv_splits[r] rows from it, with ONE
+    all-to-all for all tensors (the float32 tensors keep their autograd graph;
+    int32 / int64 tensors travel bit-cast inside the same buffer). The counts are
+    host lists, so no collective or host read happens here besides the data
+    exchange itself."""
+    n = sum(send_splits)
+    cols, float_meta, int_meta = [], [], []
+    for t in floats:
+        assert t.dtype == torch.float32 and t.shape[0] == n
+        c = t.reshape(n, -1)
+        float_meta.append((c.shape[1], t.shape[1:]))
+        cols.append(c)
+    nf = sum(w for w, _ in float_meta)
+    for t in ints:
+        assert t.shape[0] == n and t.dtype in (torch.int32, torch.int64)
+        c = t.contiguous().reshape(n, -1).view(torch.int32).view(torch.float32)
+        int_meta.append((c.shape[1], t.dtype, t.shape[1:]))
+        cols.append(c)
+    buf = torch.cat(cols, dim=1) if len(cols) > 1 else cols[0].contiguous()
+    out = _ExchangeRows.apply(list(send_splits), list(recv_splits), nf, buf)
+    m = out.shape[0]
+    res_f, res_i, off = [], [], 0
+    for w, shape in float_meta:
+        res_f.append(out[:, off:off + w].reshape(m, *shape))
+        off += w
+    for w, dtype, shape in int_meta:
+        piece = out[:, off:off + w].detach().contiguous().view(torch.int32)
+        if dtype == torch.int64:
+            piece = piece.view(torch.int64)
+        res_i.append(piece.reshape(m, *shape))
+        off += w
+    return res_f, res_i
+
+
 def cli(fn: Callable, args, verbose: bool = False, backend: str = "nccl") -> bool:
     """Runs ``fn(local_rank, world_rank, world_size, args)`` in one process per GPU
     (reference distributed.py:287-375). Under torchrun / MPI launchers the ranks

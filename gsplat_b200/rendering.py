@@ -34,6 +34,7 @@ from .distributed import (
     all_gather_tensor_list,
     all_to_all_int32,
     all_to_all_tensor_list,
+    exchange_rows,
 )
 
 RenderMode = Literal["RGB", "d", "Ed", "D", "ED", "RGB-d", "RGB-Ed", "RGB+D", "RGB+ED"]
@@ -250,7 +251,11 @@ def rasterization(
         assert batch_dims == (), "Distributed mode does not support batch dimensions"
         world_rank = torch.distributed.get_rank()
         world_size = torch.distributed.get_world_size()
-        N_world = all_gather_int32(world_size, N, device=device)
+        # Gaussian counts of all ranks, kept on the device (read only by the
+        # paths that need host split sizes)
+        N_world_dev = torch.empty(world_size, dtype=torch.int64, device=device)
+        torch.distributed.all_gather_into_tensor(
+            N_world_dev, torch.full((1,), N, dtype=torch.int64, device=device))
         C_world = [C] * world_size
         viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
         C = len(viewmats)
@@ -271,24 +276,31 @@ def rasterization(
         and not viewmats.requires_grad
     )
     compensations = None
+    nnz_device = None  # device splat count of capacity-sized packed outputs (distributed)
     tile_width = math.ceil(width / float(tile_size))
     tile_height = math.ceil(height / float(tile_size))
     isect = None  # (tiles_per_gauss, isect_ids, flatten_ids, isect_offsets) when done by the projection
     if use_fused:
         # packed and not distributed: the projection op also intersects the tiles,
         # so the splat count and the intersection sizes reach the host in one read
+        # distributed + packed: the splat count stays on the device until it is read
+        # together with the exchange counts
         fuse_isect = packed and not distributed
+        defer_count = packed and distributed
         proj = fully_fused_projection_sh(
             means, quats, scales, opacities, colors, sh_degree, viewmats, Ks, width, height,
             eps2d=eps2d, near_plane=near_plane, far_plane=far_plane, radius_clip=radius_clip,
             packed=packed, calc_compensations=(rasterize_mode == "antialiased"),
             camera_model=camera_model,
-            isect_tiling=(tile_size, tile_width, tile_height) if fuse_isect else None)
+            isect_tiling=(tile_size, tile_width, tile_height) if fuse_isect else None,
+            defer_count=defer_count)
         if packed:
             (batch_ids, camera_ids, gaussian_ids, indptr, radii, means2d, depths, conics,
              _, proj_features, opacities) = proj[:11]
             if fuse_isect:
                 isect = proj[11:]
+            if defer_count:
+                nnz_device = proj[11]
             image_ids = camera_ids if B == 1 else batch_ids * C + camera_ids
         else:
             radii, means2d, depths, conics, _, proj_features, opacities = proj
@@ -368,7 +380,42 @@ def rasterization(
         if feature_list:
             proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
 
-    if distributed:
+    if distributed and packed and nnz_device is not None:
+        # Same exchange as the reference (below), with one host read and one
+        # all-to-all: packed rows are ordered by camera, so the rows for rank r
+        # are indptr[cstart[r]] .. indptr[cstart[r + 1]].
+        cstart = [sum(C_world[:r]) for r in range(world_size + 1)]
+        bounds = indptr.index_select(0, torch.tensor(cstart, device=device)).to(torch.int64)
+        send_cnt = bounds[1:] - bounds[:-1]
+        recv_cnt = torch.empty_like(send_cnt)
+        torch.distributed.all_to_all_single(recv_cnt, send_cnt)
+        sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
+        send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
+        (batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics, opacities) = (
+            t[:nnz] for t in (batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
+                              opacities))
+        if proj_features is not None:
+            proj_features = proj_features[:nnz]
+        # camera ids local to the destination rank; gaussian ids shifted by the
+        # destination's Gaussian offset (reference rendering.py:944-959)
+        if all(c == C_world[0] for c in C_world):
+            dst = torch.div(camera_ids, C_world[0], rounding_mode="floor")
+        else:
+            dst = torch.bucketize(camera_ids, torch.tensor(cstart[1:], device=device), right=True)
+        c_off = torch.tensor(cstart[:-1], device=device, dtype=camera_ids.dtype)
+        n_off = torch.cumsum(N_world_dev, 0) - N_world_dev
+        floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
+        ints = [radii, camera_ids - c_off[dst], gaussian_ids + n_off[dst]]
+        floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits)
+        means2d, depths, conics, opacities = floats[:4]
+        if proj_features is not None:
+            proj_features = floats[4]
+        radii, camera_ids, gaussian_ids = ints
+        C = C_world[world_rank]
+        image_ids = camera_ids
+        I = B * C
+    elif distributed:
+        N_world = N_world_dev.tolist()
         if packed:
             cnts = torch.bincount(camera_ids, minlength=C)
             cnts = cnts.split(C_world, dim=0)

@@ -131,3 +131,35 @@ def test_failed_rank_is_detected_on_host():
         p.join(timeout=60)
     assert results[1] is not None and "rank 1 leaves" in results[1]
     assert results[0] is None, results[0]
+
+
+def _exchange_rows(rank, world):
+    from gsplat_b200.distributed import exchange_rows
+
+    # rank 0 has 3 rows (1 to itself, 2 to rank 1); rank 1 has 2 rows (2 to rank 0)
+    send = [1, 2] if rank == 0 else [2, 0]
+    recv = [1, 2] if rank == 0 else [2, 0]
+    n = sum(send)
+    a = (torch.arange(n * 2, dtype=torch.float32).reshape(n, 2) + 100 * rank).requires_grad_(True)
+    b = (torch.arange(n, dtype=torch.float32) + 0.5 + 100 * rank).requires_grad_(True)
+    ids32 = torch.arange(n, dtype=torch.int32).reshape(n, 1).repeat(1, 2) + 1000 * rank
+    ids64 = torch.arange(n, dtype=torch.int64) + (1 << 40) + rank
+    (fa, fb), (i32, i64) = exchange_rows(world, [a, b], [ids32, ids64], send, recv)
+    if rank == 0:
+        assert fa[:, 0].tolist() == [0.0, 100.0, 102.0] and fb.tolist() == [0.5, 100.5, 101.5]
+        assert i32[:, 0].tolist() == [0, 1000, 1001] and i64.tolist() == [1 << 40, (1 << 40) + 1, (1 << 40) + 2]
+    else:
+        assert fa[:, 0].tolist() == [2.0, 4.0] and fb.tolist() == [1.5, 2.5]
+        assert i32[:, 1].tolist() == [1, 2] and i64.tolist() == [(1 << 40) + 1, (1 << 40) + 2]
+    assert i32.dtype == torch.int32 and i64.dtype == torch.int64
+    # gradients travel back: d(sum(w * fa) + sum(fb)) with w = row position + 1
+    w = torch.arange(fa.shape[0], dtype=torch.float32)[:, None] + 1.0
+    ((fa * w).sum() + (3 * fb).sum()).backward()
+    if rank == 0:
+        assert a.grad[:, 0].tolist() == [1.0, 1.0, 2.0] and b.grad.tolist() == [3.0, 3.0, 3.0]
+    else:
+        assert a.grad[:, 1].tolist() == [2.0, 3.0] and b.grad.tolist() == [3.0, 3.0]
+
+
+def test_exchange_rows_world2_gloo():
+    run(_exchange_rows)

@@ -1,0 +1,105 @@
+"""Gaussian-sharded rasterization on two GPUs (NCCL, one process per GPU)
+against a single-process render of the gathered scene: every rank renders its
+own camera from all Gaussians through the packed all-to-all exchange; images and
+the gradients of the rank's own Gaussians must match the single-GPU pipeline
+(reference tests/_test_distributed.py runs the same comparison). Skipped with
+fewer than two GPUs."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _scene(rank, dev, N=20000):
+    g = torch.Generator().manual_seed(50 + rank)
+    means = torch.empty(N, 3)
+    means[:, 0].uniform_(-3, 3, generator=g)
+    means[:, 1].uniform_(-3, 3, generator=g)
+    means[:, 2].uniform_(3, 9, generator=g)
+    means[:, 0] += 3.0 * (rank - 0.5)  # the two shards overlap in the middle
+    quats = torch.randn(N, 4, generator=g)
+    quats = quats / quats.norm(dim=-1, keepdim=True)
+    scales = torch.exp(torch.randn(N, 3, generator=g) * 0.4 - 3.0)
+    opac = torch.sigmoid(torch.randn(N, generator=g))
+    sh = torch.randn(N, 16, 3, generator=g) * 0.1
+    sh[:, 0] += 0.5
+    vm = torch.eye(4)[None].clone()
+    vm[0, 0, 3] = -1.5 * (rank - 0.5)
+    K = torch.tensor([[[260.0, 0.0, 160.0], [0.0, 260.0, 120.0], [0.0, 0.0, 1.0]]])
+    return [t.to(dev) for t in (means, quats, scales, opac, sh, vm, K)]
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        import gsplat_b200
+
+        W, H = 320, 240
+        mine = _scene(rank, dev)
+        params = [t.clone().requires_grad_(True) for t in mine[:5]]
+        vm, K = mine[5], mine[6]
+        G = torch.randn((1, H, W, 3), generator=torch.Generator().manual_seed(7 + rank)).to(dev)
+        rc, ra, _ = gsplat_b200.rasterization(*params, vm, K, W, H, sh_degree=3, packed=True,
+                                              distributed=True)
+        (rc * G).sum().backward()
+
+        # single-process reference: all Gaussians, both cameras, summed loss
+        scenes = [_scene(r, dev) for r in range(world)]
+        full = [torch.cat([s[i] for s in scenes]).requires_grad_(True) for i in range(5)]
+        loss = 0.0
+        ref_img = None
+        for r in range(world):
+            Gr = torch.randn((1, H, W, 3), generator=torch.Generator().manual_seed(7 + r)).to(dev)
+            img, _, _ = gsplat_b200.rasterization(*full, scenes[r][5], scenes[r][6], W, H, sh_degree=3,
+                                                  packed=True)
+            loss = loss + (img * Gr).sum()
+            if r == rank:
+                ref_img = img.detach()
+        loss.backward()
+        torch.testing.assert_close(rc.detach(), ref_img, rtol=1e-4, atol=1e-5)
+        n = mine[0].shape[0]
+        for p, f in zip(params, full):
+            torch.testing.assert_close(p.grad, f.grad[rank * n:(rank + 1) * n], rtol=2e-3, atol=1e-5)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, None))
+    except Exception:  # report to the parent
+        q.put((rank, traceback.format_exc()))
+
+
+def test_distributed_packed_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = torch.multiprocessing.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    errors = [e for _, e in results if e]
+    assert not errors, errors[0]
