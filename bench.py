@@ -186,9 +186,9 @@ def train_step(params, opt, viewmat, K, W, H, G, Ga, distributed=False):
     vis = torch.zeros(n, dtype=torch.bool, device=render.device)
     gids = meta["gaussian_ids"]
     if distributed:
-        # only the local Gaussians' gradients matter; visibility of the local shard
-        vis = torch.zeros(n, dtype=torch.bool, device=render.device)
-        vis |= params["means"].grad.abs().sum(-1) > 0
+        # the local shard's Gaussians that reached any rank's image: those with a
+        # gradient (the packed ids after the exchange are the received splats')
+        vis = params["means"].grad.ne(0).any(-1)
     else:
         vis.index_fill_(0, gids, True)
     opt.step(vis)

@@ -9,7 +9,8 @@ The process group is NCCL on GPUs (one process per GPU); the same code runs on
 ``gloo`` for CPU tests.
 """
 
-from typing import Callable, List, Optional, Union
+import math
+from typing import Callable, List, Optional, Tuple, Union
 
 import torch
 import torch.distributed as dist
@@ -105,29 +106,87 @@ def all_to_all_tensor_list(world_size: int, tensor_list: List[Tensor], splits: L
     return [o.reshape(-1, *t.shape[1:]) for o, t in zip(out, tensor_list)]
 
 
+def _words(t: Tensor) -> int:
+    """4-byte words per row of a [rows, ...] tensor."""
+    return math.prod(t.shape[1:]) * t.element_size() // 4
+
+
+def _pack(tensors: List[Optional[Tensor]], words: List[int], rows: int, device) -> Tensor:
+    """[rows, sum(words)] int32 buffer with the tensors' rows side by side
+    (None -> zeros): one gsb_pack_rows launch on CUDA."""
+    buf = torch.empty((rows, sum(words)), dtype=torch.int32, device=device)
+    if device.type == "cuda":
+        import ctypes
+
+        from .cuda._backend import call, stream_of
+
+        srcs = (ctypes.c_void_p * len(words))(*[t.data_ptr() if t is not None else None for t in tensors])
+        w = (ctypes.c_int * len(words))(*words)
+        call("gsb_pack_rows", rows, len(words), srcs, w, buf.data_ptr(), stream_of(buf))
+        return buf
+    cols = [t.reshape(rows, -1).view(torch.int32) if t is not None else
+            torch.zeros((rows, wj), dtype=torch.int32, device=device) for t, wj in zip(tensors, words)]
+    return torch.cat(cols, dim=1) if cols else buf
+
+
+def _unpack(buf: Tensor, like: List[Tuple], words: List[int]) -> List[Tensor]:
+    """Splits a packed [rows, >= sum(words)] int32 buffer into new contiguous
+    tensors of the given (dtype, trailing shape): one gsb_unpack_rows launch."""
+    rows = buf.shape[0]
+    outs = [torch.empty((rows, *shape), dtype=dtype, device=buf.device) for dtype, shape in like]
+    if buf.is_cuda:
+        import ctypes
+
+        from .cuda._backend import call, stream_of
+
+        dsts = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+        w = (ctypes.c_int * len(words))(*words)
+        call("gsb_unpack_rows", rows, buf.shape[1], buf.data_ptr(), len(outs), dsts, w, stream_of(buf))
+        return outs
+    off = 0
+    for o, wj in zip(outs, words):
+        o.view(torch.int32).reshape(rows, wj).copy_(buf[:, off:off + wj])
+        off += wj
+    return outs
+
+
 class _ExchangeRows(torch.autograd.Function):
-    """One all_to_all_single of a row-packed buffer: float columns (differentiable)
-    followed by int32 columns bit-cast to float32 (not differentiable). The
-    backward sends the float-column gradients back with the splits swapped."""
+    """Row exchange of a list of float32 tensors (differentiable) and int32 /
+    int64 tensors (not differentiable) with ONE all_to_all_single of a packed
+    buffer each way; the backward sends the float gradients back with the splits
+    swapped."""
 
     @staticmethod
-    def forward(ctx, send_splits, recv_splits, n_float_cols, buf):
-        out = torch.empty((sum(recv_splits), buf.shape[1]), dtype=buf.dtype, device=buf.device)
+    def forward(ctx, send_splits, recv_splits, n_float, *tensors):
+        ctx.set_materialize_grads(False)
+        dev = tensors[0].device
+        n = sum(send_splits)
+        m = sum(recv_splits)
+        words = [_words(t) for t in tensors]
+        buf = _pack(list(tensors), words, n, dev)
+        out = torch.empty((m, buf.shape[1]), dtype=buf.dtype, device=dev)
         dist.all_to_all_single(out, buf, recv_splits, send_splits)
+        res = _unpack(out, [(t.dtype, t.shape[1:]) for t in tensors], words)
         ctx.splits = (send_splits, recv_splits)
-        ctx.nf = n_float_cols
-        return out
+        ctx.float_meta = [(t.shape[1:], w) for t, w in zip(tensors[:n_float], words[:n_float])]
+        ctx.n_inputs = len(tensors)
+        ctx.mark_non_differentiable(*res[n_float:])
+        return tuple(res)
 
     @staticmethod
-    def backward(ctx, g_out):
+    def backward(ctx, *grads):
         send_splits, recv_splits = ctx.splits
-        g = g_out[:, :ctx.nf].contiguous()
-        g_in = torch.empty((sum(send_splits), ctx.nf), dtype=g.dtype, device=g.device)
-        dist.all_to_all_single(g_in, g, send_splits, recv_splits)
-        pad = g_out.shape[1] - ctx.nf
-        if pad:
-            g_in = torch.cat([g_in, g_in.new_zeros((g_in.shape[0], pad))], dim=1)
-        return None, None, None, g_in
+        nf = len(ctx.float_meta)
+        words = [w for _, w in ctx.float_meta]
+        g = [x.contiguous() if x is not None else None for x in grads[:nf]]
+        dev = next((x.device for x in g if x is not None), None)
+        if dev is None:
+            return (None, None, None) + (None,) * ctx.n_inputs
+        buf = _pack(g, words, sum(recv_splits), dev)
+        back = torch.empty((sum(send_splits), buf.shape[1]), dtype=buf.dtype, device=dev)
+        dist.all_to_all_single(back, buf, send_splits, recv_splits)
+        res = _unpack(back, [(torch.float32, shape) for shape, _ in ctx.float_meta], words)
+        return (None, None, None) + tuple(res) + (None,) * (ctx.n_inputs - nf)
 
 
 def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], send_splits: List[int],
@@ -137,34 +196,14 @@ def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], sen
     all-to-all for all tensors (the float32 tensors keep their autograd graph;
     int32 / int64 tensors travel bit-cast inside the same buffer). The counts are
     host lists, so no collective or host read happens here besides the data
-    exchange itself."""
-    n = sum(send_splits)
-    cols, float_meta, int_meta = [], [], []
+    exchange itself. Returns (received floats, received ints)."""
     for t in floats:
-        assert t.dtype == torch.float32 and t.shape[0] == n
-        c = t.reshape(n, -1)
-        float_meta.append((c.shape[1], t.shape[1:]))
-        cols.append(c)
-    nf = sum(w for w, _ in float_meta)
+        assert t.dtype == torch.float32
     for t in ints:
-        assert t.shape[0] == n and t.dtype in (torch.int32, torch.int64)
-        c = t.contiguous().reshape(n, -1).view(torch.int32).view(torch.float32)
-        int_meta.append((c.shape[1], t.dtype, t.shape[1:]))
-        cols.append(c)
-    buf = torch.cat(cols, dim=1) if len(cols) > 1 else cols[0].contiguous()
-    out = _ExchangeRows.apply(list(send_splits), list(recv_splits), nf, buf)
-    m = out.shape[0]
-    res_f, res_i, off = [], [], 0
-    for w, shape in float_meta:
-        res_f.append(out[:, off:off + w].reshape(m, *shape))
-        off += w
-    for w, dtype, shape in int_meta:
-        piece = out[:, off:off + w].detach().contiguous().view(torch.int32)
-        if dtype == torch.int64:
-            piece = piece.view(torch.int64)
-        res_i.append(piece.reshape(m, *shape))
-        off += w
-    return res_f, res_i
+        assert t.dtype in (torch.int32, torch.int64)
+    tensors = [t.contiguous() for t in floats] + [t.contiguous() for t in ints]
+    out = _ExchangeRows.apply(list(send_splits), list(recv_splits), len(floats), *tensors)
+    return list(out[:len(floats)]), list(out[len(floats):])
 
 
 def cli(fn: Callable, args, verbose: bool = False, backend: str = "nccl") -> bool:

@@ -29,6 +29,7 @@ from .cuda._wrapper import (
     rasterize_to_pixels,
     spherical_harmonics,
 )
+from .cuda._backend import call, device_guard, ptr, stream_of
 from .distributed import (
     all_gather_int32,
     all_gather_tensor_list,
@@ -253,11 +254,23 @@ def rasterization(
         world_size = torch.distributed.get_world_size()
         # Gaussian counts of all ranks, kept on the device (read only by the
         # paths that need host split sizes)
-        N_world_dev = torch.empty(world_size, dtype=torch.int64, device=device)
-        torch.distributed.all_gather_into_tensor(
-            N_world_dev, torch.full((1,), N, dtype=torch.int64, device=device))
         C_world = [C] * world_size
-        viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
+        if viewmats.requires_grad or Ks.requires_grad:
+            N_world_dev = torch.empty(world_size, dtype=torch.int64, device=device)
+            torch.distributed.all_gather_into_tensor(
+                N_world_dev, torch.full((1,), N, dtype=torch.int64, device=device))
+            viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
+        else:
+            # one all-gather for the cameras and the Gaussian count of every rank
+            # (the int64 count travels bit-cast in two float32 slots)
+            n_bits = torch.full((C, 1), N, dtype=torch.int64, device=viewmats.device).view(torch.float32)
+            row = torch.cat([viewmats.reshape(C, 16).float(), Ks.reshape(C, 9).float(), n_bits],
+                            dim=1).contiguous()
+            gathered = torch.empty((world_size * C, 27), dtype=row.dtype, device=row.device)
+            torch.distributed.all_gather_into_tensor(gathered, row)
+            viewmats = gathered[:, :16].reshape(world_size * C, 4, 4).to(viewmats.dtype)
+            Ks = gathered[:, 16:25].reshape(world_size * C, 3, 3).to(Ks.dtype)
+            N_world_dev = gathered[::C, 25:27].contiguous().view(torch.int64).reshape(world_size)
         C = len(viewmats)
 
     # One fused kernel for projection + view-dependent SH colour + opacity
@@ -397,15 +410,16 @@ def rasterization(
         if proj_features is not None:
             proj_features = proj_features[:nnz]
         # camera ids local to the destination rank; gaussian ids shifted by the
-        # destination's Gaussian offset (reference rendering.py:944-959)
-        if all(c == C_world[0] for c in C_world):
-            dst = torch.div(camera_ids, C_world[0], rounding_mode="floor")
-        else:
-            dst = torch.bucketize(camera_ids, torch.tensor(cstart[1:], device=device), right=True)
-        c_off = torch.tensor(cstart[:-1], device=device, dtype=camera_ids.dtype)
+        # destination's Gaussian offset (reference rendering.py:944-959); every
+        # rank holds C_world[0] cameras (rasterization() gathers the same count)
         n_off = torch.cumsum(N_world_dev, 0) - N_world_dev
+        cam_local = torch.empty_like(camera_ids)
+        gid_global = torch.empty_like(gaussian_ids)
+        with device_guard(device):
+            call("gsb_exchange_ids", nnz, ptr(camera_ids), ptr(gaussian_ids), C_world[0], ptr(n_off),
+                 ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
         floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
-        ints = [radii, camera_ids - c_off[dst], gaussian_ids + n_off[dst]]
+        ints = [radii, cam_local, gid_global]
         floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits)
         means2d, depths, conics, opacities = floats[:4]
         if proj_features is not None:

@@ -6,21 +6,12 @@ the gradients of the rank's own Gaussians must match the single-GPU pipeline
 fewer than two GPUs."""
 
 import os
-import socket
 import traceback
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-
-
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _scene(rank, dev, N=20000):
@@ -42,18 +33,18 @@ def _scene(rank, dev, N=20000):
     return [t.to(dev) for t in (means, quats, scales, opac, sh, vm, K)]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, store_path, q):
     import datetime
 
     import torch.distributed as dist
 
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        # file rendezvous: no TCP port that another process on the box could hold
+        dist.init_process_group("nccl", init_method=f"file://{store_path}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
         import gsplat_b200
 
         W, H = 320, 240
@@ -89,13 +80,13 @@ def _worker(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
-def test_distributed_packed_matches_single_gpu():
+def test_distributed_packed_matches_single_gpu(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    store = str(tmp_path / "rendezvous")
+    procs = [ctx.Process(target=_worker, args=(r, 2, store, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
