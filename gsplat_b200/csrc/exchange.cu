@@ -60,18 +60,20 @@ __global__ void __launch_bounds__(256) unpack_rows_kernel(RowArrays a, long long
 }
 
 // Destination rank of camera c is c / cams_per_rank; camera ids become local to
-// that rank and Gaussian ids are shifted by that rank's Gaussian offset
-// (reference rendering.py:944-959).
+// that rank and Gaussian ids are shifted by that rank's Gaussian offset, the
+// Gaussian counts of the ranks before it (reference rendering.py:944-959).
 __global__ void exchange_ids_kernel(long long n, const int64_t *__restrict__ camera_ids,
                                     const int64_t *__restrict__ gaussian_ids, int cams_per_rank,
-                                    const int64_t *__restrict__ gauss_offsets, int64_t *__restrict__ cam_out,
+                                    const int64_t *__restrict__ gauss_counts, int64_t *__restrict__ cam_out,
                                     int64_t *__restrict__ gid_out) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         const int64_t c = camera_ids[i];
         const int64_t dst = c / cams_per_rank;
+        int64_t off = 0;
+        for (int64_t r = 0; r < dst; ++r) off += gauss_counts[r];
         cam_out[i] = c - dst * cams_per_rank;
-        gid_out[i] = gaussian_ids[i] + gauss_offsets[dst];
+        gid_out[i] = gaussian_ids[i] + off;
     }
 }
 
@@ -120,11 +122,11 @@ extern "C" int gsb_unpack_rows(long long rows, int row_words, const uint32_t *bu
 }
 
 extern "C" int gsb_exchange_ids(long long n, const int64_t *camera_ids, const int64_t *gaussian_ids,
-                                int cams_per_rank, const int64_t *gauss_offsets, int64_t *cam_out,
+                                int cams_per_rank, const int64_t *gauss_counts, int64_t *cam_out,
                                 int64_t *gid_out, cudaStream_t stream) {
     if (cams_per_rank <= 0) return set_error(kErrInvalidArgument, "cams_per_rank must be positive");
     if (n <= 0) return kOk;
     exchange_ids_kernel<<<grid_for(n), 256, 0, stream>>>(n, camera_ids, gaussian_ids, cams_per_rank,
-                                                         gauss_offsets, cam_out, gid_out);
+                                                         gauss_counts, cam_out, gid_out);
     return check_launch("exchange_ids_kernel");
 }

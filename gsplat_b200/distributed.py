@@ -124,7 +124,7 @@ def _pack(tensors: List[Optional[Tensor]], words: List[int], rows: int, device) 
         w = (ctypes.c_int * len(words))(*words)
         call("gsb_pack_rows", rows, len(words), srcs, w, buf.data_ptr(), stream_of(buf))
         return buf
-    cols = [t.reshape(rows, -1).view(torch.int32) if t is not None else
+    cols = [t[:rows].reshape(rows, -1).view(torch.int32) if t is not None else
             torch.zeros((rows, wj), dtype=torch.int32, device=device) for t, wj in zip(tensors, words)]
     return torch.cat(cols, dim=1) if cols else buf
 
@@ -168,7 +168,7 @@ class _ExchangeRows(torch.autograd.Function):
         dist.all_to_all_single(out, buf, recv_splits, send_splits)
         res = _unpack(out, [(t.dtype, t.shape[1:]) for t in tensors], words)
         ctx.splits = (send_splits, recv_splits)
-        ctx.float_meta = [(t.shape[1:], w) for t, w in zip(tensors[:n_float], words[:n_float])]
+        ctx.float_meta = [(t.shape, w) for t, w in zip(tensors[:n_float], words[:n_float])]
         ctx.n_inputs = len(tensors)
         ctx.mark_non_differentiable(*res[n_float:])
         return tuple(res)
@@ -183,9 +183,24 @@ class _ExchangeRows(torch.autograd.Function):
         if dev is None:
             return (None, None, None) + (None,) * ctx.n_inputs
         buf = _pack(g, words, sum(recv_splits), dev)
-        back = torch.empty((sum(send_splits), buf.shape[1]), dtype=buf.dtype, device=dev)
+        n = sum(send_splits)
+        back = torch.empty((n, buf.shape[1]), dtype=buf.dtype, device=dev)
         dist.all_to_all_single(back, buf, send_splits, recv_splits)
-        res = _unpack(back, [(torch.float32, shape) for shape, _ in ctx.float_meta], words)
+        # gradients have the inputs' full shapes; rows past the sent ones are
+        # left unset (see exchange_rows)
+        res = [torch.empty(shape, dtype=torch.float32, device=dev) for shape, _ in ctx.float_meta]
+        if dev.type == "cuda":
+            import ctypes
+
+            from .cuda._backend import call, stream_of
+
+            dsts = (ctypes.c_void_p * nf)(*[r.data_ptr() for r in res])
+            w = (ctypes.c_int * nf)(*words)
+            call("gsb_unpack_rows", n, back.shape[1], back.data_ptr(), nf, dsts, w, stream_of(back))
+        else:
+            for r, piece in zip(res, _unpack(back, [(torch.float32, shape[1:]) for shape, _ in ctx.float_meta],
+                                             words)):
+                r[:n] = piece
         return (None, None, None) + tuple(res) + (None,) * (ctx.n_inputs - nf)
 
 
@@ -196,7 +211,10 @@ def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], sen
     all-to-all for all tensors (the float32 tensors keep their autograd graph;
     int32 / int64 tensors travel bit-cast inside the same buffer). The counts are
     host lists, so no collective or host read happens here besides the data
-    exchange itself. Returns (received floats, received ints)."""
+    exchange itself. Tensors may hold more rows than sum(send_splits) (buffers
+    with spare capacity): only the leading rows are sent, and the gradient rows
+    past them are left unset, for producers that never read those rows back.
+    Returns (received floats, received ints)."""
     for t in floats:
         assert t.dtype == torch.float32
     for t in ints:

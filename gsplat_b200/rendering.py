@@ -397,27 +397,23 @@ def rasterization(
         # Same exchange as the reference (below), with one host read and one
         # all-to-all: packed rows are ordered by camera, so the rows for rank r
         # are indptr[cstart[r]] .. indptr[cstart[r + 1]].
-        cstart = [sum(C_world[:r]) for r in range(world_size + 1)]
-        bounds = indptr.index_select(0, torch.tensor(cstart, device=device)).to(torch.int64)
+        # every rank holds C_world[0] cameras (the same count is gathered above)
+        bounds = indptr[::C_world[0]].to(torch.int64)
         send_cnt = bounds[1:] - bounds[:-1]
         recv_cnt = torch.empty_like(send_cnt)
         torch.distributed.all_to_all_single(recv_cnt, send_cnt)
         sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
         send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
-        (batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics, opacities) = (
-            t[:nnz] for t in (batch_ids, camera_ids, gaussian_ids, radii, means2d, depths, conics,
-                              opacities))
-        if proj_features is not None:
-            proj_features = proj_features[:nnz]
         # camera ids local to the destination rank; gaussian ids shifted by the
-        # destination's Gaussian offset (reference rendering.py:944-959); every
-        # rank holds C_world[0] cameras (rasterization() gathers the same count)
-        n_off = torch.cumsum(N_world_dev, 0) - N_world_dev
+        # destination's Gaussian offset (reference rendering.py:944-959)
+        batch_ids, camera_ids, gaussian_ids = batch_ids[:nnz], camera_ids[:nnz], gaussian_ids[:nnz]
         cam_local = torch.empty_like(camera_ids)
         gid_global = torch.empty_like(gaussian_ids)
         with device_guard(device):
-            call("gsb_exchange_ids", nnz, ptr(camera_ids), ptr(gaussian_ids), C_world[0], ptr(n_off),
+            call("gsb_exchange_ids", nnz, ptr(camera_ids), ptr(gaussian_ids), C_world[0], ptr(N_world_dev),
                  ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
+        # the projection outputs keep their spare rows: the exchange sends the
+        # first nnz, and the projection's backward reads no gradient row past them
         floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
         ints = [radii, cam_local, gid_global]
         floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits)

@@ -348,11 +348,11 @@ GSB_API int gsb_pack_rows(long long rows, int n_arrays, void *const *srcs, const
                           cudaStream_t stream);
 GSB_API int gsb_unpack_rows(long long rows, int row_words, const uint32_t *buf, int n_arrays,
                             void *const *dsts, const int *words, cudaStream_t stream);
-/* Camera c goes to rank c / cams_per_rank: cam_out = c mod cams_per_rank,
- * gid_out = gaussian_ids + gauss_offsets[rank] (the reference's id remap,
- * rendering.py:944-959). All int64, device memory. */
+/* Camera c goes to rank d = c / cams_per_rank: cam_out = c mod cams_per_rank,
+ * gid_out = gaussian_ids + gauss_counts[0] + ... + gauss_counts[d - 1] (the
+ * reference's id remap, rendering.py:944-959). All int64, device memory. */
 GSB_API int gsb_exchange_ids(long long n, const int64_t *camera_ids, const int64_t *gaussian_ids,
-                             int cams_per_rank, const int64_t *gauss_offsets, int64_t *cam_out,
+                             int cams_per_rank, const int64_t *gauss_counts, int64_t *cam_out,
                              int64_t *gid_out, cudaStream_t stream);
 
 /* --- Measurement ----------------------------------------------------------
