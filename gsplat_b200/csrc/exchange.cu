@@ -24,7 +24,10 @@ struct RowArrays {
     int total; // sum of words
 };
 
-__global__ void __launch_bounds__(256) pack_rows_kernel(RowArrays a, long long rows, uint32_t *__restrict__ buf) {
+__global__ void __launch_bounds__(256) pack_rows_kernel(RowArrays a, long long rows,
+                                                        const int64_t *__restrict__ rows_device,
+                                                        uint32_t *__restrict__ buf) {
+    if (rows_device != nullptr && *rows_device < rows) rows = *rows_device;
     for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < rows;
          r += (long long)gridDim.x * blockDim.x) {
         uint32_t *dst = buf + r * a.total;
@@ -62,10 +65,12 @@ __global__ void __launch_bounds__(256) unpack_rows_kernel(RowArrays a, long long
 // Destination rank of camera c is c / cams_per_rank; camera ids become local to
 // that rank and Gaussian ids are shifted by that rank's Gaussian offset, the
 // Gaussian counts of the ranks before it (reference rendering.py:944-959).
-__global__ void exchange_ids_kernel(long long n, const int64_t *__restrict__ camera_ids,
+__global__ void exchange_ids_kernel(long long n, const int64_t *__restrict__ n_device,
+                                    const int64_t *__restrict__ camera_ids,
                                     const int64_t *__restrict__ gaussian_ids, int cams_per_rank,
                                     const int64_t *__restrict__ gauss_counts, int64_t *__restrict__ cam_out,
                                     int64_t *__restrict__ gid_out) {
+    if (n_device != nullptr && *n_device < n) n = *n_device;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         const int64_t c = camera_ids[i];
@@ -100,12 +105,12 @@ static unsigned grid_for(long long work) {
 
 using namespace gsb;
 
-extern "C" int gsb_pack_rows(long long rows, int n_arrays, void *const *srcs, const int *words, uint32_t *buf,
-                             cudaStream_t stream) {
+extern "C" int gsb_pack_rows(long long rows, const int64_t *rows_device, int n_arrays, void *const *srcs,
+                             const int *words, uint32_t *buf, cudaStream_t stream) {
     RowArrays a;
     if (int e = make_arrays(a, n_arrays, srcs, words)) return e;
     if (rows <= 0) return kOk;
-    pack_rows_kernel<<<grid_for(rows), 256, 0, stream>>>(a, rows, buf);
+    pack_rows_kernel<<<grid_for(rows), 256, 0, stream>>>(a, rows, rows_device, buf);
     return check_launch("pack_rows_kernel");
 }
 
@@ -121,12 +126,12 @@ extern "C" int gsb_unpack_rows(long long rows, int row_words, const uint32_t *bu
     return check_launch("unpack_rows_kernel");
 }
 
-extern "C" int gsb_exchange_ids(long long n, const int64_t *camera_ids, const int64_t *gaussian_ids,
-                                int cams_per_rank, const int64_t *gauss_counts, int64_t *cam_out,
-                                int64_t *gid_out, cudaStream_t stream) {
+extern "C" int gsb_exchange_ids(long long n, const int64_t *n_device, const int64_t *camera_ids,
+                                const int64_t *gaussian_ids, int cams_per_rank, const int64_t *gauss_counts,
+                                int64_t *cam_out, int64_t *gid_out, cudaStream_t stream) {
     if (cams_per_rank <= 0) return set_error(kErrInvalidArgument, "cams_per_rank must be positive");
     if (n <= 0) return kOk;
-    exchange_ids_kernel<<<grid_for(n), 256, 0, stream>>>(n, camera_ids, gaussian_ids, cams_per_rank,
+    exchange_ids_kernel<<<grid_for(n), 256, 0, stream>>>(n, n_device, camera_ids, gaussian_ids, cams_per_rank,
                                                          gauss_counts, cam_out, gid_out);
     return check_launch("exchange_ids_kernel");
 }

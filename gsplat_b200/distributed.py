@@ -111,9 +111,11 @@ def _words(t: Tensor) -> int:
     return math.prod(t.shape[1:]) * t.element_size() // 4
 
 
-def _pack(tensors: List[Optional[Tensor]], words: List[int], rows: int, device) -> Tensor:
+def _pack(tensors: List[Optional[Tensor]], words: List[int], rows: int, device,
+          rows_device: Optional[Tensor] = None) -> Tensor:
     """[rows, sum(words)] int32 buffer with the tensors' rows side by side
-    (None -> zeros): one gsb_pack_rows launch on CUDA."""
+    (None -> zeros): one gsb_pack_rows launch on CUDA. With ``rows_device`` (a
+    device int64 count) only that many leading rows are filled."""
     buf = torch.empty((rows, sum(words)), dtype=torch.int32, device=device)
     if device.type == "cuda":
         import ctypes
@@ -122,7 +124,8 @@ def _pack(tensors: List[Optional[Tensor]], words: List[int], rows: int, device) 
 
         srcs = (ctypes.c_void_p * len(words))(*[t.data_ptr() if t is not None else None for t in tensors])
         w = (ctypes.c_int * len(words))(*words)
-        call("gsb_pack_rows", rows, len(words), srcs, w, buf.data_ptr(), stream_of(buf))
+        call("gsb_pack_rows", rows, rows_device.data_ptr() if rows_device is not None else None, len(words),
+             srcs, w, buf.data_ptr(), stream_of(buf))
         return buf
     cols = [t[:rows].reshape(rows, -1).view(torch.int32) if t is not None else
             torch.zeros((rows, wj), dtype=torch.int32, device=device) for t, wj in zip(tensors, words)]
@@ -157,13 +160,15 @@ class _ExchangeRows(torch.autograd.Function):
     swapped."""
 
     @staticmethod
-    def forward(ctx, send_splits, recv_splits, n_float, *tensors):
+    def forward(ctx, send_splits, recv_splits, n_float, packed, *tensors):
         ctx.set_materialize_grads(False)
         dev = tensors[0].device
         n = sum(send_splits)
         m = sum(recv_splits)
         words = [_words(t) for t in tensors]
-        buf = _pack(list(tensors), words, n, dev)
+        # the all-to-all wants exactly the sent rows (a pre-built buffer may
+        # have spare capacity past them)
+        buf = packed[:n] if packed is not None else _pack(list(tensors), words, n, dev)
         out = torch.empty((m, buf.shape[1]), dtype=buf.dtype, device=dev)
         dist.all_to_all_single(out, buf, recv_splits, send_splits)
         res = _unpack(out, [(t.dtype, t.shape[1:]) for t in tensors], words)
@@ -181,7 +186,7 @@ class _ExchangeRows(torch.autograd.Function):
         g = [x.contiguous() if x is not None else None for x in grads[:nf]]
         dev = next((x.device for x in g if x is not None), None)
         if dev is None:
-            return (None, None, None) + (None,) * ctx.n_inputs
+            return (None, None, None, None) + (None,) * ctx.n_inputs
         buf = _pack(g, words, sum(recv_splits), dev)
         n = sum(send_splits)
         back = torch.empty((n, buf.shape[1]), dtype=buf.dtype, device=dev)
@@ -201,11 +206,19 @@ class _ExchangeRows(torch.autograd.Function):
             for r, piece in zip(res, _unpack(back, [(torch.float32, shape[1:]) for shape, _ in ctx.float_meta],
                                              words)):
                 r[:n] = piece
-        return (None, None, None) + tuple(res) + (None,) * (ctx.n_inputs - nf)
+        return (None, None, None, None) + tuple(res) + (None,) * (ctx.n_inputs - nf)
+
+
+def pack_rows(floats: List[Tensor], ints: List[Tensor], rows: int, rows_device: Optional[Tensor] = None) -> Tensor:
+    """The send buffer of exchange_rows for these tensors, built ahead of time
+    (for instance before the split sizes are read back from the device): the
+    first ``rows`` rows, or the first ``*rows_device`` of them."""
+    tensors = list(floats) + list(ints)
+    return _pack(tensors, [_words(t) for t in tensors], rows, tensors[0].device, rows_device)
 
 
 def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], send_splits: List[int],
-                  recv_splits: List[int]):
+                  recv_splits: List[int], packed: Optional[Tensor] = None):
     """Sends rows [sum(send_splits[:r]), sum(send_splits[:r+1])) of every listed
     tensor to rank r and receives recv_splits[r] rows from it, with ONE
     all-to-all for all tensors (the float32 tensors keep their autograd graph;
@@ -214,13 +227,14 @@ def exchange_rows(world_size: int, floats: List[Tensor], ints: List[Tensor], sen
     exchange itself. Tensors may hold more rows than sum(send_splits) (buffers
     with spare capacity): only the leading rows are sent, and the gradient rows
     past them are left unset, for producers that never read those rows back.
-    Returns (received floats, received ints)."""
+    ``packed`` is a buffer from pack_rows for the same tensors, if already
+    built. Returns (received floats, received ints)."""
     for t in floats:
         assert t.dtype == torch.float32
     for t in ints:
         assert t.dtype in (torch.int32, torch.int64)
     tensors = [t.contiguous() for t in floats] + [t.contiguous() for t in ints]
-    out = _ExchangeRows.apply(list(send_splits), list(recv_splits), len(floats), *tensors)
+    out = _ExchangeRows.apply(list(send_splits), list(recv_splits), len(floats), packed, *tensors)
     return list(out[:len(floats)]), list(out[len(floats):])
 
 

@@ -36,6 +36,7 @@ from .distributed import (
     all_to_all_int32,
     all_to_all_tensor_list,
     exchange_rows,
+    pack_rows,
 )
 
 RenderMode = Literal["RGB", "d", "Ed", "D", "ED", "RGB-d", "RGB-Ed", "RGB+D", "RGB+ED"]
@@ -402,21 +403,25 @@ def rasterization(
         send_cnt = bounds[1:] - bounds[:-1]
         recv_cnt = torch.empty_like(send_cnt)
         torch.distributed.all_to_all_single(recv_cnt, send_cnt)
-        sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
-        send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
-        # camera ids local to the destination rank; gaussian ids shifted by the
-        # destination's Gaussian offset (reference rendering.py:944-959)
-        batch_ids, camera_ids, gaussian_ids = batch_ids[:nnz], camera_ids[:nnz], gaussian_ids[:nnz]
+        # Before the sizes reach the host: camera ids local to the destination
+        # rank, gaussian ids shifted by the destination's Gaussian offset
+        # (reference rendering.py:944-959), and the send buffer, all bounded by
+        # the splat count still on the device. The projection outputs keep their
+        # spare rows: only the first nnz are sent, and the projection's backward
+        # reads no gradient row past them.
+        cap = camera_ids.shape[0]
         cam_local = torch.empty_like(camera_ids)
         gid_global = torch.empty_like(gaussian_ids)
         with device_guard(device):
-            call("gsb_exchange_ids", nnz, ptr(camera_ids), ptr(gaussian_ids), C_world[0], ptr(N_world_dev),
-                 ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
-        # the projection outputs keep their spare rows: the exchange sends the
-        # first nnz, and the projection's backward reads no gradient row past them
+            call("gsb_exchange_ids", cap, ptr(nnz_device), ptr(camera_ids), ptr(gaussian_ids), C_world[0],
+                 ptr(N_world_dev), ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
         floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
         ints = [radii, cam_local, gid_global]
-        floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits)
+        send_buf = pack_rows(floats, ints, cap, rows_device=nnz_device)
+        sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
+        send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
+        batch_ids, camera_ids, gaussian_ids = batch_ids[:nnz], camera_ids[:nnz], gaussian_ids[:nnz]
+        floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits, packed=send_buf)
         means2d, depths, conics, opacities = floats[:4]
         if proj_features is not None:
             proj_features = floats[4]

@@ -341,19 +341,23 @@ GSB_API int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bool 
  * (gsplat/rendering.py:907-975, gsplat/distributed.py:182-272).
  * gsb_pack_rows: buf [rows, sum(words)] (4-byte words) gets the columns of the
  * n_arrays row-major arrays srcs[j] [rows, words[j]] side by side; a NULL
- * source packs zeros. gsb_unpack_rows: the inverse, from rows of row_words
- * words (the first sum(words) of each row are read); a NULL destination skips
- * its columns. At most 16 arrays. int64 columns count as 2 words. */
-GSB_API int gsb_pack_rows(long long rows, int n_arrays, void *const *srcs, const int *words, uint32_t *buf,
-                          cudaStream_t stream);
+ * source packs zeros; with rows_device (device int64, may be NULL) only the
+ * first min(rows, *rows_device) rows are packed, so a count that is still on
+ * the device can bound the work. gsb_unpack_rows: the inverse, from rows of
+ * row_words words (the first sum(words) of each row are read); a NULL
+ * destination skips its columns. At most 16 arrays. int64 columns count as 2
+ * words. */
+GSB_API int gsb_pack_rows(long long rows, const int64_t *rows_device, int n_arrays, void *const *srcs,
+                          const int *words, uint32_t *buf, cudaStream_t stream);
 GSB_API int gsb_unpack_rows(long long rows, int row_words, const uint32_t *buf, int n_arrays,
                             void *const *dsts, const int *words, cudaStream_t stream);
 /* Camera c goes to rank d = c / cams_per_rank: cam_out = c mod cams_per_rank,
  * gid_out = gaussian_ids + gauss_counts[0] + ... + gauss_counts[d - 1] (the
- * reference's id remap, rendering.py:944-959). All int64, device memory. */
-GSB_API int gsb_exchange_ids(long long n, const int64_t *camera_ids, const int64_t *gaussian_ids,
-                             int cams_per_rank, const int64_t *gauss_counts, int64_t *cam_out,
-                             int64_t *gid_out, cudaStream_t stream);
+ * reference's id remap, rendering.py:944-959), for the first
+ * min(n, *n_device) entries (n_device may be NULL). All int64, device memory. */
+GSB_API int gsb_exchange_ids(long long n, const int64_t *n_device, const int64_t *camera_ids,
+                             const int64_t *gaussian_ids, int cams_per_rank, const int64_t *gauss_counts,
+                             int64_t *cam_out, int64_t *gid_out, cudaStream_t stream);
 
 /* --- Measurement ----------------------------------------------------------
  * FP32 FMA throughput probe (no reference counterpart): blocks x threads threads
