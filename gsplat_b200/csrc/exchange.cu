@@ -7,9 +7,7 @@
 // These kernels do each of those steps in one launch: gather the columns of
 // several row-major arrays into one row-major buffer of 4-byte words (float,
 // int32, or int64 as two words), scatter such a buffer back into separate
-// arrays, and remap the ids. One thread per row: the source / destination
-// arrays are read and written coalesced, the packed rows are contiguous per
-// thread.
+// arrays, and remap the ids.
 #include "common.cuh"
 #include "gsb_internal.h"
 
@@ -24,27 +22,52 @@ struct RowArrays {
     int total; // sum of words
 };
 
-__global__ void __launch_bounds__(256) pack_rows_kernel(RowArrays a, long long rows,
-                                                        const int64_t *__restrict__ rows_device,
-                                                        uint32_t *__restrict__ buf) {
+// Packing: a CTA moves a block of consecutive rows through shared memory so
+// that both sides are read and written coalesced: each array's rows of the
+// block are one contiguous range, and so are the block's packed rows.
+constexpr int kRowThreads = 256;
+constexpr int kRowSmemWords = 12 * 1024; // 48 KiB of staging per CTA
+
+// Staged rows are padded to an odd word count so that threads walking one
+// column of the block (stride = the row) hit distinct banks.
+__device__ __forceinline__ int stage_stride(int total) { return total | 1; }
+
+__device__ __forceinline__ int block_rows(int total) {
+    const int r = kRowSmemWords / stage_stride(total);
+    return r < 1 ? 1 : r;
+}
+
+__global__ void __launch_bounds__(kRowThreads) pack_rows_kernel(RowArrays a, long long rows,
+                                                                const int64_t *__restrict__ rows_device,
+                                                                uint32_t *__restrict__ buf) {
+    __shared__ uint32_t stage[kRowSmemWords];
     if (rows_device != nullptr && *rows_device < rows) rows = *rows_device;
-    for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < rows;
-         r += (long long)gridDim.x * blockDim.x) {
-        uint32_t *dst = buf + r * a.total;
+    const int S = stage_stride(a.total);
+    const int R = block_rows(a.total);
+    for (long long r0 = (long long)blockIdx.x * R; r0 < rows; r0 += (long long)gridDim.x * R) {
+        const int nr = (int)min((long long)R, rows - r0);
+        int first = 0;
         for (int j = 0; j < a.n; ++j) {
             const int w = a.words[j];
             const uint32_t *src = static_cast<const uint32_t *>(a.ptr[j]);
-            if (src) {
-                src += r * w;
-                for (int k = 0; k < w; ++k) dst[k] = src[k];
-            } else {
-                for (int k = 0; k < w; ++k) dst[k] = 0u;
+            for (int i = threadIdx.x; i < nr * w; i += kRowThreads) {
+                const int r = i / w, k = i - r * w;
+                stage[r * S + first + k] = src ? src[r0 * w + i] : 0u;
             }
-            dst += w;
+            first += w;
         }
+        __syncthreads();
+        uint32_t *dst = buf + r0 * a.total;
+        for (int i = threadIdx.x; i < nr * a.total; i += kRowThreads) {
+            const int r = i / a.total, k = i - r * a.total;
+            dst[i] = stage[r * S + k];
+        }
+        __syncthreads();
     }
 }
 
+// Unpacking reads each packed row whole and writes every array's row: one
+// thread per row (measured faster than the staged form for this direction).
 __global__ void __launch_bounds__(256) unpack_rows_kernel(RowArrays a, long long rows, int row_words,
                                                           const uint32_t *__restrict__ buf) {
     for (long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x; r < rows;
@@ -93,12 +116,21 @@ static int make_arrays(RowArrays &a, int n_arrays, void *const *ptrs, const int 
         a.words[j] = words[j];
         a.total += words[j];
     }
+    if ((a.total | 1) > kRowSmemWords)
+        return set_error(kErrInvalidArgument, "row packing: %d words per row (at most %d)", a.total, kRowSmemWords);
     return kOk;
 }
 
 static unsigned grid_for(long long work) {
     const long long blocks = (work + 255) / 256;
     return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+// CTAs for a row block loop: one per block of rows, at most 4 per SM worth
+static unsigned grid_for_rows(long long rows, int total) {
+    const long long R = kRowSmemWords / (total | 1) > 0 ? kRowSmemWords / (total | 1) : 1;
+    const long long blocks = (rows + R - 1) / R;
+    return (unsigned)(blocks < 148 * 4 ? (blocks > 0 ? blocks : 1) : 148 * 4);
 }
 
 } // namespace gsb
@@ -110,7 +142,7 @@ extern "C" int gsb_pack_rows(long long rows, const int64_t *rows_device, int n_a
     RowArrays a;
     if (int e = make_arrays(a, n_arrays, srcs, words)) return e;
     if (rows <= 0) return kOk;
-    pack_rows_kernel<<<grid_for(rows), 256, 0, stream>>>(a, rows, rows_device, buf);
+    pack_rows_kernel<<<grid_for_rows(rows, a.total), kRowThreads, 0, stream>>>(a, rows, rows_device, buf);
     return check_launch("pack_rows_kernel");
 }
 
