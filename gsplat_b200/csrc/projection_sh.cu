@@ -341,12 +341,16 @@ __global__ void __launch_bounds__(kFusedBwdThreads, (D >= 4 ? 3 : (D == 1 ? 4 : 
         q.v_opacities[gi] = v_op;
     }
     __syncthreads();
+    // one warp per staged row: 32 lanes copy consecutive coefficients (no
+    // index division), so each row leaves as coalesced 128-byte pieces
     const size_t total = (size_t)p.B * p.N;
-    const size_t count = (total - first) < kFusedBwdThreads ? (total - first) : kFusedBwdThreads;
+    const uint32_t count = (total - first) < kFusedBwdThreads ? (uint32_t)(total - first) : kFusedBwdThreads;
     float *dst = q.v_sh + first * K3;
-    for (size_t i = tid; i < count * K3; i += kFusedBwdThreads) {
-        const size_t r = i / K3;
-        dst[i] = s_vsh[r * stride + (i - r * K3)];
+    const uint32_t lane = tid & 31u;
+    for (uint32_t r = tid >> 5; r < count; r += kFusedBwdThreads / 32) {
+        const float *row = s_vsh + (size_t)r * stride;
+        float *out = dst + (size_t)r * K3;
+        for (uint32_t c = lane; c < K3; c += 32) out[c] = row[c];
     }
 }
 
