@@ -11,6 +11,7 @@
 // hardware approximate logarithm (__logf); this implementation uses det_logf, a
 // portable logarithm accurate to ~1 ulp, as documented in detmath.h.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gsb_internal.h"
@@ -698,6 +699,33 @@ extern "C" int gsb_isect_bucket_shards(int I, int tile_width, int tile_height) {
     return (int)bucket_plan((uint64_t)I * tile_width * tile_height, device_sms()).shards;
 }
 
+// One internal stream per device (non-blocking, created at first use) with a
+// fork and a join event, for work that can run next to the caller's stream.
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+constexpr int kMaxSideDevices = 64;
+static std::mutex g_side_mutex;
+static SideStream g_side[kMaxSideDevices];
+
+// Caller holds g_side_mutex (the events are shared by all calls on a device).
+static int side_stream(SideStream **out) {
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaGetDevice: %s", cudaGetErrorString(ce));
+    if (dev < 0 || dev >= kMaxSideDevices) return set_error(kErrUnsupported, "device %d out of range", dev);
+    SideStream &s = g_side[dev];
+    if (s.stream == nullptr) {
+        if ((ce = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking)) != cudaSuccess ||
+            (ce = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming)) != cudaSuccess ||
+            (ce = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming)) != cudaSuccess)
+            return set_error(kErrLaunch, "side stream set-up: %s", cudaGetErrorString(ce));
+    }
+    *out = &s;
+    return kOk;
+}
+
 static int set_cta_smem(const void *kern, size_t smem) {
     if (smem <= 48 * 1024) return kOk;
     cudaError_t ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -810,7 +838,19 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
     const unsigned grid = (unsigned)n_buckets;
     // size classes (0, 1024], (1024, 4096], (4096, 16384], one launch each, sized
     // for the largest bucket of the class; a CTA whose bucket is in another
-    // class returns at once
+    // class returns at once. The classes sort disjoint buckets, so the rare
+    // large ones run on a side stream next to the first class (forked from and
+    // joined back to the caller's stream with events).
+    cudaStream_t side = stream;
+    SideStream *ss = nullptr;
+    std::unique_lock<std::mutex> side_lock(g_side_mutex, std::defer_lock);
+    if (max_count > 1024) {
+        side_lock.lock(); // held until the join is recorded
+        if (int e = side_stream(&ss)) return e;
+        side = ss->stream;
+        cudaEventRecord(ss->fork, stream);
+        cudaStreamWaitEvent(side, ss->fork, 0);
+    }
     int lo = 0;
     for (int hi : {1024, 4096, kBucketSortMax}) {
         if (max_count > lo) {
@@ -825,12 +865,18 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
             // first class: one CTA per bucket; larger (rare) buckets: two CTAs per
             // SM walking all buckets, instead of launching one CTA per bucket
             const unsigned g = lo == 0 ? grid : (unsigned)std::min<uint64_t>(n_buckets, 2ull * device_sms());
-            kern<<<g, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
-                                               (uint32_t)n_buckets, (uint32_t)n_tiles, tb, lo, hi, isect_ids,
-                                               flatten_ids);
+            kern<<<g, threads, smem, lo == 0 ? stream : side>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
+                                                                (uint32_t)n_buckets, (uint32_t)n_tiles, tb, lo, hi,
+                                                                isect_ids, flatten_ids);
             if (int e = check_launch("bucket_sort_kernel")) return e;
         }
         lo = hi;
+    }
+    if (ss != nullptr) {
+        cudaEventRecord(ss->join, side);
+        cudaStreamWaitEvent(stream, ss->join, 0);
+        const cudaError_t ce = cudaGetLastError();
+        if (ce != cudaSuccess) return set_error(kErrLaunch, "bucket sort stream join: %s", cudaGetErrorString(ce));
     }
     return kOk;
 }
