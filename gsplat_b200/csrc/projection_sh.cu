@@ -99,7 +99,10 @@ __device__ __forceinline__ void sh_color(const float *coef, bool vec, const floa
 // Forward, packed layout (pass 2; pass 1 is projection_packed_count_kernel)
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(256) fused_packed_write_kernel(
+#ifndef GSB_PACKED_WRITE_MINB
+#define GSB_PACKED_WRITE_MINB 4 // measured fastest (latency-bound loads; a few bytes spill at degree 3)
+#endif
+__global__ void __launch_bounds__(256, GSB_PACKED_WRITE_MINB) fused_packed_write_kernel(
     FusedParams f, const uint32_t *vis_bits, const int64_t *block_accum, int64_t nnz,
     int32_t *indptr, int64_t *batch_ids, int64_t *camera_ids, int64_t *gaussian_ids,
     int32_t *radii, float *means2d, float *depths, float *conics, float *comps, float *colors,
