@@ -39,7 +39,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="gsb", choices=["gsb", "reference"])
-    ap.add_argument("--n", type=int, default=1_000_000, help="Gaussians per rank")
+    ap.add_argument("--n", type=int, default=None, help="Gaussians per rank (default: the workload's)")
+    ap.add_argument("--workload", default="config1", choices=["config1", "config3"],
+                    help="config1 (the headline, default) or config3 (3M Gaussians, 8 cameras at "
+                         "1920x1080, one GPU)")
     ap.add_argument("--dense", action="store_true", help="packed=False (trainer default)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -144,17 +147,21 @@ class ClockSampler:
                 "samples": len(inside), "source": "nvml", "window_s": round(t1 - t0, 4)}
 
 
-def make_params(n, seed, dev, rank=0, world=1):
+def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
     """config-1 Gaussians of one rank. With several ranks the shards sit side by
     side along x (12 units apart) and each rank's camera looks at its own shard,
     so every GPU renders one config-1 view of a scene that grows with the job
     (weak scaling); splats near the frustum edges still cross ranks through the
-    all-to-all."""
+    all-to-all. workload="config3": the 3M-Gaussian, 8-camera scene (one GPU)."""
     import torch
 
     from tests import _data
 
-    d = _data.config1(N=n, seed=seed)
+    if workload == "config3":
+        assert world == 1, "config3 is measured on one GPU"
+        d = _data.config3(N=n, seed=seed)
+    else:
+        d = _data.config1(N=n, seed=seed)
     shift = 12.0 * (rank - (world - 1) / 2.0)
     if world > 1:
         d["means"][:, 0] += shift
@@ -398,10 +405,13 @@ def run_gsb(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
-    params, d = make_params(args.n, 1 + rank, dev, rank, world)
+    if args.n is None:
+        args.n = 3_000_000 if args.workload == "config3" else 1_000_000
+    params, d = make_params(args.n, 1 + rank, dev, rank, world, args.workload)
     W, H = d["width"], d["height"]
     viewmat = d["viewmats"].to(dev)
     K = d["Ks"].to(dev)
+    n_cams = viewmat.shape[0]
     opt = gsplat_b200.SelectiveAdam([{"params": [p], "lr": LRS[k], "name": k} for k, p in params.items()],
                                     eps=1e-15, betas=(0.9, 0.999))
     # Upstream image gradients: N(0,1) images in antithetic pairs (G1, -G1, G2,
@@ -414,8 +424,8 @@ def run_gsb(args):
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     bank = []
     for _ in range(GRAD_BANK // 2):
-        G_ = torch.randn((1, H, W, 3), device=dev, generator=g)
-        Ga_ = torch.randn((1, H, W, 1), device=dev, generator=g)
+        G_ = torch.randn((n_cams, H, W, 3), device=dev, generator=g)
+        Ga_ = torch.randn((n_cams, H, W, 1), device=dev, generator=g)
         bank += [(G_, Ga_), (-G_, -Ga_)]
     step_no = [0]
 
@@ -457,7 +467,7 @@ def run_gsb(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    mpix = world * W * H / 1e6
+    mpix = world * n_cams * W * H / 1e6
     value = mpix / (ms / 1e3)
 
     # per-entry-point device time (CUDA events on the launching stream)
@@ -565,7 +575,7 @@ def run_gsb(args):
             gbs = traffic / t_bwd / 1e9
             roofline["hbm"] = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and args.workload == "config1":
         sc = cpu_scene(args.n, 1)
         cpu_reference_step(sc)
         dt, detail = cpu_reference_step(sc)
@@ -591,9 +601,11 @@ def run_gsb(args):
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic (seeded config-1 distributions, random-init Gaussians)",
-        "config": {"workload": "config1: 1M Gaussians, 1297x840 pinhole fx=fy=1150, SH deg 3, "
-                               "packed, fwd+bwd+SelectiveAdam",
-                   "gaussians_per_rank": args.n, "cameras_per_rank": 1,
+        "config": {"workload": ("config1: 1M Gaussians, 1297x840 pinhole fx=fy=1150, SH deg 3, "
+                                "packed, fwd+bwd+SelectiveAdam") if args.workload == "config1" else
+                               ("config3: 3M Gaussians, 8 cameras 1920x1080 fx=fy=1500 on a radius-8 "
+                                "sphere, SH deg 3, packed, fwd+bwd+SelectiveAdam"),
+                   "gaussians_per_rank": args.n, "cameras_per_rank": n_cams,
                    "parallelism": f"gaussian-sharded x{world}" if distributed else "single",
                    "l2": "inputs larger than L2 (params + Adam state ~700 MB)",
                    "visible_splats": nnz, "n_isects": n_isects},

@@ -390,11 +390,12 @@ __global__ void __launch_bounds__(256) shard_bases_kernel(const int64_t *__restr
 
 // Bucket b occupies [incl[b S - 1], incl[b S + S - 1]).
 // totals[0] = number of entries (-1 when it does not fit int32, like every
-// offset here), totals[1] = largest bucket, totals[2] = *nnz_device if given.
+// offset here), totals[1] = largest bucket, totals[2] = *nnz_device if given,
+// totals[3] / totals[4] = buckets of the sort classes (1024, 4096] / (4096, inf).
 __global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__restrict__ incl, uint32_t n_buckets,
                                                             uint32_t shards, int32_t *__restrict__ starts,
                                                             int32_t *__restrict__ sizes, const int64_t *nnz_device,
-                                                            int32_t *totals) {
+                                                            int32_t *totals, int32_t *__restrict__ class_list) {
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     int32_t c = 0;
     if (b < n_buckets) {
@@ -412,9 +413,24 @@ __global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__res
             totals[2] = v > 0x7fffffffll ? -1 : (int32_t)v;
         }
     }
+    // the radix-sorted size classes: counts, and the bucket ids listed
+    // (1024, 4096] from the front of class_list, > 4096 from its back
+    const uint32_t mid = __ballot_sync(0xffffffffu, c > 1024 && c <= 4096);
+    const uint32_t large = __ballot_sync(0xffffffffu, c > 4096);
+    const int lane = threadIdx.x & 31;
+    int mbase = 0, lbase = 0;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) c = max(c, __shfl_xor_sync(0xffffffffu, c, o));
-    if ((threadIdx.x & 31) == 0 && c > 0) atomicMax(totals + 1, c);
+    if (lane == 0) {
+        if (c > 0) atomicMax(totals + 1, c);
+        if (mid) mbase = atomicAdd(totals + 3, __popc(mid));
+        if (large) lbase = atomicAdd(totals + 4, __popc(large));
+    }
+    mbase = __shfl_sync(0xffffffffu, mbase, 0);
+    lbase = __shfl_sync(0xffffffffu, lbase, 0);
+    const uint32_t below = (1u << lane) - 1u;
+    if ((mid >> lane) & 1u) class_list[mbase + __popc(mid & below)] = (int32_t)b;
+    if ((large >> lane) & 1u) class_list[n_buckets - 1u - (uint32_t)(lbase + __popc(large & below))] = (int32_t)b;
 }
 
 __global__ void __launch_bounds__(256) isect_bucket_emit_kernel(IsectParams p, uint32_t n_isects,
@@ -460,9 +476,9 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
     }
 }
 
-constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (128 KiB of shared memory)
+constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (1024 threads x 16 entries)
 #ifndef GSB_BUCKET_E
-#define GSB_BUCKET_E 8 // entries per thread up to 4096-entry buckets
+#define GSB_BUCKET_E 8 // entries per thread of the bitonic sort (buckets of up to 1024 entries)
 #endif
 
 
@@ -580,9 +596,8 @@ __global__ void __launch_bounds__(1024)
                        uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
                        int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
     extern __shared__ __align__(16) uint64_t sk[];
-    // CTA c sorts buckets c, c + grid, ...: the grid is one CTA per bucket for
-    // the class that holds most buckets, and a few CTAs per SM for the rare
-    // large buckets
+    // CTA c sorts the buckets c, c + grid, ... of (lo_size, hi_size] entries
+    // (launched with one CTA per bucket)
     for (uint32_t b = blockIdx.x; b < n_buckets; b += gridDim.x) {
         const int n = sizes[b];
         if (n <= lo_size || n > hi_size) continue; // another size class
@@ -590,6 +605,425 @@ __global__ void __launch_bounds__(1024)
     }
 }
 
+
+// Buckets of more than 1024 entries: stable LSD radix sort in shared memory.
+// The keys are the depth bits minus the bucket's smallest, so only the bits
+// of the bucket's depth range are sorted, in as few passes of at most DBITS
+// bits as cover them (three for the usual 25-bit range at DBITS = 9): O(n) per
+// pass where a bitonic network is O(n log^2 n). Warp w owns the contiguous
+// entries [32 R w, 32 R (w + 1)) (R = rounds of this bucket), entry
+// 32 R w + 32 r + lane in round r of that lane, key and splat index in
+// registers. A pass ranks each warp's entries in index order with
+// warp-private digit counters (match_any groups the lanes of one digit), one
+// scan over the counters in digit-major order turns them into run bases, and
+// the entries are scattered to base + rank in shared memory and read back.
+//
+// The stable sort by depth leaves equal depths in emit order, which is not the
+// splat-index order of the reference's stable global sort: each run of equal
+// depths is then sorted by splat index by the thread holding its first entry
+// (runs of float depths are a few entries long). A bucket with a run longer
+// than kTieRun re-sorts its (depth, index) pairs with a bitonic network in
+// place.
+constexpr int kTieRun = 32;
+#ifndef GSB_BIN_COST
+#define GSB_BIN_COST 32 // most comparisons per entry of the one-pass bin sort
+#endif
+constexpr int kBinCost = GSB_BIN_COST;
+constexpr int kBinTarget = 4; // entries per sub-bin of the one-pass sort, at most
+#ifndef GSB_RADIX_MATCH
+#define GSB_RADIX_MATCH 1 // peers of a digit by match_any (1) or by one ballot per digit bit (0)
+#endif
+
+// sub-bins of the one-pass sort: fewer than 2 n / kBinTarget + 256 for n entries
+template <int CAP> constexpr int sub_bin_max() { return 2 * CAP / kBinTarget + 256; }
+// counter words: the radix digit counters [2^DBITS][warps + 1], or the one-pass
+// sort's sub-bin ends and 2 x 256 coarse-bin words
+template <int THREADS, int RMAX, int DBITS> constexpr int radix_counter_words() {
+    return (1 << DBITS) * (THREADS / 32 + 1) > sub_bin_max<THREADS * RMAX>() + 512
+               ? (1 << DBITS) * (THREADS / 32 + 1)
+               : sub_bin_max<THREADS * RMAX>() + 512;
+}
+template <int THREADS, int RMAX, int DBITS> constexpr size_t radix_smem_bytes() {
+    // keys, indices, counters, warp totals
+    return (size_t)(2 * THREADS * RMAX + radix_counter_words<THREADS, RMAX, DBITS>() + 72) * sizeof(uint32_t);
+}
+
+template <int THREADS, int RMAX, int DBITS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB)
+    bucket_radix_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
+                        const int32_t *__restrict__ list, int count, int from_back,
+                        const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
+                        uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits,
+                        int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
+    constexpr int CAP = THREADS * RMAX;
+    constexpr int NW = THREADS / 32;
+    constexpr int ND = 1 << DBITS;
+    constexpr int CW = NW + 1;               // words per digit row: (digit, warp) at digit * CW + warp
+    constexpr int NC = radix_counter_words<THREADS, RMAX, DBITS>(); // counter words
+    constexpr int kSubBinMax = sub_bin_max<CAP>();
+    constexpr int PER = ND * NW / THREADS;   // counters per thread in the scan (digit-major order)
+    static_assert(PER * THREADS == ND * NW && (PER % NW == 0 || NW % PER == 0), "scan split");
+    static_assert(NC % 4 == 0 && (2 * CAP) % 4 == 0, "vector zeroing");
+    static_assert(NW <= 32 && CAP <= 65536, "warp minima / maxima in misc[0, 64); 16-bit ranks");
+    static_assert(THREADS >= 256, "one coarse bin per thread");
+    extern __shared__ __align__(16) uint32_t smem[];
+    uint32_t *skey = smem;            // [CAP] keys
+    uint32_t *sval = smem + CAP;      // [CAP] splat indices
+    uint32_t *wcnt = smem + 2 * CAP;  // [ND][CW] digit counters, then run bases (LSD passes)
+    uint32_t *misc = wcnt + NC;       // [72] warp minima / maxima, warp scan totals, sub-bin count
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    // counter k of this thread in the scan: q = PER t + k at q + q / NW
+    const int cbase = PER >= NW ? t * (PER / NW) * CW : (PER * t / NW) * CW + (PER * t) % NW;
+    // the buckets of this size class: list[0, count) or list[n_buckets - count, n_buckets)
+    for (int c = blockIdx.x; c < count; c += gridDim.x) {
+        const uint32_t b = (uint32_t)list[from_back ? (int)n_buckets - 1 - c : c];
+        const int n = sizes[b];
+        const int start = starts[b];
+        const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
+        const int R = (n + THREADS - 1) / THREADS;
+        const int wbase = 32 * R * w + lane; // entry of round 0
+        uint32_t key[RMAX], val[RMAX], rank2[RMAX / 2]; // two 16-bit ranks per word
+        uint32_t kmin = 0xffffffffu, kmax = 0;
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+            const int i = wbase + 32 * r;
+            key[r] = 0;
+            val[r] = 0;
+            if (r < R && i < n) {
+                key[r] = depth_in[start + i];
+                val[r] = (uint32_t)id_in[start + i];
+                kmin = min(kmin, key[r]);
+                kmax = max(kmax, key[r]);
+            }
+        }
+        kmin = __reduce_min_sync(0xffffffffu, kmin);
+        kmax = __reduce_max_sync(0xffffffffu, kmax);
+        if (lane == 0) {
+            misc[w] = kmin;
+            misc[32 + w] = kmax;
+        }
+        __syncthreads();
+        {
+            const uint32_t m0 = lane < NW ? misc[lane] : 0xffffffffu;
+            const uint32_t m1 = lane < NW ? misc[32 + lane] : 0u;
+            kmin = __reduce_min_sync(0xffffffffu, m0);
+            kmax = __reduce_max_sync(0xffffffffu, m1);
+        }
+        const uint32_t range = kmax - kmin;
+        const int bits = range ? 32 - __clz(range) : 0;
+        const int passes = (bits + DBITS - 1) / DBITS;
+        const int width = passes ? (bits + passes - 1) / passes : 0;
+        const uint32_t dmask = (1u << width) - 1u;
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) key[r] -= kmin;
+        {
+            // One pass for spread-out depths: a counting sort of the entries
+            // into bins of about kBinTarget entries, then the rank of each entry
+            // inside its bin from comparisons of (depth, splat index) with the
+            // bin's other entries, which orders ties by splat index too. The
+            // bins follow the depth distribution: a histogram of the top 8 bits
+            // of the key, and each of those 256 coarse bins split into 2^s
+            // sub-bins by the next s bits, s chosen from its count. A bucket
+            // whose bins would still cost more than kBinCost comparisons per
+            // entry (many equal depths) takes the LSD passes below instead.
+            const int sh1 = bits > 8 ? bits - 8 : 0;
+            uint32_t *bend = wcnt;                 // [sub-bins] counts, cursors, then bin ends
+            uint32_t *ccnt = wcnt + kSubBinMax;    // [256] coarse counts
+            uint32_t *cinfo = ccnt + 256;          // [256] first sub-bin | split bits << 24
+            __syncthreads(); // the warp minima / maxima are read
+            for (int k = t; k < 256; k += THREADS) ccnt[k] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                const int i = wbase + 32 * r;
+                if (r < R && i < n) atomicAdd(&ccnt[key[r] >> sh1], 1u);
+            }
+            __syncthreads();
+            // split bits per coarse bin and the exclusive scan of 2^s (threads
+            // 0..255, one coarse bin each)
+            {
+                uint32_t nsub = 0, split = 0;
+                if (t < 256) {
+                    const uint32_t nc = ccnt[t];
+                    split = nc > (uint32_t)kBinTarget ? 32u - __clz((nc - 1u) / (uint32_t)kBinTarget) : 0u;
+                    split = min(split, (uint32_t)sh1);
+                    nsub = 1u << split;
+                }
+                uint32_t incl = nsub;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t u = __shfl_up_sync(0xffffffffu, incl, off);
+                    if (lane >= off) incl += u;
+                }
+                if (lane == 31) misc[w] = incl;
+                __syncthreads();
+                uint32_t m = lane < 8 ? misc[lane] : 0u;
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1) {
+                    const uint32_t u = __shfl_up_sync(0xffffffffu, m, off);
+                    if (lane >= off) m += u;
+                }
+                const uint32_t before_w = __shfl_sync(0xffffffffu, m, (w + 31) & 31);
+                if (t < 256) cinfo[t] = ((w > 0 ? before_w : 0u) + incl - nsub) | (split << 24);
+                misc[64] = __shfl_sync(0xffffffffu, m, 7); // sub-bins in all (every thread writes the same)
+            }
+            __syncthreads();
+            const int nsb = (int)misc[64];
+            for (int k = t; k < nsb; k += THREADS) bend[k] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                const int i = wbase + 32 * r;
+                if (r < R && i < n) {
+                    const uint32_t ci = cinfo[key[r] >> sh1], sp = ci >> 24;
+                    atomicAdd(&bend[(ci & 0xffffffu) + ((key[r] >> (sh1 - sp)) & ((1u << sp) - 1u))], 1u);
+                }
+            }
+            __syncthreads();
+            // exclusive scan of the sub-bin counts (thread t owns a chunk) and
+            // the sum of squared counts = comparisons of the rank step
+            const int chunk = (nsb + THREADS - 1) / THREADS;
+            const int first = min(t * chunk, nsb), last = min(first + chunk, nsb);
+            uint32_t tot = 0, sq = 0;
+            for (int k = first; k < last; ++k) {
+                const uint32_t v = bend[k];
+                tot += v;
+                sq += v * v;
+            }
+            uint32_t incl = tot;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += u;
+            }
+            sq = __reduce_add_sync(0xffffffffu, sq);
+            if (lane == 31) misc[w] = incl;
+            if (lane == 0) misc[32 + w] = sq;
+            __syncthreads();
+            uint32_t m = lane < NW ? misc[lane] : 0u;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const uint32_t u = __shfl_up_sync(0xffffffffu, m, off);
+                if (lane >= off) m += u;
+            }
+            const uint32_t before_w = __shfl_sync(0xffffffffu, m, (w + 31) & 31);
+            const uint32_t sq_all = __reduce_add_sync(0xffffffffu, lane < NW ? misc[32 + lane] : 0u);
+            if (sq_all <= (uint32_t)kBinCost * (uint32_t)n) {
+                uint32_t run = (w > 0 ? before_w : 0u) + incl - tot;
+                for (int k = first; k < last; ++k) {
+                    const uint32_t v = bend[k];
+                    bend[k] = run;
+                    run += v;
+                }
+                __syncthreads();
+                // scatter by sub-bin (in no particular order inside one)
+#pragma unroll
+                for (int r = 0; r < RMAX; ++r) {
+                    const int i = wbase + 32 * r;
+                    if (r < R && i < n) {
+                        const uint32_t ci = cinfo[key[r] >> sh1], sp = ci >> 24;
+                        const uint32_t x = (ci & 0xffffffu) + ((key[r] >> (sh1 - sp)) & ((1u << sp) - 1u));
+                        const uint32_t q = atomicAdd(&bend[x], 1u);
+                        skey[q] = key[r];
+                        sval[q] = val[r];
+                    }
+                }
+                __syncthreads();
+                // rank inside the sub-bin (bend[x] is now the end of sub-bin x,
+                // bend[x - 1] its start); the lanes of a warp hold neighbouring
+                // entries, mostly of one sub-bin
+                for (int q = t; q < n; q += THREADS) {
+                    const uint32_t k = skey[q], v = sval[q];
+                    const uint32_t ci = cinfo[k >> sh1], sp = ci >> 24;
+                    const uint32_t x = (ci & 0xffffffu) + ((k >> (sh1 - sp)) & ((1u << sp) - 1u));
+                    const int s0 = x > 0 ? (int)bend[x - 1] : 0, e0 = (int)bend[x];
+                    int rank = 0;
+                    for (int j = s0; j < e0; ++j) {
+                        const uint32_t kj = skey[j];
+                        rank += (kj < k || (kj == k && sval[j] < v)) ? 1 : 0;
+                    }
+                    keys_out[start + s0 + rank] = hi | (int64_t)(k + kmin);
+                    ids_out[start + s0 + rank] = (int32_t)v;
+                }
+                __syncthreads(); // shared memory is reused by the next bucket
+                continue;
+            }
+        }
+        for (int shift = 0; shift < bits; shift += width) {
+            __syncthreads(); // misc and the counters of the previous pass are read
+            for (int k = t; k < NC / 4; k += THREADS) reinterpret_cast<uint4 *>(wcnt)[k] = make_uint4(0, 0, 0, 0);
+            __syncthreads();
+            // warp-local ranks in index order
+#pragma unroll
+            for (int r = 0; r < RMAX / 2; ++r) rank2[r] = 0;
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                if (r < R) {
+                    const bool valid = wbase + 32 * r < n;
+                    const uint32_t vm = __ballot_sync(0xffffffffu, valid);
+                    if (valid) {
+                        const uint32_t d = (key[r] >> shift) & dmask;
+#if GSB_RADIX_MATCH
+                        const uint32_t peers = __match_any_sync(vm, d);
+#else
+                        // lanes of digit d: one ballot per digit bit
+                        uint32_t peers = vm;
+#pragma unroll
+                        for (int bit = 0; bit < DBITS; ++bit) {
+                            if (bit < width) {
+                                const uint32_t bb = __ballot_sync(vm, (d >> bit) & 1u);
+                                peers &= ((d >> bit) & 1u) ? bb : ~bb;
+                            }
+                        }
+#endif
+                        uint32_t *cnt = &wcnt[d * CW + w];
+                        const uint32_t before = *cnt;
+                        __syncwarp(vm);
+                        if (lane == 31 - __clz(peers)) *cnt = before + (uint32_t)__popc(peers);
+                        rank2[r >> 1] |= (before + (uint32_t)__popc(peers & ((1u << lane) - 1u))) << (16 * (r & 1));
+                    }
+                    __syncwarp();
+                }
+            }
+            __syncthreads();
+            {
+                // run bases: exclusive scan over the counters in digit-major order
+                uint32_t tot = 0;
+#pragma unroll
+                for (int k = 0; k < PER; ++k) tot += wcnt[cbase + (k / NW) * CW + k % NW];
+                uint32_t incl = tot;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t u = __shfl_up_sync(0xffffffffu, incl, off);
+                    if (lane >= off) incl += u;
+                }
+                if (lane == 31) misc[w] = incl;
+                __syncthreads();
+                uint32_t m = lane < NW ? misc[lane] : 0u;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t u = __shfl_up_sync(0xffffffffu, m, off);
+                    if (lane >= off) m += u;
+                }
+                const uint32_t before_w = __shfl_sync(0xffffffffu, m, (w + 31) & 31);
+                uint32_t run = (w > 0 ? before_w : 0u) + incl - tot;
+#pragma unroll
+                for (int k = 0; k < PER; ++k) {
+                    uint32_t *cp = &wcnt[cbase + (k / NW) * CW + k % NW];
+                    const uint32_t v = *cp;
+                    *cp = run;
+                    run += v;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                const int i = wbase + 32 * r;
+                if (r < R && i < n) {
+                    const uint32_t q = wcnt[((key[r] >> shift) & dmask) * CW + w] +
+                                       ((rank2[r >> 1] >> (16 * (r & 1))) & 0xffffu);
+                    skey[q] = key[r];
+                    sval[q] = val[r];
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                const int i = wbase + 32 * r;
+                if (r < R && i < n) {
+                    key[r] = skey[i];
+                    val[r] = sval[i];
+                }
+            }
+        }
+        if (bits == 0) { // one depth: no pass ran
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+                const int i = wbase + 32 * r;
+                if (r < R && i < n) {
+                    skey[i] = key[r];
+                    sval[i] = val[r];
+                }
+            }
+        }
+        __syncthreads();
+        // runs of equal depth, sorted by splat index
+        bool long_run = false;
+        for (int i = t; i < n; i += THREADS) {
+            const uint32_t k = skey[i];
+            if ((i == 0 || skey[i - 1] != k) && i + 1 < n && skey[i + 1] == k) {
+                int e = i + 1; // the run is [i, e)
+                while (e < n && e - i <= kTieRun && skey[e] == k) ++e;
+                if (e - i > kTieRun) {
+                    long_run = true;
+                } else {
+                    for (int a = i + 1; a < e; ++a) {
+                        const uint32_t v = sval[a];
+                        int c2 = a;
+                        for (; c2 > i && sval[c2 - 1] > v; --c2) sval[c2] = sval[c2 - 1];
+                        sval[c2] = v;
+                    }
+                }
+            }
+        }
+        if (__syncthreads_or(long_run)) {
+            // bitonic sort of the (depth, index) pairs in place; padding
+            // (~0, ~0) sorts last (indices are below 2^31)
+            int npad = 2;
+            while (npad < n) npad <<= 1;
+            for (int i = n + t; i < npad; i += THREADS) {
+                skey[i] = 0xffffffffu;
+                sval[i] = 0xffffffffu;
+            }
+            __syncthreads();
+            for (int k = 2; k <= npad; k <<= 1) {
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    const int lj = 31 - __clz(j);
+                    for (int q = t; q < npad / 2; q += THREADS) {
+                        const int i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
+                        const uint32_t xk = skey[i], yk = skey[i + j], xv = sval[i], yv = sval[i + j];
+                        const bool gt = xk > yk || (xk == yk && xv > yv);
+                        if (gt == ((i & k) == 0)) {
+                            skey[i] = yk;
+                            skey[i + j] = xk;
+                            sval[i] = yv;
+                            sval[i + j] = xv;
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+        }
+        for (int i = t; i < n; i += THREADS) {
+            keys_out[start + i] = hi | (int64_t)(skey[i] + kmin);
+            ids_out[start + i] = (int32_t)sval[i];
+        }
+        __syncthreads(); // shared memory is reused by the next bucket
+    }
+}
+
+// radix kernel shapes: threads, entries per thread, digit bits, CTAs per SM
+#ifndef GSB_RADIX_MID_SHAPE // buckets of (1024, 4096] entries
+#define GSB_RADIX_MID_T 256
+#define GSB_RADIX_MID_R 16
+#define GSB_RADIX_MID_D 9
+#define GSB_RADIX_MID_B 3
+#endif
+#ifndef GSB_RADIX_LARGE_SHAPE // buckets of (4096, 16384] entries
+#define GSB_RADIX_LARGE_T 512
+#define GSB_RADIX_LARGE_R 32
+#define GSB_RADIX_LARGE_D 9
+#define GSB_RADIX_LARGE_B 1
+#endif
+#define GSB_RADIX_MID GSB_RADIX_MID_T, GSB_RADIX_MID_R, GSB_RADIX_MID_D, GSB_RADIX_MID_B
+#define GSB_RADIX_LARGE GSB_RADIX_LARGE_T, GSB_RADIX_LARGE_R, GSB_RADIX_LARGE_D, GSB_RADIX_LARGE_B
+
+template <int THREADS, int RMAX, int DBITS, int MINB> struct RadixShape {
+    static constexpr int threads = THREADS;
+    static constexpr int cap = THREADS * RMAX;
+    static constexpr int per_sm = MINB;
+    static constexpr size_t smem = radix_smem_bytes<THREADS, RMAX, DBITS>();
+};
 
 static uint32_t bit_length(uint64_t v) {
     uint32_t b = 0;
@@ -772,11 +1206,11 @@ extern "C" size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, in
 
 extern "C" int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
                                         int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
-                                        const int64_t *nnz_device, int32_t *totals, void *scratch,
-                                        size_t scratch_bytes, cudaStream_t stream) {
+                                        const int64_t *nnz_device, int32_t *totals, int32_t *class_list,
+                                        void *scratch, size_t scratch_bytes, cudaStream_t stream) {
     if (shards <= 0 || n_buckets < 0 || n_buckets > 0x7fffffffll / shards)
         return set_error(kErrInvalidArgument, "bad bucket count %lld x %d shards", n_buckets, shards);
-    cudaError_t ce = cudaMemsetAsync(totals, 0, 3 * sizeof(int32_t), stream);
+    cudaError_t ce = cudaMemsetAsync(totals, 0, 5 * sizeof(int32_t), stream);
     if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
     if (n_buckets == 0) return kOk;
     if (scratch_bytes < gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards))
@@ -790,7 +1224,7 @@ extern "C" int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n
         return e;
     shard_bases_kernel<<<(unsigned)((n_shards + 255) / 256), 256, 0, stream>>>(incl, (uint32_t)n_shards, cursor);
     bucket_starts_kernel<<<(unsigned)((n_buckets + 255) / 256), 256, 0, stream>>>(
-        incl, (uint32_t)n_buckets, (uint32_t)shards, offsets, bucket_sizes, nnz_device, totals);
+        incl, (uint32_t)n_buckets, (uint32_t)shards, offsets, bucket_sizes, nnz_device, totals, class_list);
     return check_launch("bucket_starts_kernel");
 }
 
@@ -824,9 +1258,10 @@ extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const in
 extern "C" int gsb_isect_bucket_sort_max(void) { return kBucketSortMax; }
 
 extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
-                                     const int32_t *bucket_sizes, int max_count,
-                                     const uint32_t *bucket_depths, const int32_t *bucket_ids,
-                                     int64_t *isect_ids, int32_t *flatten_ids, cudaStream_t stream) {
+                                     const int32_t *bucket_sizes, int max_count, int mid_buckets,
+                                     int large_buckets, const int32_t *class_list, const uint32_t *bucket_depths,
+                                     const int32_t *bucket_ids, int64_t *isect_ids, int32_t *flatten_ids,
+                                     cudaStream_t stream) {
     const uint64_t n_tiles = (uint64_t)tile_width * (uint64_t)tile_height;
     const uint64_t n_buckets = (uint64_t)I * n_tiles;
     if (max_count > kBucketSortMax)
@@ -835,42 +1270,60 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
     if (n_buckets == 0 || max_count <= 0) return kOk;
     if (n_buckets > 0x7fffffffull) return set_error(kErrInvalidArgument, "too many buckets");
     const uint32_t tb = bit_length(n_tiles);
-    const unsigned grid = (unsigned)n_buckets;
-    // size classes (0, 1024], (1024, 4096], (4096, 16384], one launch each, sized
-    // for the largest bucket of the class; a CTA whose bucket is in another
-    // class returns at once. The classes sort disjoint buckets, so the rare
-    // large ones run on a side stream next to the first class (forked from and
-    // joined back to the caller's stream with events).
+    // Buckets of up to 1024 entries (most of them): one CTA per bucket, bitonic
+    // network in registers and shared memory; a CTA whose bucket is larger
+    // returns at once. Larger buckets: the radix kernels over the class lists,
+    // 256 threads x 16 entries up to 4096 entries, 1024 x 16 above, on a side
+    // stream next to the first class (forked from and joined back to the
+    // caller's stream with events).
+    {
+        int npad = 2;
+        while (npad < std::min(max_count, 1024)) npad <<= 1;
+        const int threads = npad / GSB_BUCKET_E < 32 ? 32 : npad / GSB_BUCKET_E;
+        const size_t smem = (size_t)threads * GSB_BUCKET_E * sizeof(uint64_t);
+        auto kern = bucket_sort_kernel<GSB_BUCKET_E>;
+        if (int e = set_cta_smem((const void *)kern, smem)) return e;
+        kern<<<(unsigned)n_buckets, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
+                                                             (uint32_t)n_buckets, (uint32_t)n_tiles, tb, 0, 1024,
+                                                             isect_ids, flatten_ids);
+        if (int e = check_launch("bucket_sort_kernel")) return e;
+    }
+    if (mid_buckets < 0 || large_buckets < 0 || (uint64_t)mid_buckets + (uint64_t)large_buckets > n_buckets)
+        return set_error(kErrInvalidArgument, "bad size class counts %d, %d", mid_buckets, large_buckets);
+    if (max_count > 1024 && mid_buckets + large_buckets == 0)
+        return set_error(kErrInvalidArgument, "buckets above 1024 entries but empty class lists");
     cudaStream_t side = stream;
     SideStream *ss = nullptr;
     std::unique_lock<std::mutex> side_lock(g_side_mutex, std::defer_lock);
-    if (max_count > 1024) {
+    if (mid_buckets + large_buckets > 0) {
         side_lock.lock(); // held until the join is recorded
         if (int e = side_stream(&ss)) return e;
         side = ss->stream;
         cudaEventRecord(ss->fork, stream);
         cudaStreamWaitEvent(side, ss->fork, 0);
     }
-    int lo = 0;
-    for (int hi : {1024, 4096, kBucketSortMax}) {
-        if (max_count > lo) {
-            const int cap = hi < max_count ? hi : max_count;
-            int npad = 2;
-            while (npad < cap) npad <<= 1;
-            const int E = hi <= 4096 ? GSB_BUCKET_E : 16;
-            const int threads = npad / E < 32 ? 32 : npad / E;
-            const size_t smem = (size_t)threads * E * sizeof(uint64_t);
-            auto kern = E == 16 ? bucket_sort_kernel<16> : bucket_sort_kernel<GSB_BUCKET_E>;
-            if (int e = set_cta_smem((const void *)kern, smem)) return e;
-            // first class: one CTA per bucket; larger (rare) buckets: two CTAs per
-            // SM walking all buckets, instead of launching one CTA per bucket
-            const unsigned g = lo == 0 ? grid : (unsigned)std::min<uint64_t>(n_buckets, 2ull * device_sms());
-            kern<<<g, threads, smem, lo == 0 ? stream : side>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
-                                                                (uint32_t)n_buckets, (uint32_t)n_tiles, tb, lo, hi,
-                                                                isect_ids, flatten_ids);
-            if (int e = check_launch("bucket_sort_kernel")) return e;
-        }
-        lo = hi;
+    const int sms = device_sms();
+    if (mid_buckets > 0) {
+        auto kern = bucket_radix_kernel<GSB_RADIX_MID>;
+        const int threads = RadixShape<GSB_RADIX_MID>::threads;
+        const size_t smem = RadixShape<GSB_RADIX_MID>::smem;
+        static_assert(RadixShape<GSB_RADIX_MID>::cap >= 4096, "mid class capacity");
+        if (int e = set_cta_smem((const void *)kern, smem)) return e;
+        kern<<<(unsigned)std::min(mid_buckets, RadixShape<GSB_RADIX_MID>::per_sm * sms), threads, smem, side>>>(
+            offsets, bucket_sizes, class_list, mid_buckets, 0, bucket_depths, bucket_ids, (uint32_t)n_buckets,
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
+        if (int e = check_launch("bucket_radix_kernel")) return e;
+    }
+    if (large_buckets > 0) {
+        auto kern = bucket_radix_kernel<GSB_RADIX_LARGE>;
+        const int threads = RadixShape<GSB_RADIX_LARGE>::threads;
+        const size_t smem = RadixShape<GSB_RADIX_LARGE>::smem;
+        static_assert(RadixShape<GSB_RADIX_LARGE>::cap >= kBucketSortMax, "large class capacity");
+        if (int e = set_cta_smem((const void *)kern, smem)) return e;
+        kern<<<(unsigned)std::min(large_buckets, RadixShape<GSB_RADIX_LARGE>::per_sm * sms), threads, smem, side>>>(
+            offsets, bucket_sizes, class_list, large_buckets, 1, bucket_depths, bucket_ids, (uint32_t)n_buckets,
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
+        if (int e = check_launch("bucket_radix_kernel")) return e;
     }
     if (ss != nullptr) {
         cudaEventRecord(ss->join, side);

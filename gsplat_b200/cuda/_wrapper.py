@@ -538,12 +538,13 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
     offsets = torch.empty(n_buckets, dtype=torch.int32, device=dev)
     bucket_sizes = torch.empty(n_buckets, dtype=torch.int32, device=dev)
     cursor = torch.empty(n_buckets * shards, dtype=torch.int32, device=dev)
-    totals = torch.empty(3, dtype=torch.int32, device=dev)
+    totals = torch.empty(5, dtype=torch.int32, device=dev)
+    class_list = torch.empty(n_buckets, dtype=torch.int32, device=dev)
     nbytes = _B.lib().gsb_isect_bucket_offsets_scratch_bytes(n_buckets, shards)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     call("gsb_isect_bucket_offsets", ptr(shard_counts), n_buckets, shards, ptr(offsets), ptr(bucket_sizes),
-         ptr(cursor), ptr(nnz_device), ptr(totals), ptr(scratch), nbytes, stream)
-    n_isects, largest, nnz = (int(v) for v in totals.tolist())
+         ptr(cursor), ptr(nnz_device), ptr(totals), ptr(class_list), ptr(scratch), nbytes, stream)
+    n_isects, largest, nnz, mid_buckets, large_buckets = (int(v) for v in totals.tolist())
     if n_isects < 0 or nnz < 0:
         raise RuntimeError("isect_tiles: more than 2^31 - 1 tile intersections or splats")
     if nnz_device is None:
@@ -560,7 +561,8 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
         call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_depths), ptr(bucket_ids),
              stream)
         call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
-             ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids), ptr(flatten_ids), stream)
+             mid_buckets, large_buckets, ptr(class_list), ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids),
+             ptr(flatten_ids), stream)
         return isect_ids, flatten_ids, offsets, nnz
     # a bucket too large for the on-chip sort: emit in splat order and sort
     # globally (stable LSD radix sort)

@@ -248,16 +248,19 @@ GSB_API int gsb_isect_count_tiles(int packed, int I, int N, int nnz, const int64
                                   int tile_width, int tile_height, const int64_t *nnz_device,
                                   int32_t *tiles_per_gauss, int32_t *shard_counts, cudaStream_t stream);
 /* 2. offsets int32 [n_buckets] (= gsb_isect_offset_encode's output),
- *    bucket_sizes int32 [n_buckets], the emit cursor int32 [n_buckets * S]
- *    and totals int32 [3] = {n_isects (-1 if above 2^31 - 1), largest bucket,
- *    *nnz_device (0 when nnz_device is NULL)}, all device memory, so one copy
- *    brings every size the host needs; scratch of
- *    gsb_isect_bucket_offsets_scratch_bytes(n_buckets, S). */
+ *    bucket_sizes int32 [n_buckets], the emit cursor int32 [n_buckets * S],
+ *    totals int32 [5] = {n_isects (-1 if above 2^31 - 1), largest bucket,
+ *    *nnz_device (0 when nnz_device is NULL), buckets with 1024 < size <= 4096,
+ *    buckets with size > 4096}, all device memory, so one copy brings every
+ *    size the host needs, and class_list int32 [n_buckets]: the ids of the
+ *    buckets with 1024 < size <= 4096 in its first totals[3] entries, of those
+ *    above 4096 in its last totals[4] entries (in no particular order); scratch
+ *    of gsb_isect_bucket_offsets_scratch_bytes(n_buckets, S). */
 GSB_API size_t gsb_isect_bucket_offsets_scratch_bytes(long long n_buckets, int shards);
 GSB_API int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_buckets, int shards,
                                      int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
-                                     const int64_t *nnz_device, int32_t *totals, void *scratch,
-                                     size_t scratch_bytes, cudaStream_t stream);
+                                     const int64_t *nnz_device, int32_t *totals, int32_t *class_list,
+                                     void *scratch, size_t scratch_bytes, cudaStream_t stream);
 /* 3. Scatter (depth bits, splat index) of every intersection into its bucket
  *    (unordered inside the bucket); n_isects = totals[0] of step 2. */
 GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
@@ -267,10 +270,15 @@ GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64
                                   uint32_t *bucket_depths, int32_t *bucket_ids, cudaStream_t stream);
 /* 4. Sort every bucket and write isect_ids int64 / flatten_ids int32
  *    [n_isects]. max_count (totals[1] of step 2) must not exceed
- *    gsb_isect_bucket_sort_max(); larger buckets take the global-sort path. */
+ *    gsb_isect_bucket_sort_max(); larger buckets take the global-sort path.
+ *    mid_buckets / large_buckets / class_list: totals[3] / totals[4] and the
+ *    class list of step 2 (buckets of up to 1024 entries are sorted by a
+ *    bitonic network, larger ones by a radix sort in shared memory walking
+ *    the list). */
 GSB_API int gsb_isect_bucket_sort_max(void);
 GSB_API int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
-                                  const int32_t *bucket_sizes, int max_count, const uint32_t *bucket_depths,
+                                  const int32_t *bucket_sizes, int max_count, int mid_buckets,
+                                  int large_buckets, const int32_t *class_list, const uint32_t *bucket_depths,
                                   const int32_t *bucket_ids, int64_t *isect_ids, int32_t *flatten_ids,
                                   cudaStream_t stream);
 

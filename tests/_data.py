@@ -49,6 +49,35 @@ def config1(N=1_000_000, seed=1):
                  z_range=(2.0, 12.0), xy_uniform=5.0)
 
 
+def look_at(eye, target=(0.0, 0.0, 0.0), up=(0.0, 0.0, 1.0)):
+    """World-to-camera 4x4 (OpenCV axes: z toward the target) for a camera at eye."""
+    eye = torch.as_tensor(eye, dtype=torch.float32)
+    z = torch.nn.functional.normalize(torch.as_tensor(target, dtype=torch.float32) - eye, dim=0)
+    u = torch.as_tensor(up, dtype=torch.float32)
+    if torch.cross(z, u, dim=0).norm() < 1e-4:
+        u = torch.tensor([0.0, 1.0, 0.0])
+    x = torch.nn.functional.normalize(torch.cross(z, u, dim=0), dim=0)
+    y = torch.cross(z, x, dim=0)
+    R = torch.stack([x, y, z])
+    vm = torch.eye(4)
+    vm[:3, :3] = R
+    vm[:3, 3] = -R @ eye
+    return vm
+
+
+def config3(N=3_000_000, seed=3, C=8):
+    """3M Gaussians with means ~ N(0, 2^2)^3, C cameras at
+    1920x1080 (fx=fy=1500) at uniformly random directions on a radius-8 sphere,
+    looking at the origin."""
+    g = torch.Generator().manual_seed(1000 + seed)
+    dirs = torch.nn.functional.normalize(torch.randn((C, 3), generator=g), dim=-1)
+    viewmats = torch.stack([look_at(8.0 * d) for d in dirs])
+    d = scene(N, seed=seed, width=1920, height=1080, fx=1500.0, cx=960.0, cy=540.0, C=C,
+              viewmats=viewmats)
+    d["means"] = torch.randn((N, 3), generator=torch.Generator().manual_seed(seed)) * 2.0
+    return d
+
+
 def to(d, device):
     return {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
 

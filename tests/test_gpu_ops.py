@@ -310,12 +310,17 @@ def _entry_points_called(fn):
     return out, names
 
 
-@pytest.mark.parametrize("mode", ["spread", "many_buckets", "cluster_on_chip", "cluster_fallback"])
+@pytest.mark.parametrize("mode", ["spread", "many_buckets", "cluster_mid_ties", "cluster_mid_distinct",
+                                  "cluster_mid_equal", "cluster_on_chip", "cluster_large_distinct",
+                                  "cluster_fallback"])
 def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     """Tile-bucket sort against the oracle's stable global sort, with many equal
     depths (ties are ordered by splat index, as in a stable sort of the emitted
     keys). The clustered cases pile thousands of splats into two tiles:
-    cluster_on_chip stays within the on-chip bucket sort (16 entries per thread),
+    cluster_mid_* fill buckets of 1024 to 4096 entries with 8 distinct depths
+    (radix passes), all-distinct depths (one-pass bin sort) and one depth;
+    cluster_on_chip (8 depths) and cluster_large_distinct stay within the on-chip
+    bucket sort with buckets above 4096 entries,
     cluster_fallback exceeds it and must switch to the global radix sort with the
     same result."""
     from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
@@ -323,7 +328,8 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     rng = np.random.default_rng(31 + len(mode))
     I, W, H = 2, 320, 240
     ts = 2 if mode == "many_buckets" else 16  # 2 x 160 x 120 buckets: the global-shard path
-    N = {"spread": 6000, "many_buckets": 6000, "cluster_on_chip": 9000, "cluster_fallback": 20000}[mode]
+    N = {"spread": 6000, "many_buckets": 6000, "cluster_on_chip": 9000, "cluster_large_distinct": 9000,
+         "cluster_fallback": 20000}.get(mode, 3000)
     tw, th = math.ceil(W / ts), math.ceil(H / ts)
     if mode.startswith("cluster"):
         m2 = np.empty((I, N, 2), np.float32)
@@ -334,6 +340,10 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
         m2 = np.stack([rng.uniform(-20, W + 20, (I, N)), rng.uniform(-20, H + 20, (I, N))], -1)
         r = rng.integers(0, 6 if mode == "many_buckets" else 40, (I, N, 2)).astype(np.int32)
     dep = rng.integers(1, 9, (I, N)).astype(np.float32) * 0.5  # 8 distinct depths
+    if mode in ("cluster_mid_distinct", "cluster_large_distinct"):
+        dep = (1.0 + rng.permutation(I * N) / 1024.0).reshape(I, N).astype(np.float32)
+    elif mode == "cluster_mid_equal":
+        dep = np.full((I, N), 2.0, np.float32)
     m2 = m2.astype(np.float32)
     (tpg, keys, ids, off), names = _entry_points_called(lambda: isect_tiles_with_offsets(
         torch.from_numpy(m2).to(DEV), torch.from_numpy(r).to(DEV), torch.from_numpy(dep).to(DEV), ts, tw, th))
@@ -348,8 +358,10 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     largest = np.bincount(ekeys >> 32).max()
     if fallback:
         assert largest > gsb_lib().gsb_isect_bucket_sort_max()
-    elif mode == "cluster_on_chip":
+    elif mode in ("cluster_on_chip", "cluster_large_distinct"):
         assert 4096 < largest <= gsb_lib().gsb_isect_bucket_sort_max()
+    elif mode.startswith("cluster_mid"):
+        assert 1024 < largest <= 4096
     shards = gsb_lib().gsb_isect_bucket_shards(I, tw, th)
     assert (shards == 16) == (mode == "many_buckets"), shards
 
