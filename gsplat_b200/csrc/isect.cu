@@ -260,7 +260,10 @@ __global__ void fill_i32_kernel(int32_t *p, uint32_t n, int32_t v) {
 // uses shard idx % 16, so that the hottest buckets do not serialise their
 // atomics on one address.
 // ---------------------------------------------------------------------------
-constexpr int kBucketShards = GSB_ISECT_BUCKET_SHARDS; // global-memory path
+#ifndef GSB_SHARDS
+#define GSB_SHARDS GSB_ISECT_BUCKET_SHARDS
+#endif
+constexpr int kBucketShards = GSB_SHARDS; // global-memory path
 static_assert((kBucketShards & (kBucketShards - 1)) == 0, "shards: power of two");
 constexpr uint32_t kCtaBucketMax = 24576; // buckets of the shared-memory path (96 KiB)
 #ifndef GSB_CTA_THREADS
@@ -315,24 +318,40 @@ struct SmemCountSink {
     __device__ __forceinline__ void put(int64_t tile_id) { atomicAdd(hist + base + tile_id, 1); }
 };
 
-// Places one entry at the slot returned by an atomic increment of its cursor
-// (global or shared memory). The bound keeps the slot inside the arrays.
-struct BucketSink {
-    uint32_t *depth_out;
-    int32_t *id_out;
+// Places one entry (depth bits << 32 | splat index) at the slot returned by an
+// atomic increment of its cursor (global or shared memory). Tiles are taken in
+// batches of K: the batch's increments are issued back to back, so the round
+// trips of global atomics overlap, and the 8-byte stores follow. The bound
+// keeps the slot inside the array; flush() places a partial batch.
+#ifndef GSB_EMIT_BATCH
+#define GSB_EMIT_BATCH 4 // global cursors (shared-memory cursors take one tile at a time)
+#endif
+
+template <int K> struct BucketSink {
+    uint64_t *out;
     int32_t *cursor;
     int64_t base;   // first cursor of the splat's image
     int32_t stride; // cursors per bucket in `cursor`
     int32_t shard;
     uint32_t limit; // n_isects
-    uint32_t depth_bits;
-    int32_t flat_id;
+    uint64_t entry;
+    uint32_t pend[K];
+    int npend = 0;
     __device__ __forceinline__ void put(int64_t tile_id) {
-        const uint32_t pos = (uint32_t)atomicAdd(cursor + (base + tile_id) * stride + shard, 1);
-        if (pos < limit) {
-            depth_out[pos] = depth_bits;
-            id_out[pos] = flat_id;
-        }
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (k == npend) pend[k] = (uint32_t)tile_id;
+        if (++npend == K) flush();
+    }
+    __device__ __forceinline__ void flush() {
+        uint32_t pos[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (k < npend) pos[k] = (uint32_t)atomicAdd(cursor + (base + pend[k]) * stride + shard, 1);
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (k < npend && pos[k] < limit) out[pos[k]] = entry;
+        npend = 0;
     }
 };
 
@@ -434,26 +453,24 @@ __global__ void __launch_bounds__(256) bucket_starts_kernel(const int64_t *__res
 }
 
 __global__ void __launch_bounds__(256) isect_bucket_emit_kernel(IsectParams p, uint32_t n_isects,
-                                                                int32_t *cursor, uint32_t *depth_out,
-                                                                int32_t *id_out) {
+                                                                int32_t *cursor, uint64_t *out) {
     const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= n_splats(p)) return;
-    BucketSink sink;
-    sink.depth_out = depth_out;
-    sink.id_out = id_out;
+    BucketSink<GSB_EMIT_BATCH> sink;
+    sink.out = out;
     sink.cursor = cursor;
     sink.base = splat_image(p, idx) * (int64_t)p.tile_width * p.tile_height;
     sink.stride = kBucketShards;
     sink.shard = (int32_t)(idx & (kBucketShards - 1));
     sink.limit = n_isects;
-    sink.depth_bits = det_f2u(p.depths[idx]);
-    sink.flat_id = (int32_t)idx;
-    splat_tiles<true, BucketSink>(p, idx, &sink);
+    sink.entry = ((uint64_t)det_f2u(p.depths[idx]) << 32) | idx;
+    splat_tiles<true, BucketSink<GSB_EMIT_BATCH>>(p, idx, &sink);
+    sink.flush();
 }
 
 __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kernel(IsectParams p, uint32_t n_buckets,
                                                                      uint32_t n_isects, const int32_t *cursor,
-                                                                     uint32_t *depth_out, int32_t *id_out) {
+                                                                     uint64_t *out) {
     extern __shared__ int32_t cur[];
     const uint32_t n = n_splats(p), G = gridDim.x;
     for (uint32_t b = threadIdx.x; b < n_buckets; b += blockDim.x) cur[b] = cursor[(size_t)b * G + blockIdx.x];
@@ -462,17 +479,16 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
     const uint32_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     const int64_t n_tiles = (int64_t)p.tile_width * p.tile_height;
     for (uint32_t idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
-        BucketSink sink;
-        sink.depth_out = depth_out;
-        sink.id_out = id_out;
+        BucketSink<1> sink;
+        sink.out = out;
         sink.cursor = cur;
         sink.base = splat_image(p, idx) * n_tiles;
         sink.stride = 1;
         sink.shard = 0;
         sink.limit = n_isects;
-        sink.depth_bits = det_f2u(p.depths[idx]);
-        sink.flat_id = (int32_t)idx;
-        splat_tiles<true, BucketSink>(p, idx, &sink);
+        sink.entry = ((uint64_t)det_f2u(p.depths[idx]) << 32) | idx;
+        splat_tiles<true, BucketSink<1>>(p, idx, &sink);
+        sink.flush();
     }
 }
 
@@ -522,15 +538,14 @@ template <int E> struct BitonicRegs {
 // padded with all-ones to a power of two, sorted ascending.
 template <int E>
 __device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n, int start,
-                                                const uint32_t *__restrict__ depth_in,
-                                                const int32_t *__restrict__ id_in, uint32_t n_tiles,
+                                                const uint64_t *__restrict__ entries, uint32_t n_tiles,
                                                 uint32_t tile_bits, int64_t *__restrict__ keys_out,
                                                 int32_t *__restrict__ ids_out) {
     const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
     if (n == 1) {
         if (threadIdx.x == 0) {
-            keys_out[start] = hi | (int64_t)depth_in[start];
-            ids_out[start] = id_in[start];
+            keys_out[start] = hi | (int64_t)(entries[start] >> 32);
+            ids_out[start] = (int32_t)(uint32_t)entries[start];
         }
         return;
     }
@@ -541,7 +556,7 @@ __device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n,
 #pragma unroll
     for (int e = 0; e < E; ++e) {
         const uint32_t i = base + e;
-        r.v[e] = i < (uint32_t)n ? ((uint64_t)depth_in[start + i] << 32) | (uint32_t)id_in[start + i] : ~0ull;
+        r.v[e] = i < (uint32_t)n ? entries[start + i] : ~0ull;
     }
     const uint32_t nthreads = blockDim.x;
     // warps whose entries all lie beyond npad (a bucket smaller than the largest)
@@ -592,7 +607,7 @@ __device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n,
 template <int E>
 __global__ void __launch_bounds__(1024)
     bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
-                       const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
+                       const uint64_t *__restrict__ entries,
                        uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
                        int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
     extern __shared__ __align__(16) uint64_t sk[];
@@ -601,7 +616,7 @@ __global__ void __launch_bounds__(1024)
     for (uint32_t b = blockIdx.x; b < n_buckets; b += gridDim.x) {
         const int n = sizes[b];
         if (n <= lo_size || n > hi_size) continue; // another size class
-        sort_one_bucket<E>(sk, b, n, starts[b], depth_in, id_in, n_tiles, tile_bits, keys_out, ids_out);
+        sort_one_bucket<E>(sk, b, n, starts[b], entries, n_tiles, tile_bits, keys_out, ids_out);
     }
 }
 
@@ -652,7 +667,7 @@ template <int THREADS, int RMAX, int DBITS, int MINB>
 __global__ void __launch_bounds__(THREADS, MINB)
     bucket_radix_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
                         const int32_t *__restrict__ list, int count, int from_back,
-                        const uint32_t *__restrict__ depth_in, const int32_t *__restrict__ id_in,
+                        const uint64_t *__restrict__ entries,
                         uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits,
                         int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
     constexpr int CAP = THREADS * RMAX;
@@ -690,8 +705,9 @@ __global__ void __launch_bounds__(THREADS, MINB)
             key[r] = 0;
             val[r] = 0;
             if (r < R && i < n) {
-                key[r] = depth_in[start + i];
-                val[r] = (uint32_t)id_in[start + i];
+                const uint64_t en = entries[start + i];
+                key[r] = (uint32_t)(en >> 32);
+                val[r] = (uint32_t)en;
                 kmin = min(kmin, key[r]);
                 kmax = max(kmax, key[r]);
             }
@@ -1232,7 +1248,7 @@ extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const in
                                      const float *means2d, const int32_t *radii, const float *depths,
                                      const float *conics, const float *opacities, int tile_size,
                                      int tile_width, int tile_height, long long n_isects, int32_t *cursor,
-                                     uint32_t *bucket_depths, int32_t *bucket_ids, cudaStream_t stream) {
+                                     uint64_t *bucket_entries, cudaStream_t stream) {
     IsectParams p;
     if (int e = make_isect_params(p, packed, I, N, nnz, image_ids, means2d, radii, depths, conics,
                                   opacities, tile_size, tile_width, tile_height))
@@ -1247,11 +1263,11 @@ extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const in
         const size_t smem = n_buckets * sizeof(int32_t);
         if (int e = set_cta_smem((const void *)isect_emit_cta_kernel, smem)) return e;
         isect_emit_cta_kernel<<<pl.shards, kCtaThreads, smem, stream>>>(
-            p, (uint32_t)n_buckets, (uint32_t)n_isects, cursor, bucket_depths, bucket_ids);
+            p, (uint32_t)n_buckets, (uint32_t)n_isects, cursor, bucket_entries);
         return check_launch("isect_emit_cta_kernel");
     }
     isect_bucket_emit_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
-        p, (uint32_t)n_isects, cursor, bucket_depths, bucket_ids);
+        p, (uint32_t)n_isects, cursor, bucket_entries);
     return check_launch("isect_bucket_emit_kernel");
 }
 
@@ -1259,8 +1275,8 @@ extern "C" int gsb_isect_bucket_sort_max(void) { return kBucketSortMax; }
 
 extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
                                      const int32_t *bucket_sizes, int max_count, int mid_buckets,
-                                     int large_buckets, const int32_t *class_list, const uint32_t *bucket_depths,
-                                     const int32_t *bucket_ids, int64_t *isect_ids, int32_t *flatten_ids,
+                                     int large_buckets, const int32_t *class_list, const uint64_t *bucket_entries,
+                                     int64_t *isect_ids, int32_t *flatten_ids,
                                      cudaStream_t stream) {
     const uint64_t n_tiles = (uint64_t)tile_width * (uint64_t)tile_height;
     const uint64_t n_buckets = (uint64_t)I * n_tiles;
@@ -1283,7 +1299,7 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
         const size_t smem = (size_t)threads * GSB_BUCKET_E * sizeof(uint64_t);
         auto kern = bucket_sort_kernel<GSB_BUCKET_E>;
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
-        kern<<<(unsigned)n_buckets, threads, smem, stream>>>(offsets, bucket_sizes, bucket_depths, bucket_ids,
+        kern<<<(unsigned)n_buckets, threads, smem, stream>>>(offsets, bucket_sizes, bucket_entries,
                                                              (uint32_t)n_buckets, (uint32_t)n_tiles, tb, 0, 1024,
                                                              isect_ids, flatten_ids);
         if (int e = check_launch("bucket_sort_kernel")) return e;
@@ -1310,7 +1326,7 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
         static_assert(RadixShape<GSB_RADIX_MID>::cap >= 4096, "mid class capacity");
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
         kern<<<(unsigned)std::min(mid_buckets, RadixShape<GSB_RADIX_MID>::per_sm * sms), threads, smem, side>>>(
-            offsets, bucket_sizes, class_list, mid_buckets, 0, bucket_depths, bucket_ids, (uint32_t)n_buckets,
+            offsets, bucket_sizes, class_list, mid_buckets, 0, bucket_entries, (uint32_t)n_buckets,
             (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
         if (int e = check_launch("bucket_radix_kernel")) return e;
     }
@@ -1321,7 +1337,7 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
         static_assert(RadixShape<GSB_RADIX_LARGE>::cap >= kBucketSortMax, "large class capacity");
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
         kern<<<(unsigned)std::min(large_buckets, RadixShape<GSB_RADIX_LARGE>::per_sm * sms), threads, smem, side>>>(
-            offsets, bucket_sizes, class_list, large_buckets, 1, bucket_depths, bucket_ids, (uint32_t)n_buckets,
+            offsets, bucket_sizes, class_list, large_buckets, 1, bucket_entries, (uint32_t)n_buckets,
             (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
         if (int e = check_launch("bucket_radix_kernel")) return e;
     }

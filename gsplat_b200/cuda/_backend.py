@@ -88,12 +88,12 @@ SIGNATURES = {
     "gsb_isect_bucket_shards": (I32, [I32, I32, I32]),
     "gsb_isect_bucket_offsets_scratch_bytes": (SZ, [I64, I32]),
     "gsb_isect_bucket_offsets": (I32, [P, I64, I32, P, P, P, P, P, P, P, SZ, P]),
-    "gsb_isect_bucket_emit": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, I64, P, P, P, P]),
+    "gsb_isect_bucket_emit": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, I64, P, P, P]),
     "gsb_isect_bucket_sort_max": (I32, []),
     "gsb_pack_rows": (I32, [I64, P, I32, P, P, P, P]),
     "gsb_unpack_rows": (I32, [I64, I32, P, I32, P, P, P]),
     "gsb_exchange_ids": (I32, [I64, P, P, P, I32, P, P, P, P]),
-    "gsb_isect_bucket_sort": (I32, [I32, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P]),
+    "gsb_isect_bucket_sort": (I32, [I32, I32, I32, P, P, I32, I32, I32, P, P, P, P, P]),
     "gsb_rasterize_fwd": (
         I32,
         [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P],

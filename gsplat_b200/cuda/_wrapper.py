@@ -556,12 +556,10 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
     if n_isects == 0:
         return isect_ids, flatten_ids, offsets, nnz
     if largest <= _B.lib().gsb_isect_bucket_sort_max():
-        bucket_depths = torch.empty(n_isects, dtype=torch.int32, device=dev)
-        bucket_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
-        call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_depths), ptr(bucket_ids),
-             stream)
+        bucket_entries = torch.empty(n_isects, dtype=torch.int64, device=dev)
+        call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_entries), stream)
         call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
-             mid_buckets, large_buckets, ptr(class_list), ptr(bucket_depths), ptr(bucket_ids), ptr(isect_ids),
+             mid_buckets, large_buckets, ptr(class_list), ptr(bucket_entries), ptr(isect_ids),
              ptr(flatten_ids), stream)
         return isect_ids, flatten_ids, offsets, nnz
     # a bucket too large for the on-chip sort: emit in splat order and sort

@@ -261,13 +261,14 @@ GSB_API int gsb_isect_bucket_offsets(const int32_t *shard_counts, long long n_bu
                                      int32_t *offsets, int32_t *bucket_sizes, int32_t *cursor,
                                      const int64_t *nnz_device, int32_t *totals, int32_t *class_list,
                                      void *scratch, size_t scratch_bytes, cudaStream_t stream);
-/* 3. Scatter (depth bits, splat index) of every intersection into its bucket
- *    (unordered inside the bucket); n_isects = totals[0] of step 2. */
+/* 3. Scatter every intersection into its bucket as one entry uint64
+ *    (depth bits << 32 | splat index) of bucket_entries [n_isects] (unordered
+ *    inside the bucket); n_isects = totals[0] of step 2. */
 GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64_t *image_ids,
                                   const float *means2d, const int32_t *radii, const float *depths,
                                   const float *conics, const float *opacities, int tile_size,
                                   int tile_width, int tile_height, long long n_isects, int32_t *cursor,
-                                  uint32_t *bucket_depths, int32_t *bucket_ids, cudaStream_t stream);
+                                  uint64_t *bucket_entries, cudaStream_t stream);
 /* 4. Sort every bucket and write isect_ids int64 / flatten_ids int32
  *    [n_isects]. max_count (totals[1] of step 2) must not exceed
  *    gsb_isect_bucket_sort_max(); larger buckets take the global-sort path.
@@ -278,9 +279,8 @@ GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64
 GSB_API int gsb_isect_bucket_sort_max(void);
 GSB_API int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
                                   const int32_t *bucket_sizes, int max_count, int mid_buckets,
-                                  int large_buckets, const int32_t *class_list, const uint32_t *bucket_depths,
-                                  const int32_t *bucket_ids, int64_t *isect_ids, int32_t *flatten_ids,
-                                  cudaStream_t stream);
+                                  int large_buckets, const int32_t *class_list, const uint64_t *bucket_entries,
+                                  int64_t *isect_ids, int32_t *flatten_ids, cudaStream_t stream);
 
 /* --- Rasterization --------------------------------------------------------
  * Replaces gsplat::rasterize_to_pixels_3dgs_fwd (Rasterization.cpp:42-119).
