@@ -18,8 +18,12 @@ from .cuda._wrapper import (
     has_reloc,
     isect_offset_encode,
     isect_tiles,
+    persp_proj,
+    proj,
+    quat_scale_to_covar_preci,
     rasterize_to_pixels,
     spherical_harmonics,
+    world_to_cam,
 )
 from .optimizers import SelectiveAdam
 from .rendering import RasterizeMode, RenderMode, rasterization
@@ -41,7 +45,11 @@ __all__ = [
     "has_reloc",
     "isect_offset_encode",
     "isect_tiles",
+    "persp_proj",
+    "proj",
+    "quat_scale_to_covar_preci",
     "rasterization",
     "rasterize_to_pixels",
     "spherical_harmonics",
+    "world_to_cam",
 ]

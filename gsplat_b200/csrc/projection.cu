@@ -2,8 +2,9 @@
 //
 // Reference behaviour: gsplat/cuda/csrc/ProjectionEWA3DGSFused.cu:38-234 (forward),
 // :316-553 (backward), ProjectionEWA3DGSPacked.cu:39-290 / 400-690 (packed COO
-// layout), with the math of gsplat/cuda/include/Utils.cuh. Camera models: pinhole
-// and orthographic.
+// layout), with the math of gsplat/cuda/include/Utils.cuh. Camera models: pinhole,
+// orthographic and fisheye (the reference's packed kernels have no fisheye branch;
+// here both layouts share the projection math, so packed fisheye works too).
 //
 // Layout: one thread owns one Gaussian of one batch element and loops over the C
 // cameras, so the Gaussian's parameters are read from HBM once and its covariance
@@ -394,8 +395,8 @@ static ProjParams make_params(int B, int C, int N, const float *means, const flo
 }
 
 static int check_camera_model(int m) {
-    if (m == kPinhole || m == kOrtho) return kOk;
-    return set_error(kErrUnsupported, "camera_model %d is not supported (pinhole=0, ortho=1)", m);
+    if (m == kPinhole || m == kOrtho || m == kFisheye) return kOk;
+    return set_error(kErrUnsupported, "camera_model %d is not supported (pinhole=0, ortho=1, fisheye=2)", m);
 }
 
 } // namespace gsb

@@ -10,6 +10,88 @@
 
 namespace gsb {
 
+// Fisheye (equidistant) projection of a camera-space point: pixel position and
+// the 2x3 Jacobian J; Utils.cuh:662-700 (the eps terms of the reference kept).
+__device__ inline void fisheye_mean_jacobian(float x, float y, float z, float fx, float fy, float cx, float cy,
+                                             float &mx, float &my, float J[2][3]) {
+    const float eps = 0.0000001f;
+    const float xy_len = sqrtf(x * x + y * y) + eps;
+    const float theta = atan2f(xy_len, z + eps);
+    mx = x * fx * theta / xy_len + cx;
+    my = y * fy * theta / xy_len + cy;
+    const float x2 = x * x + eps;
+    const float y2 = y * y;
+    const float xy = x * y;
+    const float x2y2 = x2 + y2;
+    const float x2y2z2_inv = 1.f / (x2y2 + z * z);
+    const float b = atan2f(xy_len, z) / xy_len / x2y2;
+    const float a = z * x2y2z2_inv / x2y2;
+    J[0][0] = fx * (x2 * a + y2 * b);
+    J[0][1] = fx * xy * (a - b);
+    J[0][2] = -fx * x * x2y2z2_inv;
+    J[1][0] = fy * xy * (a - b);
+    J[1][1] = fy * (y2 * a + x2 * b);
+    J[1][2] = -fy * y * x2y2z2_inv;
+}
+
+// Gradient of the fisheye projection with respect to the camera-space point
+// given dL/dmean2d and dL/dJ (row-major 2x3); Utils.cuh:702-801 (the closed-form
+// derivatives of J of the reference, including its eps terms).
+__device__ inline void fisheye_point_vjp(float x, float y, float z, float fx, float fy, const float v_m2d[2],
+                                         const float vJ[2][3], float vmc[3]) {
+    const float eps = 0.0000001f;
+    const float x2 = x * x + eps;
+    const float y2 = y * y;
+    const float xy = x * y;
+    const float x2y2 = x2 + y2;
+    const float len_xy = sqrtf(x * x + y * y) + eps;
+    const float x2y2z2 = x2y2 + z * z;
+    const float x2y2z2_inv = 1.f / x2y2z2;
+    const float b = atan2f(len_xy, z) / len_xy / x2y2;
+    const float a = z * x2y2z2_inv / x2y2;
+    vmc[0] += fx * (x2 * a + y2 * b) * v_m2d[0] + fy * xy * (a - b) * v_m2d[1];
+    vmc[1] += fx * xy * (a - b) * v_m2d[0] + fy * (y2 * a + x2 * b) * v_m2d[1];
+    vmc[2] += -fx * x * x2y2z2_inv * v_m2d[0] - fy * y * x2y2z2_inv * v_m2d[1];
+
+    const float theta = atan2f(len_xy, z);
+    const float l4 = x2y2z2 * x2y2z2;
+    const float E = -l4 * x2y2 * theta + x2y2z2 * x2y2 * len_xy * z;
+    const float F = 3 * l4 * theta - 3 * x2y2z2 * len_xy * z - 2 * x2y2 * len_xy * z;
+    const float A = x * (3 * E + x2 * F);
+    const float B = y * (E + x2 * F);
+    const float C = x * (E + y2 * F);
+    const float D = y * (3 * E + y2 * F);
+    const float S1 = x2 - y2 - z * z;
+    const float S2 = y2 - x2 - z * z;
+    const float inv1 = x2y2z2_inv * x2y2z2_inv;
+    const float inv2 = inv1 / (x2y2 * x2y2 * len_xy);
+    // dJ[r][k]/d(x, y, z)
+    const float dx00 = fx * A * inv2, dx01 = fx * B * inv2, dx02 = fx * S1 * inv1;
+    const float dx10 = fy * B * inv2, dx11 = fy * C * inv2, dx12 = 2.f * fy * xy * inv1;
+    const float dy00 = dx01, dy01 = fx * C * inv2, dy02 = 2.f * fx * xy * inv1;
+    const float dy10 = dx11, dy11 = fy * D * inv2, dy12 = fy * S2 * inv1;
+    const float dz00 = dx02, dz01 = dy02, dz02 = 2.f * fx * x * z * inv1;
+    const float dz10 = dx12, dz11 = dy12, dz12 = 2.f * fy * y * z * inv1;
+    vmc[0] += dx00 * vJ[0][0] + dx01 * vJ[0][1] + dx02 * vJ[0][2] + dx10 * vJ[1][0] + dx11 * vJ[1][1] +
+              dx12 * vJ[1][2];
+    vmc[1] += dy00 * vJ[0][0] + dy01 * vJ[0][1] + dy02 * vJ[0][2] + dy10 * vJ[1][0] + dy11 * vJ[1][1] +
+              dy12 * vJ[1][2];
+    vmc[2] += dz00 * vJ[0][0] + dz01 * vJ[0][1] + dz02 * vJ[0][2] + dz10 * vJ[1][0] + dz11 * vJ[1][1] +
+              dz12 * vJ[1][2];
+}
+
+// Symmetric 2x2 J S J^T for a full 2x3 J and a symmetric S.
+__device__ inline void jsjt_full(const M3 &S, const float J[2][3], float &s00, float &s01, float &s11) {
+    float JS[2][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) JS[r][j] = J[r][0] * S.m[0][j] + J[r][1] * S.m[1][j] + J[r][2] * S.m[2][j];
+    s00 = JS[0][0] * J[0][0] + JS[0][1] * J[0][1] + JS[0][2] * J[0][2];
+    s01 = JS[0][0] * J[1][0] + JS[0][1] * J[1][1] + JS[0][2] * J[1][2];
+    s11 = JS[1][0] * J[1][0] + JS[1][1] * J[1][1] + JS[1][2] * J[1][2];
+}
+
 struct ProjParams {
     uint32_t B, C, N;
     const float *means, *covars, *quats, *scales, *opacities, *viewmats, *Ks;
@@ -83,6 +165,10 @@ __device__ inline ProjOut project_one(const ProjParams &p, uint32_t b, uint32_t 
         jsjt(cov_c, fx, 0.f, fy, 0.f, s00, s01, s11);
         mx = fx * x + cx;
         my = fy * y + cy;
+    } else if (p.camera_model == kFisheye) {
+        float J[2][3];
+        fisheye_mean_jacobian(x, y, z, fx, fy, cx, cy, mx, my, J);
+        jsjt_full(cov_c, J, s00, s01, s11);
     } else {
         float lxp, lxn, lyp, lyn;
         persp_limits(fx, fy, cx, cy, p.W, p.H, lxp, lxn, lyp, lyn);
@@ -142,7 +228,8 @@ struct ProjGrads {
 };
 
 // VJP of project_one for one (camera, Gaussian) pair: Utils.cuh:417-467 (inverse,
-// blur), 583-660 (pinhole), 502-540 (ortho), 62-112 (world-to-camera).
+// blur), 583-660 (pinhole), 502-540 (ortho), 702-801 (fisheye), 62-112
+// (world-to-camera).
 __device__ inline void project_one_vjp(const ProjParams &p, uint32_t b, uint32_t c,
                                        const float mean[3], const M3 &covar, const float conic[3],
                                        float comp, const float v_m2d[2], float v_depth,
@@ -198,6 +285,9 @@ __device__ inline void project_one_vjp(const ProjParams &p, uint32_t b, uint32_t
         J[1][0] = 0.f;
         J[1][1] = fy;
         J[1][2] = 0.f;
+    } else if (p.camera_model == kFisheye) {
+        float mx_unused, my_unused;
+        fisheye_mean_jacobian(x, y, z, fx, fy, cx, cy, mx_unused, my_unused, J);
     } else {
         const float rz = 1.f / z;
         float lxp, lxn, lyp, lyn;
@@ -227,6 +317,20 @@ __device__ inline void project_one_vjp(const ProjParams &p, uint32_t b, uint32_t
     if (p.camera_model == kOrtho) {
         vmc[0] += fx * v_m2d[0];
         vmc[1] += fy * v_m2d[1];
+    } else if (p.camera_model == kFisheye) {
+        // v_J = G J S^T + G^T J S with S = cov_c symmetric: (G + G^T) J S
+        float JS[2][3], vJ[2][3];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+                JS[r][j] = J[r][0] * cov_c.m[0][j] + J[r][1] * cov_c.m[1][j] + J[r][2] * cov_c.m[2][j];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            vJ[0][j] = 2.f * g00 * JS[0][j] + (g01 + g10) * JS[1][j];
+            vJ[1][j] = (g10 + g01) * JS[0][j] + 2.f * g11 * JS[1][j];
+        }
+        fisheye_point_vjp(x, y, z, fx, fy, v_m2d, vJ, vmc);
     } else {
         const float rz = 1.f / z;
         const float rz2 = rz * rz;

@@ -387,8 +387,9 @@ template <int D> static void launch_bwd(const FusedBwdParams &q, cudaStream_t s)
 
 static int check_fused(int degree, int K, int camera_model, const float *quats, const float *scales,
                        const float *opacities, const float *sh) {
-    if (camera_model != kPinhole && camera_model != kOrtho)
-        return set_error(kErrUnsupported, "camera_model %d is not supported (pinhole=0, ortho=1)", camera_model);
+    if (camera_model != kPinhole && camera_model != kOrtho && camera_model != kFisheye)
+        return set_error(kErrUnsupported, "camera_model %d is not supported (pinhole=0, ortho=1, fisheye=2)",
+                         camera_model);
     if (degree < 0 || degree > 4)
         return set_error(kErrUnsupported, "spherical harmonics degree %d not in [0, 4]", degree);
     if ((degree + 1) * (degree + 1) > K || K > 64)

@@ -2,7 +2,8 @@
 
 Names, argument order, defaults, return tuples and assertion behaviour follow the
 reference's ``gsplat/cuda/_wrapper.py`` (fully_fused_projection 479-631,
-spherical_harmonics 342-372, isect_tiles 634-730, isect_offset_encode 806-826,
+spherical_harmonics 342-372, quat_scale_to_covar_preci 375-407, proj 410-476,
+isect_tiles 634-730, isect_offset_encode 806-826,
 rasterize_to_pixels 829-961, adam 326-339 and the autograd Functions
 _FullyFusedProjection 1464-1594, _RasterizeToPixels 1709-1836,
 _FullyFusedProjectionPacked 2107-2326, _SphericalHarmonics 2329-2364), so code and
@@ -11,6 +12,7 @@ hand-written sm_100a kernels of ``gsplat_b200/csrc``; there is no CPU path.
 """
 
 import math
+import warnings
 from typing import Optional, Tuple
 
 import torch
@@ -21,7 +23,7 @@ from . import _backend as _B
 from ._backend import call, check_cuda, device_guard, ptr, stream_of
 
 CameraModel = Literal["pinhole", "ortho", "fisheye", "ftheta", "lidar"]
-_CAMERA_IDS = {"pinhole": 0, "ortho": 1}
+_CAMERA_IDS = {"pinhole": 0, "ortho": 1, "fisheye": 2}
 
 
 def _camera_id(camera_model: str) -> int:
@@ -30,7 +32,7 @@ def _camera_id(camera_model: str) -> int:
     ), "ftheta camera is only supported via UT, please set with_ut=True in the rasterization()"
     if camera_model not in _CAMERA_IDS:
         raise NotImplementedError(
-            f"camera_model={camera_model!r} is not implemented by gsplat_b200 (pinhole, ortho)"
+            f"camera_model={camera_model!r} is not implemented by gsplat_b200 (pinhole, ortho, fisheye)"
         )
     return _CAMERA_IDS[camera_model]
 
@@ -153,6 +155,163 @@ class _SphericalHarmonics(torch.autograd.Function):
             call("gsb_spherical_harmonics_bwd", ctx.sh_degree, n, K, ptr(dirs), ptr(coeffs),
                  ptr(masks), ptr(v_colors), ptr(v_coeffs), ptr(v_dirs), stream_of(dirs))
         return None, v_dirs, v_coeffs, None
+
+
+# ---------------------------------------------------------------------------
+# Covariances and the simple projection
+# ---------------------------------------------------------------------------
+def world_to_cam(
+    means: Tensor,  # [..., N, 3]
+    covars: Tensor,  # [..., N, 3, 3]
+    viewmats: Tensor,  # [..., C, 4, 4]
+) -> Tuple[Tensor, Tensor]:
+    """Transforms Gaussians to camera space (reference _wrapper.py:288-323, which
+    has no kernel for it either and evaluates it with tensor ops): returns means
+    [..., C, N, 3] and covariances [..., C, N, 3, 3]."""
+    warnings.warn(
+        "world_to_cam() has no kernel; it is evaluated with tensor ops and will be removed in a "
+        "future release.",
+        DeprecationWarning,
+    )
+    batch_dims = means.shape[:-2]
+    N = means.shape[-2]
+    C = viewmats.shape[-3]
+    assert means.shape == batch_dims + (N, 3), means.shape
+    assert covars.shape == batch_dims + (N, 3, 3), covars.shape
+    assert viewmats.shape == batch_dims + (C, 4, 4), viewmats.shape
+    R = viewmats[..., :3, :3]  # [..., C, 3, 3]
+    t = viewmats[..., :3, 3]  # [..., C, 3]
+    means_c = torch.einsum("...cij,...nj->...cni", R, means) + t[..., None, :]
+    covars_c = torch.einsum("...cij,...njk,...clk->...cnil", R, covars, R)
+    return means_c, covars_c
+
+
+def quat_scale_to_covar_preci(
+    quats: Tensor,  # [..., 4]
+    scales: Tensor,  # [..., 3]
+    compute_covar: bool = True,
+    compute_preci: bool = True,
+    triu: bool = False,
+) -> Tuple[Optional[Tensor], Optional[Tensor]]:
+    """Covariance R S S R^T and precision R S^-1 S^-1 R^T matrices from
+    quaternions (any norm) and scales (reference _wrapper.py:375-407): [..., 3, 3],
+    or [..., 6] upper triangles with triu; None where not requested."""
+    batch_dims = quats.shape[:-1]
+    assert quats.shape == batch_dims + (4,), quats.shape
+    assert scales.shape == batch_dims + (3,), scales.shape
+    covars, precis = _QuatScaleToCovarPreci.apply(quats.contiguous(), scales.contiguous(), compute_covar,
+                                                  compute_preci, triu)
+    return covars if compute_covar else None, precis if compute_preci else None
+
+
+class _QuatScaleToCovarPreci(torch.autograd.Function):
+    """Reference _wrapper.py:1356-1400."""
+
+    @staticmethod
+    def forward(ctx, quats: Tensor, scales: Tensor, compute_covar: bool, compute_preci: bool, triu: bool):
+        for name, t in (("quats", quats), ("scales", scales)):
+            check_cuda(name, t)
+        batch_dims = quats.shape[:-1]
+        n = quats.numel() // 4
+        shape = batch_dims + ((6,) if triu else (3, 3))
+        covars = torch.empty(shape, dtype=quats.dtype, device=quats.device) if compute_covar else None
+        precis = torch.empty(shape, dtype=quats.dtype, device=quats.device) if compute_preci else None
+        with device_guard(quats.device):
+            call("gsb_quat_scale_to_covar_preci_fwd", n, ptr(quats), ptr(scales), int(triu), ptr(covars),
+                 ptr(precis), stream_of(quats))
+        ctx.save_for_backward(quats, scales)
+        ctx.compute_covar = compute_covar
+        ctx.compute_preci = compute_preci
+        ctx.triu = triu
+        if covars is None:
+            covars = torch.empty(shape, dtype=quats.dtype, device=quats.device)
+            ctx.mark_non_differentiable(covars)
+        if precis is None:
+            precis = torch.empty(shape, dtype=quats.dtype, device=quats.device)
+            ctx.mark_non_differentiable(precis)
+        return covars, precis
+
+    @staticmethod
+    def backward(ctx, v_covars: Tensor, v_precis: Tensor):
+        quats, scales = ctx.saved_tensors
+        if ctx.compute_covar and v_covars is not None and v_covars.is_sparse:
+            v_covars = v_covars.to_dense()
+        if ctx.compute_preci and v_precis is not None and v_precis.is_sparse:
+            v_precis = v_precis.to_dense()
+        v_covars = v_covars.contiguous() if (ctx.compute_covar and v_covars is not None) else None
+        v_precis = v_precis.contiguous() if (ctx.compute_preci and v_precis is not None) else None
+        n = quats.numel() // 4
+        v_quats = torch.empty_like(quats)
+        v_scales = torch.empty_like(scales)
+        with device_guard(quats.device):
+            call("gsb_quat_scale_to_covar_preci_bwd", n, ptr(quats), ptr(scales), int(ctx.triu), ptr(v_covars),
+                 ptr(v_precis), ptr(v_quats), ptr(v_scales), stream_of(quats))
+        return v_quats, v_scales, None, None, None
+
+
+def persp_proj(means: Tensor, covars: Tensor, Ks: Tensor, width: int, height: int) -> Tuple[Tensor, Tensor]:
+    """Perspective projection (reference _wrapper.py:410-438); deprecated there in
+    favour of ``proj(..., camera_model="pinhole")``."""
+    warnings.warn(
+        "persp_proj is deprecated and will be removed in a future release. "
+        "Use proj with ortho=False instead.",
+        DeprecationWarning,
+    )
+    return proj(means, covars, Ks, width, height, camera_model="pinhole")
+
+
+def proj(
+    means: Tensor,  # [..., C, N, 3]
+    covars: Tensor,  # [..., C, N, 3, 3]
+    Ks: Tensor,  # [..., C, 3, 3]
+    width: int,
+    height: int,
+    camera_model: CameraModel = "pinhole",
+) -> Tuple[Tensor, Tensor]:
+    """Projects camera-space Gaussians (reference _wrapper.py:441-476): returns
+    means2d [..., C, N, 2] and covariances [..., C, N, 2, 2]."""
+    model = _camera_id(camera_model)
+    batch_dims = means.shape[:-3]
+    C, N = means.shape[-3:-1]
+    assert means.shape == batch_dims + (C, N, 3), means.shape
+    assert covars.shape == batch_dims + (C, N, 3, 3), covars.shape
+    assert Ks.shape == batch_dims + (C, 3, 3), Ks.shape
+    return _Proj.apply(means.contiguous(), covars.contiguous(), Ks.contiguous(), width, height, model)
+
+
+class _Proj(torch.autograd.Function):
+    """Reference _wrapper.py:1403-1461."""
+
+    @staticmethod
+    def forward(ctx, means: Tensor, covars: Tensor, Ks: Tensor, width: int, height: int, model: int):
+        for name, t in (("means", means), ("covars", covars), ("Ks", Ks)):
+            check_cuda(name, t)
+        C, N = means.shape[-3:-1]
+        B = means.numel() // max(1, C * N * 3)
+        means2d = torch.empty(means.shape[:-1] + (2,), dtype=means.dtype, device=means.device)
+        covars2d = torch.empty(means.shape[:-1] + (2, 2), dtype=means.dtype, device=means.device)
+        with device_guard(means.device):
+            call("gsb_proj_fwd", B, C, N, ptr(means), ptr(covars), ptr(Ks), width, height, model,
+                 ptr(means2d), ptr(covars2d), stream_of(means))
+        ctx.save_for_backward(means, covars, Ks)
+        ctx.width, ctx.height, ctx.model = width, height, model
+        return means2d, covars2d
+
+    @staticmethod
+    def backward(ctx, v_means2d: Tensor, v_covars2d: Tensor):
+        means, covars, Ks = ctx.saved_tensors
+        C, N = means.shape[-3:-1]
+        B = means.numel() // max(1, C * N * 3)
+        v_means2d = (v_means2d if v_means2d is not None else torch.zeros(
+            means.shape[:-1] + (2,), dtype=means.dtype, device=means.device)).contiguous()
+        v_covars2d = (v_covars2d if v_covars2d is not None else torch.zeros(
+            means.shape[:-1] + (2, 2), dtype=means.dtype, device=means.device)).contiguous()
+        v_means = torch.empty_like(means)
+        v_covars = torch.empty_like(covars)
+        with device_guard(means.device):
+            call("gsb_proj_bwd", B, C, N, ptr(means), ptr(covars), ptr(Ks), ctx.width, ctx.height, ctx.model,
+                 ptr(v_means2d), ptr(v_covars2d), ptr(v_means), ptr(v_covars), stream_of(means))
+        return v_means, v_covars, None, None, None, None
 
 
 # ---------------------------------------------------------------------------

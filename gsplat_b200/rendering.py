@@ -286,7 +286,7 @@ def rasterization(
         and colors.dim() == num_batch_dims + 3
         and colors.shape[-2] <= 64
         and sh_degree <= 4
-        and camera_model in ("pinhole", "ortho")
+        and camera_model in ("pinhole", "ortho", "fisheye")
         and not viewmats.requires_grad
     )
     compensations = None

@@ -46,7 +46,7 @@ GSB_API int gsb_version(void);
  * opacities [B,N] (optional: opacity-aware radius); viewmats [B,C,4,4];
  * Ks [B,C,3,3]. Outputs [B,C,N,...]: radii int32 x2, means2d x2, depths,
  * conics x3, compensations (only when calc_compensations). Culled entries are
- * written as zeros. camera_model: 0 pinhole, 1 ortho. */
+ * written as zeros. camera_model: 0 pinhole, 1 ortho, 2 fisheye. */
 GSB_API int gsb_projection_fused_fwd(int B, int C, int N, const float *means, const float *covars,
                              const float *quats, const float *scales, const float *opacities,
                              const float *viewmats, const float *Ks, int width, int height,
@@ -112,6 +112,32 @@ GSB_API int gsb_projection_packed_bwd(int B, int C, int N, int nnz, const float 
                               const float *v_conics, const float *v_compensations,
                               int sparse_grad, float *v_means, float *v_covars, float *v_quats,
                               float *v_scales, float *v_viewmats, cudaStream_t stream);
+
+/* --- Covariances and simple projection -----------------------------------
+ * gsb_quat_scale_to_covar_preci_fwd / _bwd replace the torch ops
+ * gsplat::quat_scale_to_covar_preci_fwd / _bwd (gsplat/cuda/ext.cpp:712-713;
+ * gsplat/cuda/csrc/QuatScaleToCovar.cpp:39-106). quats [n,4] (any norm),
+ * scales [n,3]; covars / precis [n,6] (triu: xx xy xz yy yz zz) or [n,3,3], each
+ * optional (NULL = not computed). Backward: v_covars / v_precis optional
+ * upstream gradients in the same layout (triu off-diagonals count once, as the
+ * reference halves them); writes v_quats [n,4], v_scales [n,3].
+ *
+ * gsb_proj_fwd / _bwd replace gsplat::projection_ewa_simple_fwd / _bwd
+ * (ext.cpp:726-727; Projection.cpp:41-127): camera-space means [B,C,N,3],
+ * covars [B,C,N,3,3], Ks [B,C,3,3] -> means2d [B,C,N,2], covars2d [B,C,N,2,2]
+ * (row-major); backward: v_means2d, v_covars2d -> v_means [B,C,N,3],
+ * v_covars [B,C,N,3,3]. camera_model: 0 pinhole, 1 ortho, 2 fisheye. */
+GSB_API int gsb_quat_scale_to_covar_preci_fwd(long long n, const float *quats, const float *scales, int triu,
+                                              float *covars, float *precis, cudaStream_t stream);
+GSB_API int gsb_quat_scale_to_covar_preci_bwd(long long n, const float *quats, const float *scales, int triu,
+                                              const float *v_covars, const float *v_precis, float *v_quats,
+                                              float *v_scales, cudaStream_t stream);
+GSB_API int gsb_proj_fwd(int B, int C, int N, const float *means, const float *covars, const float *Ks,
+                         int width, int height, int camera_model, float *means2d, float *covars2d,
+                         cudaStream_t stream);
+GSB_API int gsb_proj_bwd(int B, int C, int N, const float *means, const float *covars, const float *Ks,
+                         int width, int height, int camera_model, const float *v_means2d,
+                         const float *v_covars2d, float *v_means, float *v_covars, cudaStream_t stream);
 
 /* --- Fused projection + SH (no reference counterpart as one op) -----------
  * The reference's rasterization() runs projection, view directions, SH and the

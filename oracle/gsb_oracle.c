@@ -15,6 +15,8 @@
  *   ora_raster_fwd       RasterizeToPixels3DGSFwd.cu:64-212
  *   ora_raster_bwd       RasterizeToPixels3DGSBwd.cu:74-299
  *   ora_adam             AdamCUDA.cu:48-68
+ *   ora_covar_preci_fwd / _bwd   QuatScaleToCovarCUDA.cu:36-292 (+ Utils.cuh:223-341)
+ *   ora_proj_fwd / _bwd  ProjectionEWASimple.cu:36-317 (+ Utils.cuh:473-801)
  *
  * Forward math is single precision in the reference's operation order (compiled
  * with -ffp-contract=off, libm expf/sqrtf). Gradient sums over pixels / cameras
@@ -100,9 +102,29 @@ static ora_cam cam_of(const float *viewmats, const float *Ks, size_t ci) {
     return c;
 }
 
-/* J for pinhole (with the 1.3x fov clamp) or ortho; Utils.cuh:473-581 */
+/* fisheye mean and J; Utils.cuh:662-700 (eps terms kept) */
+static void fisheye_jacobian(float fx, float fy, float cx, float cy, float x, float y, float z,
+                             float J[2][3], float *mx, float *my) {
+    const float eps = 0.0000001f;
+    float xy_len = sqrtf(x * x + y * y) + eps;
+    float theta = atan2f(xy_len, z + eps);
+    *mx = x * fx * theta / xy_len + cx;
+    *my = y * fy * theta / xy_len + cy;
+    float x2 = x * x + eps, y2 = y * y, xy = x * y, x2y2 = x2 + y2;
+    float inv = 1.f / (x2y2 + z * z);
+    float b = atan2f(xy_len, z) / xy_len / x2y2;
+    float a = z * inv / x2y2;
+    J[0][0] = fx * (x2 * a + y2 * b); J[0][1] = fx * xy * (a - b); J[0][2] = -fx * x * inv;
+    J[1][0] = fy * xy * (a - b); J[1][1] = fy * (y2 * a + x2 * b); J[1][2] = -fy * y * inv;
+}
+
+/* J for pinhole (with the 1.3x fov clamp), ortho or fisheye; Utils.cuh:473-700 */
 static void proj_jacobian(int model, const ora_cam *c, int W, int H, float x, float y, float z,
                           float J[2][3], float *mx, float *my) {
+    if (model == 2) {
+        fisheye_jacobian(c->fx, c->fy, c->cx, c->cy, x, y, z, J, mx, my);
+        return;
+    }
     if (model == 1) {
         J[0][0] = c->fx; J[0][1] = 0.f; J[0][2] = 0.f;
         J[1][0] = 0.f; J[1][1] = c->fy; J[1][2] = 0.f;
@@ -193,6 +215,46 @@ static void quat_vjp(const float *q, const double G[3][3], double vq[4]) {
     vq[2] += (vn[2] - d * y) * inv; vq[3] += (vn[3] - d * z) * inv;
 }
 
+/* fisheye: J and dL/dpoint from dL/dmean2d and dL/dJ; Utils.cuh:702-801 */
+static void fisheye_jacobian_d(double fx, double fy, double x, double y, double z, double J[2][3]) {
+    const double eps = 0.0000001;
+    double x2 = x * x + eps, y2 = y * y, xy = x * y, x2y2 = x2 + y2;
+    double len_xy = sqrt(x * x + y * y) + eps;
+    double inv = 1.0 / (x2y2 + z * z);
+    double b = atan2(len_xy, z) / len_xy / x2y2;
+    double a = z * inv / x2y2;
+    J[0][0] = fx * (x2 * a + y2 * b); J[0][1] = fx * xy * (a - b); J[0][2] = -fx * x * inv;
+    J[1][0] = fy * xy * (a - b); J[1][1] = fy * (y2 * a + x2 * b); J[1][2] = -fy * y * inv;
+}
+
+static void fisheye_point_vjp_d(double fx, double fy, double x, double y, double z, const double vm2[2],
+                                const double vJ[2][3], double vmc[3]) {
+    const double eps = 0.0000001;
+    double J[2][3];
+    fisheye_jacobian_d(fx, fy, x, y, z, J);
+    vmc[0] += J[0][0] * vm2[0] + J[1][0] * vm2[1];
+    vmc[1] += J[0][1] * vm2[0] + J[1][1] * vm2[1];
+    vmc[2] += J[0][2] * vm2[0] + J[1][2] * vm2[1];
+    double x2 = x * x + eps, y2 = y * y, xy = x * y, x2y2 = x2 + y2;
+    double len_xy = sqrt(x * x + y * y) + eps;
+    double l2 = x2y2 + z * z, inv = 1.0 / l2;
+    double theta = atan2(len_xy, z), l4 = l2 * l2;
+    double E = -l4 * x2y2 * theta + l2 * x2y2 * len_xy * z;
+    double F = 3 * l4 * theta - 3 * l2 * len_xy * z - 2 * x2y2 * len_xy * z;
+    double A = x * (3 * E + x2 * F), B = y * (E + x2 * F), C = x * (E + y2 * F), D = y * (3 * E + y2 * F);
+    double S1 = x2 - y2 - z * z, S2 = y2 - x2 - z * z;
+    double inv1 = inv * inv, inv2 = inv1 / (x2y2 * x2y2 * len_xy);
+    double dx[2][3] = {{fx * A * inv2, fx * B * inv2, fx * S1 * inv1}, {fy * B * inv2, fy * C * inv2, 2 * fy * xy * inv1}};
+    double dy[2][3] = {{dx[0][1], fx * C * inv2, 2 * fx * xy * inv1}, {dx[1][1], fy * D * inv2, fy * S2 * inv1}};
+    double dz[2][3] = {{dx[0][2], dy[0][2], 2 * fx * x * z * inv1}, {dx[1][2], dy[1][2], 2 * fy * y * z * inv1}};
+    for (int r = 0; r < 2; ++r)
+        for (int k = 0; k < 3; ++k) {
+            vmc[0] += dx[r][k] * vJ[r][k];
+            vmc[1] += dy[r][k] * vJ[r][k];
+            vmc[2] += dz[r][k] * vJ[r][k];
+        }
+}
+
 /* Dense backward, double precision throughout; one Gaussian per iteration
  * summing over cameras, like the per-(c,n) atomics of the reference. */
 void ora_projection_bwd(int B, int C, int N, const float *means, const float *covars,
@@ -253,7 +315,9 @@ void ora_projection_bwd(int B, int C, int N, const float *means, const float *co
                 double J[2][3], vmc[3] = {0, 0, 0};
                 double fx = cam.fx, fy = cam.fy, cx = cam.cx, cy = cam.cy;
                 double tx = 0, ty = 0, rz = 0, rz2 = 0, rz3 = 0, lxp = 0, lxn = 0, lyp = 0, lyn = 0;
-                if (camera_model == 1) {
+                if (camera_model == 2) {
+                    fisheye_jacobian_d(fx, fy, x, y, z, J);
+                } else if (camera_model == 1) {
                     J[0][0] = fx; J[0][1] = 0; J[0][2] = 0; J[1][0] = 0; J[1][1] = fy; J[1][2] = 0;
                     vmc[0] += fx * v_means2d[idx * 2];
                     vmc[1] += fy * v_means2d[idx * 2 + 1];
@@ -276,7 +340,14 @@ void ora_projection_bwd(int B, int C, int N, const float *means, const float *co
                     for (int j = 0; j < 3; ++j) GJ[r][j] = G[r][0] * J[0][j] + G[r][1] * J[1][j];
                 for (int i = 0; i < 3; ++i)
                     for (int j = 0; j < 3; ++j) vSc[i][j] = J[0][i] * GJ[0][j] + J[1][i] * GJ[1][j];
-                if (camera_model != 1) {
+                if (camera_model == 2) {
+                    double JS[2][3], vJ[2][3], vm2[2] = {v_means2d[idx * 2], v_means2d[idx * 2 + 1]};
+                    for (int r = 0; r < 2; ++r)
+                        for (int j = 0; j < 3; ++j) JS[r][j] = J[r][0] * Sc[0][j] + J[r][1] * Sc[1][j] + J[r][2] * Sc[2][j];
+                    for (int r = 0; r < 2; ++r)
+                        for (int j = 0; j < 3; ++j) vJ[r][j] = (G[r][0] + G[0][r]) * JS[0][j] + (G[r][1] + G[1][r]) * JS[1][j];
+                    fisheye_point_vjp_d(fx, fy, x, y, z, vm2, vJ, vmc);
+                } else if (camera_model != 1) {
                     double JS[2][3], vJ[2][3];
                     for (int r = 0; r < 2; ++r)
                         for (int j = 0; j < 3; ++j) JS[r][j] = J[r][0] * Sc[0][j] + J[r][1] * Sc[1][j] + J[r][2] * Sc[2][j];
@@ -808,5 +879,168 @@ void ora_adam(long long N, long long D, float *param, const float *grad, float *
         param[i] += -lr * mm / (sqrtf(vv) + eps);
         m[i] = mm;
         v[i] = vv;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* quat_scale_to_covar_preci: QuatScaleToCovarCUDA.cu:36-292, Utils.cuh:223-341.
+ * Forward in float in the reference's order; backward in double. */
+static void store_sym3(float *o, const double A[3][3], int triu) {
+    if (triu) {
+        o[0] = (float)A[0][0]; o[1] = (float)A[0][1]; o[2] = (float)A[0][2];
+        o[3] = (float)A[1][1]; o[4] = (float)A[1][2]; o[5] = (float)A[2][2];
+    } else {
+        for (int i = 0; i < 3; ++i)
+            for (int j = 0; j < 3; ++j) o[i * 3 + j] = (float)A[i][j];
+    }
+}
+
+void ora_covar_preci_fwd(long long n, const float *quats, const float *scales, int triu, float *covars,
+                         float *precis) {
+    int w = triu ? 6 : 9;
+    for (long long i = 0; i < n; ++i) {
+        ora_m3 R = quat_rot(quats + i * 4);
+        const float *s = scales + i * 3;
+        for (int which = 0; which < 2; ++which) {
+            float *out = which == 0 ? covars : precis;
+            if (!out) continue;
+            ora_m3 M;
+            for (int a = 0; a < 3; ++a)
+                for (int b = 0; b < 3; ++b) M.m[a][b] = R.m[a][b] * (which == 0 ? s[b] : 1.f / s[b]);
+            ora_m3 P = m3mul(M, m3t(M));
+            double A[3][3];
+            for (int a = 0; a < 3; ++a)
+                for (int b = 0; b < 3; ++b) A[a][b] = P.m[a][b];
+            store_sym3(out + i * w, A, triu);
+        }
+    }
+}
+
+static void load_grad3(const float *g, int triu, double G[3][3]) {
+    if (triu) {
+        G[0][0] = g[0]; G[0][1] = G[1][0] = 0.5 * g[1]; G[0][2] = G[2][0] = 0.5 * g[2];
+        G[1][1] = g[3]; G[1][2] = G[2][1] = 0.5 * g[4]; G[2][2] = g[5];
+    } else {
+        for (int i = 0; i < 3; ++i)
+            for (int j = 0; j < 3; ++j) G[i][j] = g[i * 3 + j];
+    }
+}
+
+void ora_covar_preci_bwd(long long n, const float *quats, const float *scales, int triu, const float *v_covars,
+                         const float *v_precis, float *v_quats, float *v_scales) {
+    int w = triu ? 6 : 9;
+    for (long long i = 0; i < n; ++i) {
+        const float *q = quats + i * 4, *s = scales + i * 3;
+        ora_m3 Rf = quat_rot(q);
+        double vq[4] = {0, 0, 0, 0}, vs[3] = {0, 0, 0};
+        for (int which = 0; which < 2; ++which) {
+            const float *g = which == 0 ? v_covars : v_precis;
+            if (!g) continue;
+            double G[3][3], M[3][3], vM[3][3], vR[3][3], sc[3];
+            load_grad3(g + i * w, triu, G);
+            for (int b = 0; b < 3; ++b) sc[b] = which == 0 ? (double)s[b] : 1.0 / (double)s[b];
+            for (int a = 0; a < 3; ++a)
+                for (int b = 0; b < 3; ++b) M[a][b] = (double)Rf.m[a][b] * sc[b];
+            for (int a = 0; a < 3; ++a)
+                for (int b = 0; b < 3; ++b) {
+                    double acc = 0;
+                    for (int k = 0; k < 3; ++k) acc += (G[a][k] + G[k][a]) * M[k][b];
+                    vM[a][b] = acc;
+                    vR[a][b] = acc * sc[b];
+                }
+            quat_vjp(q, vR, vq);
+            for (int b = 0; b < 3; ++b) {
+                double d = Rf.m[0][b] * vM[0][b] + Rf.m[1][b] * vM[1][b] + Rf.m[2][b] * vM[2][b];
+                vs[b] += which == 0 ? d : -sc[b] * sc[b] * d;
+            }
+        }
+        for (int k = 0; k < 4; ++k) v_quats[i * 4 + k] = (float)vq[k];
+        for (int k = 0; k < 3; ++k) v_scales[i * 3 + k] = (float)vs[k];
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* proj: ProjectionEWASimple.cu:36-317 with Utils.cuh:473-801. cov2d = J S J^T,
+ * dL/dS = J^T G J, dL/dJ = G J S^T + G^T J S (the PyTorch form of the reference,
+ * _torch_impl.py:42-211). Forward float, backward double. */
+void ora_proj_fwd(int B, int C, int N, const float *means, const float *covars, const float *Ks, int W, int H,
+                  int model, float *means2d, float *covars2d) {
+    for (long long i = 0; i < (long long)B * C * N; ++i) {
+        long long bc = i / N;
+        ora_cam cam;
+        memset(&cam, 0, sizeof(cam));
+        const float *K = Ks + bc * 9;
+        cam.fx = K[0]; cam.cx = K[2]; cam.fy = K[4]; cam.cy = K[5];
+        const float *m = means + i * 3, *S = covars + i * 9;
+        float J[2][3], mx, my;
+        proj_jacobian(model, &cam, W, H, m[0], m[1], m[2], J, &mx, &my);
+        float JS[2][3];
+        for (int r = 0; r < 2; ++r)
+            for (int j = 0; j < 3; ++j) JS[r][j] = J[r][0] * S[j] + J[r][1] * S[3 + j] + J[r][2] * S[6 + j];
+        for (int r = 0; r < 2; ++r)
+            for (int c = 0; c < 2; ++c)
+                covars2d[i * 4 + r * 2 + c] = JS[r][0] * J[c][0] + JS[r][1] * J[c][1] + JS[r][2] * J[c][2];
+        means2d[i * 2] = mx;
+        means2d[i * 2 + 1] = my;
+    }
+}
+
+void ora_proj_bwd(int B, int C, int N, const float *means, const float *covars, const float *Ks, int W, int H,
+                  int model, const float *v_means2d, const float *v_covars2d, float *v_means, float *v_covars) {
+    for (long long i = 0; i < (long long)B * C * N; ++i) {
+        long long bc = i / N;
+        const float *K = Ks + bc * 9;
+        double fx = K[0], cx = K[2], fy = K[4], cy = K[5];
+        double x = means[i * 3], y = means[i * 3 + 1], z = means[i * 3 + 2];
+        double S[3][3], G[2][2] = {{v_covars2d[i * 4], v_covars2d[i * 4 + 1]}, {v_covars2d[i * 4 + 2], v_covars2d[i * 4 + 3]}};
+        double vm2[2] = {v_means2d[i * 2], v_means2d[i * 2 + 1]};
+        for (int a = 0; a < 3; ++a)
+            for (int b = 0; b < 3; ++b) S[a][b] = covars[i * 9 + a * 3 + b];
+        double J[2][3], vmc[3] = {0, 0, 0};
+        double tx = 0, ty = 0, rz = 0, rz2 = 0, rz3 = 0, lxp = 0, lxn = 0, lyp = 0, lyn = 0;
+        if (model == 2) {
+            fisheye_jacobian_d(fx, fy, x, y, z, J);
+        } else if (model == 1) {
+            J[0][0] = fx; J[0][1] = 0; J[0][2] = 0; J[1][0] = 0; J[1][1] = fy; J[1][2] = 0;
+            vmc[0] = fx * vm2[0];
+            vmc[1] = fy * vm2[1];
+        } else {
+            double tfx = 0.5 * W / fx, tfy = 0.5 * H / fy;
+            lxp = (W - cx) / fx + 0.3 * tfx; lxn = cx / fx + 0.3 * tfx;
+            lyp = (H - cy) / fy + 0.3 * tfy; lyn = cy / fy + 0.3 * tfy;
+            rz = 1.0 / z; rz2 = rz * rz; rz3 = rz2 * rz;
+            tx = z * fmin(lxp, fmax(-lxn, x * rz));
+            ty = z * fmin(lyp, fmax(-lyn, y * rz));
+            J[0][0] = fx * rz; J[0][1] = 0; J[0][2] = -fx * tx * rz2;
+            J[1][0] = 0; J[1][1] = fy * rz; J[1][2] = -fy * ty * rz2;
+            vmc[0] = fx * rz * vm2[0];
+            vmc[1] = fy * rz * vm2[1];
+            vmc[2] = -(fx * x * vm2[0] + fy * y * vm2[1]) * rz2;
+        }
+        double GJ[2][3];
+        for (int r = 0; r < 2; ++r)
+            for (int j = 0; j < 3; ++j) GJ[r][j] = G[r][0] * J[0][j] + G[r][1] * J[1][j];
+        for (int a = 0; a < 3; ++a)
+            for (int b = 0; b < 3; ++b) v_covars[i * 9 + a * 3 + b] = (float)(J[0][a] * GJ[0][b] + J[1][a] * GJ[1][b]);
+        double JSt[2][3], JS[2][3], vJ[2][3];
+        for (int r = 0; r < 2; ++r)
+            for (int j = 0; j < 3; ++j) {
+                JSt[r][j] = J[r][0] * S[j][0] + J[r][1] * S[j][1] + J[r][2] * S[j][2];
+                JS[r][j] = J[r][0] * S[0][j] + J[r][1] * S[1][j] + J[r][2] * S[2][j];
+            }
+        for (int r = 0; r < 2; ++r)
+            for (int j = 0; j < 3; ++j)
+                vJ[r][j] = G[r][0] * JSt[0][j] + G[r][1] * JSt[1][j] + G[0][r] * JS[0][j] + G[1][r] * JS[1][j];
+        if (model == 2) {
+            fisheye_point_vjp_d(fx, fy, x, y, z, vm2, vJ, vmc);
+        } else if (model == 0) {
+            if (x * rz <= lxp && x * rz >= -lxn) vmc[0] += -fx * rz2 * vJ[0][2];
+            else vmc[2] += -fx * rz3 * vJ[0][2] * tx;
+            if (y * rz <= lyp && y * rz >= -lyn) vmc[1] += -fy * rz2 * vJ[1][2];
+            else vmc[2] += -fy * rz3 * vJ[1][2] * ty;
+            vmc[2] += -fx * rz2 * vJ[0][0] - fy * rz2 * vJ[1][1] + 2 * fx * tx * rz3 * vJ[0][2] +
+                      2 * fy * ty * rz3 * vJ[1][2];
+        }
+        for (int k = 0; k < 3; ++k) v_means[i * 3 + k] = (float)vmc[k];
     }
 }

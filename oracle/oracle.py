@@ -41,6 +41,10 @@ _SIG = {
     "ora_raster_bwd": [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P,
                        I64, P, P, P, P, P],
     "ora_adam": [I64, I64, P, P, P, P, P, F32, F32, F32, F32],
+    "ora_covar_preci_fwd": [I64, P, P, I32, P, P],
+    "ora_covar_preci_bwd": [I64, P, P, I32, P, P, P, P],
+    "ora_proj_fwd": [I32, I32, I32, P, P, P, I32, I32, I32, P, P],
+    "ora_proj_bwd": [I32, I32, I32, P, P, P, I32, I32, I32, P, P, P, P],
 }
 
 
@@ -236,3 +240,48 @@ def adam(param, grad, exp_avg, exp_avg_sq, valid, lr, b1, b2, eps):
     v = None if valid is None else np.ascontiguousarray(valid, np.uint8)
     lib().ora_adam(N, D, _p(param), _p(_f(grad)), _p(exp_avg), _p(exp_avg_sq), _p(v), lr, b1, b2,
                    eps)
+
+
+def covar_preci_fwd(quats, scales, triu=False, compute_covar=True, compute_preci=True):
+    """quat_scale_to_covar_preci forward (QuatScaleToCovarCUDA.cu:36-122)."""
+    quats, scales = _f(quats), _f(scales)
+    n = quats.size // 4
+    shape = quats.shape[:-1] + ((6,) if triu else (3, 3))
+    covars = np.zeros(shape, np.float32) if compute_covar else None
+    precis = np.zeros(shape, np.float32) if compute_preci else None
+    lib().ora_covar_preci_fwd(n, _p(quats), _p(scales), int(triu), _p(covars), _p(precis))
+    return covars, precis
+
+
+def covar_preci_bwd(quats, scales, triu, v_covars, v_precis):
+    """quat_scale_to_covar_preci backward (QuatScaleToCovarCUDA.cu:124-292)."""
+    quats, scales = _f(quats), _f(scales)
+    n = quats.size // 4
+    v_quats = np.zeros(quats.shape, np.float32)
+    v_scales = np.zeros(scales.shape, np.float32)
+    lib().ora_covar_preci_bwd(n, _p(quats), _p(scales), int(triu), _p(_f(v_covars)), _p(_f(v_precis)),
+                              _p(v_quats), _p(v_scales))
+    return v_quats, v_scales
+
+
+def proj_fwd(means, covars, Ks, W, H, camera_model=0):
+    """proj forward (ProjectionEWASimple.cu:36-161): camera-space [..., C, N, 3] / [..., C, N, 3, 3]."""
+    means, covars, Ks = _f(means), _f(covars), _f(Ks)
+    C, N = means.shape[-3], means.shape[-2]
+    B = means.size // max(1, C * N * 3)
+    means2d = np.zeros(means.shape[:-1] + (2,), np.float32)
+    covars2d = np.zeros(means.shape[:-1] + (2, 2), np.float32)
+    lib().ora_proj_fwd(B, C, N, _p(means), _p(covars), _p(Ks), W, H, camera_model, _p(means2d), _p(covars2d))
+    return means2d, covars2d
+
+
+def proj_bwd(means, covars, Ks, W, H, camera_model, v_means2d, v_covars2d):
+    """proj backward (ProjectionEWASimple.cu:163-317)."""
+    means, covars, Ks = _f(means), _f(covars), _f(Ks)
+    C, N = means.shape[-3], means.shape[-2]
+    B = means.size // max(1, C * N * 3)
+    v_means = np.zeros(means.shape, np.float32)
+    v_covars = np.zeros(covars.shape, np.float32)
+    lib().ora_proj_bwd(B, C, N, _p(means), _p(covars), _p(Ks), W, H, camera_model, _p(_f(v_means2d)),
+                       _p(_f(v_covars2d)), _p(v_means), _p(v_covars))
+    return v_means, v_covars

@@ -99,6 +99,69 @@ def make_covar(tm):
                         covars=covars.numpy(), precis=precis.numpy())
 
 
+def make_covar_grad(tm):
+    """tests/test_basic.py:117-152: gradients of covars and precis (full and triu)."""
+    g = torch.Generator().manual_seed(13)
+    quats = torch.randn((400, 4), generator=g)
+    scales = torch.rand((400, 3), generator=g) * 0.1 + 2e-2
+    out = {"quats": quats.numpy(), "scales": scales.numpy()}
+    for triu in (False, True):
+        q = quats.clone().requires_grad_(True)
+        s = scales.clone().requires_grad_(True)
+        covars, precis = tm._quat_scale_to_covar_preci(q, s, triu=triu)
+        vc = torch.randn(covars.shape, generator=g)
+        vp = torch.randn(precis.shape, generator=g) * 0.01
+        gq, gs = torch.autograd.grad((covars * vc).sum() + (precis * vp).sum(), (q, s))
+        tag = "triu" if triu else "full"
+        out.update({f"{tag}_covars": covars.detach().numpy(), f"{tag}_precis": precis.detach().numpy(),
+                    f"{tag}_v_covars": vc.numpy(), f"{tag}_v_precis": vp.numpy(),
+                    f"{tag}_v_quats": gq.numpy(), f"{tag}_v_scales": gs.numpy()})
+    np.savez_compressed(os.path.join(HERE, "covar_grad.npz"), **out)
+
+
+def make_proj(ti, tm, ref_root):
+    """tests/test_basic.py:155-211 (proj of camera-space Gaussians, three camera
+    models) and 214-324 (fully fused projection with the fisheye model)."""
+    means, quats, scales, opacities, viewmats, Ks, W, H = garden_subset(ref_root, 300, 17)
+    covars, _ = tm._quat_scale_to_covar_preci(quats, scales, compute_preci=False, triu=False)
+    means_c, covars_c = ti._world_to_cam(means, covars, viewmats)
+    out = {"means": means.numpy(), "quats": quats.numpy(), "scales": scales.numpy(),
+           "viewmats": viewmats.numpy(), "Ks": Ks.numpy(), "width": W, "height": H,
+           "means_c": means_c.numpy(), "covars_c": covars_c.numpy()}
+    fns = {"pinhole": ti._persp_proj, "ortho": ti._ortho_proj, "fisheye": ti._fisheye_proj}
+    g = torch.Generator().manual_seed(19)
+    for name, fn in fns.items():
+        m = means_c.clone().requires_grad_(True)
+        c = covars_c.clone().requires_grad_(True)
+        means2d, covars2d = fn(m, c, Ks, W, H)
+        vm = torch.randn(means2d.shape, generator=g)
+        vc = torch.randn(covars2d.shape, generator=g)
+        gm, gc = torch.autograd.grad((means2d * vm).sum() + (covars2d * vc).sum(), (m, c))
+        out.update({f"{name}_means2d": means2d.detach().numpy(), f"{name}_covars2d": covars2d.detach().numpy(),
+                    f"{name}_v_means2d": vm.numpy(), f"{name}_v_covars2d": vc.numpy(),
+                    f"{name}_v_means": gm.numpy(), f"{name}_v_covars": gc.numpy()})
+    # fully fused projection, fisheye
+    m = means.clone().requires_grad_(True)
+    q = quats.clone().requires_grad_(True)
+    s = scales.clone().requires_grad_(True)
+    v = viewmats.clone().requires_grad_(True)
+    cov, _ = tm._quat_scale_to_covar_preci(q, s, compute_preci=False, triu=False)
+    radii, means2d, depths, conics, _ = ti._fully_fused_projection(m, cov, v, Ks, W, H, eps2d=0.3,
+                                                                   camera_model="fisheye")
+    valid = (radii > 0).all(dim=-1)
+    vm2 = torch.randn(means2d.shape, generator=g) * valid[..., None]
+    vd = torch.randn(depths.shape, generator=g) * valid
+    vcn = torch.randn(conics.shape, generator=g) * valid[..., None]
+    loss = (means2d * vm2).sum() + (depths * vd).sum() + (conics * vcn).sum()
+    gm, gq, gs, gv = torch.autograd.grad(loss, (m, q, s, v))
+    out.update({"fused_radii": radii.numpy(), "fused_means2d": means2d.detach().numpy(),
+                "fused_depths": depths.detach().numpy(), "fused_conics": conics.detach().numpy(),
+                "fused_v_means2d": vm2.numpy(), "fused_v_depths": vd.numpy(), "fused_v_conics": vcn.numpy(),
+                "fused_v_means": gm.numpy(), "fused_v_quats": gq.numpy(), "fused_v_scales": gs.numpy(),
+                "fused_v_viewmats": gv.numpy()})
+    np.savez_compressed(os.path.join(HERE, "proj_garden.npz"), **out)
+
+
 def make_sh(ti):
     out = {}
     g = torch.Generator().manual_seed(42)
@@ -154,6 +217,8 @@ def main():
     ti, tm = import_reference(ref_root)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     make_covar(tm)
+    make_covar_grad(tm)
+    make_proj(ti, tm, ref_root)
     make_sh(ti)
     make_projection(ti, tm, ref_root)
     make_isect(ti)

@@ -59,8 +59,12 @@ def test_invalid_arguments_return_errors_without_launch():
                              None, None)
     assert rc == -1 and b"exceed" in lib.gsb_last_error()
     rc = lib.gsb_projection_fused_fwd(1, 1, 1, None, None, None, None, None, None, None, 1, 1, 0.3,
-                                      0.01, 100.0, 0.0, 0, 2, None, None, None, None, None, None)
+                                      0.01, 100.0, 0.0, 0, 3, None, None, None, None, None, None)
     assert rc == -2 and b"camera_model" in lib.gsb_last_error()
+    rc = lib.gsb_proj_fwd(1, 1, 1, None, None, None, 1, 1, 4, None, None, None)
+    assert rc == -2 and b"camera_model" in lib.gsb_last_error()
+    rc = lib.gsb_quat_scale_to_covar_preci_fwd(-1, None, None, 0, None, None, None)
+    assert rc == -1 and b"negative" in lib.gsb_last_error()
 
 
 def test_python_ops_raise_on_cpu_tensors():

@@ -86,7 +86,7 @@ def test_fused_projection_sh_matches_composition(packed, calc):
         assert_close(a, b, 1e-3, 1e-5, name=name)
 
 
-def oracle_pipeline(d, W, H, tile_size, calc, depth_channel, v_fn):
+def oracle_pipeline(d, W, H, tile_size, calc, depth_channel, v_fn, camera_model=0):
     """The reference algorithm on the CPU: projection -> SH -> AccuTile -> sort ->
     offsets -> rasterize, then the chain of backward passes to the parameters."""
     n = lambda t: t.detach().cpu().numpy()
@@ -95,7 +95,7 @@ def oracle_pipeline(d, W, H, tile_size, calc, depth_channel, v_fn):
     C = vm.shape[0]
     N = means.shape[0]
     radii, m2, dep, con, comp = O.projection_fwd(means, None, quats, scales, opac, vm, K, W, H,
-                                                 calc_compensations=calc)
+                                                 calc_compensations=calc, camera_model=camera_model)
     valid = (radii > 0).all(-1)
     campos = -np.einsum("cji,cj->ci", vm[:, :3, :3], vm[:, :3, 3])
     dirs = means[None] - campos[:, None]
@@ -119,24 +119,27 @@ def oracle_pipeline(d, W, H, tile_size, calc, depth_channel, v_fn):
     v_means, _, v_quats, v_scales, _ = O.projection_bwd(
         means, None, quats, scales, vm, K, W, H, 0.3, radii, con, comp if calc else None,
         v_m2 * valid[..., None], v_dep * valid, v_con * valid[..., None],
-        v_comp * valid if calc else None)
+        v_comp * valid if calc else None, camera_model=camera_model)
     v_means = v_means + (v_dirs * valid[..., None]).sum(0)
     return dict(render=rc, alpha=ra, v_means=v_means, v_quats=v_quats, v_scales=v_scales,
                 v_opacities=v_opac, v_sh=(v_coeffs * valid[..., None, None]).sum(0))
 
 
-@pytest.mark.parametrize("packed", [True, False])
-@pytest.mark.parametrize("mode", ["RGB", "RGB+ED"])
-@pytest.mark.parametrize("aa", [False, True])
-def test_rasterization_end_to_end_vs_oracle(packed, mode, aa):
+@pytest.mark.parametrize("packed,mode,aa,camera", [
+    (p, m, a, "pinhole") for p in (True, False) for m in ("RGB", "RGB+ED") for a in (False, True)
+] + [(True, "RGB", False, "fisheye"), (False, "RGB", True, "fisheye"), (True, "RGB", False, "ortho")])
+def test_rasterization_end_to_end_vs_oracle(packed, mode, aa, camera):
     d = _data.scene(8000, seed=31, C=2, width=160, height=120, fx=150.0)
     d["scales"] = d["scales"] * 1.5
+    if camera == "ortho":  # orthographic: pixels per world unit instead of a focal length
+        d["Ks"][:, 0, 0] = d["Ks"][:, 1, 1] = 40.0
     W, H = d["width"], d["height"]
     L = leaf(d)
     vm, K = d["viewmats"].to(DEV), d["Ks"].to(DEV)
     rc, ra, meta = gsb().rasterization(L["means"], L["quats"], L["scales"], L["opacities"], L["sh"],
                                        vm, K, W, H, sh_degree=3, packed=packed, render_mode=mode,
-                                       rasterize_mode="antialiased" if aa else "classic")
+                                       rasterize_mode="antialiased" if aa else "classic",
+                                       camera_model=camera)
     gen = np.random.default_rng(7)
     G = gen.standard_normal((2, H, W, 4 if mode == "RGB+ED" else 3)).astype(np.float32)
     Ga = gen.standard_normal((2, H, W, 1)).astype(np.float32)
@@ -154,7 +157,7 @@ def test_rasterization_end_to_end_vs_oracle(packed, mode, aa):
         vra = Ga + np.where(raw_ra > 1e-10, -G[..., 3:4] * raw_rc[..., 3:4] / a ** 2, 0.0)
         return vrc, vra.astype(np.float32)
 
-    e = oracle_pipeline(d, W, H, 16, aa, depth, v_fn)
+    e = oracle_pipeline(d, W, H, 16, aa, depth, v_fn, {"pinhole": 0, "ortho": 1, "fisheye": 2}[camera])
     exp_render = e["render"].copy()
     if depth:
         exp_render[..., 3:4] = exp_render[..., 3:4] / np.maximum(e["alpha"], 1e-10)
