@@ -6,6 +6,7 @@ All compute runs in the hand-written kernels of ``libgsplat_b200.so`` (C ABI in
 ``include/gsplat_b200.h``); there is no CPU fallback.
 """
 
+from .cuda._torch_impl import accumulate
 from .cuda._wrapper import (
     CameraModel,
     adam,
@@ -21,6 +22,7 @@ from .cuda._wrapper import (
     persp_proj,
     proj,
     quat_scale_to_covar_preci,
+    rasterize_to_indices_in_range,
     rasterize_to_pixels,
     spherical_harmonics,
     world_to_cam,
@@ -35,6 +37,7 @@ __all__ = [
     "RasterizeMode",
     "RenderMode",
     "SelectiveAdam",
+    "accumulate",
     "adam",
     "fully_fused_projection",
     "has_2dgs",
@@ -49,6 +52,7 @@ __all__ = [
     "proj",
     "quat_scale_to_covar_preci",
     "rasterization",
+    "rasterize_to_indices_in_range",
     "rasterize_to_pixels",
     "spherical_harmonics",
     "world_to_cam",

@@ -77,6 +77,8 @@ SIGNATURES = {
     "gsb_quat_scale_to_covar_preci_bwd": (I32, [I64, P, P, I32, P, P, P, P, P]),
     "gsb_proj_fwd": (I32, [I32, I32, I32, P, P, P, I32, I32, I32, P, P, P]),
     "gsb_proj_bwd": (I32, [I32, I32, I32, P, P, P, I32, I32, I32, P, P, P, P, P]),
+    "gsb_rasterize_to_indices": (I32, [I32, I32, I32, I32, I64, P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P,
+                                       P, P]),
     "gsb_spherical_harmonics_fwd": (I32, [I32, I64, I32, P, P, P, P, P]),
     "gsb_spherical_harmonics_bwd": (I32, [I32, I64, I32, P, P, P, P, P, P, P]),
     "gsb_scan_scratch_bytes": (SZ, [I64]),

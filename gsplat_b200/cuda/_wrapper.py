@@ -4,7 +4,8 @@ Names, argument order, defaults, return tuples and assertion behaviour follow th
 reference's ``gsplat/cuda/_wrapper.py`` (fully_fused_projection 479-631,
 spherical_harmonics 342-372, quat_scale_to_covar_preci 375-407, proj 410-476,
 isect_tiles 634-730, isect_offset_encode 806-826,
-rasterize_to_pixels 829-961, adam 326-339 and the autograd Functions
+rasterize_to_pixels 829-961, rasterize_to_indices_in_range 1274-1353, adam 326-339
+and the autograd Functions
 _FullyFusedProjection 1464-1594, _RasterizeToPixels 1709-1836,
 _FullyFusedProjectionPacked 2107-2326, _SphericalHarmonics 2329-2364), so code and
 tests written against the reference run unchanged. Every op launches the
@@ -820,6 +821,64 @@ def rasterize_to_pixels(
         means2d.contiguous(), conics.contiguous(), colors.contiguous(), opacities.contiguous(),
         backgrounds, masks, image_width, image_height, tile_size, isect_offsets.contiguous(),
         flatten_ids.contiguous(), absgrad)
+
+
+def rasterize_to_indices_in_range(
+    range_start: int,
+    range_end: int,
+    transmittances: Tensor,  # [..., image_height, image_width]
+    means2d: Tensor,  # [..., N, 2]
+    conics: Tensor,  # [..., N, 3]
+    opacities: Tensor,  # [..., N]
+    image_width: int,
+    image_height: int,
+    tile_size: int,
+    isect_offsets: Tensor,  # [..., tile_height, tile_width]
+    flatten_ids: Tensor,  # [n_isects]
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """The (Gaussian, pixel, image) index triples that splat batches
+    [range_start, range_end) (front to back, tile_size^2 tile-list entries per
+    batch) contribute to each pixel given its current transmittance (reference
+    _wrapper.py:1274-1353). Returns gaussian_ids, pixel_ids (row-major) and
+    image_ids, int64 [M], grouped by pixel in (image, row, column) order."""
+    image_dims = means2d.shape[:-2]
+    tile_height, tile_width = isect_offsets.shape[-2:]
+    N = means2d.shape[-2]
+    assert transmittances.shape == image_dims + (image_height, image_width), transmittances.shape
+    assert means2d.shape == image_dims + (N, 2), means2d.shape
+    assert conics.shape == image_dims + (N, 3), conics.shape
+    assert opacities.shape == image_dims + (N,), opacities.shape
+    assert isect_offsets.shape == image_dims + (tile_height, tile_width), isect_offsets.shape
+    assert tile_height * tile_size >= image_height, f"Assert Failed: {tile_height} * {tile_size} >= {image_height}"
+    assert tile_width * tile_size >= image_width, f"Assert Failed: {tile_width} * {tile_size} >= {image_width}"
+    tensors = (transmittances.contiguous(), means2d.contiguous(), conics.contiguous(), opacities.contiguous(),
+               isect_offsets.contiguous(), flatten_ids.contiguous())
+    for name, t in zip(("transmittances", "means2d", "conics", "opacities", "isect_offsets", "flatten_ids"),
+                       tensors):
+        check_cuda(name, t)
+    trans, m2, con, op, offsets, fids = tensors
+    I = math.prod(image_dims)
+    dev = means2d.device
+    n_isects = fids.numel()
+    lo = int(max(0, min(range_start, 2**31 - 1)))
+    hi = int(max(0, min(range_end, 2**31 - 1)))
+    empty = torch.empty(0, dtype=torch.int64, device=dev)
+    if n_isects == 0 or I == 0 or hi <= lo:
+        return empty, empty.clone(), empty.clone()
+    args = (lo, hi, I, N, n_isects, ptr(m2), ptr(con), ptr(op), image_width, image_height, tile_size,
+            tile_width, tile_height, ptr(offsets), ptr(fids), ptr(trans))
+    with device_guard(dev):
+        stream = stream_of(m2)
+        cnts = torch.zeros(I * image_height * image_width, dtype=torch.int32, device=dev)
+        call("gsb_rasterize_to_indices", *args, None, ptr(cnts), None, None, stream)
+        ends = _scan_i32(cnts)
+        total = int(ends[-1].item())
+        gaussian_ids = torch.empty(total, dtype=torch.int64, device=dev)
+        indices = torch.empty(total, dtype=torch.int64, device=dev)
+        if total:
+            call("gsb_rasterize_to_indices", *args, ptr(ends), None, ptr(gaussian_ids), ptr(indices), stream)
+    hw = image_width * image_height
+    return gaussian_ids, indices % hw, torch.div(indices, hw, rounding_mode="floor")
 
 
 class _RasterizeToPixels(torch.autograd.Function):

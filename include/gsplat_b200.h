@@ -346,6 +346,25 @@ GSB_API int gsb_rasterize_bwd(int I, int channels, const float *means2d, const f
                       float *v_means2d_abs, float *v_means2d, float *v_conics, float *v_colors,
                       float *v_opacities, cudaStream_t stream);
 
+/* --- Rasterize to indices -------------------------------------------------
+ * Replaces torch op gsplat::rasterize_to_indices_3dgs (gsplat/cuda/ext.cpp:737;
+ * gsplat/cuda/csrc/Rasterization.cpp:216-300, kernel RasterizeToIndices3DGS.cu).
+ * Dense layout: means2d [I,N,2], conics [I,N,3], opacities [I,N],
+ * transmittances [I,H,W]; tile_offsets / flatten_ids of the sorted intersections.
+ * Batches [range_start, range_end) of tile_size^2 tile-list entries are walked
+ * front to back. Two calls: with chunk_ends NULL it writes chunk_cnts int32
+ * [I*H*W] (pairs per pixel); with chunk_ends = inclusive prefix sum of those
+ * counts (int64) it writes gaussian_ids (flatten id % N) and pixel_ids
+ * (image*H*W + row*W + col), int64 [total], grouped by pixel in (image, row,
+ * column) order and front to back inside a pixel. tile_size 1..32. */
+GSB_API int gsb_rasterize_to_indices(int range_start, int range_end, int I, int N, long long n_isects,
+                                     const float *means2d, const float *conics, const float *opacities,
+                                     int width, int height, int tile_size, int tile_width, int tile_height,
+                                     const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                     const float *transmittances, const int64_t *chunk_ends,
+                                     int32_t *chunk_cnts, int64_t *gaussian_ids, int64_t *pixel_ids,
+                                     cudaStream_t stream);
+
 /* --- Selective Adam -------------------------------------------------------
  * Replaces gsplat::adam (gsplat/cuda/csrc/Adam.cpp:37-65, AdamCUDA.cu:34-69):
  * masked Adam without bias correction on param/grad/exp_avg/exp_avg_sq of

@@ -17,6 +17,7 @@
  *   ora_adam             AdamCUDA.cu:48-68
  *   ora_covar_preci_fwd / _bwd   QuatScaleToCovarCUDA.cu:36-292 (+ Utils.cuh:223-341)
  *   ora_proj_fwd / _bwd  ProjectionEWASimple.cu:36-317 (+ Utils.cuh:473-801)
+ *   ora_raster_indices   RasterizeToIndices3DGS.cu:36-200, Rasterization.cpp:216-300
  *
  * Forward math is single precision in the reference's operation order (compiled
  * with -ffp-contract=off, libm expf/sqrtf). Gradient sums over pixels / cameras
@@ -1043,4 +1044,50 @@ void ora_proj_bwd(int B, int C, int N, const float *means, const float *covars, 
         }
         for (int k = 0; k < 3; ++k) v_means[i * 3 + k] = (float)vmc[k];
     }
+}
+
+/* ------------------------------------------------------------------------ */
+/* rasterize_to_indices_in_range: RasterizeToIndices3DGS.cu:36-200. Pass
+ * gids/pids NULL to count only (counts[I*H*W]); with them, the pairs are written
+ * at the pixel's exclusive prefix of counts (which the caller passes in
+ * `starts`), front to back. libm expf (the kernel uses __expf). */
+void ora_raster_indices(int range_start, int range_end, int I, int N, long long n_isects, const float *means2d,
+                        const float *conics, const float *opac, int W, int H, int ts, int tw, int th,
+                        const int32_t *offsets, const int32_t *fids, const float *trans_in, int32_t *counts,
+                        const int64_t *starts, int64_t *gids, int64_t *pids) {
+    const int bs = ts * ts;
+    for (int img = 0; img < I; ++img)
+        for (int tile = 0; tile < tw * th; ++tile) {
+            int s0 = offsets[(size_t)img * tw * th + tile];
+            int s1 = (img == I - 1 && tile == tw * th - 1) ? (int)n_isects : offsets[(size_t)img * tw * th + tile + 1];
+            int nb = (s1 - s0 + bs - 1) / bs;
+            if (range_start >= nb) continue;
+            int b_end = range_end < nb ? range_end : nb;
+            for (int ly = 0; ly < ts; ++ly)
+                for (int lx = 0; lx < ts; ++lx) {
+                    int i = (tile / tw) * ts + ly, j = (tile % tw) * ts + lx;
+                    if (i >= H || j >= W) continue;
+                    size_t gp = (size_t)img * H * W + (size_t)i * W + j;
+                    float px = (float)j + 0.5f, py = (float)i + 0.5f;
+                    float T = trans_in[gp];
+                    int cnt = 0, done = 0;
+                    for (int k = s0 + range_start * bs; k < s0 + b_end * bs && k < s1 && !done; ++k) {
+                        int g = fids[k];
+                        float dx = means2d[(size_t)g * 2] - px, dy = means2d[(size_t)g * 2 + 1] - py;
+                        const float *c = conics + (size_t)g * 3;
+                        float sigma = 0.5f * (c[0] * dx * dx + c[2] * dy * dy) + c[1] * dx * dy;
+                        float alpha = fminf(ORA_MAX_ALPHA, opac[g] * expf(-sigma));
+                        if (sigma < 0.f || alpha < ORA_ALPHA_THRESHOLD) continue;
+                        float next = T * (1.f - alpha);
+                        if (next <= ORA_T_THRESHOLD) { done = 1; break; }
+                        if (gids) {
+                            gids[starts[gp] + cnt] = g % N;
+                            pids[starts[gp] + cnt] = (int64_t)gp;
+                        }
+                        ++cnt;
+                        T = next;
+                    }
+                    if (counts) counts[gp] = cnt;
+                }
+        }
 }

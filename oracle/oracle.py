@@ -45,6 +45,7 @@ _SIG = {
     "ora_covar_preci_bwd": [I64, P, P, I32, P, P, P, P],
     "ora_proj_fwd": [I32, I32, I32, P, P, P, I32, I32, I32, P, P],
     "ora_proj_bwd": [I32, I32, I32, P, P, P, I32, I32, I32, P, P, P, P],
+    "ora_raster_indices": [I32, I32, I32, I32, I64, P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P],
 }
 
 
@@ -285,3 +286,26 @@ def proj_bwd(means, covars, Ks, W, H, camera_model, v_means2d, v_covars2d):
     lib().ora_proj_bwd(B, C, N, _p(means), _p(covars), _p(Ks), W, H, camera_model, _p(_f(v_means2d)),
                        _p(_f(v_covars2d)), _p(v_means), _p(v_covars))
     return v_means, v_covars
+
+
+def raster_indices(range_start, range_end, transmittances, means2d, conics, opacities, W, H, tile_size,
+                   offsets, flatten_ids):
+    """rasterize_to_indices_in_range (RasterizeToIndices3DGS.cu:36-200): returns
+    gaussian_ids, pixel_ids, image_ids (int64) and the per-pixel counts."""
+    means2d, conics, opacities, trans = _f(means2d), _f(conics), _f(opacities), _f(transmittances)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    fids = np.ascontiguousarray(flatten_ids, np.int32)
+    N = means2d.shape[-2]
+    I = means2d.size // (2 * N)
+    th, tw = offsets.shape[-2:]
+    counts = np.zeros(I * H * W, np.int32)
+    args = (range_start, range_end, I, N, fids.size, _p(means2d), _p(conics), _p(opacities), W, H, tile_size,
+            tw, th, _p(offsets), _p(fids), _p(trans))
+    lib().ora_raster_indices(*args, _p(counts), None, None, None)
+    ends = np.cumsum(counts, dtype=np.int64)
+    starts = np.ascontiguousarray(ends - counts)
+    total = int(ends[-1]) if ends.size else 0
+    gids = np.zeros(total, np.int64)
+    pids = np.zeros(total, np.int64)
+    lib().ora_raster_indices(*args, None, _p(starts), _p(gids), _p(pids))
+    return gids, pids % (W * H), pids // (W * H), counts
