@@ -79,6 +79,7 @@ SIGNATURES = {
     "gsb_proj_bwd": (I32, [I32, I32, I32, P, P, P, I32, I32, I32, P, P, P, P, P]),
     "gsb_rasterize_to_indices": (I32, [I32, I32, I32, I32, I64, P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P,
                                        P, P]),
+    "gsb_densify_accumulate": (I32, [I64, I32, P, P, P, I32, I32, I32, P, P, P, P]),
     "gsb_spherical_harmonics_fwd": (I32, [I32, I64, I32, P, P, P, P, P]),
     "gsb_spherical_harmonics_bwd": (I32, [I32, I64, I32, P, P, P, P, P, P, P]),
     "gsb_scan_scratch_bytes": (SZ, [I64]),

@@ -365,6 +365,18 @@ GSB_API int gsb_rasterize_to_indices(int range_start, int range_end, int I, int 
                                      int32_t *chunk_cnts, int64_t *gaussian_ids, int64_t *pixel_ids,
                                      cudaStream_t stream);
 
+/* --- Densification statistics ----------------------------------------------
+ * The per-step state update of the reference's DefaultStrategy._update_state
+ * (gsplat/strategy/default.py:218-276), which has no kernel there (torch ops).
+ * grads [n,2] (means2d.grad or .absgrad), radii int32 [n,2]; packed: n = nnz
+ * pairs with gaussian_ids [n]; dense (gaussian_ids NULL): n = C*N pairs of
+ * Gaussian index % N, counted when both radii are positive. Adds
+ * |grad * (W/2*n_cameras, H/2*n_cameras)| to grad2d [N] and 1 to count [N];
+ * with max_radii [N] (optional) keeps the largest max(radii)/max(W, H). */
+GSB_API int gsb_densify_accumulate(long long n, int N, const int64_t *gaussian_ids, const float *grads,
+                                   const int32_t *radii, int width, int height, int n_cameras, float *grad2d,
+                                   float *count, float *max_radii, cudaStream_t stream);
+
 /* --- Selective Adam -------------------------------------------------------
  * Replaces gsplat::adam (gsplat/cuda/csrc/Adam.cpp:37-65, AdamCUDA.cu:34-69):
  * masked Adam without bias correction on param/grad/exp_avg/exp_avg_sq of
