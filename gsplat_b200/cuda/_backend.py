@@ -25,6 +25,20 @@ F32 = ctypes.c_float
 SZ = ctypes.c_size_t
 
 
+class GsbPeerGroup(ctypes.Structure):
+    """Mirror of ``GsbPeerGroup`` in include/gsplat_b200.h."""
+
+    _fields_ = [
+        ("arena", P * 8),
+        ("recv_offset", I64),
+        ("recv_stride", I64),
+        ("grad_offset", I64),
+        ("rank", I32),
+        ("world", I32),
+        ("error", P),
+    ]
+
+
 class GsbAdamGroup(ctypes.Structure):
     """Mirror of ``GsbAdamGroup`` in include/gsplat_b200.h."""
 
@@ -98,7 +112,18 @@ SIGNATURES = {
     "gsb_isect_bucket_emit": (I32, [I32, I32, I32, I32, P, P, P, P, P, P, I32, I32, I32, I64, P, P, P]),
     "gsb_isect_bucket_sort_max": (I32, []),
     "gsb_pack_rows": (I32, [I64, P, I32, P, P, P, P]),
-    "gsb_unpack_rows": (I32, [I64, I32, P, I32, P, P, P]),
+    "gsb_unpack_rows": (I32, [I64, P, I32, P, I32, P, P, P]),
+    "gsb_peer_mailbox_bytes": (ctypes.c_size_t, []),
+    "gsb_peer_alloc": (I32, [ctypes.c_size_t, P, P]),
+    "gsb_peer_open": (I32, [P, P]),
+    "gsb_peer_close": (I32, [P]),
+    "gsb_peer_free": (I32, [P]),
+    "gsb_peer_error_alloc": (I32, [P, P]),
+    "gsb_peer_error_free": (I32, [P]),
+    "gsb_peer_send_rows": (I32, [P, ctypes.c_ulonglong, I64, P, P, P, I32, I64, I32, P, P, P]),
+    "gsb_peer_recv_rows": (I32, [P, ctypes.c_ulonglong, I64, P, P, P, I32, I64, I32, P, P, P]),
+    "gsb_peer_send_grads": (I32, [P, ctypes.c_ulonglong, I64, P, P, I64, I32, P, P, P]),
+    "gsb_peer_recv_grads": (I32, [P, ctypes.c_ulonglong, I64, P, I32, P, P, P]),
     "gsb_exchange_ids": (I32, [I64, P, P, P, I32, P, P, P, P]),
     "gsb_isect_bucket_sort": (I32, [I32, I32, I32, P, P, I32, I32, I32, P, P, P, P, P]),
     "gsb_rasterize_fwd": (

@@ -598,15 +598,18 @@ def isect_tiles(
 
 @torch.no_grad()
 def isect_tiles_with_offsets(means2d, radii, depths, tile_size, tile_width, tile_height, packed=False,
-                             n_images=None, image_ids=None, gaussian_ids=None, conics=None, opacities=None):
+                             n_images=None, image_ids=None, gaussian_ids=None, conics=None, opacities=None,
+                             nnz_device=None):
     """isect_tiles(sort=True) followed by isect_offset_encode, as used by
     rasterization(): returns (tiles_per_gauss, isect_ids, flatten_ids, offsets
-    [I, th, tw]). The tile-bucket sort produces the offsets on the way."""
+    [I, th, tw]). The tile-bucket sort produces the offsets on the way. With
+    ``nnz_device`` (packed; a device int64 count) only that many leading rows of
+    the capacity-sized splat arrays are intersected."""
     if packed:
         assert gaussian_ids is not None, "gaussian_ids is required if packed is True"
     tiles_per_gauss, isect_ids, flatten_ids, offsets = _isect_tiles(
         means2d, radii, depths, tile_size, tile_width, tile_height, True, packed, n_images, image_ids,
-        conics, opacities)
+        conics, opacities, nnz_device)
     I = n_images if packed else math.prod(means2d.shape[:-2])
     if offsets is None:
         offsets = isect_offset_encode(isect_ids, I, tile_width, tile_height)
@@ -616,7 +619,7 @@ def isect_tiles_with_offsets(means2d, radii, depths, tile_size, tile_width, tile
 
 
 def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sort, packed, n_images,
-                 image_ids, conics, opacities):
+                 image_ids, conics, opacities, nnz_device=None):
     if packed:
         nnz = means2d.size(0)
         assert means2d.shape == (nnz, 2), means2d.shape
@@ -677,8 +680,11 @@ def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sor
                 call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)
             return tiles_per_gauss, isect_ids, flatten_ids, None
 
+        if nnz_device is not None:
+            assert packed and sort, "a device splat count needs packed, sorted intersections"
+            check_cuda("nnz_device", nnz_device)
         isect_ids, flatten_ids, offsets, _ = _bucket_isect(args, I, tile_width, tile_height,
-                                                          tiles_per_gauss, dev, stream)
+                                                          tiles_per_gauss, dev, stream, nnz_device=nnz_device)
         return tiles_per_gauss, isect_ids, flatten_ids, offsets
 
 

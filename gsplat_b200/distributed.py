@@ -144,7 +144,7 @@ def _unpack(buf: Tensor, like: List[Tuple], words: List[int]) -> List[Tensor]:
 
         dsts = (ctypes.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
         w = (ctypes.c_int * len(words))(*words)
-        call("gsb_unpack_rows", rows, buf.shape[1], buf.data_ptr(), len(outs), dsts, w, stream_of(buf))
+        call("gsb_unpack_rows", rows, None, buf.shape[1], buf.data_ptr(), len(outs), dsts, w, stream_of(buf))
         return outs
     off = 0
     for o, wj in zip(outs, words):
@@ -201,7 +201,7 @@ class _ExchangeRows(torch.autograd.Function):
 
             dsts = (ctypes.c_void_p * nf)(*[r.data_ptr() for r in res])
             w = (ctypes.c_int * nf)(*words)
-            call("gsb_unpack_rows", n, back.shape[1], back.data_ptr(), nf, dsts, w, stream_of(back))
+            call("gsb_unpack_rows", n, None, back.shape[1], back.data_ptr(), nf, dsts, w, stream_of(back))
         else:
             for r, piece in zip(res, _unpack(back, [(torch.float32, shape[1:]) for shape, _ in ctx.float_meta],
                                              words)):
@@ -282,3 +282,213 @@ def _worker(local_rank, world_rank, world_size, fn, args, backend):
     finally:
         dist.destroy_process_group()
     return True
+
+
+# ---------------------------------------------------------------------------
+# Peer-memory exchange (one node): the row exchange above without NCCL, host
+# split sizes or a second copy of the rows. See gsb_peer_* in
+# include/gsplat_b200.h for the device protocol.
+# ---------------------------------------------------------------------------
+class PeerExchange:
+    """The exchange arenas of this process group: one CUDA allocation per rank
+    (mailbox, two receive buffers, gradient buffer), mapped by every rank
+    through CUDA IPC. Created on first use and reallocated (collectively: every
+    rank makes the same decision from the same gathered sizes) when a step
+    needs more room."""
+
+    _instances = {}
+
+    def __init__(self, device: torch.device):
+        import ctypes
+
+        from .cuda import _backend as B
+
+        self.B = B
+        self.ctypes = ctypes
+        self.device = device
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        assert self.world <= 8, "peer exchange: at most 8 GPUs (one node)"
+        self.epoch = 0
+        self.arena_bytes = 0
+        self.ptrs = None
+        self.own = None
+        self.err_host = ctypes.POINTER(ctypes.c_int)()
+        self.err_dev = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            B.call("gsb_peer_error_alloc", ctypes.byref(self.err_host), ctypes.byref(self.err_dev))
+        self.group = B.GsbPeerGroup()
+        self.layout = None
+
+    @classmethod
+    def get(cls, device: torch.device) -> "PeerExchange":
+        key = (id(dist.group.WORLD), device.index)
+        inst = cls._instances.get(key)
+        if inst is None:
+            inst = cls._instances[key] = cls(device)
+        return inst
+
+    def check(self):
+        """Raises if a bounded wait of an exchange ran out (the error word is
+        host-mapped: read without a device sync)."""
+        code = self.err_host[0]
+        if code:
+            what = {1: "a destination did not consume the previous exchange",
+                    2: "a source's rows did not arrive", 3: "gradients did not arrive"}.get(code, str(code))
+            raise RuntimeError(f"peer exchange failed on rank {self.rank}: {what} (bounded wait ran out)")
+
+    def _release(self):
+        if self.ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier()
+        with torch.cuda.device(self.device):
+            for r, p in enumerate(self.ptrs):
+                if r != self.rank:
+                    self.B.call("gsb_peer_close", p)
+            self.B.call("gsb_peer_free", self.own)
+        self.ptrs = None
+
+    def ensure(self, recv_rows: int, grad_rows: int, row_words: int, grad_words: int):
+        """Arena layout for these capacities (the same numbers on every rank:
+        receive rows and the largest rank's gradient rows, from gathered
+        sizes), reallocated on every rank at once when the arena is too small."""
+        mb = self.B.lib().gsb_peer_mailbox_bytes()
+        align = lambda x: (x + 255) // 256 * 256
+        recv_bytes = align(max(1, recv_rows) * row_words * 4)
+        grad_bytes = align(max(1, grad_rows) * grad_words * 4)
+        need = mb + 2 * recv_bytes + grad_bytes
+        if self.ptrs is None or need > self.arena_bytes or self.layout != (row_words, grad_words):
+            self._release()
+            size = int(need * 1.25)
+            ctypes = self.ctypes
+            handle = (ctypes.c_char * 64)()
+            own = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                self.B.call("gsb_peer_alloc", size, ctypes.byref(own), handle)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle))
+            ptrs = []
+            with torch.cuda.device(self.device):
+                for r, h in enumerate(handles):
+                    if r == self.rank:
+                        ptrs.append(own.value)
+                        continue
+                    p = ctypes.c_void_p()
+                    self.B.call("gsb_peer_open", (ctypes.c_char * 64).from_buffer_copy(h), ctypes.byref(p))
+                    ptrs.append(p.value)
+            self.own, self.ptrs, self.arena_bytes = own.value, ptrs, size
+            self.layout = (row_words, grad_words)
+            self.epoch = 0
+            dist.barrier()
+        # receive buffers after the mailbox, the gradient buffer after them
+        recv_stride = (self.arena_bytes - mb - grad_bytes) // 2 // 256 * 256
+        g = self.group
+        for r in range(8):
+            g.arena[r] = self.ptrs[r] if r < self.world else None
+        g.recv_offset = mb
+        g.recv_stride = recv_stride
+        g.grad_offset = mb + 2 * recv_stride
+        g.rank = self.rank
+        g.world = self.world
+        g.error = self.err_dev.value
+        self.cap_recv = recv_stride // (row_words * 4)
+        self.cap_grad = (self.arena_bytes - g.grad_offset) // (grad_words * 4)
+        return g
+
+
+def _ptr_array(ctypes, tensors):
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if t is not None else None for t in tensors])
+
+
+class _PeerExchangeRows(torch.autograd.Function):
+    """exchange_rows through peer memory: rows [bounds[d], bounds[d+1]) of the
+    local packed tensors go to rank d; the received rows come back in source
+    order, in tensors of ``cap_out`` rows of which the first ``*nnz_recv`` are
+    set. Float tensors are differentiable; the backward returns the gradients of
+    the local rows (rows past ``*nnz`` left unset, as exchange_rows does)."""
+
+    @staticmethod
+    def forward(ctx, px, cap_out, grad_rows, n_float, nnz, bounds, n_world, cams_per_rank, *tensors):
+        ctx.set_materialize_grads(False)
+        B, ctypes = px.B, px.ctypes
+        words = [_words(t) for t in tensors]
+        gw = sum(words[:n_float])
+        assert tensors[0].shape[0] <= grad_rows
+        g = px.ensure(cap_out, grad_rows, sum(words), gw)
+        px.epoch += 1
+        epoch = px.epoch
+        dev = tensors[0].device
+        cap_in = tensors[0].shape[0]
+        outs = [torch.empty((cap_out, *t.shape[1:]), dtype=t.dtype, device=dev) for t in tensors]
+        route = torch.empty(2 * px.world + 1, dtype=torch.int64, device=dev)
+        nnz_recv = torch.empty(1, dtype=torch.int64, device=dev)
+        w = (ctypes.c_int * len(words))(*words)
+        stream = B.stream_of(tensors[0])
+        B.call("gsb_peer_send_rows", ctypes.byref(g), epoch, cap_in, nnz.data_ptr(), bounds.data_ptr(),
+               n_world.data_ptr(), cams_per_rank, px.cap_recv, len(tensors), _ptr_array(ctypes, tensors), w,
+               stream)
+        B.call("gsb_peer_recv_rows", ctypes.byref(g), epoch, cap_out, route.data_ptr(), nnz_recv.data_ptr(),
+               n_world.data_ptr(), cams_per_rank, px.cap_recv, len(outs), _ptr_array(ctypes, outs), w, stream)
+        ctx.px, ctx.epoch, ctx.route, ctx.nnz, ctx.nnz_recv = px, epoch, route, nnz, nnz_recv
+        ctx.float_meta = [(t.shape, wj) for t, wj in zip(tensors[:n_float], words[:n_float])]
+        ctx.n_inputs = len(tensors)
+        ctx.cap_out = cap_out
+        ctx.mark_non_differentiable(*outs[n_float:], nnz_recv)
+        return tuple(outs) + (nnz_recv,)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        px = ctx.px
+        B, ctypes = px.B, px.ctypes
+        nf = len(ctx.float_meta)
+        words = [wj for _, wj in ctx.float_meta]
+        g_in = [x.contiguous() if x is not None else None for x in grads[:nf]]
+        dev = ctx.route.device
+        g = px.group
+        w = (ctypes.c_int * nf)(*words)
+        stream = B.stream_of(ctx.route)
+        # every rank sends (zeros where a gradient is missing), so the sources'
+        # waits always end
+        B.call("gsb_peer_send_grads", ctypes.byref(g), ctx.epoch, ctx.cap_out, ctx.nnz_recv.data_ptr(),
+               ctx.route.data_ptr(), px.cap_grad, nf, _ptr_array(ctypes, g_in), w, stream)
+        res = [torch.empty(shape, dtype=torch.float32, device=dev) for shape, _ in ctx.float_meta]
+        B.call("gsb_peer_recv_grads", ctypes.byref(g), ctx.epoch, res[0].shape[0], ctx.nnz.data_ptr(), nf,
+               _ptr_array(ctypes, res), w, stream)
+        return (None,) * 8 + tuple(res) + (None,) * (ctx.n_inputs - nf)
+
+
+def peer_exchange_rows(floats: List[Tensor], ints: List[Tensor], nnz: Tensor, bounds: Tensor, n_world: Tensor,
+                       n_world_host: List[int], cams_per_rank: int):
+    """Sends local packed rows [bounds[d], bounds[d+1]) of every listed tensor
+    to rank d (bounds, nnz, n_world: device int64) through peer memory. Returns
+    (received floats, received ints, nnz_recv device int64 [1]); the received
+    tensors have cams_per_rank * sum(n_world_host) rows, the first nnz_recv set,
+    in source-rank order. Float tensors keep their autograd graph."""
+    for t in floats:
+        assert t.dtype == torch.float32
+    for t in ints:
+        assert t.dtype in (torch.int32, torch.int64)
+    dev = floats[0].device
+    px = PeerExchange.get(dev)
+    px.check()
+    world = len(n_world_host)
+    cap_out = cams_per_rank * sum(n_world_host)
+    # the packed rows of a rank: at most (all cameras) x (its Gaussians)
+    grad_rows = world * cams_per_rank * max(n_world_host)
+    tensors = [t.contiguous() for t in floats] + [t.contiguous() for t in ints]
+    out = _PeerExchangeRows.apply(px, cap_out, grad_rows, len(floats), nnz, bounds, n_world, cams_per_rank,
+                                  *tensors)
+    return list(out[:len(floats)]), list(out[len(floats):-1]), out[-1]
+
+
+def peer_exchange_available(device: torch.device) -> bool:
+    """Peer-memory exchange: every rank on this node with peer access to every
+    other (one process per GPU, NCCL process group); GSB_PEER_EXCHANGE=0 turns it off."""
+    import os
+
+    if os.environ.get("GSB_PEER_EXCHANGE", "1") == "0":
+        return False
+    if device.type != "cuda" or not dist.is_initialized() or dist.get_world_size() > 8:
+        return False
+    return dist.get_backend() == "nccl"

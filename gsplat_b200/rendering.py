@@ -31,6 +31,9 @@ from .cuda._wrapper import (
 )
 from .cuda._backend import call, device_guard, ptr, stream_of
 from .distributed import (
+    PeerExchange,
+    peer_exchange_available,
+    peer_exchange_rows,
     all_gather_int32,
     all_gather_tensor_list,
     all_to_all_int32,
@@ -249,6 +252,7 @@ def rasterization(
     if absgrad:
         assert not distributed, "AbsGrad is not supported in distributed mode."
 
+    n_world_event = None  # pinned copy of the gathered Gaussian counts (peer exchange)
     if distributed:
         assert batch_dims == (), "Distributed mode does not support batch dimensions"
         world_rank = torch.distributed.get_rank()
@@ -273,6 +277,14 @@ def rasterization(
             Ks = gathered[:, 16:25].reshape(world_size * C, 3, 3).to(Ks.dtype)
             N_world_dev = gathered[::C, 25:27].contiguous().view(torch.int64).reshape(world_size)
         C = len(viewmats)
+        if packed and peer_exchange_available(device):
+            # the Gaussian counts size the peer exchange: copied to pinned host
+            # memory now and waited for only at the exchange, so the projection
+            # kernels queued meanwhile keep the GPU busy
+            n_world_pinned = torch.empty(world_size, dtype=torch.int64, pin_memory=True)
+            n_world_pinned.copy_(N_world_dev, non_blocking=True)
+            n_world_event = torch.cuda.Event()
+            n_world_event.record()
 
     # One fused kernel for projection + view-dependent SH colour + opacity
     # compensation when the colours are per-Gaussian SH coefficients; the general
@@ -291,6 +303,7 @@ def rasterization(
     )
     compensations = None
     nnz_device = None  # device splat count of capacity-sized packed outputs (distributed)
+    peer_nnz = None  # device count of the rows received by the peer exchange (capacity-sized tensors)
     tile_width = math.ceil(width / float(tile_size))
     tile_height = math.ceil(height / float(tile_size))
     isect = None  # (tiles_per_gauss, isect_ids, flatten_ids, isect_offsets) when done by the projection
@@ -395,14 +408,15 @@ def rasterization(
             proj_features = torch.cat(feature_list, dim=-1) if len(feature_list) > 1 else feature_list[0]
 
     if distributed and packed and nnz_device is not None:
-        # Same exchange as the reference (below), with one host read and one
-        # all-to-all: packed rows are ordered by camera, so the rows for rank r
-        # are indptr[cstart[r]] .. indptr[cstart[r + 1]].
+        # Same exchange as the reference (below), through peer memory or with one
+        # host read and one all-to-all: packed rows are ordered by camera, so
+        # the rows for rank r are indptr[cstart[r]] .. indptr[cstart[r + 1]].
         # every rank holds C_world[0] cameras (the same count is gathered above)
         bounds = indptr[::C_world[0]].to(torch.int64)
-        send_cnt = bounds[1:] - bounds[:-1]
-        recv_cnt = torch.empty_like(send_cnt)
-        torch.distributed.all_to_all_single(recv_cnt, send_cnt)
+        if n_world_event is None:
+            send_cnt = bounds[1:] - bounds[:-1]
+            recv_cnt = torch.empty_like(send_cnt)
+            torch.distributed.all_to_all_single(recv_cnt, send_cnt)
         # Before the sizes reach the host: camera ids local to the destination
         # rank, gaussian ids shifted by the destination's Gaussian offset
         # (reference rendering.py:944-959), and the send buffer, all bounded by
@@ -417,6 +431,22 @@ def rasterization(
                  ptr(N_world_dev), ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
         floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
         ints = [radii, cam_local, gid_global]
+    if distributed and packed and nnz_device is not None and n_world_event is not None:
+        # peer-memory exchange: rows stored straight into the other GPUs'
+        # buffers; the received count stays on the device and reaches the host
+        # with the intersection sizes
+        n_world_event.synchronize()
+        floats, ints, peer_nnz = peer_exchange_rows(floats, ints, nnz_device, bounds, N_world_dev,
+                                                    n_world_pinned.tolist(), C_world[0])
+        means2d, depths, conics, opacities = floats[:4]
+        if proj_features is not None:
+            proj_features = floats[4]
+        radii, camera_ids, gaussian_ids = ints
+        batch_ids = torch.zeros_like(camera_ids)
+        C = C_world[world_rank]
+        image_ids = camera_ids
+        I = B * C
+    elif distributed and packed and nnz_device is not None:
         send_buf = pack_rows(floats, ints, cap, rows_device=nnz_device)
         sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
         send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
@@ -486,6 +516,12 @@ def rasterization(
 
     if isect is not None:
         tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect
+    elif peer_nnz is not None:
+        tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(
+            means2d, radii, depths, tile_size, tile_width, tile_height, packed=True, n_images=I,
+            image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics, opacities=opacities,
+            nnz_device=peer_nnz)
+        PeerExchange.get(device).check()
     else:
         # isect_tiles(sort=True, segmented) + isect_offset_encode in one pass
         tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(

@@ -408,14 +408,15 @@ GSB_API int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bool 
  * n_arrays row-major arrays srcs[j] [rows, words[j]] side by side; a NULL
  * source packs zeros; with rows_device (device int64, may be NULL) only the
  * first min(rows, *rows_device) rows are packed, so a count that is still on
- * the device can bound the work. gsb_unpack_rows: the inverse, from rows of
+ * the device can bound the work. gsb_unpack_rows: the inverse (rows_device
+ * likewise), from rows of
  * row_words words (the first sum(words) of each row are read); a NULL
  * destination skips its columns. At most 16 arrays. int64 columns count as 2
  * words. */
 GSB_API int gsb_pack_rows(long long rows, const int64_t *rows_device, int n_arrays, void *const *srcs,
                           const int *words, uint32_t *buf, cudaStream_t stream);
-GSB_API int gsb_unpack_rows(long long rows, int row_words, const uint32_t *buf, int n_arrays,
-                            void *const *dsts, const int *words, cudaStream_t stream);
+GSB_API int gsb_unpack_rows(long long rows, const int64_t *rows_device, int row_words, const uint32_t *buf,
+                            int n_arrays, void *const *dsts, const int *words, cudaStream_t stream);
 /* Camera c goes to rank d = c / cams_per_rank: cam_out = c mod cams_per_rank,
  * gid_out = gaussian_ids + gauss_counts[0] + ... + gauss_counts[d - 1] (the
  * reference's id remap, rendering.py:944-959), for the first
@@ -423,6 +424,61 @@ GSB_API int gsb_unpack_rows(long long rows, int row_words, const uint32_t *buf, 
 GSB_API int gsb_exchange_ids(long long n, const int64_t *n_device, const int64_t *camera_ids,
                              const int64_t *gaussian_ids, int cams_per_rank, const int64_t *gauss_counts,
                              int64_t *cam_out, int64_t *gid_out, cudaStream_t stream);
+
+/* --- Peer-memory exchange (multi-GPU, GPUs of one node) --------------------
+ * The same exchange as the all-to-all above, done by kernels that store the
+ * rows straight into the other GPUs' memory (CUDA IPC mappings, NVLink) and
+ * hand over with flags (release / acquire at system scope), so no split size
+ * reaches the host and no row is copied twice. Every rank owns one arena
+ * (gsb_peer_alloc; its IPC handle, 64 bytes, goes to the other ranks, which
+ * map it with gsb_peer_open): a mailbox of gsb_peer_mailbox_bytes() at offset
+ * 0, two receive buffers of cap_recv rows (exchanges alternate), and a
+ * gradient buffer with one row per local packed row. Rows from source rank r
+ * sit at rows cams_per_rank * (n_world[0] + ... + n_world[r - 1]) of a receive
+ * buffer. Exchange numbers (epoch) start at 1 and grow by one per exchange,
+ * the same on every rank. Every wait is bounded (a few seconds): a wait that
+ * runs out writes 1 (previous exchange not consumed), 2 (rows) or 3
+ * (gradients) to the group's error word, a host-mapped int
+ * (gsb_peer_error_alloc), and the kernel finishes without the data.
+ *
+ * gsb_peer_send_rows: local packed rows [0, *nnz_device) of the row-major
+ * source arrays (as gsb_pack_rows), rows bounds[d] .. bounds[d + 1] to rank d.
+ * gsb_peer_recv_rows: waits for every source, writes route int64
+ * [2*world + 1] (prefix of the counts by source, then each source's first
+ * local row), *nnz_recv, and the received rows in source order into the
+ * separate arrays (capacity cap_rows rows). gsb_peer_send_grads: the gradient
+ * rows of the received rows (separate arrays, route of that exchange) to their
+ * sources' gradient buffers, at the rows they came from.
+ * gsb_peer_recv_grads: waits for them and unpacks the first *nnz_device rows
+ * of this rank's gradient buffer into separate arrays. */
+typedef struct {
+    void *arena[8];          /* every rank's arena mapped in this process (own one at [rank]) */
+    long long recv_offset;   /* byte offset of receive buffer 0 in an arena */
+    long long recv_stride;   /* bytes from receive buffer 0 to 1 */
+    long long grad_offset;   /* byte offset of the gradient buffer */
+    int rank, world;
+    int *error;              /* device address of the host-mapped error word */
+} GsbPeerGroup;
+GSB_API size_t gsb_peer_mailbox_bytes(void);
+GSB_API int gsb_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
+GSB_API int gsb_peer_open(const void *ipc_handle, void **ptr);
+GSB_API int gsb_peer_close(void *ptr);
+GSB_API int gsb_peer_free(void *ptr);
+GSB_API int gsb_peer_error_alloc(int **host_ptr, int **device_ptr);
+GSB_API int gsb_peer_error_free(int *host_ptr);
+GSB_API int gsb_peer_send_rows(const GsbPeerGroup *g, unsigned long long epoch, long long cap_rows,
+                               const int64_t *nnz_device, const int64_t *bounds, const int64_t *n_world,
+                               int cams_per_rank, long long cap_recv, int n_arrays, void *const *srcs,
+                               const int *words, cudaStream_t stream);
+GSB_API int gsb_peer_recv_rows(const GsbPeerGroup *g, unsigned long long epoch, long long cap_rows, int64_t *route,
+                               int64_t *nnz_recv, const int64_t *n_world, int cams_per_rank, long long cap_recv,
+                               int n_arrays, void *const *dsts, const int *words, cudaStream_t stream);
+GSB_API int gsb_peer_send_grads(const GsbPeerGroup *g, unsigned long long epoch, long long cap_rows,
+                                const int64_t *nnz_recv, const int64_t *route, long long cap_grad, int n_arrays,
+                                void *const *srcs, const int *words, cudaStream_t stream);
+GSB_API int gsb_peer_recv_grads(const GsbPeerGroup *g, unsigned long long epoch, long long cap_rows,
+                                const int64_t *nnz_device, int n_arrays, void *const *dsts, const int *words,
+                                cudaStream_t stream);
 
 /* --- Measurement ----------------------------------------------------------
  * FP32 FMA throughput probe (no reference counterpart): blocks x threads threads

@@ -52,9 +52,23 @@ def _worker(rank, world, store_path, q):
         params = [t.clone().requires_grad_(True) for t in mine[:5]]
         vm, K = mine[5], mine[6]
         G = torch.randn((1, H, W, 3), generator=torch.Generator().manual_seed(7 + rank)).to(dev)
-        rc, ra, _ = gsplat_b200.rasterization(*params, vm, K, W, H, sh_degree=3, packed=True,
-                                              distributed=True)
-        (rc * G).sum().backward()
+        # several exchanges (both receive buffers of the peer path), one of them
+        # forward-only, must all give the same result
+        grads_seen = []
+        for it in range(3):
+            for p in params:
+                p.grad = None
+            rc, ra, _ = gsplat_b200.rasterization(*params, vm, K, W, H, sh_degree=3, packed=True,
+                                                  distributed=True)
+            if it == 1:
+                with torch.no_grad():
+                    gsplat_b200.rasterization(*params, vm, K, W, H, sh_degree=3, packed=True, distributed=True)
+            (rc * G).sum().backward()
+            grads_seen.append([p.grad.clone() for p in params])
+        for gs in grads_seen[1:]:
+            for a, b in zip(gs, grads_seen[0]):
+                # the rasterizer's float atomics may add in another order
+                torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5)
 
         # single-process reference: all Gaussians, both cameras, summed loss
         scenes = [_scene(r, dev) for r in range(world)]
@@ -80,17 +94,32 @@ def _worker(rank, world, store_path, q):
         q.put((rank, traceback.format_exc()))
 
 
-def test_distributed_packed_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("peer", ["1", "0"])
+def test_distributed_packed_matches_single_gpu(tmp_path, peer, monkeypatch):
+    """peer "1": the peer-memory exchange; "0": the NCCL all-to-all path."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    monkeypatch.setenv("GSB_PEER_EXCHANGE", peer)
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     store = str(tmp_path / "rendezvous")
     procs = [ctx.Process(target=_worker, args=(r, 2, store, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=300) for _ in procs]
+    import queue
+
+    results = []
+    for _ in procs:
+        try:
+            results.append(q.get(timeout=300))
+        except queue.Empty:
+            break
+        if results[-1][1]:
+            break  # a failed rank: its peer may now wait in a collective
     for p in procs:
-        p.join(timeout=60)
-    errors = [e for _, e in results if e]
+        p.join(timeout=90)
+        if p.is_alive():
+            p.kill()
+    errors = [f"rank {r}: {e}" for r, e in results if e]
     assert not errors, errors[0]
+    assert len(results) == len(procs), "a rank neither finished nor reported an error"
