@@ -177,15 +177,21 @@ def is_available() -> bool:
 
 
 # Optional per-entry-point timing: when a dict is installed here (bench.py does
-# this), every call records a pair of CUDA events on the current stream of the
-# current device around the launch, keyed by entry-point name.
+# this), every call (or, with ``timing_names`` a set, every call of those entry
+# points) records a pair of CUDA events on the current stream of the current
+# device around the launch, keyed by entry-point name. ``calls``, when a dict,
+# counts the calls by entry point (no events).
 timing = None
+timing_names = None
+calls = None
 
 
 def call(name: str, *args) -> int:
     """Calls a C-ABI function and raises RuntimeError on a negative status."""
     fn = getattr(lib(), name)
-    if timing is not None:
+    if calls is not None:
+        calls[name] = calls.get(name, 0) + 1
+    if timing is not None and (timing_names is None or name in timing_names):
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
