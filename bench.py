@@ -405,8 +405,6 @@ def run_gsb(args):
 
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
-    if args.n is None:
-        args.n = 3_000_000 if args.workload == "config3" else 1_000_000
     params, d = make_params(args.n, 1 + rank, dev, rank, world, args.workload)
     W, H = d["width"], d["height"]
     viewmat = d["viewmats"].to(dev)
@@ -648,6 +646,8 @@ def run_gsb(args):
 
 def main():
     args = parse()
+    if args.n is None:
+        args.n = 3_000_000 if args.workload == "config3" else 1_000_000
     if args.impl == "reference":
         run_reference(args)
         return
