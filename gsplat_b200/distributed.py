@@ -319,6 +319,7 @@ class PeerExchange:
             B.call("gsb_peer_error_alloc", ctypes.byref(self.err_host), ctypes.byref(self.err_dev))
         self.group = B.GsbPeerGroup()
         self.layout = None
+        self.disabled = False  # peer memory could not be set up on every rank: use the all-to-all
 
     @classmethod
     def get(cls, device: torch.device) -> "PeerExchange":
@@ -364,19 +365,43 @@ class PeerExchange:
             ctypes = self.ctypes
             handle = (ctypes.c_char * 64)()
             own = ctypes.c_void_p()
-            with torch.cuda.device(self.device):
-                self.B.call("gsb_peer_alloc", size, ctypes.byref(own), handle)
+            ok = True
+            try:
+                with torch.cuda.device(self.device):
+                    self.B.call("gsb_peer_alloc", size, ctypes.byref(own), handle)
+            except RuntimeError:
+                ok = False
             handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(handle))
+            dist.all_gather_object(handles, bytes(handle) if ok else None)
             ptrs = []
-            with torch.cuda.device(self.device):
-                for r, h in enumerate(handles):
-                    if r == self.rank:
-                        ptrs.append(own.value)
-                        continue
-                    p = ctypes.c_void_p()
-                    self.B.call("gsb_peer_open", (ctypes.c_char * 64).from_buffer_copy(h), ctypes.byref(p))
-                    ptrs.append(p.value)
+            if all(h is not None for h in handles):
+                with torch.cuda.device(self.device):
+                    for r, h in enumerate(handles):
+                        if r == self.rank:
+                            ptrs.append(own.value)
+                            continue
+                        p = ctypes.c_void_p()
+                        try:
+                            self.B.call("gsb_peer_open", (ctypes.c_char * 64).from_buffer_copy(h),
+                                        ctypes.byref(p))
+                        except RuntimeError:
+                            ok = False
+                            break
+                        ptrs.append(p.value)
+            else:
+                ok = False
+            # every rank learns whether every rank could map every arena
+            flags = [None] * self.world
+            dist.all_gather_object(flags, ok)
+            if not all(flags):
+                with torch.cuda.device(self.device):
+                    for r, p in enumerate(ptrs):
+                        if r != self.rank:
+                            self.B.call("gsb_peer_close", p)
+                    if own.value:
+                        self.B.call("gsb_peer_free", own.value)
+                self.disabled = True
+                return None
             self.own, self.ptrs, self.arena_bytes = own.value, ptrs, size
             self.layout = (row_words, grad_words)
             self.epoch = 0
@@ -413,9 +438,8 @@ class _PeerExchangeRows(torch.autograd.Function):
         ctx.set_materialize_grads(False)
         B, ctypes = px.B, px.ctypes
         words = [_words(t) for t in tensors]
-        gw = sum(words[:n_float])
         assert tensors[0].shape[0] <= grad_rows
-        g = px.ensure(cap_out, grad_rows, sum(words), gw)
+        g = px.group  # laid out by px.ensure() for these sizes (peer_exchange_rows)
         px.epoch += 1
         epoch = px.epoch
         dev = tensors[0].device
@@ -464,7 +488,9 @@ def peer_exchange_rows(floats: List[Tensor], ints: List[Tensor], nnz: Tensor, bo
     to rank d (bounds, nnz, n_world: device int64) through peer memory. Returns
     (received floats, received ints, nnz_recv device int64 [1]); the received
     tensors have cams_per_rank * sum(n_world_host) rows, the first nnz_recv set,
-    in source-rank order. Float tensors keep their autograd graph."""
+    in source-rank order. Float tensors keep their autograd graph. Returns None
+    (on every rank) when the peer arenas could not be set up everywhere; the
+    caller then uses exchange_rows."""
     for t in floats:
         assert t.dtype == torch.float32
     for t in ints:
@@ -477,6 +503,9 @@ def peer_exchange_rows(floats: List[Tensor], ints: List[Tensor], nnz: Tensor, bo
     # the packed rows of a rank: at most (all cameras) x (its Gaussians)
     grad_rows = world * cams_per_rank * max(n_world_host)
     tensors = [t.contiguous() for t in floats] + [t.contiguous() for t in ints]
+    words = [_words(t) for t in tensors]
+    if px.disabled or px.ensure(cap_out, grad_rows, sum(words), sum(words[:len(floats)])) is None:
+        return None  # peer memory not available on every rank (decided together)
     out = _PeerExchangeRows.apply(px, cap_out, grad_rows, len(floats), nnz, bounds, n_world, cams_per_rank,
                                   *tensors)
     return list(out[:len(floats)]), list(out[len(floats):-1]), out[-1]
@@ -488,6 +517,9 @@ def peer_exchange_available(device: torch.device) -> bool:
     import os
 
     if os.environ.get("GSB_PEER_EXCHANGE", "1") == "0":
+        return False
+    inst = PeerExchange._instances.get((id(dist.group.WORLD), device.index)) if dist.is_initialized() else None
+    if inst is not None and inst.disabled:
         return False
     if device.type != "cuda" or not dist.is_initialized() or dist.get_world_size() > 8:
         return False

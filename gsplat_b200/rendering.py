@@ -431,13 +431,20 @@ def rasterization(
                  ptr(N_world_dev), ptr(cam_local), ptr(gid_global), stream_of(camera_ids))
         floats = [means2d, depths, conics, opacities] + ([proj_features] if proj_features is not None else [])
         ints = [radii, cam_local, gid_global]
+    peer_out = None
     if distributed and packed and nnz_device is not None and n_world_event is not None:
         # peer-memory exchange: rows stored straight into the other GPUs'
         # buffers; the received count stays on the device and reaches the host
         # with the intersection sizes
         n_world_event.synchronize()
-        floats, ints, peer_nnz = peer_exchange_rows(floats, ints, nnz_device, bounds, N_world_dev,
-                                                    n_world_pinned.tolist(), C_world[0])
+        peer_out = peer_exchange_rows(floats, ints, nnz_device, bounds, N_world_dev, n_world_pinned.tolist(),
+                                      C_world[0])
+        if peer_out is None:  # peer memory unavailable on some rank: the all-to-all below
+            send_cnt = bounds[1:] - bounds[:-1]
+            recv_cnt = torch.empty_like(send_cnt)
+            torch.distributed.all_to_all_single(recv_cnt, send_cnt)
+    if peer_out is not None:
+        floats, ints, peer_nnz = peer_out
         means2d, depths, conics, opacities = floats[:4]
         if proj_features is not None:
             proj_features = floats[4]
