@@ -289,6 +289,33 @@ def _worker(local_rank, world_rank, world_size, fn, args, backend):
 # split sizes or a second copy of the rows. See gsb_peer_* in
 # include/gsplat_b200.h for the device protocol.
 # ---------------------------------------------------------------------------
+def _align256(x: int) -> int:
+    return (x + 255) // 256 * 256
+
+
+def arena_bytes_needed(mailbox_bytes: int, recv_rows: int, grad_rows: int, row_words: int,
+                       grad_words: int) -> int:
+    """Bytes of a peer arena holding the mailbox, two receive buffers of
+    recv_rows rows of row_words 4-byte words, and a gradient buffer of
+    grad_rows rows of grad_words words, each region 256-byte aligned."""
+    return (mailbox_bytes + 2 * _align256(max(1, recv_rows) * row_words * 4) +
+            _align256(max(1, grad_rows) * grad_words * 4))
+
+
+def arena_layout(arena_bytes: int, mailbox_bytes: int, grad_rows: int, row_words: int, grad_words: int):
+    """Offsets inside an arena of arena_bytes (the same on every rank): the
+    mailbox at 0, receive buffers 0 and 1 after it, the gradient buffer (room
+    for grad_rows rows) at the end; the receive buffers take the rest. Returns
+    recv_offset, recv_stride, grad_offset and the row capacities cap_recv,
+    cap_grad."""
+    grad_bytes = _align256(max(1, grad_rows) * grad_words * 4)
+    recv_stride = (arena_bytes - mailbox_bytes - grad_bytes) // 2 // 256 * 256
+    grad_offset = mailbox_bytes + 2 * recv_stride
+    return {"recv_offset": mailbox_bytes, "recv_stride": recv_stride, "grad_offset": grad_offset,
+            "cap_recv": recv_stride // (row_words * 4),
+            "cap_grad": (arena_bytes - grad_offset) // (grad_words * 4)}
+
+
 class PeerExchange:
     """The exchange arenas of this process group: one CUDA allocation per rank
     (mailbox, two receive buffers, gradient buffer), mapped by every rank
@@ -355,10 +382,7 @@ class PeerExchange:
         receive rows and the largest rank's gradient rows, from gathered
         sizes), reallocated on every rank at once when the arena is too small."""
         mb = self.B.lib().gsb_peer_mailbox_bytes()
-        align = lambda x: (x + 255) // 256 * 256
-        recv_bytes = align(max(1, recv_rows) * row_words * 4)
-        grad_bytes = align(max(1, grad_rows) * grad_words * 4)
-        need = mb + 2 * recv_bytes + grad_bytes
+        need = arena_bytes_needed(mb, recv_rows, grad_rows, row_words, grad_words)
         if self.ptrs is None or need > self.arena_bytes or self.layout != (row_words, grad_words):
             self._release()
             size = int(need * 1.25)
@@ -406,19 +430,18 @@ class PeerExchange:
             self.layout = (row_words, grad_words)
             self.epoch = 0
             dist.barrier()
-        # receive buffers after the mailbox, the gradient buffer after them
-        recv_stride = (self.arena_bytes - mb - grad_bytes) // 2 // 256 * 256
+        lay = arena_layout(self.arena_bytes, mb, grad_rows, row_words, grad_words)
         g = self.group
         for r in range(8):
             g.arena[r] = self.ptrs[r] if r < self.world else None
-        g.recv_offset = mb
-        g.recv_stride = recv_stride
-        g.grad_offset = mb + 2 * recv_stride
+        g.recv_offset = lay["recv_offset"]
+        g.recv_stride = lay["recv_stride"]
+        g.grad_offset = lay["grad_offset"]
         g.rank = self.rank
         g.world = self.world
         g.error = self.err_dev.value
-        self.cap_recv = recv_stride // (row_words * 4)
-        self.cap_grad = (self.arena_bytes - g.grad_offset) // (grad_words * 4)
+        self.cap_recv = lay["cap_recv"]
+        self.cap_grad = lay["cap_grad"]
         return g
 
 

@@ -163,3 +163,23 @@ def _exchange_rows(rank, world):
 
 def test_exchange_rows_world2_gloo():
     run(_exchange_rows)
+
+
+def test_peer_arena_layout():
+    """Arena layout of the peer-memory exchange (host arithmetic): every region
+    fits, none overlaps, the capacities cover the requested rows, offsets are
+    256-byte aligned, for arenas allocated with the 25% headroom and exactly."""
+    from gsplat_b200.distributed import arena_bytes_needed, arena_layout
+
+    mb = 4096
+    for recv_rows, grad_rows, rw, gw in [(1, 1, 1, 1), (2_000_000, 2_000_000, 16, 10), (8_000_000, 8_000_000, 16, 10),
+                                         (12345, 777, 13, 7), (0, 0, 3, 2)]:
+        need = arena_bytes_needed(mb, recv_rows, grad_rows, rw, gw)
+        for size in (need, int(need * 1.25)):
+            lay = arena_layout(size, mb, grad_rows, rw, gw)
+            assert lay["recv_offset"] == mb
+            assert lay["recv_stride"] % 256 == 0 and lay["grad_offset"] % 256 == 0
+            assert lay["cap_recv"] >= recv_rows and lay["cap_grad"] >= grad_rows
+            # buffer 1 ends before the gradient buffer, which ends inside the arena
+            assert mb + lay["recv_stride"] + lay["cap_recv"] * rw * 4 <= lay["grad_offset"]
+            assert lay["grad_offset"] + lay["cap_grad"] * gw * 4 <= size
