@@ -602,7 +602,9 @@ def run_gsb(args):
                                   "isect, sort, backward chain, Adam; rasterizer on every 8th tile row "
                                   "scaled x8"}
     n_isects = int(meta["isect_ids"].numel()) if "isect_ids" in meta else None
-    nnz = int(meta["gaussian_ids"].numel()) if meta.get("gaussian_ids") is not None else None
+    # visible (camera, Gaussian) pairs; distributed meta tensors keep their capacity rows
+    nnz = (int(meta["gaussian_ids"].numel()) if meta.get("gaussian_ids") is not None and not distributed
+           else None)
     # entry-point calls inside the timed region (each launches one or more kernels)
     launches = sum(calls.values()) // args.steps if calls else None
 
