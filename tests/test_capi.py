@@ -122,3 +122,57 @@ def test_bucket_shard_plan():
     lib = _backend.lib()
     assert lib.gsb_isect_bucket_shards(1, 2000, 2000) == int(m.group(1))
     assert lib.gsb_isect_bucket_shards(1, 81, 53) >= 32
+
+
+def declared_arities():
+    """Parameter count of every GSB_API prototype in the header."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"GSB_API\s+[\w\s\*]+?\b(gsb_\w+)\s*\((.*?)\)\s*;", text, flags=re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_argument_counts_match_header():
+    from gsplat_b200.cuda import _backend
+
+    arity = declared_arities()
+    assert len(arity) == len(declared_functions())
+    wrong = {n: (arity[n], len(_backend.SIGNATURES[n][1])) for n in arity
+             if len(_backend.SIGNATURES[n][1]) != arity[n]}
+    assert not wrong, wrong
+
+
+def _ctype_of(param: str):
+    """ctypes type a header parameter declaration maps to."""
+    import ctypes
+
+    p = " ".join(param.split())
+    if "*" in p or p.startswith("cudaStream_t"):
+        return ctypes.c_void_p
+    base = p.rsplit(" ", 1)[0] if " " in p else p
+    base = base.replace("const ", "")
+    return {"int": ctypes.c_int, "long long": ctypes.c_longlong, "float": ctypes.c_float,
+            "size_t": ctypes.c_size_t, "unsigned long long": ctypes.c_ulonglong,
+            "bool": ctypes.c_bool}[base]
+
+
+def test_ctypes_argument_types_match_header():
+    import ctypes
+
+    from gsplat_b200.cuda import _backend
+
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    wrong = []
+    for m in re.finditer(r"GSB_API\s+[\w\s\*]+?\b(gsb_\w+)\s*\((.*?)\)\s*;", text, flags=re.S):
+        name, params = m.group(1), m.group(2).strip()
+        if params in ("", "void"):
+            continue
+        want = [_ctype_of(q) for q in params.split(",")]
+        have = _backend.SIGNATURES[name][1]
+        # structure / array pointers are bound as pointers too
+        have = [ctypes.c_void_p if (isinstance(h, type) and issubclass(h, ctypes._Pointer)) else h for h in have]
+        if [w.__name__ for w in want] != [getattr(h, "__name__", str(h)) for h in have]:
+            wrong.append((name, [w.__name__ for w in want], [getattr(h, "__name__", str(h)) for h in have]))
+    assert not wrong, wrong[:3]
