@@ -1,17 +1,17 @@
 """``rasterization()``: the 3D Gaussian splatting render call, forward + backward.
 
 Drop-in for the reference's ``gsplat/rendering.py:256-1273`` for the 3DGS pinhole /
-orthographic path: same keyword arguments and defaults, same return value
+orthographic / fisheye path: same keyword arguments and defaults, same return value
 ``(render_colors, render_alphas, meta)`` and the same ``meta`` keys, so
 densification strategies that read ``meta["means2d"].grad`` / ``.absgrad`` work
 unchanged. The stages are the ops of ``gsplat_b200.cuda._wrapper`` (projection,
 SH, tile intersection + sort + offsets, rasterization); the multi-GPU mode shards
-Gaussians and exchanges projected splats per camera with NCCL all-to-all exactly
-like the reference (``rendering.py:689-706, 907-1022``).
+Gaussians and sends projected splats to the rank that owns their camera, like the
+reference (``rendering.py:689-706, 907-1022``), through peer memory on one node
+(or an NCCL all-to-all).
 
 Options that belong to other pipelines of the reference (3DGUT ``with_ut``,
-``with_eval3d``, lidar, distortion, rolling shutter, fisheye) raise
-``NotImplementedError``.
+``with_eval3d``, lidar, distortion, rolling shutter) raise ``NotImplementedError``.
 """
 
 import math
