@@ -7,6 +7,12 @@ differentiable through ``torch.distributed.nn.functional`` when the data
 requires grad. With ``world_size == 1`` every call returns its input unchanged.
 The process group is NCCL on GPUs (one process per GPU); the same code runs on
 ``gloo`` for CPU tests.
+
+The splat exchange of ``rasterization(distributed=True)`` uses either
+``exchange_rows`` (one packed ``all_to_all_single`` per direction) or, by default
+on one node, ``peer_exchange_rows``: kernels store the rows straight into the
+other GPUs' memory (CUDA IPC mappings of per-rank arenas) and hand over with
+system-scope flags, so no split size reaches the host.
 """
 
 import math
