@@ -280,24 +280,39 @@ def cpu_reference_step(sc, tile_row_stride=8):
     return sum(t.values()), {k: round(v * 1e3, 2) for k, v in t.items()}
 
 
+REF_BUDGET_S = 120.0  # wall time of the --impl reference steps (warm-up + timed)
+
+
 def run_reference(args):
-    """`--impl reference`: the reference algorithm timed on the host cores."""
+    """`--impl reference`: the reference algorithm timed on the host cores. Each
+    step is a bounded sample of the config-1 step: the full scene through every
+    stage, the rasterizer on every s-th row of tiles with its time scaled by the
+    row fraction; one calibration step picks s (8, 16, 32 or 64) so that all
+    warm-up and timed steps fit in REF_BUDGET_S where the host allows."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     sc = cpu_scene(args.n, 1)
     W, H = sc["width"], sc["height"]
+    _, cal = cpu_reference_step(sc, tile_row_stride=8)
+    raster_full_s = (cal["raster_fwd"] + cal["raster_bwd"]) / 1e3  # scaled to the whole image
+    other_s = sum(v for k, v in cal.items() if not k.startswith("raster")) / 1e3
+    per_step = REF_BUDGET_S / max(1, args.warmup + args.steps)
+    stride = 8
+    while stride < 64 and other_s + raster_full_s / stride > per_step:
+        stride *= 2
     for _ in range(args.warmup):
-        cpu_reference_step(sc)
+        cpu_reference_step(sc, tile_row_stride=stride)
     times, detail = [], None
     for _ in range(args.steps):
-        dt, detail = cpu_reference_step(sc)
+        dt, detail = cpu_reference_step(sc, tile_row_stride=stride)
         times.append(dt)
     ms = 1e3 * sum(times) / len(times)
     value = (W * H / 1e6) / (ms / 1e3)
     cores = os.cpu_count()
-    sample = ("config 1 (1M Gaussians, 1297x840): projection, SH, isect, sort, backward chain and "
-              "Adam on the full scene; rasterizer forward/backward on every 8th tile row, scaled x8")
+    sample = (f"config 1 (1M Gaussians, 1297x840): projection, SH, isect, sort, backward chain and Adam "
+              f"on the full scene; rasterizer forward/backward on every {stride}th tile row, scaled to "
+              "the whole image")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "MPix/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
