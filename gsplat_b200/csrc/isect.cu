@@ -148,7 +148,6 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
 template <bool EMIT, class Sink>
 __device__ uint32_t aabb_tiles(const IsectParams &p, float mx, float my, int32_t rx, int32_t ry,
                                Sink *sink) {
-    const float ts = (float)p.tile_size;
     const float trx = tile_div(p, (float)rx), try_ = tile_div(p, (float)ry);
     const float tx = tile_div(p, mx), ty = tile_div(p, my);
     const int tw = (int)p.tile_width, th = (int)p.tile_height;

@@ -208,7 +208,6 @@ template <int CDIM, int BX, int BY>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     constexpr int PPT = BX * BY;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int nwarps = blockDim.x >> 5;
     const RasterSmem s = carve<CDIM>(smem_raw);
     const uint32_t image = blockIdx.y;
     const uint32_t tile = blockIdx.x;
