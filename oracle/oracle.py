@@ -7,9 +7,12 @@ baseline import this module; the gsplat_b200 package never does.
 
 Parity pins: projection, SH, covariance, AABB tile intersection and offset
 encoding are checked against golden vectors produced by the reference's own
-PyTorch implementation (``tests/golden/make_golden.py``). The rasterizer, the
-AccuTile sweep and Adam have no executable CPU path in the reference (its torch
-rasterizer needs a CUDA op and nerfacc); they are restated from the CUDA source.
+PyTorch implementation (``tests/golden/make_golden.py``). The rasterizer forward
+and backward are checked against the reference's PyTorch rasterizer
+(``_rasterize_to_pixels`` / ``accumulate`` with autograd), run with nerfacc's two
+compositing functions restated and with this oracle's index pass standing in
+for its CUDA op. The index pass itself, the AccuTile sweep and Adam have no
+executable CPU path in the reference; they are restated from the CUDA source.
 """
 
 import ctypes

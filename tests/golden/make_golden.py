@@ -9,10 +9,13 @@ is imported on CPU -- its CUDA extension cannot be built there, so the JIT loade
 told that no CUDA toolkit exists and gsplat falls back to ``_C = None``. Inputs follow
 the reference tests: a seeded subset of the reference fixture assets/test_garden.npz
 with its three real cameras (tests/test_basic.py:85-110, gsplat/_helper.py:48-100),
-the random intersection case of tests/test_basic.py:698-736 and the SH case of
-tests/test_basic.py:2903-2939. Outputs are stored as small .npz files which the
-CPU tests (tests/test_oracle_golden.py) compare with the oracle and the GPU tests
-compare with the kernels; nothing reads the reference at test time.
+the random intersection case of tests/test_basic.py:698-736, the SH case of
+tests/test_basic.py:2903-2939 and the rasterizer case of tests/test_basic.py:1954-2063.
+Outputs are stored as small .npz files which the CPU tests (tests/test_oracle_golden.py,
+tests/test_oracle_raster_golden.py) compare with the oracle and the GPU tests compare
+with the kernels; nothing reads the reference at test time.
+
+    python tests/golden/make_golden.py /path/to/reference raster   # one fixture
 """
 
 import os
@@ -210,18 +213,145 @@ def make_isect(ti):
         isect_offsets=offsets.numpy())
 
 
+def nerfacc_standin():
+    """A module object with the two nerfacc functions that the reference's
+    PyTorch compositing imports (gsplat/cuda/_torch_impl.py:522-568). nerfacc is
+    a third-party dependency of the reference (setup.py: ``nerfacc>=0.5.3``) and is
+    not installed here; this restates its published algorithm (nerfacc 0.5.3,
+    ``nerfacc/volrend.py``) for samples given ray by ray, in order along each ray:
+
+    - ``render_weight_from_alpha``: transmittance = exclusive product of
+      (1 - alpha) along the ray, weight = transmittance * alpha;
+    - ``accumulate_along_rays``: per-ray sum of weight * value (of the weights
+      when no values are given).
+
+    Both are differentiable, like nerfacc's."""
+    import types
+
+    def render_weight_from_alpha(alphas, packed_info=None, ray_indices=None, n_rays=None, prefix_trans=None):
+        assert packed_info is None and prefix_trans is None and ray_indices is not None
+        if alphas.numel() == 0:
+            return alphas.clone(), alphas.clone()
+        if ray_indices.numel() > 1:
+            assert bool((ray_indices[1:] >= ray_indices[:-1]).all()), "samples must be grouped by ray"
+        _, seg, counts = torch.unique_consecutive(ray_indices, return_inverse=True, return_counts=True)
+        starts = torch.cumsum(counts, 0) - counts
+        pos = torch.arange(ray_indices.numel()) - starts[seg]
+        grid = torch.ones((counts.numel(), int(counts.max())), dtype=alphas.dtype)
+        grid = grid.index_put((seg, pos), 1.0 - alphas)
+        prod = torch.cumprod(grid, dim=1)
+        excl = torch.cat([torch.ones_like(prod[:, :1]), prod[:, :-1]], dim=1)
+        trans = excl[seg, pos]
+        return trans * alphas, trans
+
+    def accumulate_along_rays(weights, values=None, ray_indices=None, n_rays=None):
+        src = weights[..., None] if values is None else weights[..., None] * values
+        out = torch.zeros((n_rays, src.shape[-1]), dtype=src.dtype)
+        return out.index_add(0, ray_indices, src)
+
+    mod = types.ModuleType("nerfacc")
+    mod.render_weight_from_alpha = render_weight_from_alpha
+    mod.accumulate_along_rays = accumulate_along_rays
+    return mod
+
+
+def make_raster(ti, tm, ref_root):
+    """tests/test_basic.py:1954-2063 (test_rasterize_to_pixels) on the CPU: the
+    reference's own PyTorch rasterizer ``_rasterize_to_pixels`` (its batching over
+    the tile lists, transmittance carry-over between batches, ``accumulate``,
+    background) and autograd through it. Two pieces it calls have no CPU path
+    in the reference and are supplied here: nerfacc (``nerfacc_standin``) and the
+    CUDA op behind ``rasterize_to_indices_in_range``, replaced by the oracle's
+    restatement of RasterizeToIndices3DGS.cu (which pixel/splat pairs a batch
+    composites, given the transmittances so far). The golden outputs thus pin
+    the oracle rasterizer's forward and backward to the reference's own
+    compositing code over the oracle's index pairs. Two cameras of the fixture
+    scaled to 80x56 pixels (a partial tile row), AABB tiles from the
+    reference's own projection / _isect_tiles / _isect_offset_encode, splats
+    large and dense enough that pixels reach the transmittance threshold and
+    every third alpha hits the 0.99 clamp; ``batch_per_iter`` 100 (one pass) and
+    1 (one 256-entry batch of each tile list per pass); and a "soft" case with
+    the opacities scaled by 0.3 (no pixel near the transmittance threshold)."""
+    import math
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import oracle as O
+    import gsplat.cuda._wrapper as ref_wrapper
+
+    def indices_from_oracle(range_start, range_end, transmittances, means2d, conics, opacities, image_width,
+                            image_height, tile_size, isect_offsets, flatten_ids):
+        n = lambda t: t.detach().numpy()
+        gids, pids, iids, _ = O.raster_indices(range_start, range_end, n(transmittances), n(means2d), n(conics),
+                                               n(opacities), image_width, image_height, tile_size,
+                                               isect_offsets.numpy(), flatten_ids.numpy())
+        return torch.from_numpy(gids), torch.from_numpy(pids), torch.from_numpy(iids)
+
+    sys.modules["nerfacc"] = nerfacc_standin()
+    ref_wrapper.rasterize_to_indices_in_range = indices_from_oracle
+    # the backward of the indexed gathers accumulates in parallel on several
+    # threads (order-dependent rounding): one thread keeps the fixture reproducible
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+
+    means, quats, scales, opacities, viewmats, Ks, W0, H0 = garden_subset(ref_root, 300, 29)
+    W, H, ts = 80, 56, 16
+    C = 2
+    viewmats, Ks = viewmats[:C].contiguous(), Ks[:C].clone()
+    Ks[:, 0, :] *= W / W0
+    Ks[:, 1, :] *= H / H0
+    g = torch.Generator().manual_seed(31)
+    N = means.shape[0]
+    scales = torch.rand((N, 3), generator=g) * 0.2 + 0.05
+    opacities = torch.rand((N,), generator=g)
+    opacities[::3] = 0.995
+    covars, _ = tm._quat_scale_to_covar_preci(quats, scales, compute_preci=False, triu=False)
+    radii, means2d, depths, conics, _ = ti._fully_fused_projection(means, covars, viewmats, Ks, W, H)
+    tw, th = math.ceil(W / ts), math.ceil(H / ts)
+    _, keys, fids = ti._isect_tiles(means2d, radii, depths, ts, tw, th, sort=False)
+    order = np.argsort(keys.numpy(), kind="stable")  # stable, like the CUDA radix sort
+    keys, fids = keys[torch.from_numpy(order)], fids[torch.from_numpy(order)]
+    offsets = ti._isect_offset_encode(keys, C, tw, th)
+    opacities = torch.broadcast_to(opacities[None], (C, N)).contiguous()
+    colors = torch.rand((C, N, 3), generator=g)
+    backgrounds = torch.rand((C, 3), generator=g)
+    v_colors_img = torch.randn((C, H, W, 3), generator=g)
+    v_alphas_img = torch.randn((C, H, W, 1), generator=g)
+    out = {"width": W, "height": H, "tile_size": ts, "means2d": means2d.numpy(), "conics": conics.numpy(),
+           "colors": colors.numpy(), "opacities": opacities.numpy(), "backgrounds": backgrounds.numpy(),
+           "isect_offsets": offsets.numpy(), "flatten_ids": fids.numpy(),
+           "v_render_colors": v_colors_img.numpy(), "v_render_alphas": v_alphas_img.numpy()}
+    out["soft_opacities"] = (opacities * 0.3).numpy()
+    for tag, per_iter in (("one", 100), ("iter", 1), ("soft", 100)):
+        op_case = opacities * 0.3 if tag == "soft" else opacities
+        leaves = [t.clone().requires_grad_(True) for t in (means2d, conics, colors, op_case, backgrounds)]
+        m2, con, col, op, bg = leaves
+        rc, ra = ti._rasterize_to_pixels(m2, con, col, op, W, H, ts, offsets, fids, backgrounds=bg,
+                                         batch_per_iter=per_iter)
+        grads = torch.autograd.grad((rc * v_colors_img).sum() + (ra * v_alphas_img).sum(), leaves)
+        out.update({f"{tag}_render_colors": rc.detach().numpy(), f"{tag}_render_alphas": ra.detach().numpy()})
+        for name, gr in zip(("means2d", "conics", "colors", "opacities", "backgrounds"), grads):
+            out[f"{tag}_v_{name}"] = gr.numpy()
+    torch.set_num_threads(threads)
+    np.savez_compressed(os.path.join(HERE, "raster_garden.npz"), **out)
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GSPLAT_REFERENCE", "")
     if not ref_root or not os.path.isdir(ref_root):
-        raise SystemExit("usage: make_golden.py <reference checkout>")
+        raise SystemExit("usage: make_golden.py <reference checkout> [fixture ...]")
     ti, tm = import_reference(ref_root)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    make_covar(tm)
-    make_covar_grad(tm)
-    make_proj(ti, tm, ref_root)
-    make_sh(ti)
-    make_projection(ti, tm, ref_root)
-    make_isect(ti)
+    makers = {
+        "covar": lambda: make_covar(tm),
+        "covar_grad": lambda: make_covar_grad(tm),
+        "proj": lambda: make_proj(ti, tm, ref_root),
+        "sh": lambda: make_sh(ti),
+        "projection": lambda: make_projection(ti, tm, ref_root),
+        "isect": lambda: make_isect(ti),
+        "raster": lambda: make_raster(ti, tm, ref_root),
+    }
+    for name in sys.argv[2:] or list(makers):
+        makers[name]()
     print("golden vectors written to", HERE)
 
 

@@ -1,5 +1,6 @@
-"""Cross-check of the CPU oracle's rasterizer (the one stage with no executable
-reference on the CPU): an independent float64 PyTorch restatement of the
+"""Cross-check of the CPU oracle's rasterizer in float64 (the reference's own
+PyTorch rasterizer pins it in float32, tests/test_oracle_raster_golden.py): an
+independent float64 PyTorch restatement of the
 compositing rules of RasterizeToPixels3DGSFwd.cu (front to back per tile, alpha
 = min(0.99, o exp(-sigma)), skip sigma < 0 or alpha < 1/255, stop before the
 splat that takes the transmittance to 1e-4, background by the final
