@@ -165,6 +165,71 @@ def make_proj(ti, tm, ref_root):
     np.savez_compressed(os.path.join(HERE, "proj_garden.npz"), **out)
 
 
+def make_projection_variants(ti, tm, ref_root):
+    """tests/test_basic.py:214-324 (test_projection) beyond the default camera:
+    "ortho": the orthographic model with compensations (quats / scales input);
+    "planes": pinhole with near / far planes that cull part of the scene, a batch
+    of two scenes and camera sets ([2, N, 3], [2, C, 4, 4]), and the covariance
+    input instead of quats / scales (gradients with respect to the full 3x3
+    covariances)."""
+    means, quats, scales, opacities, viewmats, Ks, W, H = garden_subset(ref_root, 300, 37)
+    g = torch.Generator().manual_seed(41)
+    out = {"means": means.numpy(), "quats": quats.numpy(), "scales": scales.numpy(),
+           "viewmats": viewmats.numpy(), "Ks": Ks.numpy(), "width": W, "height": H}
+
+    def upstream(radii, means2d, depths, conics, comps):
+        valid = (radii > 0).all(dim=-1)
+        vm2 = torch.randn(means2d.shape, generator=g) * valid[..., None]
+        vd = torch.randn(depths.shape, generator=g) * valid
+        vcn = torch.randn(conics.shape, generator=g) * valid[..., None]
+        vcp = None if comps is None else torch.randn(comps.shape, generator=g) * valid
+        loss = (means2d * vm2).sum() + (depths * vd).sum() + (conics * vcn).sum()
+        if comps is not None:
+            loss = loss + (comps * vcp).sum()
+        return loss, vm2, vd, vcn, vcp
+
+    # ortho, compensations
+    m = means.clone().requires_grad_(True)
+    q = quats.clone().requires_grad_(True)
+    s = scales.clone().requires_grad_(True)
+    v = viewmats.clone().requires_grad_(True)
+    cov, _ = tm._quat_scale_to_covar_preci(q, s, compute_preci=False, triu=False)
+    res = ti._fully_fused_projection(m, cov, v, Ks, W, H, eps2d=0.3, calc_compensations=True,
+                                     camera_model="ortho")
+    loss, vm2, vd, vcn, vcp = upstream(*res)
+    gm, gq, gs, gv = torch.autograd.grad(loss, (m, q, s, v))
+    radii, means2d, depths, conics, comps = res
+    out.update({"ortho_radii": radii.numpy(), "ortho_means2d": means2d.detach().numpy(),
+                "ortho_depths": depths.detach().numpy(), "ortho_conics": conics.detach().numpy(),
+                "ortho_comps": comps.detach().numpy(), "ortho_v_means2d": vm2.numpy(),
+                "ortho_v_depths": vd.numpy(), "ortho_v_conics": vcn.numpy(), "ortho_v_comps": vcp.numpy(),
+                "ortho_v_means": gm.numpy(), "ortho_v_quats": gq.numpy(), "ortho_v_scales": gs.numpy(),
+                "ortho_v_viewmats": gv.numpy()})
+
+    # near / far planes, batch of two, covariance input
+    means_b = torch.stack([means, means + torch.randn(means.shape, generator=g) * 0.05])
+    covars_b, _ = tm._quat_scale_to_covar_preci(quats, scales, compute_preci=False, triu=False)
+    covars_b = torch.stack([covars_b, covars_b.flip(0)])
+    viewmats_b = torch.stack([viewmats, viewmats.clone()])
+    viewmats_b[1, :, 0, 3] += 0.1
+    Ks_b = torch.stack([Ks, Ks])
+    near, far = 0.6, 2.0
+    m = means_b.clone().requires_grad_(True)
+    c = covars_b.clone().requires_grad_(True)
+    v = viewmats_b.clone().requires_grad_(True)
+    res = ti._fully_fused_projection(m, c, v, Ks_b, W, H, eps2d=0.3, near_plane=near, far_plane=far)
+    loss, vm2, vd, vcn, _ = upstream(*res)
+    gm, gc, gv = torch.autograd.grad(loss, (m, c, v))
+    radii, means2d, depths, conics, _ = res
+    out.update({"planes_near": near, "planes_far": far, "planes_means": means_b.numpy(),
+                "planes_covars": covars_b.numpy(), "planes_viewmats": viewmats_b.numpy(), "planes_Ks": Ks_b.numpy(),
+                "planes_radii": radii.numpy(), "planes_means2d": means2d.detach().numpy(),
+                "planes_depths": depths.detach().numpy(), "planes_conics": conics.detach().numpy(),
+                "planes_v_means2d": vm2.numpy(), "planes_v_depths": vd.numpy(), "planes_v_conics": vcn.numpy(),
+                "planes_v_means": gm.numpy(), "planes_v_covars": gc.numpy(), "planes_v_viewmats": gv.numpy()})
+    np.savez_compressed(os.path.join(HERE, "projection_variants.npz"), **out)
+
+
 def make_sh(ti):
     out = {}
     g = torch.Generator().manual_seed(42)
@@ -347,6 +412,7 @@ def main():
         "proj": lambda: make_proj(ti, tm, ref_root),
         "sh": lambda: make_sh(ti),
         "projection": lambda: make_projection(ti, tm, ref_root),
+        "projection_variants": lambda: make_projection_variants(ti, tm, ref_root),
         "isect": lambda: make_isect(ti),
         "raster": lambda: make_raster(ti, tm, ref_root),
     }
