@@ -327,7 +327,14 @@ class PeerExchange:
     (mailbox, two receive buffers, gradient buffer), mapped by every rank
     through CUDA IPC. Created on first use and reallocated (collectively: every
     rank makes the same decision from the same gathered sizes) when a step
-    needs more room."""
+    needs more room.
+
+    The gradient buffer has one slot per rank and no handshake of its own: a
+    destination may write the gradients of exchange e into it once it holds
+    the rows of e, because the source sent those rows after it had read the
+    previous gradients. That holds when each backward runs after the forward
+    of its exchange was issued following the previous backward
+    (``claim_backward``); other orders take the collective path."""
 
     _instances = {}
 
@@ -343,6 +350,8 @@ class PeerExchange:
         self.world = dist.get_world_size()
         assert self.world <= 8, "peer exchange: at most 8 GPUs (one node)"
         self.epoch = 0
+        self.generation = 0  # arenas allocated so far (epochs restart with each)
+        self.bwd_horizon = 0  # self.epoch when the last peer-path backward was issued
         self.arena_bytes = 0
         self.ptrs = None
         self.own = None
@@ -361,6 +370,21 @@ class PeerExchange:
         if inst is None:
             inst = cls._instances[key] = cls(device)
         return inst
+
+    def claim_backward(self, epoch: int, generation: int) -> bool:
+        """Whether the gradients of exchange ``epoch`` (made in arena
+        ``generation``) may go through the peer gradient buffer: only if that
+        arena is still the current one and the exchange's forward was issued
+        after the last peer-path backward. Backward passes in reverse or
+        interleaved order (several distributed renders in one loss), a second
+        backward through the same graph, or an arena reallocated since the
+        forward return False: those gradients take the collective path
+        (``_peer_grads_collective``). Every rank runs the same sequence of
+        forwards and backwards, so every rank decides alike."""
+        if generation != self.generation or epoch <= self.bwd_horizon:
+            return False
+        self.bwd_horizon = self.epoch
+        return True
 
     def check(self):
         """Raises if a bounded wait of an exchange ran out (the error word is
@@ -435,6 +459,8 @@ class PeerExchange:
             self.own, self.ptrs, self.arena_bytes = own.value, ptrs, size
             self.layout = (row_words, grad_words)
             self.epoch = 0
+            self.generation += 1
+            self.bwd_horizon = 0
             dist.barrier()
         lay = arena_layout(self.arena_bytes, mb, grad_rows, row_words, grad_words)
         g = self.group
@@ -453,6 +479,35 @@ class PeerExchange:
 
 def _ptr_array(ctypes, tensors):
     return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if t is not None else None for t in tensors])
+
+
+def _peer_grads_collective(route: Tensor, bounds: Tensor, world: int, float_meta: List[Tuple],
+                           grads: List[Optional[Tensor]]) -> List[Tensor]:
+    """The gradient leg of a peer exchange through one all_to_all_single, for
+    the backward orders the peer gradient buffer cannot serve. ``route``
+    (int64 [2 * world + 1]: prefix of the received counts by source, ...) and
+    ``bounds`` (int64 [world + 1]: local rows [bounds[d], bounds[d + 1]) went to
+    rank d) are the forward exchange's; ``grads`` are the gradients of the
+    received float tensors (rows in source order, None -> zeros). Returns the
+    gradients of the local float tensors (``float_meta``: full shape, words per
+    row), rows past the sent ones left unset, like the peer path."""
+    sizes = torch.cat([route[:world + 1].to(torch.int64), bounds.to(torch.int64)]).tolist()
+    prefix, local = sizes[:world + 1], sizes[world + 1:]
+    send = [prefix[s + 1] - prefix[s] for s in range(world)]  # rows received from s go back to s
+    recv = [local[d + 1] - local[d] for d in range(world)]  # rows sent to d come back from d
+    words = [wj for _, wj in float_meta]
+    dev = route.device
+    buf = _pack(list(grads), words, prefix[world], dev)
+    back = torch.empty((sum(recv), buf.shape[1]), dtype=buf.dtype, device=dev)
+    dist.all_to_all_single(back, buf, recv, send)
+    # rows come back in destination order, which is the local row order
+    pieces = _unpack(back, [(torch.float32, shape[1:]) for shape, _ in float_meta], words)
+    res = []
+    for (shape, _), piece in zip(float_meta, pieces):
+        r = torch.empty(shape, dtype=torch.float32, device=dev)
+        r[local[0]:local[0] + piece.shape[0]] = piece
+        res.append(r)
+    return res
 
 
 class _PeerExchangeRows(torch.autograd.Function):
@@ -484,6 +539,7 @@ class _PeerExchangeRows(torch.autograd.Function):
         B.call("gsb_peer_recv_rows", ctypes.byref(g), epoch, cap_out, route.data_ptr(), nnz_recv.data_ptr(),
                n_world.data_ptr(), cams_per_rank, px.cap_recv, len(outs), _ptr_array(ctypes, outs), w, stream)
         ctx.px, ctx.epoch, ctx.route, ctx.nnz, ctx.nnz_recv = px, epoch, route, nnz, nnz_recv
+        ctx.generation, ctx.bounds = px.generation, bounds
         ctx.float_meta = [(t.shape, wj) for t, wj in zip(tensors[:n_float], words[:n_float])]
         ctx.n_inputs = len(tensors)
         ctx.cap_out = cap_out
@@ -497,6 +553,9 @@ class _PeerExchangeRows(torch.autograd.Function):
         nf = len(ctx.float_meta)
         words = [wj for _, wj in ctx.float_meta]
         g_in = [x.contiguous() if x is not None else None for x in grads[:nf]]
+        if not px.claim_backward(ctx.epoch, ctx.generation):
+            res = _peer_grads_collective(ctx.route, ctx.bounds, px.world, ctx.float_meta, g_in)
+            return (None,) * 8 + tuple(res) + (None,) * (ctx.n_inputs - nf)
         dev = ctx.route.device
         g = px.group
         w = (ctypes.c_int * nf)(*words)

@@ -183,3 +183,80 @@ def test_peer_arena_layout():
             # buffer 1 ends before the gradient buffer, which ends inside the arena
             assert mb + lay["recv_stride"] + lay["cap_recv"] * rw * 4 <= lay["grad_offset"]
             assert lay["grad_offset"] + lay["cap_grad"] * gw * 4 <= size
+
+
+def test_peer_backward_order_decisions():
+    """Which backward passes of the peer-memory exchange may use the peer
+    gradient buffer (PeerExchange.claim_backward, host logic): in-order
+    forward/backward pairs always; of reversed or interleaved backward passes
+    (several distributed renders in one loss) only the first; a second backward
+    through the same graph never; exchanges made in an arena reallocated since
+    never. The others go through the collective path."""
+    from gsplat_b200.distributed import PeerExchange
+
+    px = PeerExchange.__new__(PeerExchange)  # host state only, no arena
+    px.epoch, px.generation, px.bwd_horizon = 0, 1, 0
+
+    def fwd():
+        px.epoch += 1
+        return px.epoch, px.generation
+
+    def bwd(ex):
+        return px.claim_backward(*ex)
+
+    for _ in range(3):  # training steps in order
+        assert bwd(fwd())
+    e1, e2 = fwd(), fwd()  # two renders, one loss: autograd runs the later one first
+    assert bwd(e2) and not bwd(e1)
+    e1, e2 = fwd(), fwd()  # interleaved: the second backward may not reuse the buffer
+    assert bwd(e1) and not bwd(e2)
+    e1 = fwd()
+    assert bwd(e1) and not bwd(e1)  # retain_graph=True and a second backward
+    e1 = fwd()
+    fwd()  # a forward-only exchange in between changes nothing
+    assert bwd(e1)
+    e1 = fwd()
+    px.epoch, px.generation, px.bwd_horizon = 0, px.generation + 1, 0  # arena reallocated (ensure)
+    e2 = fwd()
+    assert not bwd(e1) and bwd(e2)
+    assert bwd(fwd())
+
+
+def _peer_grads_collective(rank, world):
+    """The collective gradient leg of the peer exchange returns, for every local
+    row, the gradient its destination computed: the same as the backward of
+    exchange_rows over the same rows. Receive tensors carry spare capacity rows
+    (as the peer path's do) and one gradient is missing (zeros)."""
+    from gsplat_b200.distributed import _peer_grads_collective, _words, exchange_rows
+
+    torch.manual_seed(3 + rank)
+    send = [2, 3] if rank == 0 else [4, 0]  # local rows to rank 0, rank 1
+    n = sum(send)
+    cap_in = n + 2  # spare rows past the sent ones, never read back
+    a = torch.randn(cap_in, 3, requires_grad=True)
+    b = torch.randn(cap_in, requires_grad=True)
+    c = torch.randn(cap_in, 2, requires_grad=True)
+    recv_t = torch.empty(world, dtype=torch.int64)
+    dist.all_to_all_single(recv_t, torch.tensor(send, dtype=torch.int64))
+    recv = recv_t.tolist()
+    (fa, fb, fc), _ = exchange_rows(world, [a, b, c], [], send, recv)
+    m = sum(recv)
+    ga, gb = torch.randn(m, 3), torch.randn(m)
+    ((fa * ga).sum() + (fb * gb).sum() + 0 * fc.sum()).backward()
+    # the peer path's view of the same exchange
+    prefix = [0]
+    for r in recv:
+        prefix.append(prefix[-1] + r)
+    route = torch.tensor(prefix + [0] * world, dtype=torch.int64)
+    bounds = torch.tensor([0, send[0], n], dtype=torch.int64)
+    cap_out = m + 5
+    pad = lambda g: torch.cat([g, torch.full((cap_out - m, *g.shape[1:]), float("nan"))])
+    meta = [(t.shape, _words(t)) for t in (a, b, c)]
+    res = _peer_grads_collective(route, bounds, world, meta, [pad(ga), pad(gb), None])
+    assert [r.shape for r in res] == [a.shape, b.shape, c.shape]
+    assert torch.equal(res[0][:n], a.grad[:n]) and torch.equal(res[1][:n], b.grad[:n])
+    assert torch.equal(res[2][:n], torch.zeros(n, 2))
+
+
+def test_peer_grads_collective_world2_gloo():
+    run(_peer_grads_collective)
