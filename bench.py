@@ -203,7 +203,7 @@ def train_step(params, opt, viewmat, K, W, H, G, Ga, distributed=False):
     return loss, meta
 
 
-FLOP_PER_PAIR = {"fwd": 26, "bwd": 68}  # CDIM = 3 (20 + 2 C and 50 + 6 C)
+FLOP_PER_PAIR = {"fwd": 26, "bwd": 68}  # CDIM = 3: 20 + 2 CDIM forward, 50 + 6 CDIM backward
 
 
 def cpu_scene(n, seed):
