@@ -111,6 +111,7 @@ __global__ void exchange_ids_kernel(long long n, const int64_t *__restrict__ n_d
 static int make_arrays(RowArrays &a, int n_arrays, void *const *ptrs, const int *words) {
     if (n_arrays <= 0 || n_arrays > kMaxRowArrays)
         return set_error(kErrInvalidArgument, "row packing: %d arrays (1..%d)", n_arrays, kMaxRowArrays);
+    if (ptrs == nullptr || words == nullptr) return set_error(kErrInvalidArgument, "row packing: no array list");
     a.n = n_arrays;
     a.total = 0;
     for (int j = 0; j < n_arrays; ++j) {
@@ -485,6 +486,7 @@ extern "C" int gsb_peer_alloc(size_t bytes, void **ptr, void *ipc_handle) {
 }
 
 extern "C" int gsb_peer_open(const void *ipc_handle, void **ptr) {
+    if (ipc_handle == nullptr || ptr == nullptr) return set_error(kErrInvalidArgument, "peer open");
     cudaIpcMemHandle_t h;
     memcpy(&h, ipc_handle, sizeof(h));
     const cudaError_t ce = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
@@ -505,6 +507,7 @@ extern "C" int gsb_peer_free(void *ptr) {
 }
 
 extern "C" int gsb_peer_error_alloc(int **host_ptr, int **device_ptr) {
+    if (host_ptr == nullptr || device_ptr == nullptr) return set_error(kErrInvalidArgument, "peer error word");
     void *h = nullptr;
     cudaError_t ce = cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped);
     if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaHostAlloc: %s", cudaGetErrorString(ce));

@@ -67,6 +67,40 @@ def test_invalid_arguments_return_errors_without_launch():
     assert rc == -1 and b"negative" in lib.gsb_last_error()
 
 
+def test_peer_exchange_arguments_checked_before_any_cuda_call():
+    """The peer-memory exchange entry points reject a missing or inconsistent
+    group, missing array lists and exchange number 0 before touching the
+    device."""
+    import ctypes
+
+    from gsplat_b200.cuda import _backend
+
+    lib = _backend.lib()
+    assert lib.gsb_peer_mailbox_bytes() >= 4096
+    assert lib.gsb_peer_open(None, None) == -1 and b"peer open" in lib.gsb_last_error()
+    assert lib.gsb_peer_error_alloc(None, None) == -1 and b"error word" in lib.gsb_last_error()
+    assert lib.gsb_peer_alloc(0, None, None) == -1
+    w = (ctypes.c_int * 1)(2)
+    srcs = (ctypes.c_void_p * 1)(None)
+    rc = lib.gsb_peer_send_rows(None, 1, 0, None, None, None, 1, 0, 1, srcs, w, None)
+    assert rc == -1 and b"rank / world" in lib.gsb_last_error()
+    g = _backend.GsbPeerGroup()
+    g.rank, g.world = 0, 2  # arenas not mapped
+    rc = lib.gsb_peer_recv_rows(ctypes.byref(g), 1, 0, None, None, None, 1, 0, 1, srcs, w, None)
+    assert rc == -1 and b"not mapped" in lib.gsb_last_error()
+    g.world = 1
+    g.arena[0] = 4096  # never dereferenced: the checks below fail first
+    rc = lib.gsb_peer_send_grads(ctypes.byref(g), 1, 0, None, None, 0, 1, srcs, w, None)
+    assert rc == -1 and b"error word" in lib.gsb_last_error()
+    g.error = 8192
+    rc = lib.gsb_peer_recv_grads(ctypes.byref(g), 1, 0, None, 1, None, None, None)
+    assert rc == -1 and b"no array list" in lib.gsb_last_error()
+    rc = lib.gsb_peer_recv_grads(ctypes.byref(g), 0, 0, None, 1, srcs, w, None)
+    assert rc == -1 and b"peer recv grads" in lib.gsb_last_error()
+    rc = lib.gsb_pack_rows(4, None, 1, None, None, None, None)
+    assert rc == -1 and b"no array list" in lib.gsb_last_error()
+
+
 def test_python_ops_raise_on_cpu_tensors():
     import torch
 
