@@ -138,6 +138,7 @@ using namespace gsb;
 extern "C" int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bool *valid,
                               float b1, float b2, cudaStream_t stream) {
     if (n_groups < 0) return set_error(kErrInvalidArgument, "negative group count");
+    if (n_groups > 0 && groups == nullptr) return set_error(kErrInvalidArgument, "adam: no group list");
     int done = 0;
     while (done < n_groups) {
         AdamBatch B = {};

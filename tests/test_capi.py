@@ -65,6 +65,9 @@ def test_invalid_arguments_return_errors_without_launch():
     assert rc == -2 and b"camera_model" in lib.gsb_last_error()
     rc = lib.gsb_quat_scale_to_covar_preci_fwd(-1, None, None, 0, None, None, None)
     assert rc == -1 and b"negative" in lib.gsb_last_error()
+    rc = lib.gsb_adam_multi(2, None, None, 0.9, 0.999, None)
+    assert rc == -1 and b"no group list" in lib.gsb_last_error()
+    assert lib.gsb_adam_multi(0, None, None, 0.9, 0.999, None) == 0  # nothing to do, nothing launched
 
 
 def test_peer_exchange_arguments_checked_before_any_cuda_call():
