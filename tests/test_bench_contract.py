@@ -1,0 +1,42 @@
+"""bench.py's reference arm on the host cores (the one bench leg that needs no
+GPU): one JSON line with the contract's keys, the same metric / unit / direction
+as the GPU arm, rank 0 alone printing under torchrun. A small scene keeps it to
+seconds."""
+
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench(*args, env=None):
+    e = dict(os.environ)
+    e.update(env or {})
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], cwd=ROOT, env=e,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return [line for line in r.stdout.splitlines() if line.startswith("{")]
+
+
+def test_reference_arm_json_line():
+    import bench
+
+    lines = _bench("--impl", "reference", "--n", "2000", "--steps", "1", "--warmup", "1")
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert d["metric"] == bench.METRIC and d["unit"] == "MPix/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    assert d["steps"] == 1 and d["warmup"] == 1 and d["n_gpus"] == 1 and d["scaling"] == "weak"
+    assert d["vs_baseline"] is None and d["dtype"] == "fp32" and "synthetic" in d["data"]
+    assert d["config"]["workload"].startswith("config1") and d["config"]["gaussians_per_rank"] == 2000
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and "2000" in cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "MPix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_prints_on_rank_0_only():
+    assert _bench("--impl", "reference", "--n", "2000", "--steps", "1", "--warmup", "1",
+                  env={"RANK": "1", "WORLD_SIZE": "2"}) == []
