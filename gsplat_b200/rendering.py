@@ -109,6 +109,34 @@ def normalize_features_layout(features, batch_dims, C, trailing_dims, batch_ids=
     return torch.broadcast_to(features.unsqueeze(len(batch_dims)), batch_dims + (C, N, *trailing_dims))
 
 
+def _trim_local_meta(meta: Dict, n: int) -> None:
+    """Distributed packed mode: the local projection outputs in ``meta`` have
+    the projection's capacity rows, of which the first ``n`` (the local splat
+    count, known on the host once the sizes are read) are set; keep those, like
+    the reference's exact-size outputs. ``means2d`` enters the exchange at full
+    capacity, so ``meta["means2d"]`` becomes a leaf view of its first ``n`` rows
+    whose ``.grad`` is filled from the capacity tensor's gradient when the
+    backward reaches it: what a densification strategy reads after
+    ``retain_grad()`` and ``backward()``."""
+    for k in ("batch_ids", "camera_ids", "gaussian_ids", "radii", "depths", "conics", "opacities"):
+        t = meta.get(k)
+        if t is not None:
+            meta[k] = t[:n]
+    m = meta.get("means2d")
+    if m is None:
+        return
+    view = m.detach()[:n]
+    if m.requires_grad:
+        view.requires_grad_(True)
+
+        def tap(grad):
+            piece = grad[:n].clone()
+            view.grad = piece if view.grad is None else view.grad + piece
+
+        m.register_hook(tap)
+    meta["means2d"] = view
+
+
 def _reshape_view(C: int, world_view: Tensor, N_world) -> Tensor:
     view_list = list(
         map(
@@ -437,6 +465,9 @@ def rasterization(
         # buffers; the received count stays on the device and reaches the host
         # with the intersection sizes
         n_world_event.synchronize()
+        # the local splat count, for meta: read with the intersection sizes
+        local_nnz = torch.empty(1, dtype=torch.int64, pin_memory=True)
+        local_nnz.copy_(nnz_device.reshape(1), non_blocking=True)
         peer_out = peer_exchange_rows(floats, ints, nnz_device, bounds, N_world_dev, n_world_pinned.tolist(),
                                       C_world[0])
         if peer_out is None:  # peer memory unavailable on some rank: the all-to-all below
@@ -458,6 +489,7 @@ def rasterization(
         sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
         send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
         batch_ids, camera_ids, gaussian_ids = batch_ids[:nnz], camera_ids[:nnz], gaussian_ids[:nnz]
+        _trim_local_meta(meta, nnz)
         floats, ints = exchange_rows(world_size, floats, ints, send_splits, recv_splits, packed=send_buf)
         means2d, depths, conics, opacities = floats[:4]
         if proj_features is not None:
@@ -529,6 +561,7 @@ def rasterization(
             image_ids=image_ids, gaussian_ids=gaussian_ids, conics=conics, opacities=opacities,
             nnz_device=peer_nnz)
         PeerExchange.get(device).check()
+        _trim_local_meta(meta, int(local_nnz[0]))  # the copy is ordered before the size read
     else:
         # isect_tiles(sort=True, segmented) + isect_offset_encode in one pass
         tiles_per_gauss, isect_ids, flatten_ids, isect_offsets = isect_tiles_with_offsets(

@@ -260,3 +260,37 @@ def _peer_grads_collective(rank, world):
 
 def test_peer_grads_collective_world2_gloo():
     run(_peer_grads_collective)
+
+
+def test_trim_local_meta_exact_rows_and_means2d_grad():
+    """Distributed packed mode keeps the projection's capacity rows on the
+    device until the sizes are read; rasterization() then trims the local
+    entries of meta to the splat count (rendering._trim_local_meta). meta's
+    means2d is exact-size and its .grad, after retain_grad() and backward(), is
+    the gradient of those rows, accumulated over repeated backward passes,
+    like the reference's exact-size means2d."""
+    from gsplat_b200.rendering import _trim_local_meta
+
+    cap, n = 10, 6
+    x = torch.randn(cap, 2, requires_grad=True)
+    means2d = x * 3.0  # the projection output (capacity rows, non-leaf)
+    meta = {"batch_ids": torch.zeros(cap, dtype=torch.int64), "camera_ids": torch.zeros(cap, dtype=torch.int64),
+            "gaussian_ids": torch.arange(cap), "radii": torch.ones(cap, 2, dtype=torch.int32),
+            "means2d": means2d, "depths": torch.rand(cap), "conics": torch.rand(cap, 3),
+            "opacities": torch.rand(cap)}
+    _trim_local_meta(meta, n)
+    for k, t in meta.items():
+        assert t.shape[0] == n, k
+    m = meta["means2d"]
+    m.retain_grad()  # what a strategy does before backward
+    assert torch.equal(m, means2d[:n].detach())
+    w = torch.arange(cap * 2, dtype=torch.float32).reshape(cap, 2)
+    loss = (means2d[:n] * w[:n]).sum()  # the exchange reads only the set rows
+    loss.backward(retain_graph=True)
+    assert torch.equal(m.grad, w[:n])
+    loss.backward()
+    assert torch.equal(m.grad, 2 * w[:n])
+    # without autograd (a forward under no_grad) there is nothing to fill
+    meta = {"means2d": torch.randn(cap, 2)}
+    _trim_local_meta(meta, n)
+    assert meta["means2d"].shape == (n, 2) and not meta["means2d"].requires_grad
