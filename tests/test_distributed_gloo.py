@@ -294,3 +294,36 @@ def test_trim_local_meta_exact_rows_and_means2d_grad():
     meta = {"means2d": torch.randn(cap, 2)}
     _trim_local_meta(meta, n)
     assert meta["means2d"].shape == (n, 2) and not meta["means2d"].requires_grad
+
+
+def _peer_availability(rank, world):
+    from gsplat_b200.distributed import peer_exchange_available
+
+    # peer memory needs CUDA devices and an NCCL group: a gloo group or a CPU
+    # device answers no, and the library then takes the all-to-all path
+    assert not peer_exchange_available(torch.device("cpu"))
+    assert not peer_exchange_available(torch.device("cuda", rank))
+    os.environ["GSB_PEER_EXCHANGE"] = "0"
+    assert not peer_exchange_available(torch.device("cuda", rank))
+
+
+def test_peer_exchange_not_offered_without_nccl_world2_gloo():
+    run(_peer_availability)
+
+
+def test_peer_exchange_error_codes_are_reported():
+    """A bounded wait that ran out leaves a code in the host-mapped error word;
+    PeerExchange.check() raises with the rank and what did not arrive."""
+    import ctypes
+
+    from gsplat_b200.distributed import PeerExchange
+
+    px = PeerExchange.__new__(PeerExchange)
+    px.rank = 1
+    word = ctypes.c_int(0)
+    px.err_host = ctypes.pointer(word)
+    px.check()  # no error recorded
+    for code, text in ((1, "did not consume"), (2, "rows did not arrive"), (3, "gradients did not arrive")):
+        word.value = code
+        with pytest.raises(RuntimeError, match=f"rank 1: .*{text}"):
+            px.check()
