@@ -34,7 +34,6 @@ from .distributed import (
     PeerExchange,
     peer_exchange_available,
     peer_exchange_rows,
-    all_gather_int32,
     all_gather_tensor_list,
     all_to_all_int32,
     all_to_all_tensor_list,

@@ -16,7 +16,6 @@ executable CPU path in the reference; they are restated from the CUDA source.
 """
 
 import ctypes
-import os
 
 import numpy as np
 

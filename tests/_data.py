@@ -7,7 +7,6 @@ N(0.5, 0.2) and higher bands N(0, 0.05); pinhole cameras. The golden fixtures in
 tests/golden/ come from the reference's own test data instead.
 """
 
-import numpy as np
 import torch
 
 

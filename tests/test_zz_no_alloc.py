@@ -7,8 +7,6 @@ is collected last so that a run stopping at the first failure has run everything
 else first; it also passes when run on its own in a fresh process.
 """
 
-import ctypes
-
 import pytest
 import torch
 
