@@ -24,10 +24,6 @@ import torch.distributed.nn.functional as distF
 from torch import Tensor
 
 
-def _comm_device(t_device: torch.device) -> torch.device:
-    return t_device
-
-
 def all_gather_int32(world_size: int, value: Union[int, Tensor],
                      device: Optional[torch.device] = None) -> List:
     """Gathers one int32 from every rank (reference distributed.py:25-66)."""

@@ -327,3 +327,37 @@ def test_peer_exchange_error_codes_are_reported():
         word.value = code
         with pytest.raises(RuntimeError, match=f"rank 1: .*{text}"):
             px.check()
+
+
+def _cli_fn(local_rank, world_rank, world_size, path):
+    import torch.distributed as d
+
+    t = torch.tensor([world_rank + 1])
+    d.all_reduce(t)
+    with open(f"{path}.{world_rank}", "w") as f:
+        f.write(f"{local_rank} {world_rank} {world_size} {int(t)}")
+
+
+def test_cli_launcher_gloo(tmp_path):
+    """distributed.cli (reference distributed.py:287-375): spawned ranks when no
+    launcher environment is set, and the ranks a torchrun-style environment names."""
+    import subprocess
+    import sys
+
+    from gsplat_b200.distributed import cli
+
+    path = str(tmp_path / "spawned")
+    assert cli(_cli_fn, path, backend="gloo") is True
+    assert open(path + ".0").read() == "0 0 1 1"
+
+    path = str(tmp_path / "env")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path.insert(0, %r); from gsplat_b200.distributed import cli; "
+            "from tests.test_distributed_gloo import _cli_fn; cli(_cli_fn, %r, backend='gloo')") % (root, path)
+    port = str(_free_port())
+    procs = [subprocess.Popen([sys.executable, "-c", code], cwd=root,
+                              env=dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="2",
+                                       MASTER_ADDR="127.0.0.1", MASTER_PORT=port))
+             for r in range(2)]
+    assert [p.wait(timeout=120) for p in procs] == [0, 0]
+    assert open(path + ".0").read() == "0 0 2 3" and open(path + ".1").read() == "1 1 2 3"
