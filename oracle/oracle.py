@@ -11,7 +11,9 @@ PyTorch implementation (``tests/golden/make_golden.py``). The rasterizer forward
 and backward are checked against the reference's PyTorch rasterizer
 (``_rasterize_to_pixels`` / ``accumulate`` with autograd), run with nerfacc's two
 compositing functions restated and with this oracle's index pass standing in
-for its CUDA op. The index pass itself, the AccuTile sweep and Adam have no
+for its CUDA op; and the whole training-step pipeline (projection to rasterizer,
+forward and backward to the Gaussian parameters) against the reference's
+pure-PyTorch ``_rasterization``. The index pass itself, the AccuTile sweep and Adam have no
 executable CPU path in the reference; they are restated from the CUDA source.
 """
 

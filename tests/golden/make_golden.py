@@ -10,10 +10,12 @@ told that no CUDA toolkit exists and gsplat falls back to ``_C = None``. Inputs 
 the reference tests: a seeded subset of the reference fixture assets/test_garden.npz
 with its three real cameras (tests/test_basic.py:85-110, gsplat/_helper.py:48-100),
 the random intersection case of tests/test_basic.py:698-736, the SH case of
-tests/test_basic.py:2903-2939 and the rasterizer case of tests/test_basic.py:1954-2063.
-Outputs are stored as small .npz files which the CPU tests (tests/test_oracle_golden.py,
-tests/test_oracle_raster_golden.py) compare with the oracle and the GPU tests compare
-with the kernels; nothing reads the reference at test time.
+tests/test_basic.py:2903-2939, the rasterizer case of tests/test_basic.py:1954-2063 and
+the end-to-end case of tests/test_rasterization.py (the reference's pure-PyTorch
+``_rasterization`` with autograd). Outputs are stored as small .npz files which the
+CPU tests (tests/test_oracle_golden.py, tests/test_oracle_raster_golden.py,
+tests/test_oracle_rasterization_golden.py) compare with the oracle and the GPU tests
+compare with the kernels; nothing reads the reference at test time.
 
     python tests/golden/make_golden.py /path/to/reference raster   # one fixture
 """
@@ -400,6 +402,81 @@ def make_raster(ti, tm, ref_root):
     np.savez_compressed(os.path.join(HERE, "raster_garden.npz"), **out)
 
 
+def make_rasterization(ti, tm, ref_root):
+    """tests/test_rasterization.py (rasterization() against _rasterization()) on
+    the CPU: the reference's own pure-PyTorch ``gsplat.rendering._rasterization``
+    (projection by _fully_fused_projection, SH colours by _maybe_evaluate_sh,
+    compositing by _rasterize_to_pixels, expected depth) and autograd through it
+    to the Gaussian parameters. The CUDA ops it calls are replaced by the
+    reference's own PyTorch counterparts where they exist (isect_tiles ->
+    _isect_tiles in AABB mode, sorted stably; isect_offset_encode ->
+    _isect_offset_encode; spherical_harmonics -> _spherical_harmonics with the
+    visibility mask applied) and otherwise as in ``make_raster`` (the oracle's
+    index pass, nerfacc restated). One garden camera scaled to 80x56, 400
+    Gaussians with SH degree 3; "classic" RGB and "antialiased" RGB+ED."""
+    import math
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import oracle as O
+    import gsplat.cuda._wrapper as ref_wrapper
+    import gsplat.rendering as ref_rendering
+
+    def indices_from_oracle(range_start, range_end, transmittances, means2d, conics, opacities, image_width,
+                            image_height, tile_size, isect_offsets, flatten_ids):
+        n = lambda t: t.detach().numpy()
+        gids, pids, iids, _ = O.raster_indices(range_start, range_end, n(transmittances), n(means2d), n(conics),
+                                               n(opacities), image_width, image_height, tile_size,
+                                               isect_offsets.numpy(), flatten_ids.numpy())
+        return torch.from_numpy(gids), torch.from_numpy(pids), torch.from_numpy(iids)
+
+    def isect_tiles_torch(means2d, radii, depths, tile_size, tile_width, tile_height, **unused):
+        tpg, keys, fids = ti._isect_tiles(means2d.detach(), radii, depths.detach(), tile_size, tile_width,
+                                          tile_height, sort=False)
+        order = torch.from_numpy(np.argsort(keys.numpy(), kind="stable"))
+        return tpg, keys[order], fids[order]
+
+    def sh_torch(degrees_to_use, dirs, coeffs, masks=None):
+        out = ti._spherical_harmonics(degrees_to_use, dirs, coeffs)
+        return out if masks is None else torch.where(masks[..., None], out, torch.zeros_like(out))
+
+    sys.modules["nerfacc"] = nerfacc_standin()
+    ref_wrapper.rasterize_to_indices_in_range = indices_from_oracle
+    ref_rendering.isect_tiles = isect_tiles_torch
+    ref_rendering.isect_offset_encode = lambda ids, n, tw, th: ti._isect_offset_encode(ids, n, tw, th)
+    ref_rendering.spherical_harmonics = sh_torch
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)  # reproducible accumulation order in the backward
+
+    means, quats, scales, opacities, viewmats, Ks, W0, H0 = garden_subset(ref_root, 400, 43)
+    W, H = 80, 56
+    viewmats, Ks = viewmats[:1].contiguous(), Ks[:1].clone()
+    Ks[:, 0, :] *= W / W0
+    Ks[:, 1, :] *= H / H0
+    N = means.shape[0]
+    g = torch.Generator().manual_seed(47)
+    scales = torch.rand((N, 3), generator=g) * 0.2 + 0.05
+    opacities = torch.rand((N,), generator=g) * 0.9 + 0.05
+    sh = torch.randn((N, 16, 3), generator=g) * 0.05
+    sh[:, 0, :] = torch.randn((N, 3), generator=g) * 0.2 + 0.5
+    G = torch.randn((1, H, W, 4), generator=g)
+    Ga = torch.randn((1, H, W, 1), generator=g)
+    out = {"width": W, "height": H, "means": means.numpy(), "quats": quats.numpy(), "scales": scales.numpy(),
+           "opacities": opacities.numpy(), "sh": sh.numpy(), "viewmats": viewmats.numpy(), "Ks": Ks.numpy(),
+           "G": G.numpy(), "Ga": Ga.numpy()}
+    for tag, mode, rmode in (("classic", "RGB", "classic"), ("aa", "RGB+ED", "antialiased")):
+        leaves = [t.clone().requires_grad_(True) for t in (means, quats, scales, opacities, sh)]
+        rc, ra, _ = ref_rendering._rasterization(*leaves[:4], leaves[4], viewmats, Ks, W, H, sh_degree=3,
+                                                 render_mode=mode, rasterize_mode=rmode)
+        loss = (rc * G[..., :rc.shape[-1]]).sum() + (ra * Ga).sum()
+        grads = torch.autograd.grad(loss, leaves)
+        out.update({f"{tag}_render": rc.detach().numpy(), f"{tag}_alpha": ra.detach().numpy()})
+        for name, gr in zip(("means", "quats", "scales", "opacities", "sh"), grads):
+            out[f"{tag}_v_{name}"] = gr.numpy()
+    torch.set_num_threads(threads)
+    assert math.isfinite(float(out["classic_render"].sum()))
+    np.savez_compressed(os.path.join(HERE, "rasterization_garden.npz"), **out)
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GSPLAT_REFERENCE", "")
     if not ref_root or not os.path.isdir(ref_root):
@@ -415,6 +492,7 @@ def main():
         "projection_variants": lambda: make_projection_variants(ti, tm, ref_root),
         "isect": lambda: make_isect(ti),
         "raster": lambda: make_raster(ti, tm, ref_root),
+        "rasterization": lambda: make_rasterization(ti, tm, ref_root),
     }
     for name in sys.argv[2:] or list(makers):
         makers[name]()
