@@ -30,6 +30,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd+Adam ms/iter at 1M Gaussians 1297x840; MPix/s at 1/2/4/8 GPUs"
 GRAD_BANK = 4
+WORKLOADS = {
+    "config1": "config1: 1M Gaussians, 1297x840 pinhole fx=fy=1150, SH deg 3, packed, fwd+bwd+SelectiveAdam",
+    "config3": ("config3: 3M Gaussians, 8 cameras 1920x1080 fx=fy=1500 on a radius-8 sphere, SH deg 3, "
+                "packed, fwd+bwd+SelectiveAdam"),
+    "config4": ("config4: 6M Gaussians sharded over the ranks, 32 cameras 1600x1200 fx=fy=1200 on a radius-8 "
+                "sphere split over the ranks, SH deg 3, packed, fwd+bwd+SelectiveAdam"),
+}
 LRS = {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacities": 5e-2, "sh": 2.5e-3}
 
 
@@ -40,9 +47,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="gsb", choices=["gsb", "reference"])
     ap.add_argument("--n", type=int, default=None, help="Gaussians per rank (default: the workload's)")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config3"],
-                    help="config1 (the headline, default) or config3 (3M Gaussians, 8 cameras at "
-                         "1920x1080, one GPU)")
+    ap.add_argument("--workload", default="config1", choices=["config1", "config3", "config4"],
+                    help="config1 (the headline, default), config3 (3M Gaussians, 8 cameras at "
+                         "1920x1080, one GPU) or config4 (6M Gaussians sharded over the ranks, 32 "
+                         "cameras at 1600x1200 split over the ranks: total work fixed)")
     ap.add_argument("--dense", action="store_true", help="packed=False (trainer default)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -152,7 +160,9 @@ def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
     side along x (12 units apart) and each rank's camera looks at its own shard,
     so every GPU renders one config-1 view of a scene that grows with the job
     (weak scaling); splats near the frustum edges still cross ranks through the
-    all-to-all. workload="config3": the 3M-Gaussian, 8-camera scene (one GPU)."""
+    all-to-all. workload="config3": the 3M-Gaussian, 8-camera scene (one GPU).
+    workload="config4": this rank's shard and cameras of the 6M-Gaussian,
+    32-camera scene (the job's work stays the same as ranks are added)."""
     import torch
 
     from tests import _data
@@ -160,10 +170,12 @@ def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
     if workload == "config3":
         assert world == 1, "config3 is measured on one GPU"
         d = _data.config3(N=n, seed=seed)
+    elif workload == "config4":
+        d = _data.config4(N=n, rank=rank, world=world)
     else:
         d = _data.config1(N=n, seed=seed)
     shift = 12.0 * (rank - (world - 1) / 2.0)
-    if world > 1:
+    if world > 1 and workload == "config1":
         d["means"][:, 0] += shift
         d["viewmats"] = d["viewmats"].clone()
         d["viewmats"][:, 0, 3] = -shift
@@ -638,15 +650,12 @@ def run_gsb(args):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload == "config4" else "weak",
         "vs_baseline": None,
         "dtype": "fp32",
         "data": "synthetic (seeded config-1 distributions, random-init Gaussians)",
-        "config": {"workload": ("config1: 1M Gaussians, 1297x840 pinhole fx=fy=1150, SH deg 3, "
-                                "packed, fwd+bwd+SelectiveAdam") if args.workload == "config1" else
-                               ("config3: 3M Gaussians, 8 cameras 1920x1080 fx=fy=1500 on a radius-8 "
-                                "sphere, SH deg 3, packed, fwd+bwd+SelectiveAdam"),
-                   "gaussians_per_rank": args.n, "cameras_per_rank": n_cams,
+        "config": {"workload": WORKLOADS[args.workload],
+                   "gaussians_per_rank": int(params["means"].shape[0]), "cameras_per_rank": n_cams,
                    "parallelism": f"gaussian-sharded x{world}" if distributed else "single",
                    "l2": "inputs larger than L2 (params + Adam state ~700 MB)",
                    "visible_splats": nnz, "n_isects": n_isects},
@@ -670,7 +679,8 @@ def run_gsb(args):
 def main():
     args = parse()
     if args.n is None:
-        args.n = 3_000_000 if args.workload == "config3" else 1_000_000
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        args.n = {"config3": 3_000_000, "config4": 6_000_000 // world}.get(args.workload, 1_000_000)
     if args.impl == "reference":
         run_reference(args)
         return

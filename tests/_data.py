@@ -77,6 +77,25 @@ def config3(N=3_000_000, seed=3, C=8):
     return d
 
 
+def config4(N=750_000, seed=4, rank=0, world=1, C=32):
+    """BASELINE config 4, one rank's part: its shard of a 6M-Gaussian scene
+    (means ~ N(0, 2^2)^3, the other distributions as config 0; N Gaussians drawn
+    with the rank's own seed, i.i.d. like a strided slice [rank::world] of the
+    whole scene) and its C / world of the C cameras at 1600x1200 (fx=fy=1200):
+    uniformly random directions on a radius-8 sphere looking at the origin, the
+    same C poses on every rank."""
+    assert C % world == 0, "the cameras split evenly over the ranks"
+    g = torch.Generator().manual_seed(2000 + seed)
+    dirs = torch.nn.functional.normalize(torch.randn((C, 3), generator=g), dim=-1)
+    per = C // world
+    viewmats = torch.stack([look_at(8.0 * d) for d in dirs[rank * per:(rank + 1) * per]])
+    shard_seed = 1000 * seed + rank
+    d = scene(N, seed=shard_seed, width=1600, height=1200, fx=1200.0, cx=800.0, cy=600.0, C=per,
+              viewmats=viewmats)
+    d["means"] = torch.randn((N, 3), generator=torch.Generator().manual_seed(shard_seed)) * 2.0
+    return d
+
+
 def to(d, device):
     return {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
 

@@ -40,3 +40,27 @@ def test_reference_arm_json_line():
 def test_reference_arm_prints_on_rank_0_only():
     assert _bench("--impl", "reference", "--n", "2000", "--steps", "1", "--warmup", "1",
                   env={"RANK": "1", "WORLD_SIZE": "2"}) == []
+
+
+def test_config4_shards_and_cameras():
+    """config 4 (the reference's multi-GPU configuration): every rank holds its own
+    shard of the Gaussians and C / world of the 32 cameras; over the ranks the
+    cameras are the one-rank set, in order, so the job's work is the same at any
+    rank count (strong scaling)."""
+    import torch
+
+    import bench
+
+    dev = torch.device("cpu")
+    _, one = bench.make_params(800, 1, dev, 0, 1, "config4")
+    assert one["viewmats"].shape == (32, 4, 4) and (one["width"], one["height"]) == (1600, 1200)
+    for world in (2, 4, 8):
+        parts = [bench.make_params(800 // world, 1 + r, dev, r, world, "config4") for r in range(world)]
+        assert all(p["means"].shape[0] == 800 // world for p, _ in parts)
+        assert torch.equal(torch.cat([d["viewmats"] for _, d in parts]), one["viewmats"])
+        assert not torch.equal(parts[0][0]["means"], parts[1][0]["means"])
+
+
+def test_reference_arm_samples_config1_only():
+    lines = _bench("--impl", "reference", "--workload", "config4", "--steps", "1", "--warmup", "1")
+    assert len(lines) == 1 and "unavailable" in json.loads(lines[0])
