@@ -65,8 +65,10 @@ struct RasterParams {
     float *alphas;  // [I, H, W]
     int32_t *last_ids;
     int32_t *pair_counts; // optional [I, H, W]: splats that contributed to each pixel
+    float *final_Ts;      // optional [I, H, W]: final transmittance of each pixel
     bool write_alpha;
     // backward inputs / outputs
+    const float *T_final; // optional [I, H, W] final transmittances (else 1 - alphas)
     const float *v_renders, *v_alphas;
     float *v_means2d, *v_conics, *v_colors, *v_opacities, *v_means2d_abs;
     bool first_chunk;
@@ -321,6 +323,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
                 p.alphas[pix] = 0.f;
                 p.last_ids[pix] = 0;
                 if (p.pair_counts) p.pair_counts[pix] = 0;
+                if (p.final_Ts) p.final_Ts[pix] = 1.f;
             }
             continue;
         }
@@ -330,6 +333,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
             p.alphas[pix] = 1.f - T[k];
             p.last_ids[pix] = cur[k];
             if (p.pair_counts) p.pair_counts[pix] = npairs[k];
+            if (p.final_Ts) p.final_Ts[pix] = T[k];
         }
     }
 }
@@ -488,7 +492,10 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
         px[k] = (float)j + 0.5f;
         py[k] = (float)i + 0.5f;
         const size_t pix = img_pix + (inside ? i * p.W + j : 0);
-        const float Tf = inside ? 1.f - p.alphas[pix] : 0.f;
+        // The final transmittance saved by the forward when given; 1 - alpha
+        // otherwise (the reference's form, which loses the low bits of T when
+        // the pixel is nearly opaque: alpha = 0.9999 carries T to ~3e-4).
+        const float Tf = inside ? (p.T_final ? p.T_final[pix] : 1.f - p.alphas[pix]) : 0.f;
         T[k] = Tf;
         bin_final[k] = inside ? p.last_ids[pix] : -1;
         float dotbg = 0.f;
@@ -716,7 +723,7 @@ static int rasterize_fwd(int I, int channels, const float *means2d, const float 
                          const bool *masks, int width, int height, int tile_size, int tile_width,
                          int tile_height, const int32_t *tile_offsets, const int32_t *flatten_ids,
                          long long n_isects, float *renders, float *alphas, int32_t *last_ids,
-                         int32_t *pair_counts, cudaStream_t stream) {
+                         float *final_Ts, int32_t *pair_counts, cudaStream_t stream) {
     if (int e = check_raster_args(I, width, height, tile_size, tile_width, tile_height, channels)) return e;
     if (I == 0 || width == 0 || height == 0) return kOk;
     RasterParams p = {};
@@ -740,6 +747,7 @@ static int rasterize_fwd(int I, int channels, const float *means2d, const float 
     p.alphas = alphas;
     p.last_ids = last_ids;
     p.pair_counts = pair_counts;
+    p.final_Ts = final_Ts;
     int coff = 0;
     while (coff < channels) {
         const int n = next_chunk(channels - coff);
@@ -760,7 +768,7 @@ extern "C" int gsb_rasterize_fwd(int I, int channels, const float *means2d, cons
                                  int32_t *last_ids, cudaStream_t stream) {
     return rasterize_fwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
                          height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
-                         n_isects, renders, alphas, last_ids, nullptr, stream);
+                         n_isects, renders, alphas, last_ids, nullptr, nullptr, stream);
 }
 
 extern "C" int gsb_rasterize_fwd_counted(int I, int channels, const float *means2d,
@@ -774,19 +782,30 @@ extern "C" int gsb_rasterize_fwd_counted(int I, int channels, const float *means
                                          cudaStream_t stream) {
     return rasterize_fwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
                          height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
-                         n_isects, renders, alphas, last_ids, pair_counts, stream);
+                         n_isects, renders, alphas, last_ids, nullptr, pair_counts, stream);
 }
 
-extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, const float *conics,
-                                 const float *colors, const float *opacities,
-                                 const float *backgrounds, const bool *masks, int width, int height,
-                                 int tile_size, int tile_width, int tile_height,
-                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
-                                 long long n_isects, const float *render_alphas,
-                                 const int32_t *last_ids, const float *v_render_colors,
-                                 const float *v_render_alphas, float *v_means2d_abs,
-                                 float *v_means2d, float *v_conics, float *v_colors,
-                                 float *v_opacities, cudaStream_t stream) {
+extern "C" int gsb_rasterize_fwd_ex(int I, int channels, const float *means2d, const float *conics,
+                                    const float *colors, const float *opacities,
+                                    const float *backgrounds, const bool *masks, int width,
+                                    int height, int tile_size, int tile_width, int tile_height,
+                                    const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                    long long n_isects, float *renders, float *alphas,
+                                    int32_t *last_ids, float *final_Ts, int32_t *pair_counts,
+                                    cudaStream_t stream) {
+    return rasterize_fwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
+                         height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
+                         n_isects, renders, alphas, last_ids, final_Ts, pair_counts, stream);
+}
+
+static int rasterize_bwd(int I, int channels, const float *means2d, const float *conics,
+                         const float *colors, const float *opacities, const float *backgrounds,
+                         const bool *masks, int width, int height, int tile_size, int tile_width,
+                         int tile_height, const int32_t *tile_offsets, const int32_t *flatten_ids,
+                         long long n_isects, const float *render_alphas, const float *final_Ts,
+                         const int32_t *last_ids, const float *v_render_colors,
+                         const float *v_render_alphas, float *v_means2d_abs, float *v_means2d,
+                         float *v_conics, float *v_colors, float *v_opacities, cudaStream_t stream) {
     if (int e = check_raster_args(I, width, height, tile_size, tile_width, tile_height, channels)) return e;
     if (I == 0 || width == 0 || height == 0 || n_isects <= 0) return kOk;
     RasterParams p = {};
@@ -807,6 +826,7 @@ extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, cons
     p.flatten_ids = flatten_ids;
     p.cstride = channels;
     p.alphas = const_cast<float *>(render_alphas);
+    p.T_final = final_Ts;
     p.last_ids = const_cast<int32_t *>(last_ids);
     p.v_renders = v_render_colors;
     p.v_alphas = v_render_alphas;
@@ -824,4 +844,38 @@ extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, cons
         coff += n;
     }
     return kOk;
+}
+
+extern "C" int gsb_rasterize_bwd(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, const float *render_alphas,
+                                 const int32_t *last_ids, const float *v_render_colors,
+                                 const float *v_render_alphas, float *v_means2d_abs,
+                                 float *v_means2d, float *v_conics, float *v_colors,
+                                 float *v_opacities, cudaStream_t stream) {
+    return rasterize_bwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
+                         height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
+                         n_isects, render_alphas, nullptr, last_ids, v_render_colors,
+                         v_render_alphas, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities,
+                         stream);
+}
+
+extern "C" int gsb_rasterize_bwd_ex(int I, int channels, const float *means2d, const float *conics,
+                                    const float *colors, const float *opacities,
+                                    const float *backgrounds, const bool *masks, int width,
+                                    int height, int tile_size, int tile_width, int tile_height,
+                                    const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                    long long n_isects, const float *render_alphas,
+                                    const float *final_Ts, const int32_t *last_ids,
+                                    const float *v_render_colors, const float *v_render_alphas,
+                                    float *v_means2d_abs, float *v_means2d, float *v_conics,
+                                    float *v_colors, float *v_opacities, cudaStream_t stream) {
+    return rasterize_bwd(I, channels, means2d, conics, colors, opacities, backgrounds, masks, width,
+                         height, tile_size, tile_width, tile_height, tile_offsets, flatten_ids,
+                         n_isects, render_alphas, final_Ts, last_ids, v_render_colors,
+                         v_render_alphas, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities,
+                         stream);
 }

@@ -134,6 +134,15 @@ SIGNATURES = {
         I32,
         [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P, P],
     ),
+    "gsb_rasterize_fwd_ex": (
+        I32,
+        [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P, P, P],
+    ),
+    "gsb_rasterize_bwd_ex": (
+        I32,
+        [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P, P, P, P, P,
+         P, P, P],
+    ),
     "gsb_fp32_fma_probe": (I32, [P, I32, I32, I32, P]),
     "gsb_rasterize_bwd": (
         I32,

@@ -903,13 +903,16 @@ class _RasterizeToPixels(torch.autograd.Function):
         renders = torch.empty(image_dims + (height, width, channels), dtype=torch.float32, device=dev)
         alphas = torch.empty(image_dims + (height, width, 1), dtype=torch.float32, device=dev)
         last_ids = torch.empty(image_dims + (height, width), dtype=torch.int32, device=dev)
+        # the forward's final transmittances, kept for the backward (1 - alphas
+        # loses the low bits of T in nearly opaque pixels)
+        final_Ts = torch.empty(image_dims + (height, width), dtype=torch.float32, device=dev)
         with device_guard(dev):
-            call("gsb_rasterize_fwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
+            call("gsb_rasterize_fwd_ex", I, channels, ptr(means2d), ptr(conics), ptr(colors),
                  ptr(opacities), ptr(backgrounds), ptr(masks), width, height, tile_size, tw, th,
                  ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(), ptr(renders),
-                 ptr(alphas), ptr(last_ids), stream_of(means2d))
+                 ptr(alphas), ptr(last_ids), ptr(final_Ts), None, stream_of(means2d))
         ctx.save_for_backward(means2d, conics, colors, opacities, backgrounds, masks,
-                              isect_offsets, flatten_ids, alphas, last_ids)
+                              isect_offsets, flatten_ids, alphas, last_ids, final_Ts)
         ctx.width = width
         ctx.height = height
         ctx.tile_size = tile_size
@@ -919,7 +922,7 @@ class _RasterizeToPixels(torch.autograd.Function):
     @staticmethod
     def backward(ctx, v_render_colors, v_render_alphas):
         (means2d, conics, colors, opacities, backgrounds, masks, isect_offsets, flatten_ids,
-         render_alphas, last_ids) = ctx.saved_tensors
+         render_alphas, last_ids, final_Ts) = ctx.saved_tensors
         image_dims = isect_offsets.shape[:-2]
         I = math.prod(image_dims)
         th, tw = isect_offsets.shape[-2:]
@@ -937,17 +940,18 @@ class _RasterizeToPixels(torch.autograd.Function):
         v_means2d, v_conics, v_colors, v_opacities = views[:4]
         v_means2d_abs = views[4] if ctx.absgrad else None
         with device_guard(means2d.device):
-            call("gsb_rasterize_bwd", I, channels, ptr(means2d), ptr(conics), ptr(colors),
+            call("gsb_rasterize_bwd_ex", I, channels, ptr(means2d), ptr(conics), ptr(colors),
                  ptr(opacities), ptr(backgrounds), ptr(masks), ctx.width, ctx.height,
                  ctx.tile_size, tw, th, ptr(isect_offsets), ptr(flatten_ids), flatten_ids.numel(),
-                 ptr(render_alphas), ptr(last_ids), ptr(v_render_colors), ptr(v_render_alphas),
+                 ptr(render_alphas), ptr(final_Ts), ptr(last_ids), ptr(v_render_colors),
+                 ptr(v_render_alphas),
                  ptr(v_means2d_abs), ptr(v_means2d), ptr(v_conics), ptr(v_colors),
                  ptr(v_opacities), stream_of(means2d))
         if ctx.absgrad:
             means2d.absgrad = v_means2d_abs
         v_backgrounds = None
         if ctx.needs_input_grad[4]:
-            v_backgrounds = (v_render_colors * (1.0 - render_alphas).float()).sum(dim=(-3, -2))
+            v_backgrounds = (v_render_colors * final_Ts[..., None]).sum(dim=(-3, -2))
         return (v_means2d, v_conics, v_colors, v_opacities, v_backgrounds,
                 None, None, None, None, None, None, None)
 

@@ -346,6 +346,38 @@ GSB_API int gsb_rasterize_bwd(int I, int channels, const float *means2d, const f
                       float *v_means2d_abs, float *v_means2d, float *v_conics, float *v_colors,
                       float *v_opacities, cudaStream_t stream);
 
+/* Same as gsb_rasterize_fwd, and optionally writes final_Ts float [I,H,W], the
+ * final transmittance of each pixel as the forward computed it (render_alphas is
+ * 1 - final_Ts rounded once), and pair_counts int32 [I,H,W] (see
+ * gsb_rasterize_fwd_counted). Either may be NULL. The forward half of the pair
+ * behind gsplat::rasterize_to_pixels_3dgs_fwd (Rasterization.cpp:42-119) that
+ * keeps the transmittance for the backward. */
+GSB_API int gsb_rasterize_fwd_ex(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, float *renders, float *alphas,
+                                 int32_t *last_ids, float *final_Ts, int32_t *pair_counts,
+                                 cudaStream_t stream);
+
+/* Same as gsb_rasterize_bwd (gsplat::rasterize_to_pixels_3dgs_bwd,
+ * Rasterization.cpp:121-214) with the final transmittances of the forward
+ * (gsb_rasterize_fwd_ex) as an input: the backward then starts from the
+ * forward's own T instead of 1 - render_alphas, whose float32 rounding leaves
+ * nearly opaque pixels (alpha ~ 0.9999) with a relative error of up to ~3e-4 in
+ * T. final_Ts may be NULL (then 1 - render_alphas, the reference's form). */
+GSB_API int gsb_rasterize_bwd_ex(int I, int channels, const float *means2d, const float *conics,
+                                 const float *colors, const float *opacities,
+                                 const float *backgrounds, const bool *masks, int width, int height,
+                                 int tile_size, int tile_width, int tile_height,
+                                 const int32_t *tile_offsets, const int32_t *flatten_ids,
+                                 long long n_isects, const float *render_alphas,
+                                 const float *final_Ts, const int32_t *last_ids,
+                                 const float *v_render_colors, const float *v_render_alphas,
+                                 float *v_means2d_abs, float *v_means2d, float *v_conics,
+                                 float *v_colors, float *v_opacities, cudaStream_t stream);
+
 /* --- Rasterize to indices -------------------------------------------------
  * Replaces torch op gsplat::rasterize_to_indices_3dgs (gsplat/cuda/ext.cpp:737;
  * gsplat/cuda/csrc/Rasterization.cpp:216-300, kernel RasterizeToIndices3DGS.cu).

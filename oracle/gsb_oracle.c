@@ -216,44 +216,67 @@ static void quat_vjp(const float *q, const double G[3][3], double vq[4]) {
     vq[2] += (vn[2] - d * y) * inv; vq[3] += (vn[3] - d * z) * inv;
 }
 
-/* fisheye: J and dL/dpoint from dL/dmean2d and dL/dJ; Utils.cuh:702-801 */
-static void fisheye_jacobian_d(double fx, double fy, double x, double y, double z, double J[2][3]) {
-    const double eps = 0.0000001;
-    double x2 = x * x + eps, y2 = y * y, xy = x * y, x2y2 = x2 + y2;
-    double len_xy = sqrt(x * x + y * y) + eps;
-    double inv = 1.0 / (x2y2 + z * z);
-    double b = atan2(len_xy, z) / len_xy / x2y2;
-    double a = z * inv / x2y2;
-    J[0][0] = fx * (x2 * a + y2 * b); J[0][1] = fx * xy * (a - b); J[0][2] = -fx * x * inv;
-    J[1][0] = fy * xy * (a - b); J[1][1] = fy * (y2 * a + x2 * b); J[1][2] = -fy * y * inv;
+/* Forward-mode dual numbers: a value and its derivatives with respect to three
+ * inputs (the fisheye Jacobian below and the SH bases). */
+typedef struct {
+    double v, d[3];
+} dual3;
+
+static dual3 dc(double v) { dual3 r = {v, {0, 0, 0}}; return r; }
+static dual3 dadd(dual3 a, dual3 b) { dual3 r; r.v = a.v + b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] + b.d[i]; return r; }
+static dual3 dsub(dual3 a, dual3 b) { dual3 r; r.v = a.v - b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] - b.d[i]; return r; }
+static dual3 dmul(dual3 a, dual3 b) { dual3 r; r.v = a.v * b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] * b.v + a.v * b.d[i]; return r; }
+static dual3 dscale(double s, dual3 a) { dual3 r; r.v = s * a.v; for (int i = 0; i < 3; ++i) r.d[i] = s * a.d[i]; return r; }
+
+static dual3 ddiv(dual3 a, dual3 b) {
+    dual3 r; r.v = a.v / b.v;
+    for (int i = 0; i < 3; ++i) r.d[i] = (a.d[i] * b.v - a.v * b.d[i]) / (b.v * b.v);
+    return r;
+}
+static dual3 dsqrt(dual3 a) { dual3 r; r.v = sqrt(a.v); for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] / (2.0 * r.v); return r; }
+static dual3 datan2(dual3 y, dual3 x) {
+    dual3 r; r.v = atan2(y.v, x.v);
+    double n = x.v * x.v + y.v * y.v;
+    for (int i = 0; i < 3; ++i) r.d[i] = (x.v * y.d[i] - y.v * x.d[i]) / n;
+    return r;
 }
 
+/* Fisheye (equidistant) J of Utils.cuh:662-700 as dual numbers over the
+ * camera-space point: J's values and, in .d, dJ/d(x, y, z) by forward-mode
+ * differentiation of the same formula (eps terms kept as the reference has them). */
+static void fisheye_jacobian_dual(double fx, double fy, double x, double y, double z, dual3 J[2][3]) {
+    const double eps = 0.0000001;
+    dual3 X = {x, {1, 0, 0}}, Y = {y, {0, 1, 0}}, Z = {z, {0, 0, 1}};
+    dual3 x2 = dadd(dmul(X, X), dc(eps)), y2 = dmul(Y, Y), xy = dmul(X, Y), x2y2 = dadd(x2, y2);
+    dual3 len_xy = dadd(dsqrt(dadd(dmul(X, X), y2)), dc(eps));
+    dual3 inv = ddiv(dc(1.0), dadd(x2y2, dmul(Z, Z)));
+    dual3 b = ddiv(ddiv(datan2(len_xy, Z), len_xy), x2y2);
+    dual3 a = ddiv(dmul(Z, inv), x2y2);
+    J[0][0] = dscale(fx, dadd(dmul(x2, a), dmul(y2, b)));
+    J[0][1] = dscale(fx, dmul(xy, dsub(a, b)));
+    J[0][2] = dscale(-fx, dmul(X, inv));
+    J[1][0] = dscale(fy, dmul(xy, dsub(a, b)));
+    J[1][1] = dscale(fy, dadd(dmul(y2, a), dmul(x2, b)));
+    J[1][2] = dscale(-fy, dmul(Y, inv));
+}
+
+static void fisheye_jacobian_d(double fx, double fy, double x, double y, double z, double J[2][3]) {
+    dual3 Jd[2][3];
+    fisheye_jacobian_dual(fx, fy, x, y, z, Jd);
+    for (int r = 0; r < 2; ++r)
+        for (int k = 0; k < 3; ++k) J[r][k] = Jd[r][k].v;
+}
+
+/* dL/dpoint = J^T dL/dmean2d + sum_rk dL/dJ_rk dJ_rk/dpoint (Utils.cuh:702-801). */
 static void fisheye_point_vjp_d(double fx, double fy, double x, double y, double z, const double vm2[2],
                                 const double vJ[2][3], double vmc[3]) {
-    const double eps = 0.0000001;
-    double J[2][3];
-    fisheye_jacobian_d(fx, fy, x, y, z, J);
-    vmc[0] += J[0][0] * vm2[0] + J[1][0] * vm2[1];
-    vmc[1] += J[0][1] * vm2[0] + J[1][1] * vm2[1];
-    vmc[2] += J[0][2] * vm2[0] + J[1][2] * vm2[1];
-    double x2 = x * x + eps, y2 = y * y, xy = x * y, x2y2 = x2 + y2;
-    double len_xy = sqrt(x * x + y * y) + eps;
-    double l2 = x2y2 + z * z, inv = 1.0 / l2;
-    double theta = atan2(len_xy, z), l4 = l2 * l2;
-    double E = -l4 * x2y2 * theta + l2 * x2y2 * len_xy * z;
-    double F = 3 * l4 * theta - 3 * l2 * len_xy * z - 2 * x2y2 * len_xy * z;
-    double A = x * (3 * E + x2 * F), B = y * (E + x2 * F), C = x * (E + y2 * F), D = y * (3 * E + y2 * F);
-    double S1 = x2 - y2 - z * z, S2 = y2 - x2 - z * z;
-    double inv1 = inv * inv, inv2 = inv1 / (x2y2 * x2y2 * len_xy);
-    double dx[2][3] = {{fx * A * inv2, fx * B * inv2, fx * S1 * inv1}, {fy * B * inv2, fy * C * inv2, 2 * fy * xy * inv1}};
-    double dy[2][3] = {{dx[0][1], fx * C * inv2, 2 * fx * xy * inv1}, {dx[1][1], fy * D * inv2, fy * S2 * inv1}};
-    double dz[2][3] = {{dx[0][2], dy[0][2], 2 * fx * x * z * inv1}, {dx[1][2], dy[1][2], 2 * fy * y * z * inv1}};
-    for (int r = 0; r < 2; ++r)
-        for (int k = 0; k < 3; ++k) {
-            vmc[0] += dx[r][k] * vJ[r][k];
-            vmc[1] += dy[r][k] * vJ[r][k];
-            vmc[2] += dz[r][k] * vJ[r][k];
-        }
+    dual3 J[2][3];
+    fisheye_jacobian_dual(fx, fy, x, y, z, J);
+    for (int i = 0; i < 3; ++i) {
+        vmc[i] += J[0][i].v * vm2[0] + J[1][i].v * vm2[1];
+        for (int r = 0; r < 2; ++r)
+            for (int k = 0; k < 3; ++k) vmc[i] += vJ[r][k] * J[r][k].d[i];
+    }
 }
 
 /* Dense backward, double precision throughout; one Gaussian per iteration
@@ -480,16 +503,6 @@ void ora_sh_fwd(int deg, long long n, int K, const float *dirs, const float *coe
  * SphericalHarmonicsCUDA.cu:130-388. They are evaluated by forward-mode dual
  * numbers over sh_bases to keep this restatement independent of the kernel's
  * hand-derived gradient formulas. */
-typedef struct {
-    double v, d[3];
-} dual3;
-
-static dual3 dc(double v) { dual3 r = {v, {0, 0, 0}}; return r; }
-static dual3 dadd(dual3 a, dual3 b) { dual3 r; r.v = a.v + b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] + b.d[i]; return r; }
-static dual3 dsub(dual3 a, dual3 b) { dual3 r; r.v = a.v - b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] - b.d[i]; return r; }
-static dual3 dmul(dual3 a, dual3 b) { dual3 r; r.v = a.v * b.v; for (int i = 0; i < 3; ++i) r.d[i] = a.d[i] * b.v + a.v * b.d[i]; return r; }
-static dual3 dscale(double s, dual3 a) { dual3 r; r.v = s * a.v; for (int i = 0; i < 3; ++i) r.d[i] = s * a.d[i]; return r; }
-
 static void sh_bases_dual(int deg, dual3 x, dual3 y, dual3 z, dual3 *Y) {
     Y[0] = dc(0.2820947917738781);
     if (deg < 1) return;
@@ -781,9 +794,10 @@ void ora_raster_fwd(int I, int CH, const float *means2d, const float *conics, co
 void ora_raster_bwd(int I, int CH, const float *means2d, const float *conics, const float *colors,
                     const float *opac, const float *bg, const uint8_t *masks, int W, int H, int ts,
                     int tw, int th, const int32_t *offsets, const int32_t *fids, long long n_isects,
-                    const float *render_alphas, const int32_t *last_ids, const float *v_renders,
-                    const float *v_alphas, long long n_splats, float *v_means2d_abs,
-                    float *v_means2d, float *v_conics, float *v_colors, float *v_opac) {
+                    const float *render_alphas, int t_from_alphas, const int32_t *last_ids,
+                    const float *v_renders, const float *v_alphas, long long n_splats,
+                    float *v_means2d_abs, float *v_means2d, float *v_conics, float *v_colors,
+                    float *v_opac) {
     ora_rp p = {I, CH, W, H, ts, tw, th, means2d, conics, colors, opac, bg, masks, offsets, fids, n_isects};
     /* per-splat gradient accumulators in double: 2 xy, 3 conic, 1 opacity, 2 abs, CH colour */
     const int G = 8 + CH;
@@ -803,8 +817,26 @@ void ora_raster_bwd(int I, int CH, const float *means2d, const float *conics, co
                 for (int px = tx * ts; px < imin((tx + 1) * ts, W); ++px) {
                     size_t pix = ((size_t)img * H + py) * W + px;
                     float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
-                    double Tf = 1.0 - (double)render_alphas[pix], T = Tf;
                     int32_t last = last_ids[pix];
+                    /* Final transmittance: by default recomputed in double over the
+                     * pairs the forward kept (the exact product the PyTorch path's
+                     * autograd differentiates); with t_from_alphas, 1 - alpha as in
+                     * RasterizeToPixels3DGSBwd.cu:130. */
+                    double Tf = 1.0;
+                    if (t_from_alphas) {
+                        Tf = 1.0 - (double)render_alphas[pix];
+                    } else {
+                        for (int32_t k = s; k <= imin(e - 1, last); ++k) {
+                            int32_t g = fids[k];
+                            const float *cn = conics + (size_t)g * 3;
+                            float dx = means2d[(size_t)g * 2] - fx, dy = means2d[(size_t)g * 2 + 1] - fy;
+                            float sigma = 0.5f * (cn[0] * dx * dx + cn[2] * dy * dy) + cn[1] * dx * dy;
+                            float alpha = fminf(ORA_MAX_ALPHA, opac[g] * expf(-sigma));
+                            if (sigma < 0.f || alpha < ORA_ALPHA_THRESHOLD) continue;
+                            Tf *= 1.0 - (double)alpha;
+                        }
+                    }
+                    double T = Tf;
                     const float *vc = v_renders + pix * CH;
                     double va = v_alphas[pix], bgd = 0;
                     double *bb = buf;

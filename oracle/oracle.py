@@ -42,7 +42,7 @@ _SIG = {
     "ora_sort_pairs": [I64, P, P],
     "ora_isect_offsets": [I64, P, I32, I32, I32, P],
     "ora_raster_fwd": [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P],
-    "ora_raster_bwd": [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P,
+    "ora_raster_bwd": [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, I32, P, P, P,
                        I64, P, P, P, P, P],
     "ora_adam": [I64, I64, P, P, P, P, P, F32, F32, F32, F32],
     "ora_covar_preci_fwd": [I64, P, P, I32, P, P],
@@ -212,7 +212,11 @@ def raster_fwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, fla
 
 def raster_bwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, flatten_ids,
                render_alphas, last_ids, v_renders, v_alphas, backgrounds=None, masks=None,
-               absgrad=False):
+               absgrad=False, t_from_alphas=False):
+    """Rasterizer backward in float64 (RasterizeToPixels3DGSBwd.cu:99-299). The
+    final transmittance of each pixel is recomputed in float64 over the pairs up
+    to ``last_ids`` (the exact value the PyTorch path differentiates);
+    ``t_from_alphas`` uses 1 - render_alphas instead (the CUDA reference's form)."""
     means2d, conics, colors, opacities, backgrounds = map(
         _f, (means2d, conics, colors, opacities, backgrounds))
     render_alphas, v_renders, v_alphas = _f(render_alphas), _f(v_renders), _f(v_alphas)
@@ -233,7 +237,8 @@ def raster_bwd(means2d, conics, colors, opacities, W, H, tile_size, offsets, fla
     v_op = np.zeros(opacities.shape, np.float32)
     lib().ora_raster_bwd(I, CH, _p(means2d), _p(conics), _p(colors), _p(opacities),
                          _p(backgrounds), _p(m), W, H, tile_size, tw, th, _p(offsets), _p(fids),
-                         fids.size, _p(render_alphas), _p(last_ids), _p(v_renders), _p(v_alphas),
+                         fids.size, _p(render_alphas), int(bool(t_from_alphas)), _p(last_ids),
+                         _p(v_renders), _p(v_alphas),
                          n_splats, _p(v_abs), _p(v_m2d), _p(v_con), _p(v_col), _p(v_op))
     return v_m2d, v_con, v_col, v_op, v_abs
 
