@@ -477,6 +477,131 @@ def make_rasterization(ti, tm, ref_root):
     np.savez_compressed(os.path.join(HERE, "rasterization_garden.npz"), **out)
 
 
+def indices_torch(range_start, range_end, transmittances, means2d, conics, opacities, image_width,
+                  image_height, tile_size, isect_offsets, flatten_ids):
+    """The index pass behind ``rasterize_to_indices_in_range`` written directly in
+    PyTorch from its CUDA source (RasterizeToIndices3DGS.cu:100-185), independent
+    of the oracle: for every pixel of every tile, walk the tile-list entries of
+    batches [range_start, range_end) front to back starting from the pixel's
+    transmittance; skip a pair when sigma < 0 or alpha = min(0.99, o exp(-sigma))
+    < 1/255; stop (exclusively) at the first kept pair that would take the
+    transmittance to <= 1e-4; emit the kept pairs before it. Decisions are taken
+    in float32 (the CUDA kernel's arithmetic) whatever the dtype of the inputs.
+    Returns gaussian_ids, pixel_ids, image_ids (int64), grouped by pixel."""
+    f32 = lambda t: t.detach().to(torch.float32)
+    image_dims = means2d.shape[:-2]
+    I = int(np.prod(image_dims)) if len(image_dims) else 1
+    N = means2d.shape[-2]
+    th, tw = isect_offsets.shape[-2:]
+    m2 = f32(means2d).reshape(I * N, 2)
+    con = f32(conics).reshape(I * N, 3)
+    op = f32(opacities).reshape(I * N)
+    trans = f32(transmittances).reshape(I, image_height * image_width)
+    offs = isect_offsets.reshape(-1).tolist() + [flatten_ids.numel()]
+    bs = tile_size * tile_size
+    out_g, out_p, out_i = [], [], []
+    ly, lx = torch.meshgrid(torch.arange(tile_size), torch.arange(tile_size), indexing="ij")
+    ly, lx = ly.reshape(-1), lx.reshape(-1)
+    for t in range(I * th * tw):
+        img, tile = divmod(t, th * tw)
+        ty, tx = divmod(tile, tw)
+        lo = offs[t] + bs * range_start
+        hi = min(offs[t + 1], offs[t] + bs * range_end)
+        if hi <= lo:
+            continue
+        py, px = ty * tile_size + ly, tx * tile_size + lx
+        inside = (py < image_height) & (px < image_width)
+        py, px = py[inside], px[inside]
+        pix = py * image_width + px
+        fid = flatten_ids[lo:hi].to(torch.int64)  # flat index into [I * N]
+        dx = m2[fid, 0][None, :] - (px.to(torch.float32) + 0.5)[:, None]
+        dy = m2[fid, 1][None, :] - (py.to(torch.float32) + 0.5)[:, None]
+        c = con[fid]
+        sigma = 0.5 * (c[:, 0][None] * dx * dx + c[:, 2][None] * dy * dy) + c[:, 1][None] * dx * dy
+        alpha = torch.clamp_max(op[fid][None] * torch.exp(-sigma), 0.99)
+        keep = (sigma >= 0) & (alpha >= 1.0 / 255.0)
+        factor = torch.where(keep, 1.0 - alpha, torch.ones_like(alpha))
+        T = trans[img, pix][:, None] * torch.cumprod(factor, dim=1)  # after each entry
+        stop = keep & (T <= 1e-4)
+        # pairs before each pixel's first stopping entry
+        before = torch.cumsum(stop.to(torch.int32), dim=1) == 0
+        emit = keep & before
+        rows, cols = torch.nonzero(emit, as_tuple=True)  # row-major: grouped by pixel, in list order
+        out_g.append(fid[cols] % N)
+        out_p.append(pix[rows])
+        out_i.append(torch.full_like(rows, img))
+    if not out_g:
+        e = torch.zeros(0, dtype=torch.int64)
+        return e, e.clone(), e.clone()
+    g, p_, i_ = torch.cat(out_g), torch.cat(out_p), torch.cat(out_i)
+    order = torch.argsort(i_ * (image_height * image_width) + p_, stable=True)
+    return g[order], p_[order], i_[order]
+
+
+def make_config0(ti, tm, ref_root):
+    """BASELINE config 0 end to end: the reference's own pure-PyTorch
+    ``gsplat.rendering._rasterization`` on the seeded config-0 scene of
+    tests/_data.py (10k Gaussians, one 256x256 pinhole camera, fx=fy=300, SH
+    degree 3, RGB), forward and autograd backward to means, quats, scales,
+    opacities and SH with N(0,1) upstream gradients. Run twice: in float64 (the
+    golden truth) and in float32 (the reference's own float32 error against that
+    truth, stored as per-tensor summaries). The CUDA ops it calls are replaced by
+    the reference's PyTorch counterparts (_isect_tiles sorted stably,
+    _isect_offset_encode, _spherical_harmonics), the index pass by
+    ``indices_torch`` and nerfacc by ``nerfacc_standin``; no oracle code runs."""
+    import math
+
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("gsb_test_data", os.path.join(os.path.dirname(HERE), "_data.py"))
+    _data = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(_data)
+    import gsplat.cuda._wrapper as ref_wrapper
+    import gsplat.rendering as ref_rendering
+
+    def isect_tiles_torch(means2d, radii, depths, tile_size, tile_width, tile_height, **unused):
+        tpg, keys, fids = ti._isect_tiles(means2d.detach().float(), radii, depths.detach().float(), tile_size,
+                                          tile_width, tile_height, sort=False)
+        order = torch.from_numpy(np.argsort(keys.numpy(), kind="stable"))
+        return tpg, keys[order], fids[order]
+
+    def sh_torch(degrees_to_use, dirs, coeffs, masks=None):
+        out = ti._spherical_harmonics(degrees_to_use, dirs, coeffs)
+        return out if masks is None else torch.where(masks[..., None], out, torch.zeros_like(out))
+
+    sys.modules["nerfacc"] = nerfacc_standin()
+    ref_wrapper.rasterize_to_indices_in_range = indices_torch
+    ref_rendering.isect_tiles = isect_tiles_torch
+    ref_rendering.isect_offset_encode = lambda ids, n, tw, th: ti._isect_offset_encode(ids, n, tw, th)
+    ref_rendering.spherical_harmonics = sh_torch
+
+    d = _data.config0()
+    W, H = d["width"], d["height"]
+    g = torch.Generator().manual_seed(1)  # upstream gradients (seed + 1)
+    G = torch.randn((1, H, W, 3), generator=g)
+    Ga = torch.randn((1, H, W, 1), generator=g)
+    names = ("means", "quats", "scales", "opacities", "sh")
+    out = {"width": W, "height": H, "G": G.numpy(), "Ga": Ga.numpy()}
+    for k in names:
+        out[f"input_{k}"] = d[k].numpy()
+    res = {}
+    for dt in (torch.float64, torch.float32):
+        leaves = [d[k].to(dt).clone().requires_grad_(True) for k in names]
+        rc, ra, meta = ref_rendering._rasterization(*leaves, d["viewmats"].to(dt), d["Ks"].to(dt), W, H,
+                                                    sh_degree=3, render_mode="RGB")
+        loss = (rc * G.to(dt)).sum() + (ra * Ga.to(dt)).sum()
+        grads = torch.autograd.grad(loss, leaves)
+        res[dt] = {"render": rc.detach(), "alpha": ra.detach(),
+                   **{f"v_{k}": gr for k, gr in zip(names, grads)}}
+    for k, v in res[torch.float64].items():
+        out[k] = v.to(torch.float32).numpy()  # the float64 truth, rounded once
+        e = (res[torch.float32][k].double() - v).abs()
+        bar = e > 1e-5 + 1e-4 * v.abs()
+        out[f"ref32_{k}"] = np.array([float(e.max()), float(e.max() / v.abs().max()), float(bar.double().mean())])
+    assert math.isfinite(float(out["render"].sum()))
+    np.savez_compressed(os.path.join(HERE, "config0.npz"), **out)
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GSPLAT_REFERENCE", "")
     if not ref_root or not os.path.isdir(ref_root):
@@ -493,6 +618,7 @@ def main():
         "isect": lambda: make_isect(ti),
         "raster": lambda: make_raster(ti, tm, ref_root),
         "rasterization": lambda: make_rasterization(ti, tm, ref_root),
+        "config0": lambda: make_config0(ti, tm, ref_root),
     }
     for name in sys.argv[2:] or list(makers):
         makers[name]()

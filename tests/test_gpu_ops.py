@@ -13,7 +13,7 @@ import torch
 
 from oracle import oracle as O
 from tests import _data
-from tests._compare import as_np, assert_close, assert_equal
+from tests._compare import as_np, assert_close, assert_equal, assert_parity
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
@@ -103,11 +103,17 @@ def test_projection_backward_vs_oracle(calc):
         as_np(d["Ks"]), d["width"], d["height"], 0.3, as_np(radii), as_np(conics),
         as_np(comps) if calc else None, as_np(vm2), as_np(vd), as_np(vc),
         as_np(vcomp) if calc else None)
-    # fp32 kernel vs float64 oracle on identical forward outputs
-    assert_close(gm, em, 1e-4, 1e-4, name="v_means")
-    assert_close(gq, eq, 1e-3, 1e-4, name="v_quats")
-    assert_close(gs, es, 1e-3, 1e-3, name="v_scales")
-    assert_close(gv, ev, 1e-3, 1e-2, name="v_viewmats")
+    # fp32 kernel vs float64 oracle on identical forward outputs: the 1e-4 /
+    # 1e-5 bar, except for the few elements whose float32 evaluation is
+    # ill-conditioned (thin Gaussians: conic = inverse of a nearly singular 2x2
+    # covariance); every element within 1e-5 of the gradient's magnitude
+    # (observed on a B200: at most 2.5e-4 of the v_scales elements outside the
+    # bar, none of the others; largest error 1e-6 of the magnitude)
+    assert_parity(gm, em, "v_means", max_bad_frac=1e-4, max_scaled=5e-6)
+    assert_parity(gq, eq, "v_quats", max_bad_frac=1e-4, max_scaled=5e-6)
+    assert_parity(gs, es, "v_scales", max_bad_frac=5e-4, max_scaled=5e-6)
+    # v_viewmats sums the contributions of every Gaussian of the camera
+    assert_parity(gv, ev, "v_viewmats", max_scaled=5e-6)
 
 
 def test_projection_garden_golden():
@@ -456,12 +462,14 @@ def test_rasterize_vs_oracle(channels, tile_size, packed):
     e = O.raster_bwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]), as_np(r["opac"]),
                      r["W"], r["H"], tile_size, as_np(r["offsets"]), as_np(r["fids"]), ea, elast,
                      as_np(vr), as_np(va), backgrounds=as_np(bg))
-    # Backward: fp32 atomics (order-dependent) vs float64 sums.
-    for got, exp, name, rtol, atol in ((grads[0], e[0], "v_means2d", 1e-3, 1e-4),
-                                       (grads[1], e[1], "v_conics", 1e-3, 1e-4),
-                                       (grads[2], e[2], "v_colors", 1e-4, 1e-5),
-                                       (grads[3], e[3], "v_opacities", 1e-3, 1e-4)):
-        assert_close(got, exp, rtol, atol, max_bad_frac=1e-3, name=name)
+    # Backward: float32 kernel (atomics in any order) vs the oracle's float64
+    # sums, both from the same final transmittance. The 1e-4 / 1e-5 bar except
+    # for sums that cancel (observed on a B200: at most 2.3e-4 of the v_conics
+    # elements, none elsewhere), every element within 5e-6 of the gradient's
+    # magnitude (observed at most 1.4e-6).
+    for got, exp, name in ((grads[0], e[0], "v_means2d"), (grads[1], e[1], "v_conics"),
+                           (grads[2], e[2], "v_colors"), (grads[3], e[3], "v_opacities")):
+        assert_parity(got, exp, name, max_bad_frac=5e-4, max_scaled=5e-6)
 
 
 def test_rasterize_masks_and_absgrad():
@@ -478,8 +486,8 @@ def test_rasterize_masks_and_absgrad():
     e = O.raster_bwd(as_np(r["means2d"]), as_np(r["conics"]), as_np(r["colors"]), as_np(r["opac"]),
                      r["W"], r["H"], 16, as_np(r["offsets"]), as_np(r["fids"]), ea, elast, as_np(vr),
                      np.zeros_like(ea), masks=as_np(masks), absgrad=True)
-    assert_close(means2d.grad, e[0], 1e-3, 1e-4, max_bad_frac=1e-3, name="v_means2d")
-    assert_close(means2d.absgrad, e[4], 1e-3, 1e-4, max_bad_frac=1e-3, name="absgrad")
+    assert_parity(means2d.grad, e[0], "v_means2d", max_bad_frac=1e-4, max_scaled=5e-6)
+    assert_parity(means2d.absgrad, e[4], "absgrad", max_bad_frac=1e-4, max_scaled=5e-6)
 
 
 # ---------------------------------------------------------------------------

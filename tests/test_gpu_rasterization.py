@@ -11,7 +11,7 @@ import torch
 
 from oracle import oracle as O
 from tests import _data
-from tests._compare import as_np, assert_close
+from tests._compare import assert_parity, as_np, assert_close
 from tests._pipeline import oracle_pipeline
 
 pytestmark = pytest.mark.gpu
@@ -130,12 +130,11 @@ def test_rasterization_end_to_end_vs_oracle(packed, mode, aa, camera):
     loss = (rc * torch.from_numpy(G).to(DEV)).sum() + (ra * torch.from_numpy(Ga).to(DEV)).sum()
     grads = torch.autograd.grad(loss, [L[k] for k in ("means", "quats", "scales", "opacities", "sh")])
     for g, k in zip(grads, ("v_means", "v_quats", "v_scales", "v_opacities", "v_sh")):
-        ref = e[k]
-        scale = np.abs(ref).max() + 1e-12
-        # float32 GPU chain vs float64-accumulated oracle chain; atol relative to
-        # the gradient's magnitude, and a few Gaussians may sit on an alpha
-        # threshold decision that one side takes and the other does not
-        assert_close(g, ref, 2e-3, 1e-4 * scale, max_bad_frac=2e-3, name=k)
+        # float32 GPU chain vs the oracle chain (float32 forward, float64
+        # backward): the 1e-4 / 1e-5 bar except for sums that cancel (observed
+        # on a B200: at most 3.3e-4 of the elements), every element within 2e-5
+        # of the gradient's magnitude (observed at most 5.9e-6)
+        assert_parity(g, e[k], k, max_bad_frac=1e-3, max_scaled=2e-5)
 
 
 def test_rasterization_meta_and_absgrad():

@@ -38,15 +38,17 @@ def test_noalloc_scan_matches_caller_scratch_scan_twice():
 
     lib = _backend.lib()
     g = torch.Generator(device=DEV).manual_seed(0)
-    # two calls in a row; the second is smaller, so stale tile sums from the
-    # first call are still in the static scratch when it runs
-    for n in (3_000_001, 40_000):
+    # calls in a row; later ones are smaller, so stale tile sums from earlier
+    # calls are still in the static scratch when they run. Sizes: several
+    # thousand tiles, one value short of a 2048-value tile boundary, one past it.
+    for n in (3_000_001, 40_000, 2 * 2048 - 1, 2048 + 1):
         x = torch.randint(0, 1000, (n,), device=DEV, dtype=torch.int32, generator=g)
         ref = _scan_with_caller_scratch(lib, x)
         got = _scan_noalloc(lib, x)
         torch.cuda.synchronize()
         assert torch.equal(got, ref)  # integer scan: bit-exact
-        assert int(got[-1]) == int(x.long().sum())
+        # and against an independent prefix sum
+        assert torch.equal(got, torch.cumsum(x.long(), 0))
 
 
 def test_noalloc_scan_rejects_sizes_beyond_its_scratch():
