@@ -34,50 +34,61 @@ __device__ inline void fisheye_mean_jacobian(float x, float y, float z, float fx
     J[1][2] = -fy * y * x2y2z2_inv;
 }
 
-// Gradient of the fisheye projection with respect to the camera-space point
-// given dL/dmean2d and dL/dJ (row-major 2x3); Utils.cuh:702-801 (the closed-form
-// derivatives of J of the reference, including its eps terms).
+// Gradient of the fisheye projection with respect to the camera-space point p =
+// (x, y, z) given dL/dmean2d and dL/dJ (row-major 2x3), for the J of
+// fisheye_mean_jacobian (the reference's Utils.cuh:662-700, eps terms included).
+//
+// Derivation. With s = x^2 + eps + y^2, rho = |(x, y)| + eps, theta =
+// atan2(rho, z), q = 1 / (s + z^2), a = z q / s and b = theta / (rho s), J is
+//   J00 = fx ((x^2 + eps) a + y^2 b)   J01 = fx x y (a - b)   J02 = -fx x q
+//   J10 = fy x y (a - b)               J11 = fy (y^2 a + (x^2 + eps) b)
+//   J12 = -fy y q,
+// i.e. polynomial coefficients in x, y times the three scalar functions a, b, q.
+// By the product rule, sum_rk vJ_rk dJ_rk/dp = (derivative of the coefficients
+// with a, b, q held) + G_a grad(a) + G_b grad(b) + G_q grad(q), where G_f is the
+// sum of vJ_rk times the coefficient of f in J_rk. The scalar gradients:
+//   grad(q) = -2 q^2 (x, y, z)
+//   grad(a) = (-2 x a (q + 1/s), -2 y a (q + 1/s), (q / s)(1 - 2 z^2 q))
+//   grad(b) = (x beta, y beta, -t / s),  t = 1 / (rho^2 + z^2),
+//             beta = z t / (r rho s) - b (1 / (r rho) + 2 / s),  r = |(x, y)|
+// (d theta / d rho = z t, d theta / dz = -rho t, d rho / d(x, y) = (x, y) / r).
 __device__ inline void fisheye_point_vjp(float x, float y, float z, float fx, float fy, const float v_m2d[2],
                                          const float vJ[2][3], float vmc[3]) {
     const float eps = 0.0000001f;
-    const float x2 = x * x + eps;
-    const float y2 = y * y;
-    const float xy = x * y;
-    const float x2y2 = x2 + y2;
-    const float len_xy = sqrtf(x * x + y * y) + eps;
-    const float x2y2z2 = x2y2 + z * z;
-    const float x2y2z2_inv = 1.f / x2y2z2;
-    const float b = atan2f(len_xy, z) / len_xy / x2y2;
-    const float a = z * x2y2z2_inv / x2y2;
-    vmc[0] += fx * (x2 * a + y2 * b) * v_m2d[0] + fy * xy * (a - b) * v_m2d[1];
-    vmc[1] += fx * xy * (a - b) * v_m2d[0] + fy * (y2 * a + x2 * b) * v_m2d[1];
-    vmc[2] += -fx * x * x2y2z2_inv * v_m2d[0] - fy * y * x2y2z2_inv * v_m2d[1];
-
-    const float theta = atan2f(len_xy, z);
-    const float l4 = x2y2z2 * x2y2z2;
-    const float E = -l4 * x2y2 * theta + x2y2z2 * x2y2 * len_xy * z;
-    const float F = 3 * l4 * theta - 3 * x2y2z2 * len_xy * z - 2 * x2y2 * len_xy * z;
-    const float A = x * (3 * E + x2 * F);
-    const float B = y * (E + x2 * F);
-    const float C = x * (E + y2 * F);
-    const float D = y * (3 * E + y2 * F);
-    const float S1 = x2 - y2 - z * z;
-    const float S2 = y2 - x2 - z * z;
-    const float inv1 = x2y2z2_inv * x2y2z2_inv;
-    const float inv2 = inv1 / (x2y2 * x2y2 * len_xy);
-    // dJ[r][k]/d(x, y, z)
-    const float dx00 = fx * A * inv2, dx01 = fx * B * inv2, dx02 = fx * S1 * inv1;
-    const float dx10 = fy * B * inv2, dx11 = fy * C * inv2, dx12 = 2.f * fy * xy * inv1;
-    const float dy00 = dx01, dy01 = fx * C * inv2, dy02 = 2.f * fx * xy * inv1;
-    const float dy10 = dx11, dy11 = fy * D * inv2, dy12 = fy * S2 * inv1;
-    const float dz00 = dx02, dz01 = dy02, dz02 = 2.f * fx * x * z * inv1;
-    const float dz10 = dx12, dz11 = dy12, dz12 = 2.f * fy * y * z * inv1;
-    vmc[0] += dx00 * vJ[0][0] + dx01 * vJ[0][1] + dx02 * vJ[0][2] + dx10 * vJ[1][0] + dx11 * vJ[1][1] +
-              dx12 * vJ[1][2];
-    vmc[1] += dy00 * vJ[0][0] + dy01 * vJ[0][1] + dy02 * vJ[0][2] + dy10 * vJ[1][0] + dy11 * vJ[1][1] +
-              dy12 * vJ[1][2];
-    vmc[2] += dz00 * vJ[0][0] + dz01 * vJ[0][1] + dz02 * vJ[0][2] + dz10 * vJ[1][0] + dz11 * vJ[1][1] +
-              dz12 * vJ[1][2];
+    const float xe = x * x + eps, yy = y * y, xy = x * y;
+    const float s = xe + yy;
+    const float inv_s = 1.f / s;
+    const float r = sqrtf(x * x + yy);
+    const float rho = r + eps;
+    const float inv_rho = 1.f / rho;
+    const float inv_r = r > 0.f ? 1.f / r : 0.f; // d rho / d(x, y) = (x, y) / r
+    const float theta = atan2f(rho, z);
+    const float q = 1.f / (s + z * z);
+    const float a = z * q * inv_s;
+    const float b = theta * inv_rho * inv_s;
+    const float d = a - b;
+    // dL/dmean2d through J (J^T v)
+    const float J00 = fx * (xe * a + yy * b), J01 = fx * xy * d, J02 = -fx * x * q;
+    const float J10 = fy * xy * d, J11 = fy * (yy * a + xe * b), J12 = -fy * y * q;
+    vmc[0] += J00 * v_m2d[0] + J10 * v_m2d[1];
+    vmc[1] += J01 * v_m2d[0] + J11 * v_m2d[1];
+    vmc[2] += J02 * v_m2d[0] + J12 * v_m2d[1];
+    // dL/dJ through dJ/dp
+    const float w00 = fx * vJ[0][0], w01 = fx * vJ[0][1], w02 = fx * vJ[0][2];
+    const float w10 = fy * vJ[1][0], w11 = fy * vJ[1][1], w12 = fy * vJ[1][2];
+    const float wxy = w01 + w10;
+    const float Ga = w00 * xe + wxy * xy + w11 * yy;
+    const float Gb = w00 * yy - wxy * xy + w11 * xe;
+    const float Gq = -(w02 * x + w12 * y);
+    const float ex = 2.f * x * (w00 * a + w11 * b) + y * wxy * d - w02 * q;
+    const float ey = 2.f * y * (w00 * b + w11 * a) + x * wxy * d - w12 * q;
+    const float t = 1.f / (rho * rho + z * z);
+    const float ra = -2.f * a * (q + inv_s);
+    const float beta = z * t * inv_r * inv_rho * inv_s - b * (inv_r * inv_rho + 2.f * inv_s);
+    const float qq = -2.f * q * q;
+    vmc[0] += ex + x * (Ga * ra + Gb * beta + Gq * qq);
+    vmc[1] += ey + y * (Ga * ra + Gb * beta + Gq * qq);
+    vmc[2] += Ga * q * inv_s * (1.f - 2.f * z * z * q) - Gb * t * inv_s + Gq * qq * z;
 }
 
 // Symmetric 2x2 J S J^T for a full 2x3 J and a symmetric S.

@@ -136,14 +136,18 @@ def _trim_local_meta(meta: Dict, n: int) -> None:
     meta["means2d"] = view
 
 
-def _reshape_view(C: int, world_view: Tensor, N_world) -> Tensor:
-    view_list = list(
-        map(
-            lambda x: x.split(int(x.shape[0] / C), dim=0),
-            world_view.split([C * N_i for N_i in N_world], dim=0),
-        )
-    )
-    return torch.stack([torch.cat(l, dim=0) for l in zip(*view_list)], dim=0)
+def _camera_major(C: int, rows: Tensor, N_world) -> Tensor:
+    """Rows received from every rank, in rank order, each rank r sending a
+    camera-major block of C x N_r rows, rearranged into [C, sum_r N_r, ...]: camera
+    c holds rank 0's Gaussians, then rank 1's, ... (one gather)."""
+    counts = torch.as_tensor([int(n) for n in N_world], dtype=torch.int64, device=rows.device)
+    first = torch.cumsum(counts, 0) - counts  # first global Gaussian of each rank
+    block = first * C  # first received row of each rank's block
+    owner = torch.repeat_interleave(torch.arange(len(N_world), device=rows.device), counts)
+    local = torch.arange(owner.numel(), device=rows.device) - first[owner]
+    cam = torch.arange(C, device=rows.device)[:, None]
+    src = block[owner][None] + cam * counts[owner][None] + local[None]  # [C, sum_r N_r]
+    return rows[src.reshape(-1)].reshape((C, owner.numel()) + rows.shape[1:])
 
 
 def rasterization(
@@ -528,15 +532,15 @@ def rasterization(
             out_splits = [C * N_i for N_i in N_world]
             (radii,) = all_to_all_tensor_list(world_size, [radii.flatten(0, 1)], splits=splits,
                                               output_splits=out_splits)
-            radii = _reshape_view(C, radii, N_world)
+            radii = _camera_major(C, radii, N_world)
             tensors = [means2d.flatten(0, 1), depths.flatten(0, 1), conics.flatten(0, 1),
                        opacities.flatten(0, 1)]
             if proj_features is not None:
                 tensors.append(proj_features.flatten(0, 1))
             out = all_to_all_tensor_list(world_size, tensors, splits=splits, output_splits=out_splits)
-            means2d, depths, conics, opacities = [_reshape_view(C, t, N_world) for t in out[:4]]
+            means2d, depths, conics, opacities = [_camera_major(C, t, N_world) for t in out[:4]]
             if proj_features is not None:
-                proj_features = _reshape_view(C, out[4], N_world)
+                proj_features = _camera_major(C, out[4], N_world)
         I = B * C
 
     if render_mode_has_depth_channel(render_mode):
