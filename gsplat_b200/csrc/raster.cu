@@ -35,10 +35,7 @@
 
 // Compile-time choices of the backward kernel (defaults are the tuned ones).
 #ifndef GSB_BWD_MINB
-#define GSB_BWD_MINB 10
-#endif
-#ifndef GSB_RAST_SPLIT_FLUSH
-#define GSB_RAST_SPLIT_FLUSH 1
+#define GSB_BWD_MINB 12
 #endif
 #ifndef GSB_RAST_FAST_RCP
 #define GSB_RAST_FAST_RCP 1
@@ -74,11 +71,11 @@ struct RasterParams {
     bool first_chunk;
 };
 
-// Staged splat: mean, opacity, conic and sig_max = ln(255 o), the largest sigma
-// at which alpha = o exp(-sigma) still reaches 1/255.
+// Staged splat: mean, opacity, conic and sig2_max = 2 ln(255 o), twice the
+// largest sigma at which alpha = o exp(-sigma) still reaches 1/255.
 struct __align__(16) SplatRec {
     float x, y, o, a;
-    float b, c, sig_max, pad1;
+    float b, c, sig2_max, pad1;
 };
 
 struct RasterSmem {
@@ -86,13 +83,13 @@ struct RasterSmem {
     SplatRec *recs;
     float4 *boxes;
     float *colors;
-    uint8_t *lists; // [nwarps][kBatch]
+    uint8_t *lists; // [nwarps][kBatch] 16-bit entries
 };
 
 template <int CDIM> __host__ __device__ constexpr size_t raster_smem_bytes(int nwarps) {
     return (size_t)kBatch * sizeof(SplatRec) + (size_t)kBatch * sizeof(float4) +
            (size_t)kBatch * sizeof(int32_t) + (size_t)kBatch * CDIM * sizeof(float) +
-           (size_t)nwarps * kBatch;
+           (size_t)nwarps * kBatch * 2;
 }
 
 template <int CDIM> __device__ __forceinline__ RasterSmem carve(unsigned char *base) {
@@ -126,7 +123,7 @@ __device__ __forceinline__ void stage_splat(const RasterParams &p, const RasterS
     r.a = a;
     r.b = b;
     r.c = c;
-    r.sig_max = o > 0.f ? __logf(o * 255.f) : -1.f;
+    r.sig2_max = o > 0.f ? 2.f * __logf(o * 255.f) : -1.f;
     r.pad1 = 0.f;
     s.recs[i] = r;
     const float *cp = p.colors + (size_t)g * p.cstride + p.coff;
@@ -177,15 +174,26 @@ __device__ __forceinline__ bool box_hits(const float4 &bx, const WarpRect &r) {
     return !(bx.y < r.x0 || bx.x > r.x1 || bx.w < r.y0 || bx.z > r.y1);
 }
 
+// exp(-x / 2) for the pair evaluation: ex2.approx of x * (-log2(e) / 2). The
+// product rounds exactly like (x / 2) * log2(e) (halving is exact), so this is
+// the hardware exponential of -sigma evaluated the same way as __expf(-sigma).
+__device__ __forceinline__ float exp_neg_half(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * -0.72134752044448170368f));
+    return y;
+}
+
 // Shared per-pair evaluation: identical in forward and backward so both make the
 // same decisions. A pair contributes when sigma >= 0 and alpha = min(0.99,
-// o exp(-sigma)) >= 1/255 (reference RasterizeToPixels3DGSFwd.cu:170-176). The
-// cheap test sigma > sig_max = ln(255 o) rejects almost every non-contributing
-// pair before the exponential; it is equivalent to alpha < 1/255 up to the
-// rounding of the two transcendental evaluations, and the exact alpha test is
-// still applied to the pairs that pass it.
+// o exp(-sigma)) >= 1/255 (reference RasterizeToPixels3DGSFwd.cu:170-176), with
+// sigma = 0.5 (a dx^2 + c dy^2) + b dx dy evaluated as half the quadratic form
+// d . (conic d): the products g = conic d are the mean gradient's factors too.
+// The cheap test 2 sigma > sig2_max = 2 ln(255 o) rejects almost every
+// non-contributing pair before the exponential; it is equivalent to alpha <
+// 1/255 up to the rounding of the two transcendental evaluations, and the exact
+// alpha test is still applied to the pairs that pass it.
 struct PairEval {
-    float dx, dy, sigma, vis, alpha;
+    float dx, dy, gx, gy, vis, ov, alpha;
     bool keep;
 };
 
@@ -193,11 +201,14 @@ __device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float
     PairEval e;
     e.dx = r.x - px;
     e.dy = r.y - py;
-    e.sigma = 0.5f * (r.a * e.dx * e.dx + r.c * e.dy * e.dy) + r.b * e.dx * e.dy;
-    e.keep = e.sigma >= 0.f && e.sigma <= r.sig_max;
+    e.gx = r.a * e.dx + r.b * e.dy;
+    e.gy = r.b * e.dx + r.c * e.dy;
+    const float s2 = e.dx * e.gx + e.dy * e.gy; // 2 sigma
+    e.keep = s2 >= 0.f && s2 <= r.sig2_max;
     if (e.keep) {
-        e.vis = __expf(-e.sigma);
-        e.alpha = fminf(kMaxAlpha, r.o * e.vis);
+        e.vis = exp_neg_half(s2);
+        e.ov = r.o * e.vis;
+        e.alpha = fminf(kMaxAlpha, e.ov);
         e.keep = e.alpha >= kAlphaThreshold;
     }
     return e;
@@ -256,7 +267,7 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
         const int32_t end = (image == p.I - 1 && tile == p.tile_w * p.tile_h - 1)
                                 ? (int32_t)p.n_isects
                                 : p.offsets[tile_flat + 1];
-        uint8_t *mylist = s.lists + warp * kBatch;
+        uint8_t *mylist = s.lists + warp * kBatch * 2;
         for (int32_t bstart = start; bstart < end; bstart += kBatch) {
             bool all_done = true;
 #pragma unroll
@@ -373,19 +384,24 @@ __device__ __forceinline__ float halving_reduce(float *v, int lane, int &idx, bo
     return r;
 }
 
-template <int N> struct Pow2Ceil {
-    static constexpr int value = N <= 1 ? 1 : 2 * Pow2Ceil<(N + 1) / 2>::value;
-};
-template <> struct Pow2Ceil<1> { static constexpr int value = 1; };
 
 // Per-splat gradient slots: [0, CDIM) colour, then conic a, b, c, mean x, y,
-// opacity, |mean x|, |mean y|.
+// opacity, |mean x|, |mean y|. The backward accumulates the conic and mean slots
+// without their constant factors (sum of w dx dx, w dx dy, w dy dy, w gx, w gy
+// with w = o vis v_alpha = -v_sigma); `scale` restores them on the way out.
 template <int CDIM>
-__device__ __forceinline__ float *grad_slot(const RasterParams &p, int j, int32_t g) {
+__device__ __forceinline__ float *grad_slot(const RasterParams &p, int j, int32_t g, float &scale) {
+    scale = 1.f;
     if (j < CDIM) return p.v_colors + (size_t)g * p.cstride + p.coff + j;
     j -= CDIM;
-    if (j < 3) return p.v_conics + (size_t)g * 3 + j;
-    if (j < 5) return p.v_means2d + (size_t)g * 2 + (j - 3);
+    if (j < 3) {
+        scale = j == 1 ? -1.f : -0.5f;
+        return p.v_conics + (size_t)g * 3 + j;
+    }
+    if (j < 5) {
+        scale = -1.f;
+        return p.v_means2d + (size_t)g * 2 + (j - 3);
+    }
     if (j == 5) return p.v_opacities + g;
     return p.v_means2d_abs ? p.v_means2d_abs + (size_t)g * 2 + (j - 6) : nullptr;
 }
@@ -404,8 +420,9 @@ __device__ __forceinline__ void flush_range(const RasterParams &p, const float *
         bool writer;
         const float r = halving_reduce<V>(v, lane, idx, writer);
         if (writer) {
-            float *dst = grad_slot<CDIM>(p, FIRST + idx, g);
-            if (dst) atomicAdd(dst, r);
+            float scale;
+            float *dst = grad_slot<CDIM>(p, FIRST + idx, g, scale);
+            if (dst) atomicAdd(dst, r * scale);
         }
         flush_range<CDIM, FIRST + V, COUNT - V>(p, acc, lane, g);
     }
@@ -414,41 +431,21 @@ __device__ __forceinline__ void flush_range(const RasterParams &p, const float *
 template <int CDIM, int NV>
 __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, const float *acc, int lane,
                                                   int32_t g) {
-#if GSB_RAST_SPLIT_FLUSH
     flush_range<CDIM, 0, NV>(p, acc, lane, g);
-#else
-    constexpr int FIRST = NV < 32 ? NV : 32;
-    constexpr int V1 = Pow2Ceil<FIRST>::value;
-    float v1[V1];
-#pragma unroll
-    for (int i = 0; i < V1; ++i) v1[i] = i < FIRST ? acc[i] : 0.f;
-    int idx;
-    bool writer;
-    float r = halving_reduce<V1>(v1, lane, idx, writer);
-    if (writer && idx < FIRST) {
-        float *dst = grad_slot<CDIM>(p, idx, g);
-        if (dst) atomicAdd(dst, r);
-    }
-    if constexpr (NV > 32) {
-        constexpr int REST = NV - 32;
-        constexpr int V2 = Pow2Ceil<REST>::value;
-        float v2[V2];
-#pragma unroll
-        for (int i = 0; i < V2; ++i) v2[i] = i < REST ? acc[32 + i] : 0.f;
-        r = halving_reduce<V2>(v2, lane, idx, writer);
-        if (writer && idx < REST) {
-            float *dst = grad_slot<CDIM>(p, 32 + idx, g);
-            if (dst) atomicAdd(dst, r);
-        }
-    }
-#endif
 }
 
 // ABS: accumulate |v_mean2d| per pair (absgrad). IL: interleaved pixel layout
 // for 16x16 tiles with 4 pixels per thread: warp w covers rows 8w .. 8w + 7 as
-// four 8x4 sub-blocks and lane l owns pixel (l % 8, l / 8) of every sub-block,
-// so a splat that touches one sub-block runs the per-pair code of one of the
-// four unrolled pixel slots instead of all four.
+// four 8x4 quarters and lane l owns pixel (l % 8, l / 8) of every quarter, so a
+// splat whose culling box misses a quarter skips that pixel slot in every lane
+// (a warp-uniform branch: the quarter mask is computed once per splat and warp).
+//
+// Per pixel the backward keeps T (recovered back to front), S = buf . v_colour
+// (the colour behind the current splat, only ever needed dotted with the
+// upstream colour gradient), the upstream colour gradient, tv = T_final
+// (v_alpha - bg . v_colour) and the last contributor. With cv = colour . v_colour
+// the reference's v_alpha = sum_c (colour_c T - buf_c ra) v_c + ra tv becomes
+// T cv - ra (S - tv), and S grows by alpha T cv.
 template <int CDIM, int BX, int BY, bool ABS, bool IL>
 __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? GSB_BWD_MINB : 8) : 1))
     raster_bwd_kernel(RasterParams p) {
@@ -465,12 +462,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
     const size_t img_pix = (size_t)image * p.H * p.W;
     const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
 
-    // Per pixel: T (recovered back to front), the colour buffer, the upstream
-    // colour gradient, tv = T_final (v_alpha - bg . v_colour) (the only way the
-    // final transmittance, the alpha gradient and the background enter the
-    // gradients) and the last contributor (-1 outside the image: every splat
-    // index is larger, so those pixels are skipped).
-    float px[PPT], py[PPT], T[PPT], buf[PPT][CDIM], vc[PPT][CDIM], tv[PPT];
+    float px[PPT], py[PPT], T[PPT], S[PPT], vc[PPT][CDIM], tv[PPT];
     int32_t bin_final[PPT];
     bool has = false;
     int32_t my_max = -1;
@@ -497,12 +489,12 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
         // the pixel is nearly opaque: alpha = 0.9999 carries T to ~3e-4).
         const float Tf = inside ? (p.T_final ? p.T_final[pix] : 1.f - p.alphas[pix]) : 0.f;
         T[k] = Tf;
+        S[k] = 0.f;
         bin_final[k] = inside ? p.last_ids[pix] : -1;
         float dotbg = 0.f;
 #pragma unroll
         for (int c = 0; c < CDIM; ++c) {
             vc[k][c] = inside ? p.v_renders[pix * p.cstride + p.coff + c] : 0.f;
-            buf[k][c] = 0.f;
             if (bg) dotbg += bg[c] * vc[k][c];
         }
         const float va = (inside && p.first_chunk) ? p.v_alphas[pix] : 0.f;
@@ -520,6 +512,8 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
     int32_t warp_max = my_max;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) warp_max = max(warp_max, __shfl_xor_sync(0xffffffffu, warp_max, o));
+    // pixel-centre rectangles of the warp's four quarters (interleaved layout)
+    const float qx0 = (float)tx0 + 0.5f, qy0 = (float)(ty0 + warp * 8) + 0.5f;
 
     const int32_t start = p.offsets[tile_flat];
     const int32_t end = (image == p.I - 1 && tile == p.tile_w * p.tile_h - 1) ? (int32_t)p.n_isects
@@ -532,26 +526,46 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
     __syncthreads();
     const int32_t block_max = block_max_s;
     const int32_t last = min(end - 1, block_max);
-    uint8_t *mylist = s.lists + warp * kBatch;
+    uint8_t *mylist = s.lists + warp * kBatch * 2;
     for (int32_t bend = last; bend >= start; bend -= kBatch) {
         const int nb = min(kBatch, bend + 1 - start);
         __syncthreads();
         for (int i = threadIdx.x; i < nb; i += blockDim.x)
             stage_splat<CDIM>(p, s, i, p.flatten_ids[bend - i]);
         __syncthreads();
+        // per-warp list of the splats whose box meets the warp's pixels, with
+        // the quarters they meet (bits 8..11 of each 16-bit entry)
         int cnt = 0;
+        uint16_t *mylist16 = reinterpret_cast<uint16_t *>(mylist);
         if (wr.any) {
             for (int base = 0; base < nb; base += 32) {
                 const int i = base + lane;
-                const bool hit = i < nb && (bend - i) <= warp_max && box_hits(s.boxes[i], wr);
+                uint32_t q = 0;
+                if (i < nb && (bend - i) <= warp_max) {
+                    const float4 bx = s.boxes[i];
+                    if (box_hits(bx, wr)) {
+                        if (IL) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float x0 = qx0 + (k & 1) * 8, y0 = qy0 + (k >> 1) * 4;
+                                if (!(bx.y < x0 || bx.x > x0 + 7.f || bx.w < y0 || bx.z > y0 + 3.f)) q |= 1u << k;
+                            }
+                        } else {
+                            q = 0xfu;
+                        }
+                    }
+                }
+                const bool hit = q != 0;
                 const uint32_t bal = __ballot_sync(0xffffffffu, hit);
-                if (hit) mylist[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint8_t)i;
+                if (hit) mylist16[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(i | (q << 8));
                 cnt += __popc(bal);
             }
         }
         __syncwarp();
         for (int li = 0; li < cnt; ++li) {
-            const int i = mylist[li];
+            const uint32_t ent = mylist16[li];
+            const int i = ent & 0xff;
+            const uint32_t qmask = ent >> 8;
             const int32_t gidx = bend - i;
             constexpr int NV = CDIM + (ABS ? 8 : 6);
             float acc[NV];
@@ -564,6 +578,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
             for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
 #pragma unroll
             for (int k = 0; k < PPT; ++k) {
+                if (IL && !(qmask & (1u << k))) continue;
                 if (gidx > bin_final[k]) continue;
                 const PairEval e = eval_pair(r, px[k], py[k]);
                 if (!e.keep) continue;
@@ -576,20 +591,20 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
 #endif
                 T[k] *= ra;
                 const float fac = e.alpha * T[k];
-                float v_alpha = 0.f;
+                float cv = 0.f;
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) {
                     acc[c] += fac * vc[k][c];
-                    v_alpha += (col[c] * T[k] - buf[k][c] * ra) * vc[k][c];
+                    cv += col[c] * vc[k][c];
                 }
-                v_alpha += ra * tv[k];
-                if (r.o * e.vis <= kMaxAlpha) {
-                    const float v_sigma = -r.o * e.vis * v_alpha;
-                    acc[CDIM + 0] += 0.5f * v_sigma * e.dx * e.dx;
-                    acc[CDIM + 1] += v_sigma * e.dx * e.dy;
-                    acc[CDIM + 2] += 0.5f * v_sigma * e.dy * e.dy;
-                    const float gx = v_sigma * (r.a * e.dx + r.b * e.dy);
-                    const float gy = v_sigma * (r.b * e.dx + r.c * e.dy);
+                const float v_alpha = T[k] * cv - ra * (S[k] - tv[k]);
+                if (e.ov <= kMaxAlpha) {
+                    const float w = e.ov * v_alpha; // -v_sigma
+                    const float wx = w * e.dx, wy = w * e.dy;
+                    acc[CDIM + 0] += wx * e.dx;
+                    acc[CDIM + 1] += wx * e.dy;
+                    acc[CDIM + 2] += wy * e.dy;
+                    const float gx = w * e.gx, gy = w * e.gy;
                     acc[CDIM + 3] += gx;
                     acc[CDIM + 4] += gy;
                     acc[CDIM + 5] += e.vis * v_alpha;
@@ -598,8 +613,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
                         acc[CDIM + 7] += fabsf(gy);
                     }
                 }
-#pragma unroll
-                for (int c = 0; c < CDIM; ++c) buf[k][c] += col[c] * fac;
+                S[k] += fac * cv;
             }
             if (!__any_sync(0xffffffffu, any)) continue;
             flush_splat_grads<CDIM, NV>(p, acc, lane, s.ids[i]);
