@@ -36,6 +36,15 @@ WORKLOADS = {
                 "packed, fwd+bwd+SelectiveAdam"),
     "config4": ("config4: 6M Gaussians sharded over the ranks, 32 cameras 1600x1200 fx=fy=1200 on a radius-8 "
                 "sphere split over the ranks, SH deg 3, packed, fwd+bwd+SelectiveAdam"),
+    "config2": ("config2: 500k Gaussians, 4 cameras 1024x1024 fx=fy=1024 on a radius-6 ring, SH deg 3, RGB+ED, "
+                "antialiased, absgrad, packed, fwd+bwd"),
+}
+# rasterization() options and whether the step ends with the optimizer, per workload
+STEP_MODES = {
+    "config1": dict(render_mode="RGB", rasterize_mode="classic", absgrad=False, adam=True),
+    "config3": dict(render_mode="RGB", rasterize_mode="classic", absgrad=False, adam=True),
+    "config4": dict(render_mode="RGB", rasterize_mode="classic", absgrad=False, adam=True),
+    "config2": dict(render_mode="RGB+ED", rasterize_mode="antialiased", absgrad=True, adam=False),
 }
 LRS = {"means": 1.6e-4, "scales": 5e-3, "quats": 1e-3, "opacities": 5e-2, "sh": 2.5e-3}
 
@@ -47,13 +56,17 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="gsb", choices=["gsb", "reference"])
     ap.add_argument("--n", type=int, default=None, help="Gaussians per rank (default: the workload's)")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config3", "config4"],
-                    help="config1 (the headline, default), config3 (3M Gaussians, 8 cameras at "
-                         "1920x1080, one GPU) or config4 (6M Gaussians sharded over the ranks, 32 "
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"],
+                    help="config1 (the headline, default), config2 (500k Gaussians, 4 cameras at "
+                         "1024x1024, RGB+ED, antialiased, absgrad, fwd+bwd), config3 (3M Gaussians, 8 "
+                         "cameras at 1920x1080) or config4 (6M Gaussians sharded over the ranks, 32 "
                          "cameras at 1600x1200 split over the ranks: total work fixed)")
-    ap.add_argument("--dense", action="store_true", help="packed=False (trainer default)")
+    ap.add_argument("--dense", action="store_true",
+                    help="rasterization(packed=False), the reference trainer's default layout")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded config-4 measurement reported under 'sharded'")
     ap.add_argument("--profile-ops", action="store_true", help="print per-op breakdown to stderr")
     return ap.parse_args()
 
@@ -156,20 +169,32 @@ class ClockSampler:
 
 
 def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
-    """config-1 Gaussians of one rank. With several ranks the shards sit side by
-    side along x (12 units apart) and each rank's camera looks at its own shard,
-    so every GPU renders one config-1 view of a scene that grows with the job
-    (weak scaling); splats near the frustum edges still cross ranks through the
-    all-to-all. workload="config3": the 3M-Gaussian, 8-camera scene (one GPU).
-    workload="config4": this rank's shard and cameras of the 6M-Gaussian,
-    32-camera scene (the job's work stays the same as ranks are added)."""
+    """The Gaussians and cameras of one rank.
+
+    config1: n Gaussians of config 1 per rank. With several ranks the shards sit
+    side by side along x (12 units apart) and each rank's camera looks at its
+    own shard, so every GPU renders one config-1 view of a scene that grows with
+    the job (weak scaling); splats near the frustum edges still cross ranks
+    through the exchange.
+    config2 / config3: the whole scene of n Gaussians (4 / 8 cameras), each rank
+    holding the strided shard [rank::world] of the Gaussians (the reference
+    trainer's layout) and its consecutive share of the cameras: the job's work
+    stays the same as ranks are added.
+    config4: this rank's shard of n Gaussians and its cameras of the
+    6M-Gaussian, 32-camera scene (the job's work stays the same)."""
     import torch
 
     from tests import _data
 
-    if workload == "config3":
-        assert world == 1, "config3 is measured on one GPU"
-        d = _data.config3(N=n, seed=seed)
+    if workload in ("config2", "config3"):
+        d = _data.config2(N=n) if workload == "config2" else _data.config3(N=n)
+        C = d["viewmats"].shape[0]
+        assert C % world == 0, f"{workload}: {C} cameras do not split over {world} ranks"
+        per = C // world
+        for k in ("means", "quats", "scales", "opacities", "sh"):
+            d[k] = d[k][rank::world].contiguous()
+        d["viewmats"] = d["viewmats"][rank * per:(rank + 1) * per].contiguous()
+        d["Ks"] = d["Ks"][rank * per:(rank + 1) * per].contiguous()
     elif workload == "config4":
         d = _data.config4(N=n, rank=rank, world=world)
     else:
@@ -190,32 +215,45 @@ def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
     return params, d
 
 
-def train_step(params, opt, viewmat, K, W, H, G, Ga, distributed=False):
+def train_step(params, opt, viewmat, K, W, H, G, Ga, distributed=False, packed=True, mode=None):
+    """One step through the public API: rasterization() forward, loss.backward()
+    and (unless the workload's mode says otherwise) SelectiveAdam.step over the
+    visible Gaussians (the reference trainer's visibility, simple_trainer.py)."""
     import torch
 
     import gsplat_b200
 
+    mode = mode or STEP_MODES["config1"]
     render, alpha, meta = gsplat_b200.rasterization(
         params["means"], params["quats"], torch.exp(params["scales"]),
         torch.sigmoid(params["opacities"]), params["sh"], viewmat, K, W, H, near_plane=0.01,
-        far_plane=100.0, sh_degree=3, packed=True, distributed=distributed)
-    loss = (render * G).sum() + (alpha * Ga).sum()
+        far_plane=100.0, sh_degree=3, packed=packed, distributed=distributed,
+        render_mode=mode["render_mode"], rasterize_mode=mode["rasterize_mode"], absgrad=mode["absgrad"])
+    loss = (render * G[..., :render.shape[-1]]).sum() + (alpha * Ga).sum()
     loss.backward()
+    if not mode["adam"]:
+        for p in params.values():
+            p.grad = None
+        return loss, meta
     n = params["means"].shape[0]
-    vis = torch.zeros(n, dtype=torch.bool, device=render.device)
-    gids = meta["gaussian_ids"]
     if distributed:
         # the local shard's Gaussians that reached any rank's image: those with a
         # gradient (the packed ids after the exchange are the received splats')
         vis = params["means"].grad.ne(0).any(-1)
+    elif packed:
+        vis = torch.zeros(n, dtype=torch.bool, device=render.device)
+        vis.index_fill_(0, meta["gaussian_ids"], True)
     else:
-        vis.index_fill_(0, gids, True)
+        vis = (meta["radii"] > 0).all(-1).any(0)
     opt.step(vis)
     opt.zero_grad(set_to_none=True)
     return loss, meta
 
 
-FLOP_PER_PAIR = {"fwd": 26, "bwd": 68}  # CDIM = 3: 20 + 2 CDIM forward, 50 + 6 CDIM backward
+def flop_per_pair(cdim):
+    """Algorithmic FP32 work per contributing (pixel, splat) pair of the
+    rasterizer: 20 + 2 CDIM forward, 50 + 6 CDIM backward (26 / 68 for RGB)."""
+    return {"fwd": 20 + 2 * cdim, "bwd": 50 + 6 * cdim}
 
 
 def cpu_scene(n, seed):
@@ -293,6 +331,7 @@ def cpu_reference_step(sc, tile_row_stride=8):
 
 
 REF_BUDGET_S = 120.0  # wall time of the --impl reference steps (warm-up + timed)
+CPU_BASELINE_STEPS = 3  # timed host steps of the cpu_baseline leg
 
 
 def run_reference(args):
@@ -339,6 +378,7 @@ def run_reference(args):
                    "gaussians_per_rank": args.n, "cameras_per_rank": 1,
                    "parallelism": "host cores of rank 0", "stages_ms": detail},
         "cpu_baseline": {"value": value, "unit": "MPix/s", "cores": cores, "kind": "port",
+                         "torch_threads": __import__("torch").get_num_threads(), "openmp_threads": cores,
                          "sample": sample},
         "e2e": {"value": value, "unit": "MPix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -377,8 +417,7 @@ def contributing_pairs(meta, W, H, dev):
 
     offsets = meta["isect_offsets"].contiguous()
     fids = meta["flatten_ids"]
-    n = meta["means2d"].shape[0]
-    ones = torch.zeros((n, 1), device=dev)
+    ones = torch.zeros(meta["means2d"].shape[:-1] + (1,), device=dev)
     I = int(offsets.numel() // (offsets.shape[-1] * offsets.shape[-2]))
     th, tw = offsets.shape[-2:]
     renders = torch.empty((I, H, W, 1), device=dev)
@@ -420,6 +459,73 @@ def ncu_traffic(name):
     return None
 
 
+SHARDED_STEPS = 10  # timed steps of the sharded config-4 measurement (at most --steps)
+
+
+def measure_sharded(args, dev, rank, world, distributed):
+    """The reference's sharded multi-GPU configuration at the
+    job's N: 6M Gaussians split evenly over the ranks, 32 cameras at 1600x1200
+    split over the ranks, rasterization(distributed=True) exchanging the
+    projected splats, backward and SelectiveAdam on every rank. Total work is
+    fixed, so the per-N values give the strong-scaling curve. W >= 3 warm-up
+    steps, then min(K, SHARDED_STEPS) steps between barrier + synchronize, timed
+    with CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import gsplat_b200
+
+    n = 6_000_000 // world
+    params, d = make_params(n, 1 + rank, dev, rank, world, "config4")
+    W, H = d["width"], d["height"]
+    viewmat, K = d["viewmats"].to(dev), d["Ks"].to(dev)
+    n_cams = viewmat.shape[0]
+    opt = gsplat_b200.SelectiveAdam([{"params": [p], "lr": LRS[k], "name": k} for k, p in params.items()],
+                                    eps=1e-15, betas=(0.9, 0.999))
+    g = torch.Generator(device=dev).manual_seed(200 + rank)
+    G = torch.randn((n_cams, H, W, 3), device=dev, generator=g)
+    Ga = torch.randn((n_cams, H, W, 1), device=dev, generator=g)
+    bank = [(G, Ga), (-G, -Ga)]
+    mode = STEP_MODES["config4"]
+
+    def barrier():
+        if distributed:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    warm = max(3, min(args.warmup, 5))
+    steps = max(1, min(args.steps, SHARDED_STEPS))
+    for i in range(warm):
+        train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        loss, meta = train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
+    end.record()
+    barrier()
+    ms = start.elapsed_time(end) / steps
+    if distributed:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    mpix = world * n_cams * W * H / 1e6
+    n_isects = torch.tensor([meta["isect_ids"].numel()], device=dev, dtype=torch.float64)
+    if distributed:
+        dist.all_reduce(n_isects)
+    exchange = None
+    if distributed:
+        exchange = "peer memory" if os.environ.get("GSB_PEER_EXCHANGE", "1") != "0" else "nccl all_to_all"
+    out = {"workload": WORKLOADS["config4"], "value": mpix / (ms / 1e3), "unit": "MPix/s",
+           "ms_per_step": ms, "steps": steps, "warmup": warm, "scaling": "strong",
+           "gaussians_per_rank": n, "cameras_per_rank": n_cams, "n_isects_job": int(n_isects.item()),
+           "exchange": exchange, "timing": "CUDA events over the timed steps, max over ranks"}
+    del params, opt, bank, meta, loss
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_gsb(args):
     import torch
     import torch.distributed as dist
@@ -439,6 +545,8 @@ def run_gsb(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
 
     params, d = make_params(args.n, 1 + rank, dev, rank, world, args.workload)
+    packed = not args.dense
+    mode = STEP_MODES[args.workload]
     W, H = d["width"], d["height"]
     viewmat = d["viewmats"].to(dev)
     K = d["Ks"].to(dev)
@@ -455,7 +563,7 @@ def run_gsb(args):
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     bank = []
     for _ in range(GRAD_BANK // 2):
-        G_ = torch.randn((n_cams, H, W, 3), device=dev, generator=g)
+        G_ = torch.randn((n_cams, H, W, 4 if mode["render_mode"] == "RGB+ED" else 3), device=dev, generator=g)
         Ga_ = torch.randn((n_cams, H, W, 1), device=dev, generator=g)
         bank += [(G_, Ga_), (-G_, -Ga_)]
     step_no = [0]
@@ -473,7 +581,7 @@ def run_gsb(args):
     sampler = ClockSampler(dev)
     sampler.__enter__()
     for _ in range(args.warmup):
-        train_step(params, opt, viewmat, K, W, H, *grads(), distributed)
+        train_step(params, opt, viewmat, K, W, H, *grads(), distributed, packed, mode)
     barrier()
 
     # device-timed region: K full steps, inputs resident in HBM. Only the
@@ -491,7 +599,7 @@ def run_gsb(args):
     clock0 = time.time()
     start.record()
     for _ in range(args.steps):
-        loss, meta = train_step(params, opt, viewmat, K, W, H, *grads(), distributed)
+        loss, meta = train_step(params, opt, viewmat, K, W, H, *grads(), distributed, packed, mode)
     end.record()
     host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
     barrier()
@@ -518,7 +626,7 @@ def run_gsb(args):
     n_ops_steps = min(args.steps, 20)
     _backend.timing = {}
     for _ in range(n_ops_steps):
-        train_step(params, opt, viewmat, K, W, H, *grads(), distributed)
+        train_step(params, opt, viewmat, K, W, H, *grads(), distributed, packed, mode)
     barrier()
     for name, evs in _backend.timing.items():
         tot = sum(s.elapsed_time(e) for s, e in evs)
@@ -572,7 +680,7 @@ def run_gsb(args):
             compute.wait_event(ready)
             if it + 1 < args.steps:
                 nxt = prefetch(it + 1)
-            loss, _ = train_step(params, opt, dv, dK, W, H, dG, dGa, distributed)
+            loss, _ = train_step(params, opt, dv, dK, W, H, dG, dGa, distributed, packed, mode)
             lh = loss_host[it % 2]
             lh.copy_(loss.detach(), non_blocking=True)
             done = torch.cuda.Event()
@@ -597,27 +705,35 @@ def run_gsb(args):
                "pipelining": "inputs of step i+1 copied on a side stream during step i; "
                              "loss of step i read after step i+1 is issued"}
 
+    # the sharded configuration at this N (its own key; `value` stays the
+    # headline workload's)
+    sharded = None
+    if args.workload == "config1" and not args.no_sharded:
+        sharded = measure_sharded(args, dev, rank, world, distributed)
+
     roofline = None
     cpu_baseline = None
     if rank == 0 and ops.get("gsb_rasterize_bwd_ex"):
         pairs, walked = contributing_pairs(meta, W, H, dev)
         peak = fp32_peak_tflops(dev)
         t_bwd = raster_ms["gsb_rasterize_bwd_ex"] / 1e3
-        achieved = FLOP_PER_PAIR["bwd"] * pairs / t_bwd / 1e12
+        cdim = 4 if mode["render_mode"] == "RGB+ED" else 3
+        fpp = flop_per_pair(cdim)
+        achieved = fpp["bwd"] * pairs / t_bwd / 1e12
         traffic = ncu_traffic("raster_bwd_config1")
-        roofline = {"kernel": "raster_bwd_kernel<3,4>", "bound": "fp32", "achieved": achieved,
+        roofline = {"kernel": f"raster_bwd_kernel<{cdim},4>", "bound": "fp32", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                     "traffic": traffic,
                     "peak_source": "measured FP32 FMA probe (gsb_fp32_fma_probe) on this GPU; "
                                    "the kernel is FP32-issue bound (no tensor-core contraction, "
                                    "DRAM ~1%), so neither MEASURED_PEAKS figure applies",
-                    "algorithmic": f"{FLOP_PER_PAIR['bwd']} FLOP per contributing (pixel, splat) pair; "
+                    "algorithmic": f"{fpp['bwd']} FLOP per contributing (pixel, splat) pair; "
                                    f"{pairs} pairs per launch",
                     "walked_pairs": walked,
                     "walked_note": "(pixel, splat) pairs up to each pixel's last contributor, the unit "
                                    "a per-pixel rasterizer evaluates; this kernel culls most of them "
                                    "before any arithmetic, so the contributing pairs are the unit",
-                    "fwd": {"achieved": FLOP_PER_PAIR["fwd"] * pairs /
+                    "fwd": {"achieved": fpp["fwd"] * pairs /
                             (raster_ms["gsb_rasterize_fwd_ex"] / 1e3) / 1e12,
                             "unit": "TFLOP/s"}}
         hbm_peak = measured_hbm_gbs()
@@ -627,11 +743,18 @@ def run_gsb(args):
                                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "config1":
         sc = cpu_scene(args.n, 1)
-        cpu_reference_step(sc)
-        dt, detail = cpu_reference_step(sc)
+        cpu_reference_step(sc)  # warm-up
+        times = []
+        for _ in range(CPU_BASELINE_STEPS):
+            dt, detail = cpu_reference_step(sc)
+            times.append(dt)
+        dt = statistics.median(times)
         cpu_baseline = {"value": (W * H / 1e6) / dt, "unit": "MPix/s", "cores": os.cpu_count(),
-                        "kind": "port", "ms_per_step": dt * 1e3, "stages_ms": detail,
-                        "sample": "config 1 step of the CPU restatement (oracle/): full projection, SH, "
+                        "torch_threads": torch.get_num_threads(), "openmp_threads": os.cpu_count(),
+                        "kind": "port", "ms_per_step": dt * 1e3, "steps": CPU_BASELINE_STEPS,
+                        "step_ms_all": [round(t * 1e3, 1) for t in times], "stages_ms": detail,
+                        "sample": f"config 1 step of the CPU restatement (oracle/), median of "
+                                  f"{CPU_BASELINE_STEPS} steps after a warm-up: full projection, SH, "
                                   "isect, sort, backward chain, Adam; rasterizer on every 8th tile row "
                                   "scaled x8"}
     n_isects = int(meta["isect_ids"].numel()) if "isect_ids" in meta else None
@@ -650,17 +773,21 @@ def run_gsb(args):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "strong" if args.workload == "config4" else "weak",
+        "scaling": "weak" if args.workload == "config1" else "strong",
         "vs_baseline": None,
         "dtype": "fp32",
-        "data": "synthetic (seeded config-1 distributions, random-init Gaussians)",
+        "data": f"synthetic (seeded {args.workload} distributions, random-init Gaussians)",
         "config": {"workload": WORKLOADS[args.workload],
                    "gaussians_per_rank": int(params["means"].shape[0]), "cameras_per_rank": n_cams,
                    "parallelism": f"gaussian-sharded x{world}" if distributed else "single",
+                   "packed": packed, "render_mode": mode["render_mode"],
+                   "rasterize_mode": mode["rasterize_mode"], "absgrad": mode["absgrad"],
+                   "optimizer": "SelectiveAdam" if mode["adam"] else None,
                    "l2": "inputs larger than L2 (params + Adam state ~700 MB)",
                    "visible_splats": nnz, "n_isects": n_isects},
         "clocks": sampler.summary(clock0, clock1),
         "e2e": e2e,
+        "sharded": sharded,
         "roofline": roofline,
         "cpu_baseline": cpu_baseline,
         "gpu_launches": launches,
@@ -680,7 +807,8 @@ def main():
     args = parse()
     if args.n is None:
         world = int(os.environ.get("WORLD_SIZE", "1"))
-        args.n = {"config3": 3_000_000, "config4": 6_000_000 // world}.get(args.workload, 1_000_000)
+        args.n = {"config2": 500_000, "config3": 3_000_000, "config4": 6_000_000 // world}.get(args.workload,
+                                                                                             1_000_000)
     if args.impl == "reference":
         run_reference(args)
         return

@@ -5,7 +5,8 @@
 // p += -lr m / (sqrt(v) + eps). No bias correction. Rows with valid[row] == false
 // are left untouched (neither the state nor the parameter is read or written).
 //
-// All parameter groups of one optimizer step go through a single launch. Each
+// All parameter groups of one optimizer step go through a single launch (groups
+// of any size: elements are indexed in 64 bits). Each
 // group is streamed with 128-bit loads/stores when its arrays are 16-byte
 // aligned; a float4 whose four rows are all hidden is skipped without touching
 // HBM, so the traffic is proportional to the visible fraction.
@@ -32,7 +33,9 @@ struct AdamBatch {
 // (Granlund and Montgomery, PLDI 1994). With M = ceil(2^64 / D) = (2^64 + r) / D,
 // 0 <= r < D, e M / 2^64 = e / D + e r / (D 2^64), and the second term is below
 // 2^-32 < 1 / D, so it never carries e / D past the next integer:
-// floor(e M / 2^64) = floor(e / D).
+// floor(e M / 2^64) = floor(e / D). Groups of 2^32 elements or more are indexed
+// from each block's first element (64-bit, one division per block), so the
+// per-element offsets from that block's first row stay below 2^32.
 __device__ __forceinline__ uint32_t row_of(uint32_t e, unsigned long long magic) {
     return magic == 0ull ? e : (uint32_t)__umul64hi((unsigned long long)e, magic);
 }
@@ -57,20 +60,21 @@ __device__ __forceinline__ void adam_elem(float &p, float g, float &m, float &v,
 #endif
 constexpr int kAdamVec = GSB_ADAM_VEC; // float4 (or scalar) items per thread, kAdamThreads apart
 
-// Visibility of the rows of elements e .. e+3.
-__device__ __forceinline__ void rows_visible(const bool *valid, uint32_t e, uint32_t D,
+// Visibility of the rows of elements e .. e+3, where e = (first row of the
+// block) * D + le: le is the offset from the block's first row (< 2^32).
+__device__ __forceinline__ void rows_visible(const bool *valid, size_t row0, uint32_t le, uint32_t D,
                                              unsigned long long magic, bool vis[4]) {
     if (valid == nullptr) {
         vis[0] = vis[1] = vis[2] = vis[3] = true;
         return;
     }
-    const uint32_t r0 = row_of(e, magic);
-    const uint32_t rem = e - r0 * D;
+    const uint32_t r0 = row_of(le, magic);
+    const uint32_t rem = le - r0 * D;
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
         const uint32_t rr = rem + j;
         const uint32_t row = r0 + (rr >= D) + (rr >= 2 * D) + (rr >= 3 * D);
-        vis[j] = valid[row];
+        vis[j] = valid[row0 + row];
     }
 }
 
@@ -78,20 +82,25 @@ __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
     int gi = 0;
     while (gi + 1 < B.n_groups && (long long)blockIdx.x >= B.block_start[gi + 1]) ++gi;
     const GsbAdamGroup &G = B.g[gi];
-    const uint32_t local_block = (uint32_t)((long long)blockIdx.x - B.block_start[gi]);
+    const size_t local_block = (size_t)((long long)blockIdx.x - B.block_start[gi]);
     const uint32_t D = (uint32_t)G.D;
-    const uint32_t numel = (uint32_t)G.numel;
+    const size_t numel = (size_t)G.numel;
     const float lr = G.lr, eps = G.eps, b1 = B.b1, b2 = B.b2;
     if (B.vec[gi]) {
+        // elements of this block: [first, first + kAdamVec * kAdamThreads * 4)
+        const size_t first = local_block * ((size_t)kAdamVec * kAdamThreads * 4);
+        const size_t row0 = first / D;
+        const uint32_t lbase = (uint32_t)(first - row0 * D);
         float4 p[kAdamVec], g[kAdamVec], m[kAdamVec], v[kAdamVec];
         bool vis[kAdamVec][4], act[kAdamVec];
         // issue every load of this thread before any arithmetic
 #pragma unroll
         for (int it = 0; it < kAdamVec; ++it) {
-            const uint32_t e0 = ((local_block * kAdamVec + it) * kAdamThreads + threadIdx.x) * 4u;
+            const uint32_t lo = ((uint32_t)it * kAdamThreads + threadIdx.x) * 4u;
+            const size_t e0 = first + lo;
             act[it] = e0 < numel;
             if (act[it]) {
-                rows_visible(B.valid, e0, D, B.row_magic[gi], vis[it]);
+                rows_visible(B.valid, row0, lbase + lo, D, B.row_magic[gi], vis[it]);
                 act[it] = vis[it][0] | vis[it][1] | vis[it][2] | vis[it][3];
             }
             if (act[it]) {
@@ -104,7 +113,7 @@ __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
 #pragma unroll
         for (int it = 0; it < kAdamVec; ++it) {
             if (!act[it]) continue;
-            const uint32_t e0 = ((local_block * kAdamVec + it) * kAdamThreads + threadIdx.x) * 4u;
+            const size_t e0 = first + ((uint32_t)it * kAdamThreads + threadIdx.x) * 4u;
             float pp[4] = {p[it].x, p[it].y, p[it].z, p[it].w}, gg[4] = {g[it].x, g[it].y, g[it].z, g[it].w};
             float mm[4] = {m[it].x, m[it].y, m[it].z, m[it].w}, vv[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
 #pragma unroll
@@ -115,11 +124,15 @@ __global__ void __launch_bounds__(kAdamThreads) adam_multi_kernel(AdamBatch B) {
             *reinterpret_cast<float4 *>(G.exp_avg_sq + e0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
         }
     } else {
+        const size_t first = local_block * ((size_t)kAdamVec * kAdamThreads);
+        const size_t row0 = first / D;
+        const uint32_t lbase = (uint32_t)(first - row0 * D);
 #pragma unroll
         for (int it = 0; it < kAdamVec; ++it) {
-            const uint32_t t = (local_block * kAdamVec + it) * kAdamThreads + threadIdx.x;
+            const uint32_t lo = (uint32_t)it * kAdamThreads + threadIdx.x;
+            const size_t t = first + lo;
             if (t >= numel) continue;
-            if (B.valid != nullptr && !B.valid[row_of(t, B.row_magic[gi])]) continue;
+            if (B.valid != nullptr && !B.valid[row0 + row_of(lbase + lo, B.row_magic[gi])]) continue;
             float p = G.param[t], m = G.exp_avg[t], v = G.exp_avg_sq[t];
             adam_elem(p, G.grad[t], m, v, lr, b1, b2, eps);
             G.param[t] = p;
@@ -156,8 +169,6 @@ extern "C" int gsb_adam_multi(int n_groups, const GsbAdamGroup *groups, const bo
                              aligned16(g.exp_avg) && aligned16(g.exp_avg_sq);
             B.vec[n] = vec ? 1 : 0;
             B.block_start[n] = blocks;
-            if (g.numel >= (1ll << 31))
-                return set_error(kErrInvalidArgument, "adam: group %d has more than 2^31 elements", done + n);
             const long long items = vec ? g.numel / 4 : g.numel;
             blocks += (items + (long long)kAdamThreads * kAdamVec - 1) / ((long long)kAdamThreads * kAdamVec);
         }

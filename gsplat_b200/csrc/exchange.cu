@@ -10,6 +10,8 @@
 // arrays, and remap the ids.
 #include <cstring>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "gsb_internal.h"
 
@@ -163,6 +165,10 @@ __device__ __forceinline__ int peer_block_rows(int total) {
 }
 constexpr long long kSpinLimit = 1ll << 21; // x ~0.5-2 us per poll: a few seconds at most
 
+// Polls a wait makes before it gives up (gsb_peer_set_wait_limit); read when a
+// launch is set up, so it applies to the launches that follow the call.
+static std::atomic<long long> g_wait_limit{kSpinLimit};
+
 struct PeerMailbox {
     unsigned long long rows_flag[kMaxPeers];     // [src]: exchange number of src's rows for this rank
     long long rows_count[kMaxPeers];             // [src]: rows src sent here
@@ -177,6 +183,7 @@ static_assert(sizeof(PeerMailbox) <= kMailboxBytes, "mailbox");
 struct PeerView {
     char *arena[kMaxPeers];
     long long recv_offset, recv_stride, grad_offset;
+    long long wait_limit; // polls before a wait gives up
     int rank, world;
     int *error;
 };
@@ -196,9 +203,10 @@ __device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned lo
 }
 
 // Waits until *flag >= want; returns false (after recording `kind`) when the
-// bound runs out.
-__device__ bool wait_flag(const unsigned long long *flag, unsigned long long want, int *error, int kind) {
-    for (long long it = 0; it < kSpinLimit; ++it) {
+// bound of `limit` polls runs out.
+__device__ bool wait_flag(const unsigned long long *flag, unsigned long long want, int *error, int kind,
+                          long long limit) {
+    for (long long it = 0; it < limit; ++it) {
         if (load_acquire_sys(flag) >= want) return true;
         __nanosleep(128);
     }
@@ -221,7 +229,7 @@ __device__ __forceinline__ long long region_start(const int64_t *n_world, int ca
 __global__ void peer_wait_consumed_kernel(PeerView v, unsigned long long epoch) {
     const int d = threadIdx.x;
     if (d >= v.world || epoch < 2) return;
-    wait_flag(&mailbox(v, v.rank)->consumed_flag[d], epoch - 1, v.error, 1);
+    wait_flag(&mailbox(v, v.rank)->consumed_flag[d], epoch - 1, v.error, 1, v.wait_limit);
 }
 
 // Row block staging as in pack_rows_kernel; each staged word goes to the
@@ -297,7 +305,7 @@ __global__ void peer_wait_rows_kernel(PeerView v, unsigned long long epoch, int6
     const int r = threadIdx.x;
     PeerMailbox *me = mailbox(v, v.rank);
     if (r < v.world) {
-        const bool ok = wait_flag(&me->rows_flag[r], epoch, v.error, 2);
+        const bool ok = wait_flag(&me->rows_flag[r], epoch, v.error, 2, v.wait_limit);
         cnt[r] = ok ? me->rows_count[r] : 0;
         route[v.world + 1 + r] = ok ? me->rows_first[r] : 0;
     }
@@ -411,7 +419,7 @@ __global__ void __launch_bounds__(kRowThreads) peer_send_grads_kernel(RowArrays 
 __global__ void peer_wait_grads_kernel(PeerView v, unsigned long long epoch) {
     const int d = threadIdx.x;
     if (d >= v.world) return;
-    wait_flag(&mailbox(v, v.rank)->grad_flag[d], epoch, v.error, 3);
+    wait_flag(&mailbox(v, v.rank)->grad_flag[d], epoch, v.error, 3, v.wait_limit);
 }
 
 static int make_view(PeerView &v, const GsbPeerGroup *g) {
@@ -427,6 +435,7 @@ static int make_view(PeerView &v, const GsbPeerGroup *g) {
     v.rank = g->rank;
     v.world = g->world;
     v.error = g->error;
+    v.wait_limit = g_wait_limit.load();
     if (v.error == nullptr) return set_error(kErrInvalidArgument, "peer group: no error word");
     return kOk;
 }
@@ -469,6 +478,12 @@ extern "C" int gsb_exchange_ids(long long n, const int64_t *n_device, const int6
 // ---- peer-memory exchange ---------------------------------------------------
 
 extern "C" size_t gsb_peer_mailbox_bytes(void) { return (size_t)kMailboxBytes; }
+
+extern "C" long long gsb_peer_set_wait_limit(long long polls) {
+    const long long prev = g_wait_limit.load();
+    g_wait_limit.store(polls > 0 ? polls : kSpinLimit);
+    return prev;
+}
 
 extern "C" int gsb_peer_alloc(size_t bytes, void **ptr, void *ipc_handle) {
     if (ptr == nullptr || ipc_handle == nullptr || bytes == 0) return set_error(kErrInvalidArgument, "peer alloc");

@@ -37,6 +37,9 @@
 #ifndef GSB_BWD_MINB
 #define GSB_BWD_MINB 12
 #endif
+#ifndef GSB_BWD_MINB_SMALL
+#define GSB_BWD_MINB_SMALL 1
+#endif
 #ifndef GSB_RAST_FAST_RCP
 #define GSB_RAST_FAST_RCP 1
 #endif
@@ -447,7 +450,7 @@ __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, const f
 // the reference's v_alpha = sum_c (colour_c T - buf_c ra) v_c + ra tv becomes
 // T cv - ra (S - tv), and S grows by alpha T cv.
 template <int CDIM, int BX, int BY, bool ABS, bool IL>
-__global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? GSB_BWD_MINB : 8) : 1))
+__global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? GSB_BWD_MINB : 8) : GSB_BWD_MINB_SMALL))
     raster_bwd_kernel(RasterParams p) {
     constexpr int PPT = BX * BY;
     static_assert(!IL || PPT == 4, "interleaved layout: 4 pixels per thread");

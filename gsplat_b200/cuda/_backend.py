@@ -118,6 +118,7 @@ SIGNATURES = {
     "gsb_peer_open": (I32, [P, P]),
     "gsb_peer_close": (I32, [P]),
     "gsb_peer_free": (I32, [P]),
+    "gsb_peer_set_wait_limit": (I64, [I64]),
     "gsb_peer_error_alloc": (I32, [P, P]),
     "gsb_peer_error_free": (I32, [P]),
     "gsb_peer_send_rows": (I32, [P, ctypes.c_ulonglong, I64, P, P, P, I32, I64, I32, P, P, P]),

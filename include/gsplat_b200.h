@@ -5,13 +5,22 @@
  *
  * Conventions
  *  - All tensors are device pointers to contiguous row-major fp32 / int32 / int64
- *    arrays; the caller allocates every output and scratch buffer (the library
- *    never allocates device memory). Optional inputs and outputs are NULL.
+ *    arrays; the caller allocates every output and scratch buffer. The compute
+ *    entry points never allocate device memory. The exceptions are the set-up
+ *    calls of the peer-memory exchange: gsb_peer_alloc allocates the calling
+ *    rank's exchange arena (cudaMalloc) and gsb_peer_error_alloc a host-mapped
+ *    error word (cudaHostAlloc); gsb_peer_free / gsb_peer_error_free release
+ *    them. Optional inputs and outputs are NULL.
  *  - Every function launches asynchronously on `stream` and returns 0 on success
  *    or a negative status (-1 invalid argument, -2 unsupported, -3 launch error);
  *    gsb_last_error() returns the message of the calling thread's last error.
- *  - Functions are stateless and reentrant; call them with the device that owns
- *    the pointers current.
+ *  - Functions hold no state between calls and may be called from several
+ *    threads, with these exceptions: gsb_isect_bucket_sort runs its larger
+ *    bucket classes on one internal side stream per device (created on first
+ *    use, forked from and joined back to `stream` with events; calls on one
+ *    device are serialised on it by a mutex); gsb_inclusive_scan_i32_noalloc
+ *    keeps its tile sums in one static device array per device (documented
+ *    there). Call every function with the device that owns the pointers current.
  *  - Outputs documented as "zero-initialised by the caller" are accumulated into
  *    with atomics, matching the reference's at::zeros allocations.
  *
@@ -492,6 +501,12 @@ typedef struct {
     int *error;              /* device address of the host-mapped error word */
 } GsbPeerGroup;
 GSB_API size_t gsb_peer_mailbox_bytes(void);
+/* Number of polls a wait of the peer exchange makes before it gives up
+ * (records its kind in the group's error word and lets its kernel finish);
+ * applies to the exchange calls made after it, process-wide. polls <= 0
+ * restores the default (a few seconds). Returns the previous limit. No
+ * reference counterpart: the reference's NCCL collectives have no bounded wait. */
+GSB_API long long gsb_peer_set_wait_limit(long long polls);
 GSB_API int gsb_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
 GSB_API int gsb_peer_open(const void *ipc_handle, void **ptr);
 GSB_API int gsb_peer_close(void *ptr);

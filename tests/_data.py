@@ -48,6 +48,20 @@ def config1(N=1_000_000, seed=1):
                  z_range=(2.0, 12.0), xy_uniform=5.0)
 
 
+def config2(N=500_000, seed=2, C=4):
+    """BASELINE config 2 (the feature variant): N Gaussians with means ~ N(0,1)^3,
+    the other distributions as config 0, and C cameras at 1024x1024 (fx=fy=1024,
+    cx=cy=512) at angles 2 pi k / C on a radius-6 ring in the x-z plane, looking at
+    the origin."""
+    import math
+
+    viewmats = torch.stack([look_at((6.0 * math.cos(2 * math.pi * k / C), 0.0, 6.0 * math.sin(2 * math.pi * k / C)),
+                                    up=(0.0, 1.0, 0.0)) for k in range(C)])
+    d = scene(N, seed=seed, width=1024, height=1024, fx=1024.0, cx=512.0, cy=512.0, C=C, viewmats=viewmats)
+    d["means"] = torch.randn((N, 3), generator=torch.Generator().manual_seed(seed))
+    return d
+
+
 def look_at(eye, target=(0.0, 0.0, 0.0), up=(0.0, 0.0, 1.0)):
     """World-to-camera 4x4 (OpenCV axes: z toward the target) for a camera at eye."""
     eye = torch.as_tensor(eye, dtype=torch.float32)

@@ -14,7 +14,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _scene(rank, dev, N=20000):
+def _scene(rank, dev, N=20000, C=1):
     g = torch.Generator().manual_seed(50 + rank)
     means = torch.empty(N, 3)
     means[:, 0].uniform_(-3, 3, generator=g)
@@ -27,13 +27,16 @@ def _scene(rank, dev, N=20000):
     opac = torch.sigmoid(torch.randn(N, generator=g))
     sh = torch.randn(N, 16, 3, generator=g) * 0.1
     sh[:, 0] += 0.5
-    vm = torch.eye(4)[None].clone()
-    vm[0, 0, 3] = -1.5 * (rank - 0.5)
-    K = torch.tensor([[[260.0, 0.0, 160.0], [0.0, 260.0, 120.0], [0.0, 0.0, 1.0]]])
+    # the rank's C cameras: small sideways and vertical offsets around its shard
+    vm = torch.eye(4)[None].repeat(C, 1, 1)
+    for c in range(C):
+        vm[c, 0, 3] = -1.5 * (rank - 0.5) + 0.4 * c
+        vm[c, 1, 3] = -0.3 * c
+    K = torch.tensor([[260.0, 0.0, 160.0], [0.0, 260.0, 120.0], [0.0, 0.0, 1.0]])[None].repeat(C, 1, 1)
     return [t.to(dev) for t in (means, quats, scales, opac, sh, vm, K)]
 
 
-def _worker(rank, world, store_path, q):
+def _worker(rank, world, store_path, q, C=1):
     import datetime
 
     import torch.distributed as dist
@@ -48,10 +51,10 @@ def _worker(rank, world, store_path, q):
         import gsplat_b200
 
         W, H = 320, 240
-        mine = _scene(rank, dev)
+        mine = _scene(rank, dev, C=C)
         params = [t.clone().requires_grad_(True) for t in mine[:5]]
         vm, K = mine[5], mine[6]
-        G = torch.randn((1, H, W, 3), generator=torch.Generator().manual_seed(7 + rank)).to(dev)
+        G = torch.randn((C, H, W, 3), generator=torch.Generator().manual_seed(7 + rank)).to(dev)
         # several exchanges (both receive buffers of the peer path), one of them
         # forward-only, must all give the same result
         grads_seen = []
@@ -70,13 +73,13 @@ def _worker(rank, world, store_path, q):
                 # the rasterizer's float atomics may add in another order
                 torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5)
 
-        # single-process reference: all Gaussians, both cameras, summed loss
-        scenes = [_scene(r, dev) for r in range(world)]
+        # single-process reference: all Gaussians, every rank's cameras, summed loss
+        scenes = [_scene(r, dev, C=C) for r in range(world)]
         full = [torch.cat([s[i] for s in scenes]).requires_grad_(True) for i in range(5)]
         loss = 0.0
         ref_img = None
         for r in range(world):
-            Gr = torch.randn((1, H, W, 3), generator=torch.Generator().manual_seed(7 + r)).to(dev)
+            Gr = torch.randn((C, H, W, 3), generator=torch.Generator().manual_seed(7 + r)).to(dev)
             img, _, _ = gsplat_b200.rasterization(*full, scenes[r][5], scenes[r][6], W, H, sh_degree=3,
                                                   packed=True)
             loss = loss + (img * Gr).sum()
@@ -95,15 +98,18 @@ def _worker(rank, world, store_path, q):
 
 
 @pytest.mark.parametrize("peer", ["1", "0"])
-def test_distributed_packed_matches_single_gpu(tmp_path, peer, monkeypatch):
-    """peer "1": the peer-memory exchange; "0": the NCCL all-to-all path."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("cams", [1, 3])
+@pytest.mark.parametrize("world", [2, 4])
+def test_distributed_packed_matches_single_gpu(tmp_path, peer, cams, world, monkeypatch):
+    """peer "1": the peer-memory exchange; "0": the NCCL all-to-all path; `cams`
+    cameras per rank (config 4 has 4 per rank at 8 GPUs); 2 or 4 ranks."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     monkeypatch.setenv("GSB_PEER_EXCHANGE", peer)
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     store = str(tmp_path / "rendezvous")
-    procs = [ctx.Process(target=_worker, args=(r, 2, store, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, store, q, cams)) for r in range(world)]
     for p in procs:
         p.start()
     import queue
