@@ -603,6 +603,173 @@ __device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n,
     }
 }
 
+// Buckets above kBucketSortMax entries are first split into sub-buckets by
+// the leading bits of their entries (depth bits << 32 | splat index: the order
+// of the final sort), written in sub-bucket order to a second array; every
+// sub-bucket then goes through the on-chip sorts above like a bucket of its own,
+// at its final position. The list of sub-buckets lives on the device.
+struct SubBuckets {
+    const int *count;    // number of sub-buckets (device); null: not a sub-bucket pass
+    const int32_t *start, *size, *bucket; // first entry, entries, (image, tile) bucket
+    int cap;             // records the arrays hold (a larger count has overflowed)
+};
+
+constexpr int kSplitThreads = 1024;
+constexpr int kSplitBits = 12; // at most 4096 sub-buckets per split bucket
+constexpr int kSplitTargetBits = 8; // ~256 entries per sub-bucket on average
+
+// One CTA per bucket of more than kBucketSortMax entries (persistent over the
+// class list of buckets above 4096 entries, skipping the others): the smallest
+// and largest entry, a histogram of the top kSplitBits bits of (entry - smallest),
+// its exclusive scan, the scatter of the entries into `out` at the bucket's
+// positions in sub-bucket order, and one sub-bucket record per non-empty bin.
+// A sub-bucket above kBucketSortMax entries (more than that many entries with
+// the same leading bits: equal depths) sets *overflow.
+__global__ void __launch_bounds__(kSplitThreads)
+    bucket_split_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
+                        const int32_t *__restrict__ list, int count, uint32_t n_buckets,
+                        const uint64_t *__restrict__ entries, uint64_t *__restrict__ out,
+                        int *sub_count, int32_t *__restrict__ sub_start, int32_t *__restrict__ sub_size,
+                        int32_t *__restrict__ sub_bucket, int sub_cap, int *overflow) {
+    constexpr int NB = 1 << kSplitBits;
+    constexpr int PER = NB / kSplitThreads;
+    __shared__ uint32_t hist[NB];
+    __shared__ uint32_t cur[NB];
+    __shared__ unsigned long long red[2][32];
+    __shared__ uint32_t wsum[32];
+    __shared__ int sbase;
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    for (int c = blockIdx.x; c < count; c += gridDim.x) {
+        const uint32_t b = (uint32_t)list[(int)n_buckets - 1 - c];
+        const int n = sizes[b];
+        if (n <= kBucketSortMax) continue;
+        const int start = starts[b];
+        unsigned long long lo = ~0ull, hi = 0ull;
+        for (int i = t; i < n; i += kSplitThreads) {
+            const unsigned long long e = entries[start + i];
+            lo = min(lo, e);
+            hi = max(hi, e);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        if (lane == 0) {
+            red[0][w] = lo;
+            red[1][w] = hi;
+        }
+        for (int k = t; k < NB; k += kSplitThreads) hist[k] = 0;
+        __syncthreads();
+        lo = red[0][lane];
+        hi = red[1][lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        const unsigned long long range = hi - lo;
+        const int bits = range ? 64 - __clzll((long long)range) : 0;
+        // about kSplitTarget entries per sub-bucket on average (fewer, larger
+        // sub-buckets keep the per-sub-bucket cost of the sorts small)
+        const int nbits = 32 - __clz((unsigned)(n - 1));
+        const int sbits = min(kSplitBits, max(1, nbits - kSplitTargetBits));
+        const int shift = bits > sbits ? bits - sbits : 0;
+        for (int i = t; i < n; i += kSplitThreads)
+            atomicAdd(&hist[(uint32_t)((entries[start + i] - lo) >> shift)], 1u);
+        __syncthreads();
+        // exclusive scan of the histogram: PER consecutive bins per thread
+        uint32_t v[PER], tot = 0, nonempty = 0;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            v[k] = hist[t * PER + k];
+            tot += v[k];
+            nonempty += v[k] > 0;
+        }
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) wsum[w] = incl;
+        __syncthreads();
+        if (w == 0) {
+            uint32_t x = wsum[lane], xi = x;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, xi, o);
+                if (lane >= o) xi += y;
+            }
+            wsum[lane] = xi - x;
+        }
+        // the sub-bucket records: one block-wide count of the non-empty bins
+        uint32_t ne_incl = nonempty;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, ne_incl, o);
+            if (lane >= o) ne_incl += y;
+        }
+        __syncthreads();
+        uint32_t base = wsum[w] + incl - tot;
+        __syncthreads();
+        if (lane == 31) wsum[w] = ne_incl;
+        __syncthreads();
+        if (w == 0) {
+            uint32_t x = wsum[lane], xi = x;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, xi, o);
+                if (lane >= o) xi += y;
+            }
+            wsum[lane] = xi - x;
+            if (lane == 31) sbase = atomicAdd(sub_count, (int)xi);
+        }
+        __syncthreads();
+        uint32_t rec = (uint32_t)sbase + wsum[w] + ne_incl - nonempty;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            cur[t * PER + k] = base;
+            if (v[k] > 0) {
+                if ((int)rec < sub_cap) {
+                    sub_start[rec] = start + (int)base;
+                    sub_size[rec] = (int)v[k];
+                    sub_bucket[rec] = (int32_t)b;
+                } else {
+                    *overflow = 1;
+                }
+                if (v[k] > (uint32_t)kBucketSortMax) *overflow = 1;
+                ++rec;
+            }
+            base += v[k];
+        }
+        __syncthreads();
+        for (int i = t; i < n; i += kSplitThreads) {
+            const unsigned long long e = entries[start + i];
+            const uint32_t pos = atomicAdd(&cur[(uint32_t)((e - lo) >> shift)], 1u);
+            out[start + pos] = e;
+        }
+        __syncthreads(); // hist / cur are reused by the next bucket
+    }
+}
+
+// The bitonic on-chip sort of sub-buckets of up to 1024 entries (persistent
+// over the device list of sub-buckets; larger ones are left to the radix kernels).
+template <int E>
+__global__ void __launch_bounds__(1024)
+    sub_bucket_sort_kernel(const SubBuckets sub, const uint64_t *__restrict__ entries, uint32_t n_tiles,
+                           uint32_t tile_bits, int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
+    extern __shared__ __align__(16) uint64_t sk[];
+    const int count = min(*sub.count, sub.cap);
+    for (int c = blockIdx.x; c < count; c += gridDim.x) {
+        const int n = sub.size[c];
+        if (n > 1024) continue;
+        sort_one_bucket<E>(sk, (uint32_t)sub.bucket[c], n, sub.start[c], entries, n_tiles, tile_bits, keys_out,
+                           ids_out);
+        __syncthreads(); // the shared copy is reused by the next sub-bucket
+    }
+}
+
 template <int E>
 __global__ void __launch_bounds__(1024)
     bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
@@ -668,7 +835,8 @@ __global__ void __launch_bounds__(THREADS, MINB)
                         const int32_t *__restrict__ list, int count, int from_back,
                         const uint64_t *__restrict__ entries,
                         uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits,
-                        int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
+                        int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out,
+                        const SubBuckets sub, int lo_size, int hi_size) {
     constexpr int CAP = THREADS * RMAX;
     constexpr int NW = THREADS / 32;
     constexpr int ND = 1 << DBITS;
@@ -688,12 +856,25 @@ __global__ void __launch_bounds__(THREADS, MINB)
     const int t = threadIdx.x, lane = t & 31, w = t >> 5;
     // counter k of this thread in the scan: q = PER t + k at q + q / NW
     const int cbase = PER >= NW ? t * (PER / NW) * CW : (PER * t / NW) * CW + (PER * t) % NW;
-    // the buckets of this size class: list[0, count) or list[n_buckets - count, n_buckets)
+    // the buckets of this size class: list[0, count) or list[n_buckets - count,
+    // n_buckets); or, with sub.count set, the sub-buckets of split buckets
+    if (sub.count != nullptr) count = min(*sub.count, sub.cap);
     for (int c = blockIdx.x; c < count; c += gridDim.x) {
-        const uint32_t b = (uint32_t)list[from_back ? (int)n_buckets - 1 - c : c];
-        const int n = sizes[b];
-        const int start = starts[b];
-        const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
+        uint32_t b, hb;
+        int n, start;
+        if (sub.count != nullptr) {
+            b = (uint32_t)c;
+            n = sub.size[c];
+            start = sub.start[c];
+            hb = (uint32_t)sub.bucket[c];
+        } else {
+            b = (uint32_t)list[from_back ? (int)n_buckets - 1 - c : c];
+            n = sizes[b];
+            start = starts[b];
+            hb = b;
+        }
+        if (n <= lo_size || n > hi_size) continue; // another size class
+        const int64_t hi = ((int64_t)(hb / n_tiles) << (32 + tile_bits)) | ((int64_t)(hb % n_tiles) << 32);
         const int R = (n + THREADS - 1) / THREADS;
         const int wbase = 32 * R * w + lane; // entry of round 0
         uint32_t key[RMAX], val[RMAX], rank2[RMAX / 2]; // two 16-bit ranks per word
@@ -1272,16 +1453,61 @@ extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const in
 
 extern "C" int gsb_isect_bucket_sort_max(void) { return kBucketSortMax; }
 
-extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
-                                     const int32_t *bucket_sizes, int max_count, int mid_buckets,
-                                     int large_buckets, const int32_t *class_list, const uint64_t *bucket_entries,
-                                     int64_t *isect_ids, int32_t *flatten_ids,
-                                     cudaStream_t stream) {
+// Scratch of the split path for buckets above kBucketSortMax entries: the
+// sub-bucket count, the entries in sub-bucket order and the sub-bucket records
+// (a split bucket has more than kBucketSortMax entries and at most 2^kSplitBits
+// sub-buckets, so there are fewer than n_isects / 4 of them).
+struct SplitScratch {
+    int *count;
+    uint64_t *entries;
+    int32_t *start, *size, *bucket;
+    int cap;
+};
+
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+static size_t split_scratch_layout(long long n_isects, char *base, SplitScratch *ss) {
+    const size_t n = n_isects > 0 ? (size_t)n_isects : 0;
+    const size_t cap = n / (kBucketSortMax / (1 << kSplitBits)) + 4096;
+    size_t off = 0;
+    const size_t o_count = off;
+    off += 256;
+    const size_t o_entries = off;
+    off += align256(n * sizeof(uint64_t));
+    const size_t o_start = off;
+    off += align256(cap * sizeof(int32_t));
+    const size_t o_size = off;
+    off += align256(cap * sizeof(int32_t));
+    const size_t o_bucket = off;
+    off += align256(cap * sizeof(int32_t));
+    if (ss != nullptr) {
+        ss->count = reinterpret_cast<int *>(base + o_count);
+        ss->entries = reinterpret_cast<uint64_t *>(base + o_entries);
+        ss->start = reinterpret_cast<int32_t *>(base + o_start);
+        ss->size = reinterpret_cast<int32_t *>(base + o_size);
+        ss->bucket = reinterpret_cast<int32_t *>(base + o_bucket);
+        ss->cap = (int)std::min<size_t>(cap, 0x7fffffff);
+    }
+    return off;
+}
+
+static int bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
+                       const int32_t *bucket_sizes, int max_count, int mid_buckets, int large_buckets,
+                       const int32_t *class_list, const uint64_t *bucket_entries, long long n_isects,
+                       void *scratch, size_t scratch_bytes, int *overflow, int64_t *isect_ids,
+                       int32_t *flatten_ids, cudaStream_t stream) {
     const uint64_t n_tiles = (uint64_t)tile_width * (uint64_t)tile_height;
     const uint64_t n_buckets = (uint64_t)I * n_tiles;
-    if (max_count > kBucketSortMax)
-        return set_error(kErrUnsupported, "bucket of %d entries exceeds the on-chip sort (%d)", max_count,
-                         kBucketSortMax);
+    const bool split = max_count > kBucketSortMax;
+    SplitScratch ss = {};
+    if (split) {
+        if (scratch == nullptr || overflow == nullptr)
+            return set_error(kErrUnsupported, "bucket of %d entries exceeds the on-chip sort (%d)", max_count,
+                             kBucketSortMax);
+        if (scratch_bytes < split_scratch_layout(n_isects, nullptr, nullptr))
+            return set_error(kErrInvalidArgument, "bucket sort scratch too small");
+        split_scratch_layout(n_isects, static_cast<char *>(scratch), &ss);
+    }
     if (n_buckets == 0 || max_count <= 0) return kOk;
     if (n_buckets > 0x7fffffffull) return set_error(kErrInvalidArgument, "too many buckets");
     const uint32_t tb = bit_length(n_tiles);
@@ -1308,14 +1534,14 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
     if (max_count > 1024 && mid_buckets + large_buckets == 0)
         return set_error(kErrInvalidArgument, "buckets above 1024 entries but empty class lists");
     cudaStream_t side = stream;
-    SideStream *ss = nullptr;
+    SideStream *sstream = nullptr;
     std::unique_lock<std::mutex> side_lock(g_side_mutex, std::defer_lock);
     if (mid_buckets + large_buckets > 0) {
         side_lock.lock(); // held until the join is recorded
-        if (int e = side_stream(&ss)) return e;
-        side = ss->stream;
-        cudaEventRecord(ss->fork, stream);
-        cudaStreamWaitEvent(side, ss->fork, 0);
+        if (int e = side_stream(&sstream)) return e;
+        side = sstream->stream;
+        cudaEventRecord(sstream->fork, stream);
+        cudaStreamWaitEvent(side, sstream->fork, 0);
     }
     const int sms = device_sms();
     if (mid_buckets > 0) {
@@ -1326,7 +1552,7 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
         kern<<<(unsigned)std::min(mid_buckets, RadixShape<GSB_RADIX_MID>::per_sm * sms), threads, smem, side>>>(
             offsets, bucket_sizes, class_list, mid_buckets, 0, bucket_entries, (uint32_t)n_buckets,
-            (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids, SubBuckets{}, 1024, 4096);
         if (int e = check_launch("bucket_radix_kernel")) return e;
     }
     if (large_buckets > 0) {
@@ -1337,14 +1563,77 @@ extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, con
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
         kern<<<(unsigned)std::min(large_buckets, RadixShape<GSB_RADIX_LARGE>::per_sm * sms), threads, smem, side>>>(
             offsets, bucket_sizes, class_list, large_buckets, 1, bucket_entries, (uint32_t)n_buckets,
-            (uint32_t)n_tiles, tb, isect_ids, flatten_ids);
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids, SubBuckets{}, 4096, kBucketSortMax);
         if (int e = check_launch("bucket_radix_kernel")) return e;
     }
-    if (ss != nullptr) {
-        cudaEventRecord(ss->join, side);
-        cudaStreamWaitEvent(stream, ss->join, 0);
+    if (split && large_buckets > 0) {
+        // buckets above kBucketSortMax: split into sub-buckets, then the same
+        // on-chip sorts over the device list of sub-buckets
+        cudaError_t ce = cudaMemsetAsync(ss.count, 0, sizeof(int), side);
+        if (ce == cudaSuccess) ce = cudaMemsetAsync(overflow, 0, sizeof(int), side);
+        if (ce != cudaSuccess) return set_error(kErrLaunch, "cudaMemsetAsync: %s", cudaGetErrorString(ce));
+        bucket_split_kernel<<<(unsigned)std::min(large_buckets, 2 * sms), kSplitThreads, 0, side>>>(
+            offsets, bucket_sizes, class_list, large_buckets, (uint32_t)n_buckets, bucket_entries, ss.entries,
+            ss.count, ss.start, ss.size, ss.bucket, ss.cap, overflow);
+        if (int e = check_launch("bucket_split_kernel")) return e;
+        const SubBuckets sub{ss.count, ss.start, ss.size, ss.bucket, ss.cap};
+        {
+            const int threads = 1024 / GSB_BUCKET_E;
+            const size_t smem = (size_t)threads * GSB_BUCKET_E * sizeof(uint64_t);
+            auto kern = sub_bucket_sort_kernel<GSB_BUCKET_E>;
+            if (int e = set_cta_smem((const void *)kern, smem)) return e;
+            kern<<<(unsigned)(16 * sms), threads, smem, side>>>(sub, ss.entries, (uint32_t)n_tiles, tb, isect_ids,
+                                                                flatten_ids);
+            if (int e = check_launch("sub_bucket_sort_kernel")) return e;
+        }
+        {
+            auto kern = bucket_radix_kernel<GSB_RADIX_MID>;
+            const size_t smem = RadixShape<GSB_RADIX_MID>::smem;
+            if (int e = set_cta_smem((const void *)kern, smem)) return e;
+            kern<<<(unsigned)(RadixShape<GSB_RADIX_MID>::per_sm * sms), RadixShape<GSB_RADIX_MID>::threads, smem,
+                   side>>>(offsets, bucket_sizes, class_list, 0, 0, ss.entries, (uint32_t)n_buckets,
+                           (uint32_t)n_tiles, tb, isect_ids, flatten_ids, sub, 1024, 4096);
+            if (int e = check_launch("bucket_radix_kernel")) return e;
+        }
+        {
+            auto kern = bucket_radix_kernel<GSB_RADIX_LARGE>;
+            const size_t smem = RadixShape<GSB_RADIX_LARGE>::smem;
+            if (int e = set_cta_smem((const void *)kern, smem)) return e;
+            kern<<<(unsigned)(RadixShape<GSB_RADIX_LARGE>::per_sm * sms), RadixShape<GSB_RADIX_LARGE>::threads,
+                   smem, side>>>(offsets, bucket_sizes, class_list, 0, 0, ss.entries, (uint32_t)n_buckets,
+                                 (uint32_t)n_tiles, tb, isect_ids, flatten_ids, sub, 4096, kBucketSortMax);
+            if (int e = check_launch("bucket_radix_kernel")) return e;
+        }
+    }
+    if (sstream != nullptr) {
+        cudaEventRecord(sstream->join, side);
+        cudaStreamWaitEvent(stream, sstream->join, 0);
         const cudaError_t ce = cudaGetLastError();
         if (ce != cudaSuccess) return set_error(kErrLaunch, "bucket sort stream join: %s", cudaGetErrorString(ce));
     }
     return kOk;
+}
+
+extern "C" int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
+                                     const int32_t *bucket_sizes, int max_count, int mid_buckets,
+                                     int large_buckets, const int32_t *class_list, const uint64_t *bucket_entries,
+                                     int64_t *isect_ids, int32_t *flatten_ids,
+                                     cudaStream_t stream) {
+    return bucket_sort(I, tile_width, tile_height, offsets, bucket_sizes, max_count, mid_buckets, large_buckets,
+                       class_list, bucket_entries, 0, nullptr, 0, nullptr, isect_ids, flatten_ids, stream);
+}
+
+extern "C" size_t gsb_isect_bucket_sort_scratch_bytes(long long n_isects) {
+    return split_scratch_layout(n_isects, nullptr, nullptr);
+}
+
+extern "C" int gsb_isect_bucket_sort_ex(int I, int tile_width, int tile_height, const int32_t *offsets,
+                                        const int32_t *bucket_sizes, int max_count, int mid_buckets,
+                                        int large_buckets, const int32_t *class_list,
+                                        const uint64_t *bucket_entries, long long n_isects, void *scratch,
+                                        size_t scratch_bytes, int *overflow, int64_t *isect_ids,
+                                        int32_t *flatten_ids, cudaStream_t stream) {
+    return bucket_sort(I, tile_width, tile_height, offsets, bucket_sizes, max_count, mid_buckets, large_buckets,
+                       class_list, bucket_entries, n_isects, scratch, scratch_bytes, overflow, isect_ids,
+                       flatten_ids, stream);
 }

@@ -127,6 +127,8 @@ SIGNATURES = {
     "gsb_peer_recv_grads": (I32, [P, ctypes.c_ulonglong, I64, P, I32, P, P, P]),
     "gsb_exchange_ids": (I32, [I64, P, P, P, I32, P, P, P, P]),
     "gsb_isect_bucket_sort": (I32, [I32, I32, I32, P, P, I32, I32, I32, P, P, P, P, P]),
+    "gsb_isect_bucket_sort_scratch_bytes": (SZ, [I64]),
+    "gsb_isect_bucket_sort_ex": (I32, [I32, I32, I32, P, P, I32, I32, I32, P, P, I64, P, SZ, P, P, P, P]),
     "gsb_rasterize_fwd": (
         I32,
         [I32, I32, P, P, P, P, P, P, I32, I32, I32, I32, I32, P, P, I64, P, P, P, P],

@@ -721,15 +721,27 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
     flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
     if n_isects == 0:
         return isect_ids, flatten_ids, offsets, nnz
+    bucket_entries = torch.empty(n_isects, dtype=torch.int64, device=dev)
+    call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_entries), stream)
     if largest <= _B.lib().gsb_isect_bucket_sort_max():
-        bucket_entries = torch.empty(n_isects, dtype=torch.int64, device=dev)
-        call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_entries), stream)
         call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
              mid_buckets, large_buckets, ptr(class_list), ptr(bucket_entries), ptr(isect_ids),
              ptr(flatten_ids), stream)
         return isect_ids, flatten_ids, offsets, nnz
-    # a bucket too large for the on-chip sort: emit in splat order and sort
-    # globally (stable LSD radix sort)
+    # buckets above the on-chip maximum: split on the device into sub-buckets
+    # by their leading (depth, index) bits, each sorted on chip; one more host
+    # read tells whether a sub-bucket was still too large (many equal depths)
+    nbytes = _B.lib().gsb_isect_bucket_sort_scratch_bytes(n_isects)
+    split_scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+    call("gsb_isect_bucket_sort_ex", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
+         mid_buckets, large_buckets, ptr(class_list), ptr(bucket_entries), n_isects, ptr(split_scratch), nbytes,
+         ptr(overflow), ptr(isect_ids), ptr(flatten_ids), stream)
+    del bucket_entries, split_scratch
+    if not int(overflow.item()):
+        return isect_ids, flatten_ids, offsets, nnz
+    # a run of equal depths too large for the on-chip sort: emit in splat order
+    # and sort globally (stable LSD radix sort)
     n_live = tiles_per_gauss.numel() if nnz is None else nnz
     cum = _scan_i32(tiles_per_gauss.view(-1)[:n_live])
     call("gsb_isect_emit", *args, ptr(cum), ptr(isect_ids), ptr(flatten_ids), stream)

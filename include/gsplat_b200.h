@@ -316,6 +316,23 @@ GSB_API int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const 
                                   const int32_t *bucket_sizes, int max_count, int mid_buckets,
                                   int large_buckets, const int32_t *class_list, const uint64_t *bucket_entries,
                                   int64_t *isect_ids, int32_t *flatten_ids, cudaStream_t stream);
+/* Same as gsb_isect_bucket_sort, also for buckets above gsb_isect_bucket_sort_max()
+ * entries: each is split on the device into sub-buckets of its leading (depth,
+ * splat index) bits, which then take the on-chip sorts. scratch:
+ * gsb_isect_bucket_sort_scratch_bytes(n_isects) bytes (used only when
+ * max_count is above the on-chip maximum). overflow (device int32, written on
+ * that path only) is set to 1 when a sub-bucket is still above the on-chip
+ * maximum (more entries with the same depth than fit on chip): the outputs are
+ * then incomplete and the caller sorts with the global path (gsb_isect_emit +
+ * gsb_radix_sort_pairs). Together they replace the cub radix sort of
+ * IntersectTile.cu:478-521 for such buckets. */
+GSB_API size_t gsb_isect_bucket_sort_scratch_bytes(long long n_isects);
+GSB_API int gsb_isect_bucket_sort_ex(int I, int tile_width, int tile_height, const int32_t *offsets,
+                                     const int32_t *bucket_sizes, int max_count, int mid_buckets,
+                                     int large_buckets, const int32_t *class_list,
+                                     const uint64_t *bucket_entries, long long n_isects, void *scratch,
+                                     size_t scratch_bytes, int *overflow, int64_t *isect_ids,
+                                     int32_t *flatten_ids, cudaStream_t stream);
 
 /* --- Rasterization --------------------------------------------------------
  * Replaces gsplat::rasterize_to_pixels_3dgs_fwd (Rasterization.cpp:42-119).

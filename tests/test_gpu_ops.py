@@ -318,6 +318,7 @@ def _entry_points_called(fn):
 
 @pytest.mark.parametrize("mode", ["spread", "many_buckets", "cluster_mid_ties", "cluster_mid_distinct",
                                   "cluster_mid_equal", "cluster_on_chip", "cluster_large_distinct",
+                                  "cluster_split", "cluster_split_distinct", "cluster_split_equal",
                                   "cluster_fallback"])
 def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     """Tile-bucket sort against the oracle's stable global sort, with many equal
@@ -326,15 +327,19 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     cluster_mid_* fill buckets of 1024 to 4096 entries with 8 distinct depths
     (radix passes), all-distinct depths (one-pass bin sort) and one depth;
     cluster_on_chip (8 depths) and cluster_large_distinct stay within the on-chip
-    bucket sort with buckets above 4096 entries,
-    cluster_fallback exceeds it and must switch to the global radix sort with the
-    same result."""
+    bucket sort with buckets above 4096 entries; cluster_split* exceed it (8
+    depths, distinct depths, one depth) and are split on the device into
+    sub-buckets by their leading (depth, index) bits; cluster_fallback puts more
+    entries than fit on chip on one depth far from the bucket's other depth, so
+    one sub-bucket is still too large and the global radix sort must take over,
+    with the same result."""
     from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
 
     rng = np.random.default_rng(31 + len(mode))
     I, W, H = 2, 320, 240
     ts = 2 if mode == "many_buckets" else 16  # 2 x 160 x 120 buckets: the global-shard path
     N = {"spread": 6000, "many_buckets": 6000, "cluster_on_chip": 9000, "cluster_large_distinct": 9000,
+         "cluster_split": 20000, "cluster_split_distinct": 20000, "cluster_split_equal": 20000,
          "cluster_fallback": 20000}.get(mode, 3000)
     tw, th = math.ceil(W / ts), math.ceil(H / ts)
     if mode.startswith("cluster"):
@@ -346,10 +351,13 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
         m2 = np.stack([rng.uniform(-20, W + 20, (I, N)), rng.uniform(-20, H + 20, (I, N))], -1)
         r = rng.integers(0, 6 if mode == "many_buckets" else 40, (I, N, 2)).astype(np.int32)
     dep = rng.integers(1, 9, (I, N)).astype(np.float32) * 0.5  # 8 distinct depths
-    if mode in ("cluster_mid_distinct", "cluster_large_distinct"):
+    if mode in ("cluster_mid_distinct", "cluster_large_distinct", "cluster_split_distinct"):
         dep = (1.0 + rng.permutation(I * N) / 1024.0).reshape(I, N).astype(np.float32)
-    elif mode == "cluster_mid_equal":
+    elif mode in ("cluster_mid_equal", "cluster_split_equal"):
         dep = np.full((I, N), 2.0, np.float32)
+    elif mode == "cluster_fallback":
+        dep = np.full((I, N), 2.0, np.float32)
+        dep[:, ::4096] = 900.0  # a few far depths: the range's leading bits are the depth's
     m2 = m2.astype(np.float32)
     (tpg, keys, ids, off), names = _entry_points_called(lambda: isect_tiles_with_offsets(
         torch.from_numpy(m2).to(DEV), torch.from_numpy(r).to(DEV), torch.from_numpy(dep).to(DEV), ts, tw, th))
@@ -359,10 +367,12 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     assert_equal(ids, eids, "flatten_ids")
     assert_equal(off, O.isect_offset_encode(ekeys, I, tw, th), "offsets")
     fallback = mode == "cluster_fallback"
+    split = mode.startswith("cluster_split") or fallback
     assert ("gsb_radix_sort_pairs" in names) == fallback, names
-    assert ("gsb_isect_bucket_sort" in names) != fallback, names
+    assert ("gsb_isect_bucket_sort_ex" in names) == split, names
+    assert ("gsb_isect_bucket_sort" in names) == (not split), names
     largest = np.bincount(ekeys >> 32).max()
-    if fallback:
+    if split:
         assert largest > gsb_lib().gsb_isect_bucket_sort_max()
     elif mode in ("cluster_on_chip", "cluster_large_distinct"):
         assert 4096 < largest <= gsb_lib().gsb_isect_bucket_sort_max()
