@@ -719,7 +719,11 @@ def run_gsb(args):
         t_bwd = raster_ms["gsb_rasterize_bwd_ex"] / 1e3
         cdim = 4 if mode["render_mode"] == "RGB+ED" else 3
         fpp = flop_per_pair(cdim)
-        achieved = fpp["bwd"] * pairs / t_bwd / 1e12
+        # the algorithmic unit of the survey's roofline table: every (pixel,
+        # splat) pair a per-pixel rasterizer evaluates, i.e. the tile list up to
+        # each pixel's last contributor (walked pairs)
+        achieved = fpp["bwd"] * walked / t_bwd / 1e12
+        achieved_contrib = fpp["bwd"] * pairs / t_bwd / 1e12
         traffic = ncu_traffic("raster_bwd_config1")
         roofline = {"kernel": f"raster_bwd_kernel<{cdim},4>", "bound": "fp32", "achieved": achieved,
                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
@@ -727,13 +731,17 @@ def run_gsb(args):
                     "peak_source": "measured FP32 FMA probe (gsb_fp32_fma_probe) on this GPU; "
                                    "the kernel is FP32-issue bound (no tensor-core contraction, "
                                    "DRAM ~1%), so neither MEASURED_PEAKS figure applies",
-                    "algorithmic": f"{fpp['bwd']} FLOP per contributing (pixel, splat) pair; "
-                                   f"{pairs} pairs per launch",
-                    "walked_pairs": walked,
-                    "walked_note": "(pixel, splat) pairs up to each pixel's last contributor, the unit "
-                                   "a per-pixel rasterizer evaluates; this kernel culls most of them "
-                                   "before any arithmetic, so the contributing pairs are the unit",
-                    "fwd": {"achieved": fpp["fwd"] * pairs /
+                    "algorithmic": f"{fpp['bwd']} FLOP per evaluated (pixel, splat) pair; {walked} pairs per "
+                                   "launch: each pixel's tile list up to its last contributor",
+                    "contributing_pairs": pairs,
+                    "achieved_contributing": achieved_contrib,
+                    "frac_contributing": achieved_contrib / peak,
+                    "contributing_note": "the stricter unit: only the pairs that pass the alpha test before "
+                                         "each pixel's transmittance stop (this kernel culls most of the "
+                                         "others before any arithmetic)",
+                    "fwd": {"achieved": fpp["fwd"] * walked /
+                            (raster_ms["gsb_rasterize_fwd_ex"] / 1e3) / 1e12,
+                            "achieved_contributing": fpp["fwd"] * pairs /
                             (raster_ms["gsb_rasterize_fwd_ex"] / 1e3) / 1e12,
                             "unit": "TFLOP/s"}}
         hbm_peak = measured_hbm_gbs()

@@ -35,7 +35,7 @@
 
 // Compile-time choices of the backward kernel (defaults are the tuned ones).
 #ifndef GSB_BWD_MINB
-#define GSB_BWD_MINB 12
+#define GSB_BWD_MINB 14
 #endif
 #ifndef GSB_BWD_MINB_SMALL
 #define GSB_BWD_MINB_SMALL 1
@@ -50,7 +50,10 @@
 
 namespace gsb {
 
-constexpr int kBatch = 256;
+#ifndef GSB_RAST_BATCH
+#define GSB_RAST_BATCH 128
+#endif
+constexpr int kBatch = GSB_RAST_BATCH; // splats staged per batch
 
 struct RasterParams {
     uint32_t I, n_isects;
