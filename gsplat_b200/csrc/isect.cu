@@ -492,121 +492,10 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
 }
 
 constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (1024 threads x 16 entries)
-#ifndef GSB_BUCKET_E
-#define GSB_BUCKET_E 8 // entries per thread of the bitonic sort (buckets of up to 1024 entries)
-#endif
-
-
-// Bitonic compare-exchange of entries held in registers. Entry index i =
-// threadIdx.x * E + e (blocked: thread t owns E consecutive entries); the
-// network stage (k, j) pairs i with i ^ j, ascending where (i & k) == 0.
-//   j <  E       : both entries are in the same thread (register exchange);
-//   j <  32 E    : the partner is lane ^ (j / E) of the same warp (shuffle);
-//   j >= 32 E    : the partner is in another warp; these stages run on the
-//                  shared-memory copy between two block barriers.
-template <int E> struct BitonicRegs {
-    uint64_t v[E];
-
-    template <int J> __device__ __forceinline__ void reg_stage(uint32_t base, uint32_t k) {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-            if (e & J) continue;
-            const uint64_t a = v[e], b = v[e + J];
-            const bool asc = ((base + e) & k) == 0;
-            const bool swap = (a > b) == asc;
-            v[e] = swap ? b : a;
-            v[e + J] = swap ? a : b;
-        }
-    }
-
-    __device__ __forceinline__ void shfl_stage(uint32_t base, uint32_t k, uint32_t j) {
-        const int lane_mask = (int)(j / E);
-        // base is a multiple of E <= j < k: bits j and k of base + e are those of
-        // base, so every entry of the thread keeps the same side
-        const bool keep_min = (((base & j) == 0) == ((base & k) == 0));
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-            const uint64_t other = __shfl_xor_sync(0xffffffffu, v[e], lane_mask);
-            const bool other_smaller = other < v[e];
-            v[e] = (other_smaller == keep_min) ? other : v[e];
-        }
-    }
-};
-
-// One CTA per bucket: entries packed as (depth bits << 32 | splat index),
-// padded with all-ones to a power of two, sorted ascending.
-template <int E>
-__device__ __forceinline__ void sort_one_bucket(uint64_t *sk, uint32_t b, int n, int start,
-                                                const uint64_t *__restrict__ entries, uint32_t n_tiles,
-                                                uint32_t tile_bits, int64_t *__restrict__ keys_out,
-                                                int32_t *__restrict__ ids_out) {
-    const int64_t hi = ((int64_t)(b / n_tiles) << (32 + tile_bits)) | ((int64_t)(b % n_tiles) << 32);
-    if (n == 1) {
-        if (threadIdx.x == 0) {
-            keys_out[start] = hi | (int64_t)(entries[start] >> 32);
-            ids_out[start] = (int32_t)(uint32_t)entries[start];
-        }
-        return;
-    }
-    uint32_t npad = 2;
-    while (npad < (uint32_t)n) npad <<= 1;
-    const uint32_t base = threadIdx.x * E;
-    BitonicRegs<E> r;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const uint32_t i = base + e;
-        r.v[e] = i < (uint32_t)n ? entries[start + i] : ~0ull;
-    }
-    const uint32_t nthreads = blockDim.x;
-    // warps whose entries all lie beyond npad (a bucket smaller than the largest)
-    // hold padding only; they join the block barriers and nothing else
-    const bool warp_active = (threadIdx.x & ~31u) * E < npad;
-    for (uint32_t k = 2; k <= npad; k <<= 1) {
-        uint32_t j = k >> 1;
-        if (j >= 32u * E) {
-            // cross-warp stages through shared memory
-#pragma unroll
-            for (int e = 0; e < E; ++e) sk[base + e] = r.v[e];
-            __syncthreads();
-            for (; j >= 32u * E; j >>= 1) {
-                uint32_t lj = 31 - __clz(j);
-                for (uint32_t q = threadIdx.x; q < npad / 2; q += nthreads) {
-                    const uint32_t i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
-                    const uint64_t a = sk[i], c = sk[i + j];
-                    const bool asc = (i & k) == 0;
-                    if ((a > c) == asc) {
-                        sk[i] = c;
-                        sk[i + j] = a;
-                    }
-                }
-                __syncthreads();
-            }
-#pragma unroll
-            for (int e = 0; e < E; ++e) r.v[e] = sk[base + e];
-            __syncthreads(); // the copy is reused by the next k
-        }
-        if (!warp_active) continue; // only padding: nothing to exchange
-        for (; j >= (uint32_t)E; j >>= 1) r.shfl_stage(base, k, j);
-        // j = min(k / 2, E / 2): the in-thread stages, unrolled with constant distances
-        if (E >= 16 && j >= 8) r.template reg_stage<(E >= 16 ? 8 : 1)>(base, k);
-        if (E >= 8 && j >= 4) r.template reg_stage<(E >= 8 ? 4 : 1)>(base, k);
-        if (j >= 2) r.template reg_stage<2>(base, k);
-        r.template reg_stage<1>(base, k);
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const uint32_t i = base + e;
-        if (i < (uint32_t)n) {
-            keys_out[start + i] = hi | (int64_t)(r.v[e] >> 32);
-            ids_out[start + i] = (int32_t)(uint32_t)r.v[e];
-        }
-    }
-}
-
 // Buckets above kBucketSortMax entries are first split into sub-buckets by
 // the leading bits of their entries (depth bits << 32 | splat index: the order
 // of the final sort), written in sub-bucket order to a second array; every
-// sub-bucket then goes through the on-chip sorts above like a bucket of its own,
+// sub-bucket then goes through the on-chip sort below like a bucket of its own,
 // at its final position. The list of sub-buckets lives on the device.
 struct SubBuckets {
     const int *count;    // number of sub-buckets (device); null: not a sub-bucket pass
@@ -753,41 +642,9 @@ __global__ void __launch_bounds__(kSplitThreads)
     }
 }
 
-// The bitonic on-chip sort of sub-buckets of up to 1024 entries (persistent
-// over the device list of sub-buckets; larger ones are left to the radix kernels).
-template <int E>
-__global__ void __launch_bounds__(1024)
-    sub_bucket_sort_kernel(const SubBuckets sub, const uint64_t *__restrict__ entries, uint32_t n_tiles,
-                           uint32_t tile_bits, int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
-    extern __shared__ __align__(16) uint64_t sk[];
-    const int count = min(*sub.count, sub.cap);
-    for (int c = blockIdx.x; c < count; c += gridDim.x) {
-        const int n = sub.size[c];
-        if (n > 1024) continue;
-        sort_one_bucket<E>(sk, (uint32_t)sub.bucket[c], n, sub.start[c], entries, n_tiles, tile_bits, keys_out,
-                           ids_out);
-        __syncthreads(); // the shared copy is reused by the next sub-bucket
-    }
-}
-
-template <int E>
-__global__ void __launch_bounds__(1024)
-    bucket_sort_kernel(const int32_t *__restrict__ starts, const int32_t *__restrict__ sizes,
-                       const uint64_t *__restrict__ entries,
-                       uint32_t n_buckets, uint32_t n_tiles, uint32_t tile_bits, int lo_size, int hi_size,
-                       int64_t *__restrict__ keys_out, int32_t *__restrict__ ids_out) {
-    extern __shared__ __align__(16) uint64_t sk[];
-    // CTA c sorts the buckets c, c + grid, ... of (lo_size, hi_size] entries
-    // (launched with one CTA per bucket)
-    for (uint32_t b = blockIdx.x; b < n_buckets; b += gridDim.x) {
-        const int n = sizes[b];
-        if (n <= lo_size || n > hi_size) continue; // another size class
-        sort_one_bucket<E>(sk, b, n, starts[b], entries, n_tiles, tile_bits, keys_out, ids_out);
-    }
-}
-
-
-// Buckets of more than 1024 entries: stable LSD radix sort in shared memory.
+// The on-chip sort of one bucket (or sub-bucket) per CTA: stable LSD radix sort
+// in shared memory, in three shapes by bucket size (256 threads x 4 entries up
+// to 1024, 256 x 16 up to 4096, 512 x 32 up to kBucketSortMax).
 // The keys are the depth bits minus the bucket's smallest, so only the bits
 // of the bucket's depth range are sorted, in as few passes of at most DBITS
 // bits as cover them (three for the usual 25-bit range at DBITS = 9): O(n) per
@@ -858,6 +715,7 @@ __global__ void __launch_bounds__(THREADS, MINB)
     const int cbase = PER >= NW ? t * (PER / NW) * CW : (PER * t / NW) * CW + (PER * t) % NW;
     // the buckets of this size class: list[0, count) or list[n_buckets - count,
     // n_buckets); or, with sub.count set, the sub-buckets of split buckets
+    // (list == nullptr: every bucket, filtered by size)
     if (sub.count != nullptr) count = min(*sub.count, sub.cap);
     for (int c = blockIdx.x; c < count; c += gridDim.x) {
         uint32_t b, hb;
@@ -868,7 +726,7 @@ __global__ void __launch_bounds__(THREADS, MINB)
             start = sub.start[c];
             hb = (uint32_t)sub.bucket[c];
         } else {
-            b = (uint32_t)list[from_back ? (int)n_buckets - 1 - c : c];
+            b = list == nullptr ? (uint32_t)c : (uint32_t)list[from_back ? (int)n_buckets - 1 - c : c];
             n = sizes[b];
             start = starts[b];
             hb = b;
@@ -1212,6 +1070,10 @@ __global__ void __launch_bounds__(THREADS, MINB)
 #define GSB_RADIX_LARGE_B 1
 #endif
 #define GSB_RADIX_MID GSB_RADIX_MID_T, GSB_RADIX_MID_R, GSB_RADIX_MID_D, GSB_RADIX_MID_B
+#ifndef GSB_RADIX_SMALL_B
+#define GSB_RADIX_SMALL_B 6
+#endif
+#define GSB_RADIX_SMALL 256, 4, 9, GSB_RADIX_SMALL_B
 #define GSB_RADIX_LARGE GSB_RADIX_LARGE_T, GSB_RADIX_LARGE_R, GSB_RADIX_LARGE_D, GSB_RADIX_LARGE_B
 
 template <int THREADS, int RMAX, int DBITS, int MINB> struct RadixShape {
@@ -1511,23 +1373,20 @@ static int bucket_sort(int I, int tile_width, int tile_height, const int32_t *of
     if (n_buckets == 0 || max_count <= 0) return kOk;
     if (n_buckets > 0x7fffffffull) return set_error(kErrInvalidArgument, "too many buckets");
     const uint32_t tb = bit_length(n_tiles);
-    // Buckets of up to 1024 entries (most of them): one CTA per bucket, bitonic
-    // network in registers and shared memory; a CTA whose bucket is larger
-    // returns at once. Larger buckets: the radix kernels over the class lists,
-    // 256 threads x 16 entries up to 4096 entries, 1024 x 16 above, on a side
-    // stream next to the first class (forked from and joined back to the
-    // caller's stream with events).
+    // Buckets of up to 1024 entries (most of them): one CTA (256 threads x 4
+    // entries) per bucket; a CTA whose bucket is larger returns at once. Larger
+    // buckets: the same sort in larger shapes over the class lists, 256 threads
+    // x 16 entries up to 4096 entries, 512 x 32 above, on a side stream next to
+    // the first class (forked from and joined back to the caller's stream with
+    // events).
     {
-        int npad = 2;
-        while (npad < std::min(max_count, 1024)) npad <<= 1;
-        const int threads = npad / GSB_BUCKET_E < 32 ? 32 : npad / GSB_BUCKET_E;
-        const size_t smem = (size_t)threads * GSB_BUCKET_E * sizeof(uint64_t);
-        auto kern = bucket_sort_kernel<GSB_BUCKET_E>;
+        auto kern = bucket_radix_kernel<GSB_RADIX_SMALL>;
+        const size_t smem = RadixShape<GSB_RADIX_SMALL>::smem;
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
-        kern<<<(unsigned)n_buckets, threads, smem, stream>>>(offsets, bucket_sizes, bucket_entries,
-                                                             (uint32_t)n_buckets, (uint32_t)n_tiles, tb, 0, 1024,
-                                                             isect_ids, flatten_ids);
-        if (int e = check_launch("bucket_sort_kernel")) return e;
+        kern<<<(unsigned)n_buckets, RadixShape<GSB_RADIX_SMALL>::threads, smem, stream>>>(
+            offsets, bucket_sizes, nullptr, (int)n_buckets, 0, bucket_entries, (uint32_t)n_buckets,
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids, SubBuckets{}, 0, 1024);
+        if (int e = check_launch("bucket_radix_kernel")) return e;
     }
     if (mid_buckets < 0 || large_buckets < 0 || (uint64_t)mid_buckets + (uint64_t)large_buckets > n_buckets)
         return set_error(kErrInvalidArgument, "bad size class counts %d, %d", mid_buckets, large_buckets);
@@ -1578,13 +1437,13 @@ static int bucket_sort(int I, int tile_width, int tile_height, const int32_t *of
         if (int e = check_launch("bucket_split_kernel")) return e;
         const SubBuckets sub{ss.count, ss.start, ss.size, ss.bucket, ss.cap};
         {
-            const int threads = 1024 / GSB_BUCKET_E;
-            const size_t smem = (size_t)threads * GSB_BUCKET_E * sizeof(uint64_t);
-            auto kern = sub_bucket_sort_kernel<GSB_BUCKET_E>;
+            auto kern = bucket_radix_kernel<GSB_RADIX_SMALL>;
+            const size_t smem = RadixShape<GSB_RADIX_SMALL>::smem;
             if (int e = set_cta_smem((const void *)kern, smem)) return e;
-            kern<<<(unsigned)(16 * sms), threads, smem, side>>>(sub, ss.entries, (uint32_t)n_tiles, tb, isect_ids,
-                                                                flatten_ids);
-            if (int e = check_launch("sub_bucket_sort_kernel")) return e;
+            kern<<<(unsigned)(RadixShape<GSB_RADIX_SMALL>::per_sm * sms), RadixShape<GSB_RADIX_SMALL>::threads, smem,
+                   side>>>(offsets, bucket_sizes, nullptr, 0, 0, ss.entries, (uint32_t)n_buckets,
+                           (uint32_t)n_tiles, tb, isect_ids, flatten_ids, sub, 0, 1024);
+            if (int e = check_launch("bucket_radix_kernel")) return e;
         }
         {
             auto kern = bucket_radix_kernel<GSB_RADIX_MID>;
