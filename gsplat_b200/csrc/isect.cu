@@ -492,6 +492,13 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
 }
 
 constexpr int kBucketSortMax = 16384; // largest bucket sorted on chip (1024 threads x 16 entries)
+#ifndef GSB_SPLIT_MIN
+#define GSB_SPLIT_MIN 16384
+#endif
+// buckets above kSplitMin entries are split into sub-buckets (kSplitMin >= 4096:
+// the split walks the class list of buckets above 4096 entries)
+constexpr int kSplitMin = GSB_SPLIT_MIN;
+static_assert(kSplitMin >= 4096 && kSplitMin <= kBucketSortMax, "split threshold");
 // Buckets above kBucketSortMax entries are first split into sub-buckets by
 // the leading bits of their entries (depth bits << 32 | splat index: the order
 // of the final sort), written in sub-bucket order to a second array; every
@@ -531,7 +538,7 @@ __global__ void __launch_bounds__(kSplitThreads)
     for (int c = blockIdx.x; c < count; c += gridDim.x) {
         const uint32_t b = (uint32_t)list[(int)n_buckets - 1 - c];
         const int n = sizes[b];
-        if (n <= kBucketSortMax) continue;
+        if (n <= kSplitMin) continue;
         const int start = starts[b];
         unsigned long long lo = ~0ull, hi = 0ull;
         for (int i = t; i < n; i += kSplitThreads) {
@@ -1313,7 +1320,7 @@ extern "C" int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const in
     return check_launch("isect_bucket_emit_kernel");
 }
 
-extern "C" int gsb_isect_bucket_sort_max(void) { return kBucketSortMax; }
+extern "C" int gsb_isect_bucket_sort_max(void) { return kSplitMin; }
 
 // Scratch of the split path for buckets above kBucketSortMax entries: the
 // sub-bucket count, the entries in sub-bucket order and the sub-bucket records
@@ -1330,7 +1337,7 @@ static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 static size_t split_scratch_layout(long long n_isects, char *base, SplitScratch *ss) {
     const size_t n = n_isects > 0 ? (size_t)n_isects : 0;
-    const size_t cap = n / (kBucketSortMax / (1 << kSplitBits)) + 4096;
+    const size_t cap = n / (kSplitMin / (1 << kSplitBits)) + 4096;
     size_t off = 0;
     const size_t o_count = off;
     off += 256;
@@ -1360,7 +1367,7 @@ static int bucket_sort(int I, int tile_width, int tile_height, const int32_t *of
                        int32_t *flatten_ids, cudaStream_t stream) {
     const uint64_t n_tiles = (uint64_t)tile_width * (uint64_t)tile_height;
     const uint64_t n_buckets = (uint64_t)I * n_tiles;
-    const bool split = max_count > kBucketSortMax;
+    const bool split = max_count > kSplitMin;
     SplitScratch ss = {};
     if (split) {
         if (scratch == nullptr || overflow == nullptr)
@@ -1422,7 +1429,7 @@ static int bucket_sort(int I, int tile_width, int tile_height, const int32_t *of
         if (int e = set_cta_smem((const void *)kern, smem)) return e;
         kern<<<(unsigned)std::min(large_buckets, RadixShape<GSB_RADIX_LARGE>::per_sm * sms), threads, smem, side>>>(
             offsets, bucket_sizes, class_list, large_buckets, 1, bucket_entries, (uint32_t)n_buckets,
-            (uint32_t)n_tiles, tb, isect_ids, flatten_ids, SubBuckets{}, 4096, kBucketSortMax);
+            (uint32_t)n_tiles, tb, isect_ids, flatten_ids, SubBuckets{}, 4096, kSplitMin);
         if (int e = check_launch("bucket_radix_kernel")) return e;
     }
     if (split && large_buckets > 0) {

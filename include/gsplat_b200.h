@@ -306,11 +306,11 @@ GSB_API int gsb_isect_bucket_emit(int packed, int I, int N, int nnz, const int64
                                   uint64_t *bucket_entries, cudaStream_t stream);
 /* 4. Sort every bucket and write isect_ids int64 / flatten_ids int32
  *    [n_isects]. max_count (totals[1] of step 2) must not exceed
- *    gsb_isect_bucket_sort_max(); larger buckets take the global-sort path.
+ *    gsb_isect_bucket_sort_max(); larger buckets take gsb_isect_bucket_sort_ex.
  *    mid_buckets / large_buckets / class_list: totals[3] / totals[4] and the
- *    class list of step 2 (buckets of up to 1024 entries are sorted by a
- *    bitonic network, larger ones by a radix sort in shared memory walking
- *    the list). */
+ *    class list of step 2 (every bucket is sorted by a radix sort in shared
+ *    memory, one CTA per bucket; buckets above 1024 entries by larger CTAs
+ *    walking the list). */
 GSB_API int gsb_isect_bucket_sort_max(void);
 GSB_API int gsb_isect_bucket_sort(int I, int tile_width, int tile_height, const int32_t *offsets,
                                   const int32_t *bucket_sizes, int max_count, int mid_buckets,
