@@ -517,10 +517,21 @@ def measure_sharded(args, dev, rank, world, distributed):
     exchange = None
     if distributed:
         exchange = "peer memory" if os.environ.get("GSB_PEER_EXCHANGE", "1") != "0" else "nccl all_to_all"
+    # per-entry-point device time of this rank, from two instrumented steps after
+    # the timed ones (the exchange entry points include waiting for the others)
+    from gsplat_b200.cuda import _backend
+
+    _backend.timing = {}
+    for i in range(2):
+        train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
+    barrier()
+    ops = {name: round(sum(a.elapsed_time(b) for a, b in evs) / 2, 3) for name, evs in _backend.timing.items()}
+    _backend.timing = None
     out = {"workload": WORKLOADS["config4"], "value": mpix / (ms / 1e3), "unit": "MPix/s",
            "ms_per_step": ms, "steps": steps, "warmup": warm, "scaling": "strong",
            "gaussians_per_rank": n, "cameras_per_rank": n_cams, "n_isects_job": int(n_isects.item()),
-           "exchange": exchange, "timing": "CUDA events over the timed steps, max over ranks"}
+           "exchange": exchange, "timing": "CUDA events over the timed steps, max over ranks",
+           "ops_ms_rank0": ops}
     del params, opt, bank, meta, loss
     torch.cuda.empty_cache()
     return out
@@ -803,6 +814,7 @@ def run_gsb(args):
         "ops_source": (f"CUDA events around every entry point over {n_ops_steps} further steps after the "
                        "timed region; ms_per_step_timed_region: the rasterizer inside it"),
         "host_issue_ms_per_step": host_ms,
+        "host_cpus": len(os.sched_getaffinity(0)),
     }
     if rank == 0:
         print(json.dumps(result), flush=True)
