@@ -500,11 +500,18 @@ def measure_sharded(args, dev, rank, world, distributed):
     barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    mem0 = torch.cuda.memory_stats(dev)
+    wall0 = time.perf_counter()
     start.record()
     for i in range(steps):
         loss, meta = train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
     end.record()
+    host_ms = (time.perf_counter() - wall0) * 1e3 / steps
     barrier()
+    mem1 = torch.cuda.memory_stats(dev)
+    # device allocations (cudaMalloc) and allocator retries inside the timed steps
+    alloc = {k: mem1.get(k, 0) - mem0.get(k, 0) for k in ("num_device_alloc", "num_device_free", "num_alloc_retries")}
+    alloc["peak_gb"] = round(mem1.get("allocated_bytes.all.peak", 0) / 2**30, 1)
     ms = start.elapsed_time(end) / steps
     if distributed:
         t = torch.tensor([ms], device=dev)
@@ -531,7 +538,7 @@ def measure_sharded(args, dev, rank, world, distributed):
            "ms_per_step": ms, "steps": steps, "warmup": warm, "scaling": "strong",
            "gaussians_per_rank": n, "cameras_per_rank": n_cams, "n_isects_job": int(n_isects.item()),
            "exchange": exchange, "timing": "CUDA events over the timed steps, max over ranks",
-           "ops_ms_rank0": ops}
+           "host_issue_ms_per_step": host_ms, "allocator": alloc, "ops_ms_rank0": ops}
     del params, opt, bank, meta, loss
     torch.cuda.empty_cache()
     return out
@@ -606,6 +613,7 @@ def run_gsb(args):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     barrier()
+    mem0 = torch.cuda.memory_stats(dev)
     wall0 = time.perf_counter()
     clock0 = time.time()
     start.record()
@@ -614,6 +622,8 @@ def run_gsb(args):
     end.record()
     host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
     barrier()
+    mem1 = torch.cuda.memory_stats(dev)
+    alloc = {k: mem1.get(k, 0) - mem0.get(k, 0) for k in ("num_device_alloc", "num_device_free", "num_alloc_retries")}
     clock1 = time.time()
     sampler.__exit__(None, None, None)
     ms = start.elapsed_time(end) / args.steps
@@ -814,6 +824,7 @@ def run_gsb(args):
         "ops_source": (f"CUDA events around every entry point over {n_ops_steps} further steps after the "
                        "timed region; ms_per_step_timed_region: the rasterizer inside it"),
         "host_issue_ms_per_step": host_ms,
+        "allocator": alloc,
         "host_cpus": len(os.sched_getaffinity(0)),
     }
     if rank == 0:

@@ -223,12 +223,9 @@ __device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
-// IL: the interleaved layout of the backward (4 pixels per thread, lane l owns
-// pixel l of each 8x4 quarter of its warp's 16x8 rows) with per-quarter culling.
-template <int CDIM, int BX, int BY, bool IL>
+template <int CDIM, int BX, int BY>
 __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     constexpr int PPT = BX * BY;
-    static_assert(!IL || PPT == 4, "interleaved layout: 4 pixels per thread");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const RasterSmem s = carve<CDIM>(smem_raw);
     const uint32_t image = blockIdx.y;
@@ -244,16 +241,9 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     float rx0 = 1e30f, rx1 = -1e30f, ry0 = 1e30f, ry1 = -1e30f;
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
-        uint32_t ly, lx;
-        if (IL) {
-            ly = warp * 8 + (k >> 1) * 4 + (lane >> 3);
-            lx = (k & 1) * 8 + (lane & 7);
-        } else {
-            // thread owns a BX x BY block of pixels; blocks are laid out row-major
-            const uint32_t tpr = p.tile_size / BX;
-            ly = (threadIdx.x / tpr) * BY + k / BX;
-            lx = (threadIdx.x % tpr) * BX + k % BX;
-        }
+        // thread owns a BX x BY block of pixels; blocks are laid out row-major
+        const uint32_t tpr = p.tile_size / BX;
+        const uint32_t ly = (threadIdx.x / tpr) * BY + k / BX, lx = (threadIdx.x % tpr) * BX + k % BX;
         const uint32_t i = ty0 + ly, j = tx0 + lx;
         inside[k] = ly < p.tile_size && i < p.H && j < p.W;
         px[k] = (float)j + 0.5f;
@@ -293,34 +283,15 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
             for (int i = threadIdx.x; i < nb; i += blockDim.x)
                 stage_splat<CDIM>(p, s, i, p.flatten_ids[bstart + i]);
             __syncthreads();
-            // per-warp list of splats that can touch this warp's live pixels,
-            // with the quarters they meet (bits 8..11 of each 16-bit entry)
+            // per-warp list of splats that can touch this warp's live pixels
             int cnt = 0;
-            uint16_t *mylist16 = reinterpret_cast<uint16_t *>(mylist);
             const bool warp_live = wr.any && !__all_sync(0xffffffffu, all_done);
             if (warp_live) {
-                const float qx0 = (float)tx0 + 0.5f, qy0 = (float)(ty0 + warp * 8) + 0.5f;
                 for (int base = 0; base < nb; base += 32) {
                     const int i = base + lane;
-                    uint32_t q = 0;
-                    if (i < nb) {
-                        const float4 bx = s.boxes[i];
-                        if (box_hits(bx, wr)) {
-                            if (IL) {
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    const float x0 = qx0 + (k & 1) * 8, y0 = qy0 + (k >> 1) * 4;
-                                    if (!(bx.y < x0 || bx.x > x0 + 7.f || bx.w < y0 || bx.z > y0 + 3.f))
-                                        q |= 1u << k;
-                                }
-                            } else {
-                                q = 0xfu;
-                            }
-                        }
-                    }
-                    const bool hit = q != 0;
+                    const bool hit = i < nb && box_hits(s.boxes[i], wr);
                     const uint32_t bal = __ballot_sync(0xffffffffu, hit);
-                    if (hit) mylist16[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(i | (q << 8));
+                    if (hit) mylist[cnt + __popc(bal & ((1u << lane) - 1u))] = (uint8_t)i;
                     cnt += __popc(bal);
                 }
             }
@@ -345,16 +316,13 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
 #pragma unroll
                 for (int k = 0; k < PPT; ++k) stop &= done[k];
                 if (stop) break;
-                const uint32_t ent = mylist16[li];
-                const int i = ent & 0xff;
-                const uint32_t qmask = ent >> 8;
+                const int i = mylist[li];
                 const SplatRec r = s.recs[i];
                 float col[CDIM];
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
 #pragma unroll
                 for (int k = 0; k < PPT; ++k) {
-                    if (IL && !(qmask & (1u << k))) continue;
                     if (done[k]) continue;
                     apply(k, eval_pair(r, px[k], py[k]), i, col);
                 }
@@ -679,9 +647,7 @@ static int launch_variant(bool fwd, const RasterParams &p, cudaStream_t stream) 
     const size_t smem = raster_smem_bytes<CDIM>(nt / 32);
     dim3 grid(p.tile_w * p.tile_h, p.I);
     if (fwd) {
-        constexpr bool kFwdIL = GSB_RAST_INTERLEAVE && BX * BY == 4;
-        auto kern = (kFwdIL && p.tile_size == 16) ? raster_fwd_kernel<CDIM, BX, BY, kFwdIL>
-                                                  : raster_fwd_kernel<CDIM, BX, BY, false>;
+        auto kern = raster_fwd_kernel<CDIM, BX, BY>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         kern<<<grid, nt, smem, stream>>>(p);
         return check_launch("raster_fwd_kernel");

@@ -688,6 +688,19 @@ def _isect_tiles(means2d, radii, depths, tile_size, tile_width, tile_height, sor
         return tiles_per_gauss, isect_ids, flatten_ids, offsets
 
 
+def _sized(n: int, dtype, dev) -> Tensor:
+    """An uninitialised 1-D tensor of n elements whose allocation is rounded up
+    to the next multiple of 1/16 of n's power of two (at most ~6% more). Buffers
+    sized by data-dependent counts (intersections, splats) change size a little
+    from step to step; rounded, successive steps request the same sizes and the
+    caching allocator serves them from its cache instead of new device
+    allocations (which synchronise the device, at multi-GB sizes for many ms)."""
+    if n <= 4096:
+        return torch.empty(n, dtype=dtype, device=dev)
+    step = 1 << max(0, n.bit_length() - 5)
+    return torch.empty((n + step - 1) // step * step, dtype=dtype, device=dev)[:n]
+
+
 def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream, nnz_device=None):
     """Sorted intersections through the tile-bucket path: per-splat and
     per-(image, tile) counts, bucket offsets, one host read of (n_isects, largest
@@ -717,11 +730,11 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
         nnz = None
     else:
         args = args[:3] + (nnz,) + args[4:]
-    isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
-    flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+    isect_ids = _sized(n_isects, torch.int64, dev)
+    flatten_ids = _sized(n_isects, torch.int32, dev)
     if n_isects == 0:
         return isect_ids, flatten_ids, offsets, nnz
-    bucket_entries = torch.empty(n_isects, dtype=torch.int64, device=dev)
+    bucket_entries = _sized(n_isects, torch.int64, dev)
     call("gsb_isect_bucket_emit", *args, n_isects, ptr(cursor), ptr(bucket_entries), stream)
     if largest <= _B.lib().gsb_isect_bucket_sort_max():
         call("gsb_isect_bucket_sort", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
@@ -732,7 +745,7 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
     # by their leading (depth, index) bits, each sorted on chip; one more host
     # read tells whether a sub-bucket was still too large (many equal depths)
     nbytes = _B.lib().gsb_isect_bucket_sort_scratch_bytes(n_isects)
-    split_scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    split_scratch = _sized(nbytes, torch.uint8, dev)
     overflow = torch.zeros(1, dtype=torch.int32, device=dev)
     call("gsb_isect_bucket_sort_ex", I, tile_width, tile_height, ptr(offsets), ptr(bucket_sizes), largest,
          mid_buckets, large_buckets, ptr(class_list), ptr(bucket_entries), n_isects, ptr(split_scratch), nbytes,
@@ -944,7 +957,7 @@ class _RasterizeToPixels(torch.autograd.Function):
         # the kernel accumulates with atomics: all gradients live in one zeroed
         # buffer (a single fill)
         likes = [means2d, conics, colors, opacities] + ([means2d] if ctx.absgrad else [])
-        flat = torch.zeros(sum(t.numel() for t in likes), dtype=means2d.dtype, device=means2d.device)
+        flat = _sized(sum(t.numel() for t in likes), means2d.dtype, means2d.device).zero_()
         views, off = [], 0
         for t in likes:
             views.append(flat[off:off + t.numel()].view(t.shape))
