@@ -501,12 +501,17 @@ def measure_sharded(args, dev, rank, world, distributed):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     mem0 = torch.cuda.memory_stats(dev)
+    from gsplat_b200.cuda import _backend
+
+    _backend.host_wait = [0.0, 0]
     wall0 = time.perf_counter()
     start.record()
     for i in range(steps):
         loss, meta = train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
     end.record()
     host_ms = (time.perf_counter() - wall0) * 1e3 / steps
+    host_blocked_ms = _backend.host_wait[0] * 1e3 / steps
+    _backend.host_wait = None
     barrier()
     mem1 = torch.cuda.memory_stats(dev)
     # device allocations (cudaMalloc) and allocator retries inside the timed steps
@@ -526,8 +531,6 @@ def measure_sharded(args, dev, rank, world, distributed):
         exchange = "peer memory" if os.environ.get("GSB_PEER_EXCHANGE", "1") != "0" else "nccl all_to_all"
     # per-entry-point device time of this rank, from two instrumented steps after
     # the timed ones (the exchange entry points include waiting for the others)
-    from gsplat_b200.cuda import _backend
-
     _backend.timing = {}
     for i in range(2):
         train_step(params, opt, viewmat, K, W, H, *bank[i % 2], distributed, True, mode)
@@ -538,7 +541,8 @@ def measure_sharded(args, dev, rank, world, distributed):
            "ms_per_step": ms, "steps": steps, "warmup": warm, "scaling": "strong",
            "gaussians_per_rank": n, "cameras_per_rank": n_cams, "n_isects_job": int(n_isects.item()),
            "exchange": exchange, "timing": "CUDA events over the timed steps, max over ranks",
-           "host_issue_ms_per_step": host_ms, "allocator": alloc, "ops_ms_rank0": ops}
+           "host_issue_ms_per_step": host_ms, "host_blocked_ms_per_step": host_blocked_ms,
+           "allocator": alloc, "ops_ms_rank0": ops}
     del params, opt, bank, meta, loss
     torch.cuda.empty_cache()
     return out
@@ -614,6 +618,7 @@ def run_gsb(args):
     end = torch.cuda.Event(enable_timing=True)
     barrier()
     mem0 = torch.cuda.memory_stats(dev)
+    _backend.host_wait = [0.0, 0]
     wall0 = time.perf_counter()
     clock0 = time.time()
     start.record()
@@ -621,6 +626,10 @@ def run_gsb(args):
         loss, meta = train_step(params, opt, viewmat, K, W, H, *grads(), distributed, packed, mode)
     end.record()
     host_ms = (time.perf_counter() - wall0) * 1e3 / args.steps
+    # host time blocked in the step's size reads (waiting for the device)
+    host_blocked_ms = _backend.host_wait[0] * 1e3 / args.steps
+    host_reads = _backend.host_wait[1] / args.steps
+    _backend.host_wait = None
     barrier()
     mem1 = torch.cuda.memory_stats(dev)
     alloc = {k: mem1.get(k, 0) - mem0.get(k, 0) for k in ("num_device_alloc", "num_device_free", "num_alloc_retries")}
@@ -824,6 +833,8 @@ def run_gsb(args):
         "ops_source": (f"CUDA events around every entry point over {n_ops_steps} further steps after the "
                        "timed region; ms_per_step_timed_region: the rasterizer inside it"),
         "host_issue_ms_per_step": host_ms,
+        "host_blocked_ms_per_step": host_blocked_ms,
+        "host_reads_per_step": host_reads,
         "allocator": alloc,
         "host_cpus": len(os.sched_getaffinity(0)),
     }

@@ -264,7 +264,10 @@ __global__ void fill_i32_kernel(int32_t *p, uint32_t n, int32_t v) {
 #endif
 constexpr int kBucketShards = GSB_SHARDS; // global-memory path
 static_assert((kBucketShards & (kBucketShards - 1)) == 0, "shards: power of two");
-constexpr uint32_t kCtaBucketMax = 24576; // buckets of the shared-memory path (96 KiB)
+#ifndef GSB_CTA_BUCKET_MAX
+#define GSB_CTA_BUCKET_MAX 24576
+#endif
+constexpr uint32_t kCtaBucketMax = GSB_CTA_BUCKET_MAX; // buckets of the shared-memory path (96 KiB)
 #ifndef GSB_CTA_THREADS
 #define GSB_CTA_THREADS 1024
 #define GSB_CTAS_PER_SM 1

@@ -9,6 +9,7 @@ for the kernels.
 import ctypes
 import os
 import threading
+import time
 from typing import Optional
 
 import torch
@@ -216,6 +217,34 @@ def call(name: str, *args) -> int:
         msg = lib().gsb_last_error()
         raise RuntimeError(msg.decode() if msg else f"{name} failed with status {rc}")
     return rc
+
+
+# Optional accounting of the host time spent blocked in device-to-host reads of
+# sizes (the wrapper's only synchronising calls): when a two-element list
+# [seconds, reads] is installed here, read_back() adds to it.
+host_wait = None
+
+
+def read_back(t: torch.Tensor) -> list:
+    """``t.tolist()``: a blocking device-to-host read of a few values."""
+    if host_wait is None:
+        return t.tolist()
+    t0 = time.perf_counter()
+    out = t.tolist()
+    host_wait[0] += time.perf_counter() - t0
+    host_wait[1] += 1
+    return out
+
+
+def wait_event(ev) -> None:
+    """``ev.synchronize()``, accounted like read_back()."""
+    if host_wait is None:
+        ev.synchronize()
+        return
+    t0 = time.perf_counter()
+    ev.synchronize()
+    host_wait[0] += time.perf_counter() - t0
+    host_wait[1] += 1
 
 
 def ptr(t: Optional[torch.Tensor]):

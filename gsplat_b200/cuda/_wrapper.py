@@ -723,7 +723,7 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     call("gsb_isect_bucket_offsets", ptr(shard_counts), n_buckets, shards, ptr(offsets), ptr(bucket_sizes),
          ptr(cursor), ptr(nnz_device), ptr(totals), ptr(class_list), ptr(scratch), nbytes, stream)
-    n_isects, largest, nnz, mid_buckets, large_buckets = (int(v) for v in totals.tolist())
+    n_isects, largest, nnz, mid_buckets, large_buckets = (int(v) for v in _B.read_back(totals))
     if n_isects < 0 or nnz < 0:
         raise RuntimeError("isect_tiles: more than 2^31 - 1 tile intersections or splats")
     if nnz_device is None:
@@ -751,7 +751,7 @@ def _bucket_isect(args, I, tile_width, tile_height, tiles_per_gauss, dev, stream
          mid_buckets, large_buckets, ptr(class_list), ptr(bucket_entries), n_isects, ptr(split_scratch), nbytes,
          ptr(overflow), ptr(isect_ids), ptr(flatten_ids), stream)
     del bucket_entries, split_scratch
-    if not int(overflow.item()):
+    if not int(_B.read_back(overflow)[0]):
         return isect_ids, flatten_ids, offsets, nnz
     # a run of equal depths too large for the on-chip sort: emit in splat order
     # and sort globally (stable LSD radix sort)

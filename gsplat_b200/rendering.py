@@ -29,6 +29,7 @@ from .cuda._wrapper import (
     rasterize_to_pixels,
     spherical_harmonics,
 )
+from .cuda import _backend as _B
 from .cuda._backend import call, device_guard, ptr, stream_of
 from .distributed import (
     PeerExchange,
@@ -467,7 +468,7 @@ def rasterization(
         # peer-memory exchange: rows stored straight into the other GPUs'
         # buffers; the received count stays on the device and reaches the host
         # with the intersection sizes
-        n_world_event.synchronize()
+        _B.wait_event(n_world_event)
         # the local splat count, for meta: read with the intersection sizes
         local_nnz = torch.empty(1, dtype=torch.int64, pin_memory=True)
         local_nnz.copy_(nnz_device.reshape(1), non_blocking=True)
@@ -489,7 +490,7 @@ def rasterization(
         I = B * C
     elif distributed and packed and nnz_device is not None:
         send_buf = pack_rows(floats, ints, cap, rows_device=nnz_device)
-        sizes = torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]).tolist()
+        sizes = _B.read_back(torch.cat([send_cnt, recv_cnt, nnz_device.to(torch.int64)]))
         send_splits, recv_splits, nnz = sizes[:world_size], sizes[world_size:2 * world_size], sizes[-1]
         batch_ids, camera_ids, gaussian_ids = batch_ids[:nnz], camera_ids[:nnz], gaussian_ids[:nnz]
         _trim_local_meta(meta, nnz)
@@ -502,7 +503,7 @@ def rasterization(
         image_ids = camera_ids
         I = B * C
     elif distributed:
-        N_world = N_world_dev.tolist()
+        N_world = _B.read_back(N_world_dev)
         if packed:
             cnts = torch.bincount(camera_ids, minlength=C)
             cnts = cnts.split(C_world, dim=0)

@@ -382,6 +382,45 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     assert (shards == 16) == (mode == "many_buckets"), shards
 
 
+@pytest.mark.parametrize("case", ["dense", "packed_ordered", "packed_any", "large_images"])
+def test_isect_global_shards_multi_image_vs_oracle(case):
+    """Three images with more (image, tile) buckets than one CTA's shared memory
+    holds: the counts and cursors live in global memory, 16 shards per bucket
+    (splat idx in shard idx % 16). Dense splats, packed rows in image order and
+    in any order, and images of more tiles than one CTA's shared memory holds
+    must all give the oracle's stable global sort bit for bit (8 distinct depths,
+    so many ties between splats of one bucket)."""
+    from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
+
+    rng = np.random.default_rng(17)
+    I, W, H, N = 3, 320, 240, 4000
+    ts = 1 if case == "large_images" else 2
+    tw, th = math.ceil(W / ts), math.ceil(H / ts)
+    n = I * N
+    m2 = np.stack([rng.uniform(-20, W + 20, n), rng.uniform(-20, H + 20, n)], -1).astype(np.float32)
+    r = rng.integers(0, 6, (n, 2)).astype(np.int32)
+    dep = (rng.integers(1, 9, n) * 0.5).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(DEV)
+    if case in ("dense", "large_images"):
+        m2, r, dep = m2.reshape(I, N, 2), r.reshape(I, N, 2), dep.reshape(I, N)
+        tpg, keys, ids, off = isect_tiles_with_offsets(t(m2), t(r), t(dep), ts, tw, th)
+        etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th)
+    else:
+        iid = np.repeat(np.arange(I), N)
+        if case == "packed_any":
+            iid = rng.permutation(iid)
+        iid = iid.astype(np.int64)
+        tpg, keys, ids, off = isect_tiles_with_offsets(t(m2), t(r), t(dep), ts, tw, th, packed=True,
+                                                       n_images=I, image_ids=t(iid),
+                                                       gaussian_ids=t(np.arange(n)))
+        etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th, image_ids=iid, n_images=I)
+    assert I * tw * th > 24576 and gsb_lib().gsb_isect_bucket_shards(I, tw, th) == 16
+    assert_equal(tpg, etpg, "tiles_per_gauss")
+    assert_equal(keys, ekeys, "isect_ids")
+    assert_equal(ids, eids, "flatten_ids")
+    assert_equal(off, O.isect_offset_encode(ekeys, I, tw, th), "offsets")
+
+
 def gsb_lib():
     from gsplat_b200.cuda import _backend
 
