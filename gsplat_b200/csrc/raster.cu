@@ -46,6 +46,9 @@
 #ifndef GSB_RAST_INTERLEAVE
 #define GSB_RAST_INTERLEAVE 1
 #endif
+#ifndef GSB_RAST_PAIR
+#define GSB_RAST_PAIR 1
+#endif
 
 
 namespace gsb {
@@ -198,26 +201,94 @@ __device__ __forceinline__ float exp_neg_half(float x) {
 // non-contributing pair before the exponential; it is equivalent to alpha <
 // 1/255 up to the rounding of the two transcendental evaluations, and the exact
 // alpha test is still applied to the pairs that pass it.
+// Every operation of the evaluation is rounded explicitly (gx = b dy + (a dx),
+// gy = c dy + (b dx), 2 sigma = dy gy + (dx gx), each a fused multiply-add of a
+// rounded product), so the scalar form below and the paired form (two pixels
+// of one row through sm_100's two-wide FP32 instructions, whose halves round
+// like the scalar instructions) give the same bits for a pixel. The forward,
+// with two pixels of one row per thread, takes the paired form; the backward
+// the scalar one (measured: the paired form there evaluates pixel slots whose
+// quarter the splat misses and ran ~3% slower).
 struct PairEval {
     float dx, dy, gx, gy, vis, ov, alpha;
     bool keep;
 };
 
-__device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float py) {
-    PairEval e;
-    e.dx = r.x - px;
-    e.dy = r.y - py;
-    e.gx = r.a * e.dx + r.b * e.dy;
-    e.gy = r.b * e.dx + r.c * e.dy;
-    const float s2 = e.dx * e.gx + e.dy * e.gy; // 2 sigma
+__device__ __forceinline__ void finish_pair(const SplatRec &r, float s2, PairEval &e) {
     e.keep = s2 >= 0.f && s2 <= r.sig2_max;
     if (e.keep) {
         e.vis = exp_neg_half(s2);
-        e.ov = r.o * e.vis;
+        e.ov = __fmul_rn(r.o, e.vis);
         e.alpha = fminf(kMaxAlpha, e.ov);
         e.keep = e.alpha >= kAlphaThreshold;
     }
+}
+
+__device__ __forceinline__ PairEval eval_pair(const SplatRec &r, float px, float py) {
+    PairEval e;
+    e.dx = __fsub_rn(r.x, px);
+    e.dy = __fsub_rn(r.y, py);
+    e.gx = __fmaf_rn(r.b, e.dy, __fmul_rn(r.a, e.dx));
+    e.gy = __fmaf_rn(r.c, e.dy, __fmul_rn(r.b, e.dx));
+    finish_pair(r, __fmaf_rn(e.dy, e.gy, __fmul_rn(e.dx, e.gx)), e); // 2 sigma
     return e;
+}
+
+// Two-wide FP32 operations on a 64-bit register pair (lo, hi).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// A staged splat's fields duplicated into both halves, for the paired form.
+struct SplatPair {
+    uint64_t x, a, b, c;
+};
+__device__ __forceinline__ SplatPair splat_pair(const SplatRec &r) {
+    SplatPair q;
+    q.x = f2(r.x, r.x);
+    q.a = f2(r.a, r.a);
+    q.b = f2(r.b, r.b);
+    q.c = f2(r.c, r.c);
+    return q;
+}
+
+// eval_pair of the pixels (px.lo, py) and (px.hi, py) of one row.
+__device__ __forceinline__ void eval_pair2(const SplatRec &r, const SplatPair &q, uint64_t px, float py,
+                                           PairEval &e0, PairEval &e1) {
+    const float dy = __fsub_rn(r.y, py);
+    const uint64_t DY = f2(dy, dy);
+    const uint64_t DX = f2_sub(q.x, px);
+    const uint64_t GX = f2_fma(q.b, DY, f2_mul(q.a, DX));
+    const uint64_t GY = f2_fma(q.c, DY, f2_mul(q.b, DX));
+    const uint64_t S2 = f2_fma(DY, GY, f2_mul(DX, GX));
+    float s0, s1;
+    f2_split(DX, e0.dx, e1.dx);
+    f2_split(GX, e0.gx, e1.gx);
+    f2_split(GY, e0.gy, e1.gy);
+    f2_split(S2, s0, s1);
+    e0.dy = e1.dy = dy;
+    finish_pair(r, s0, e0);
+    finish_pair(r, s1, e1);
 }
 
 // ---------------------------------------------------------------------------
@@ -265,6 +336,8 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
     }
     const WarpRect wr = warp_rect(has, rx0, rx1, ry0, ry1);
     const float *bg = p.backgrounds ? p.backgrounds + (size_t)image * p.cstride + p.coff : nullptr;
+    constexpr bool kPairFwd = GSB_RAST_PAIR && PPT == 2 && BY == 1;
+    const uint64_t px01 = f2(px[0], px[PPT > 1 ? 1 : 0]);
 
     const size_t tile_flat = (size_t)image * p.tile_w * p.tile_h + tile;
     bool masked = p.masks != nullptr && !p.masks[tile_flat];
@@ -321,10 +394,19 @@ __global__ void __launch_bounds__(256) raster_fwd_kernel(RasterParams p) {
                 float col[CDIM];
 #pragma unroll
                 for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
+                if constexpr (kPairFwd) {
+                    // the thread's two pixels share a row: one paired evaluation
+                    const SplatPair sp = splat_pair(r);
+                    PairEval e0, e1;
+                    eval_pair2(r, sp, px01, py[0], e0, e1);
+                    if (!done[0]) apply(0, e0, i, col);
+                    if (!done[1]) apply(1, e1, i, col);
+                } else {
 #pragma unroll
-                for (int k = 0; k < PPT; ++k) {
-                    if (done[k]) continue;
-                    apply(k, eval_pair(r, px[k], py[k]), i, col);
+                    for (int k = 0; k < PPT; ++k) {
+                        if (done[k]) continue;
+                        apply(k, eval_pair(r, px[k], py[k]), i, col);
+                    }
                 }
             }
 
@@ -585,12 +667,8 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
             float col[CDIM];
 #pragma unroll
             for (int c = 0; c < CDIM; ++c) col[c] = s.colors[i * CDIM + c];
-#pragma unroll
-            for (int k = 0; k < PPT; ++k) {
-                if (IL && !(qmask & (1u << k))) continue;
-                if (gidx > bin_final[k]) continue;
-                const PairEval e = eval_pair(r, px[k], py[k]);
-                if (!e.keep) continue;
+            // the kept pair's contribution to the splat's sums and to pixel k's state
+            auto add_pair = [&](const int k, const PairEval &e) {
                 any = true;
 #if GSB_RAST_FAST_RCP
                 // approximate reciprocal, as the reference's default fast-math build
@@ -623,6 +701,14 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
                     }
                 }
                 S[k] += fac * cv;
+            };
+#pragma unroll
+            for (int k = 0; k < PPT; ++k) {
+                if (IL && !(qmask & (1u << k))) continue;
+                if (gidx > bin_final[k]) continue;
+                const PairEval e = eval_pair(r, px[k], py[k]);
+                if (!e.keep) continue;
+                add_pair(k, e);
             }
             if (!__any_sync(0xffffffffu, any)) continue;
             flush_splat_grads<CDIM, NV>(p, acc, lane, s.ids[i]);
