@@ -102,7 +102,7 @@ def _worker(rank, world, store_path, q, C=1):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_distributed_packed_matches_single_gpu(tmp_path, peer, cams, world, monkeypatch):
     """peer "1": the peer-memory exchange; "0": the NCCL all-to-all path; `cams`
-    cameras per rank (config 4 has 4 per rank at 8 GPUs); 2 or 4 ranks."""
+    cameras per rank (config 4 has 4 per rank at 8 GPUs); 2, 4 or 8 ranks."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     monkeypatch.setenv("GSB_PEER_EXCHANGE", peer)
