@@ -82,11 +82,21 @@ __device__ __forceinline__ LinePair ellipse_line(float A, float B, float C, floa
     return r;
 }
 
-// AccuTile sweep (IntersectTile.cu:54-126 and 195-253). Returns the number of
-// tiles; emits them when `sink` is non-null.
-template <bool EMIT, class Sink>
-__device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, float B, float C,
-                             float opacity, Sink *sink) {
+// AccuTile sweep (IntersectTile.cu:54-126 and 195-253), in two parts: the set-up
+// (level set, tile box, sweep direction) and the sweep over the box's columns.
+// After the set-up the sweep runs along x when is_y is false and along y
+// otherwise (the shorter side of the box, swapped into the *_x fields);
+// ellipse_line still takes the unswapped centre.
+struct TileSweep {
+    float A, B, C, disc, t, mx, my;
+    float bmin_x, bmax_x, bmin_y, bmax_y, amin_y, amax_y;
+    int rmin_x, rmax_x, rmin_y, rmax_y;
+    bool is_y;
+};
+
+// False when the splat's tile box is empty.
+__device__ __forceinline__ bool accutile_setup(const IsectParams &p, float mx, float my, float A, float B,
+                                               float C, float opacity, TileSweep &s) {
     const float disc = DET_SUB(DET_MUL(B, B), DET_MUL(A, C));
     const float t = det_fmin(kGaussianExtend * kGaussianExtend,
                              DET_MUL(2.0f, det_logf(DET_DIV(opacity, kAlphaThreshold))));
@@ -97,18 +107,17 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
     float bmax_x = DET_ADD(mx, x_ext), bmax_y = DET_ADD(my, y_ext);
     const float bxc = DET_DIV(DET_MUL(B, x_ext), C);
     const float bya = DET_DIV(DET_MUL(B, y_ext), A);
-    float amin_x = DET_ADD(my, bxc), amin_y = DET_ADD(mx, bya);
-    float amax_x = DET_SUB(my, bxc), amax_y = DET_SUB(mx, bya);
-    const float ts = (float)p.tile_size;
+    float amin_y = DET_ADD(mx, bya), amax_y = DET_SUB(mx, bya);
+    float amin_x = DET_ADD(my, bxc), amax_x = DET_SUB(my, bxc);
     const int tw = (int)p.tile_width, th = (int)p.tile_height;
     int rmin_x = max(0, min(tw, det_f2i_rz(tile_div(p, bmin_x))));
     int rmin_y = max(0, min(th, det_f2i_rz(tile_div(p, bmin_y))));
     int rmax_x = max(0, min(tw, det_f2i_rz(DET_ADD(tile_div(p, bmax_x), 1.f))));
     int rmax_y = max(0, min(th, det_f2i_rz(DET_ADD(tile_div(p, bmax_y), 1.f))));
     const int y_span = rmax_y - rmin_y, x_span = rmax_x - rmin_x;
-    if (y_span * x_span == 0) return 0;
-    const bool is_y = y_span < x_span;
-    if (is_y) {
+    if (y_span * x_span == 0) return false;
+    s.is_y = y_span < x_span;
+    if (s.is_y) {
         int ti;
         float tf;
         ti = rmin_x; rmin_x = rmin_y; rmin_y = ti;
@@ -118,31 +127,145 @@ __device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, 
         tf = amin_x; amin_x = amin_y; amin_y = tf;
         tf = amax_x; amax_x = amax_y; amax_y = tf;
     }
+    s.A = A;
+    s.B = B;
+    s.C = C;
+    s.disc = disc;
+    s.t = t;
+    s.mx = mx;
+    s.my = my;
+    s.bmin_x = bmin_x;
+    s.bmax_x = bmax_x;
+    s.bmin_y = bmin_y;
+    s.bmax_y = bmax_y;
+    s.amin_y = amin_y;
+    s.amax_y = amax_y;
+    s.rmin_x = rmin_x;
+    s.rmax_x = rmax_x;
+    s.rmin_y = rmin_y;
+    s.rmax_y = rmax_y;
+    return true;
+}
+
+__device__ __forceinline__ LinePair sweep_line(const TileSweep &s, float coord) {
+    return ellipse_line(s.A, s.B, s.C, s.disc, s.t, s.mx, s.my, s.is_y, coord);
+}
+
+// Tiles [v0, v1) of column u (absolute) between the lines min_line and
+// max_line with the level set's extents lo / hi on them.
+__device__ __forceinline__ void sweep_rows(const IsectParams &p, const TileSweep &s, float min_line,
+                                           float max_line, const LinePair &lo, const LinePair &hi, int &v0,
+                                           int &v1) {
+    const float emin = (min_line <= s.amin_y && s.amin_y < max_line) ? s.bmin_y : det_fmin(lo.lo, hi.lo);
+    const float emax = (min_line <= s.amax_y && s.amax_y < max_line) ? s.bmax_y : det_fmax(lo.hi, hi.hi);
+    v0 = max(s.rmin_y, min(s.rmax_y, det_f2i_rz(tile_div(p, emin))));
+    v1 = min(s.rmax_y, max(s.rmin_y, det_f2i_rz(DET_ADD(tile_div(p, emax), 1.f))));
+}
+
+__device__ __forceinline__ int64_t sweep_tile(const IsectParams &p, const TileSweep &s, int u, int v) {
+    const int tw = (int)p.tile_width;
+    return s.is_y ? (int64_t)u * tw + v : (int64_t)v * tw + u;
+}
+
+// The sequential sweep: each column's lower line is the previous column's
+// upper one. Returns the number of tiles; emits them when EMIT.
+template <bool EMIT, class Sink>
+__device__ uint32_t accutile_sweep(const IsectParams &p, const TileSweep &s, Sink *sink) {
+    const float ts = (float)p.tile_size;
     uint32_t count = 0;
-    LinePair cur_hi = {bmax_y, bmin_y};
-    float min_line = DET_MUL((float)rmin_x, ts);
-    LinePair cur_lo = (bmin_x <= min_line) ? ellipse_line(A, B, C, disc, t, mx, my, is_y, min_line)
-                                           : cur_hi;
-    for (int u = rmin_x; u < rmax_x; ++u) {
+    LinePair cur_hi = {s.bmax_y, s.bmin_y};
+    float min_line = DET_MUL((float)s.rmin_x, ts);
+    LinePair cur_lo = (s.bmin_x <= min_line) ? sweep_line(s, min_line) : cur_hi;
+    for (int u = s.rmin_x; u < s.rmax_x; ++u) {
         const float max_line = DET_ADD(min_line, ts);
-        if (max_line <= bmax_x) cur_hi = ellipse_line(A, B, C, disc, t, mx, my, is_y, max_line);
-        const float emin = (min_line <= amin_y && amin_y < max_line) ? bmin_y
-                                                                    : det_fmin(cur_lo.lo, cur_hi.lo);
-        const float emax = (min_line <= amax_y && amax_y < max_line) ? bmax_y
-                                                                    : det_fmax(cur_lo.hi, cur_hi.hi);
-        const int v0 = max(rmin_y, min(rmax_y, det_f2i_rz(tile_div(p, emin))));
-        const int v1 = min(rmax_y, max(rmin_y, det_f2i_rz(DET_ADD(tile_div(p, emax), 1.f))));
+        if (max_line <= s.bmax_x) cur_hi = sweep_line(s, max_line);
+        int v0, v1;
+        sweep_rows(p, s, min_line, max_line, cur_lo, cur_hi, v0, v1);
         if (v1 > v0) {
             count += (uint32_t)(v1 - v0);
             if (EMIT) {
-                for (int v = v0; v < v1; ++v)
-                    sink->put(is_y ? (int64_t)u * tw + v : (int64_t)v * tw + u);
+                for (int v = v0; v < v1; ++v) sink->put(sweep_tile(p, s, u, v));
             }
         }
         cur_lo = cur_hi;
         min_line = max_line;
     }
     return count;
+}
+
+template <bool EMIT, class Sink>
+__device__ uint32_t accutile(const IsectParams &p, float mx, float my, float A, float B, float C,
+                             float opacity, Sink *sink) {
+    TileSweep s;
+    if (!accutile_setup(p, mx, my, A, B, C, opacity, s)) return 0;
+    return accutile_sweep<EMIT, Sink>(p, s, sink);
+}
+
+// Column k (0-based) of the sweep on its own, with the values the sequential
+// sweep carries recomputed: its lines are (rmin_x + k) ts and (rmin_x + k + 1)
+// ts (the sequential sweep's repeated additions of ts are exact: integers below
+// 2^24), and the upper extent a column carries is that of the last line W + 1 <=
+// k + 1 with line(W + 1) <= bmax_x (the lines increase), or the box's corner
+// values {bmax_y, bmin_y} when there is none.
+__device__ __forceinline__ void accutile_column(const IsectParams &p, const TileSweep &s, int k, int &v0,
+                                                int &v1) {
+    const float ts = (float)p.tile_size;
+    const int ncol = s.rmax_x - s.rmin_x;
+    int W = ncol - 1; // largest w with line(w + 1) <= bmax_x, or -1
+    while (W >= 0 && !(DET_MUL((float)(s.rmin_x + W + 1), ts) <= s.bmax_x)) --W;
+    const LinePair corner = {s.bmax_y, s.bmin_y};
+    auto upper = [&](int j) -> LinePair { // the extent carried after column j
+        if (W < 0) return corner;
+        return sweep_line(s, DET_MUL((float)(s.rmin_x + min(j, W) + 1), ts));
+    };
+    const float min_line = DET_MUL((float)(s.rmin_x + k), ts);
+    const float max_line = DET_MUL((float)(s.rmin_x + k + 1), ts);
+    LinePair lo;
+    if (k == 0) lo = (s.bmin_x <= min_line) ? sweep_line(s, min_line) : corner;
+    else lo = upper(k - 1);
+    sweep_rows(p, s, min_line, max_line, lo, upper(k), v0, v1);
+}
+
+// Sweep of a splat by the whole warp (all 32 lanes call with the same s and
+// their own sink for that splat): each lane takes columns lane, lane + 32, ...;
+// a warp scan over the columns' tile counts then spreads the tiles evenly over
+// the lanes. Returns the splat's tile count (in every lane).
+template <bool EMIT, class Sink>
+__device__ uint32_t accutile_warp(const IsectParams &p, const TileSweep &s, Sink *sink) {
+    const int lane = (int)(threadIdx.x & 31u);
+    const int ncol = s.rmax_x - s.rmin_x;
+    uint32_t total = 0;
+    for (int cbase = 0; cbase < ncol; cbase += 32) {
+        const int k = cbase + lane;
+        int v0 = 0, v1 = 0;
+        if (k < ncol) accutile_column(p, s, k, v0, v1);
+        const int cnt = v1 > v0 ? v1 - v0 : 0;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const int excl = incl - cnt;
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        total += (uint32_t)tot;
+        if (EMIT) {
+            for (int tb = 0; tb < tot; tb += 32) {
+                const int t = tb + lane;
+                // column j of tile t: the number of lanes whose inclusive count is <= t
+                int j = 0;
+#pragma unroll
+                for (int step = 16; step > 0; step >>= 1) {
+                    const int val = __shfl_sync(0xffffffffu, incl, j + step - 1);
+                    if (val <= t) j += step;
+                }
+                const int ej = __shfl_sync(0xffffffffu, excl, j & 31);
+                const int vj = __shfl_sync(0xffffffffu, v0, j & 31);
+                if (t < tot) sink->put(sweep_tile(p, s, s.rmin_x + cbase + j, vj + (t - ej)));
+            }
+        }
+    }
+    return total;
 }
 
 template <bool EMIT, class Sink>
@@ -312,12 +435,14 @@ struct CountSink {
     __device__ __forceinline__ void put(int64_t tile_id) {
         atomicAdd(counts + (base + tile_id) * kBucketShards + shard, 1);
     }
+    __device__ __forceinline__ void flush() {}
 };
 
 struct SmemCountSink {
     int32_t *hist; // shared memory, one counter per bucket
     int64_t base;
     __device__ __forceinline__ void put(int64_t tile_id) { atomicAdd(hist + base + tile_id, 1); }
+    __device__ __forceinline__ void flush() {}
 };
 
 // Places one entry (depth bits << 32 | splat index) at the slot returned by an
@@ -368,6 +493,84 @@ __device__ __forceinline__ uint32_t n_splats(const IsectParams &p) {
     return n < 0 ? 0u : (n < (int64_t)p.nnz ? (uint32_t)n : p.nnz);
 }
 
+// Shared-memory (CTA) path: splats whose tile box holds more than this many
+// tiles are swept by their whole warp (accutile_warp) after the lanes' own
+// small splats, since one thread per splat leaves the warp waiting on its
+// largest splat (config 1: count 52 -> 39 us, emit 81 -> 68 us at 96; 8 and 32
+// were slower). The global-shard kernels keep one thread per splat: there the
+// warp sweep's registers (48 -> 80 for the batched-cursor emit) cost more
+// than it saved (config 4: emit 27.6 -> 32.7 ms).
+#ifndef GSB_WARP_SWEEP_TILES
+#define GSB_WARP_SWEEP_TILES 96
+#endif
+constexpr uint32_t kWarpSweepTiles = GSB_WARP_SWEEP_TILES;
+
+__device__ __forceinline__ TileSweep shfl_sweep(const TileSweep &s, int src) {
+    TileSweep w;
+    w.A = __shfl_sync(0xffffffffu, s.A, src);
+    w.B = __shfl_sync(0xffffffffu, s.B, src);
+    w.C = __shfl_sync(0xffffffffu, s.C, src);
+    w.disc = __shfl_sync(0xffffffffu, s.disc, src);
+    w.t = __shfl_sync(0xffffffffu, s.t, src);
+    w.mx = __shfl_sync(0xffffffffu, s.mx, src);
+    w.my = __shfl_sync(0xffffffffu, s.my, src);
+    w.bmin_x = __shfl_sync(0xffffffffu, s.bmin_x, src);
+    w.bmax_x = __shfl_sync(0xffffffffu, s.bmax_x, src);
+    w.bmin_y = __shfl_sync(0xffffffffu, s.bmin_y, src);
+    w.bmax_y = __shfl_sync(0xffffffffu, s.bmax_y, src);
+    w.amin_y = __shfl_sync(0xffffffffu, s.amin_y, src);
+    w.amax_y = __shfl_sync(0xffffffffu, s.amax_y, src);
+    w.rmin_x = __shfl_sync(0xffffffffu, s.rmin_x, src);
+    w.rmax_x = __shfl_sync(0xffffffffu, s.rmax_x, src);
+    w.rmin_y = __shfl_sync(0xffffffffu, s.rmin_y, src);
+    w.rmax_y = __shfl_sync(0xffffffffu, s.rmax_y, src);
+    w.is_y = __shfl_sync(0xffffffffu, (int)s.is_y, src) != 0;
+    return w;
+}
+
+// The tiles of splat idx of every lane (valid: the lane has a splat), counted
+// or emitted through sink_of(splat) -> Sink; called by all 32 lanes of the
+// warp. Returns the lane's splat's tile count.
+template <bool EMIT, class Sink, class SinkOf>
+__device__ __forceinline__ uint32_t splat_tiles_warp(const IsectParams &p, uint32_t idx, bool valid,
+                                                     SinkOf sink_of) {
+    uint32_t count = 0;
+    bool big = false;
+    TileSweep s;
+    if (valid) {
+        const int32_t rx = p.radii[(size_t)idx * 2], ry = p.radii[(size_t)idx * 2 + 1];
+        if (rx > 0 && ry > 0) {
+            const float mx = p.means2d[(size_t)idx * 2], my = p.means2d[(size_t)idx * 2 + 1];
+            if (p.conics != nullptr && p.opacities != nullptr) {
+                if (accutile_setup(p, mx, my, p.conics[(size_t)idx * 3], p.conics[(size_t)idx * 3 + 1],
+                                   p.conics[(size_t)idx * 3 + 2], p.opacities[idx], s)) {
+                    big = (uint32_t)(s.rmax_x - s.rmin_x) * (uint32_t)(s.rmax_y - s.rmin_y) > kWarpSweepTiles;
+                    if (!big) {
+                        Sink k = sink_of(idx);
+                        count = accutile_sweep<EMIT, Sink>(p, s, &k);
+                        k.flush();
+                    }
+                }
+            } else {
+                Sink k = sink_of(idx);
+                count = aabb_tiles<EMIT, Sink>(p, mx, my, rx, ry, &k);
+                k.flush();
+            }
+        }
+    }
+    uint32_t todo = __ballot_sync(0xffffffffu, big);
+    while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const TileSweep w = shfl_sweep(s, src);
+        Sink k = sink_of(__shfl_sync(0xffffffffu, idx, src));
+        const uint32_t c = accutile_warp<EMIT, Sink>(p, w, &k);
+        k.flush();
+        if ((int)(threadIdx.x & 31u) == src) count = c;
+    }
+    return count;
+}
+
 // global-memory shards
 __global__ void __launch_bounds__(256) isect_count_tiles_kernel(IsectParams p, int32_t *tiles_per_gauss,
                                                                 int32_t *shard_counts) {
@@ -392,11 +595,17 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_count_cta_ker
     const uint32_t chunk = (n + G - 1) / G;
     const uint32_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     const int64_t n_tiles = (int64_t)p.tile_width * p.tile_height;
-    for (uint32_t idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
-        SmemCountSink sink;
-        sink.hist = hist;
-        sink.base = splat_image(p, idx) * n_tiles;
-        tiles_per_gauss[idx] = (int32_t)splat_tiles<true, SmemCountSink>(p, idx, &sink);
+    // the same number of rounds for every thread: the warp sweep needs whole warps
+    for (uint32_t base = lo; base < hi; base += blockDim.x) {
+        const uint32_t idx = base + threadIdx.x;
+        const bool valid = idx < hi;
+        const uint32_t c = splat_tiles_warp<true, SmemCountSink>(p, idx, valid, [&](uint32_t i) {
+            SmemCountSink sink;
+            sink.hist = hist;
+            sink.base = splat_image(p, i) * n_tiles;
+            return sink;
+        });
+        if (valid) tiles_per_gauss[idx] = (int32_t)c;
     }
     __syncthreads();
     for (uint32_t b = threadIdx.x; b < n_buckets; b += blockDim.x) matrix[(size_t)b * G + blockIdx.x] = hist[b];
@@ -480,17 +689,19 @@ __global__ void __launch_bounds__(kCtaThreads, GSB_CTA_MINB) isect_emit_cta_kern
     const uint32_t chunk = (n + G - 1) / G;
     const uint32_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
     const int64_t n_tiles = (int64_t)p.tile_width * p.tile_height;
-    for (uint32_t idx = lo + threadIdx.x; idx < hi; idx += blockDim.x) {
-        BucketSink<1> sink;
-        sink.out = out;
-        sink.cursor = cur;
-        sink.base = splat_image(p, idx) * n_tiles;
-        sink.stride = 1;
-        sink.shard = 0;
-        sink.limit = n_isects;
-        sink.entry = ((uint64_t)det_f2u(p.depths[idx]) << 32) | idx;
-        splat_tiles<true, BucketSink<1>>(p, idx, &sink);
-        sink.flush();
+    for (uint32_t base = lo; base < hi; base += blockDim.x) {
+        const uint32_t idx = base + threadIdx.x;
+        splat_tiles_warp<true, BucketSink<1>>(p, idx, idx < hi, [&](uint32_t i) {
+            BucketSink<1> sink;
+            sink.out = out;
+            sink.cursor = cur;
+            sink.base = splat_image(p, i) * n_tiles;
+            sink.stride = 1;
+            sink.shard = 0;
+            sink.limit = n_isects;
+            sink.entry = ((uint64_t)det_f2u(p.depths[i]) << 32) | i;
+            return sink;
+        });
     }
 }
 

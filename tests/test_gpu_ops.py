@@ -382,6 +382,42 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     assert (shards == 16) == (mode == "many_buckets"), shards
 
 
+@pytest.mark.parametrize("images", [1, 2])
+def test_isect_large_splats_warp_sweep_vs_oracle(images):
+    """Splats covering up to several hundred tiles (AccuTile ellipses with sigma
+    up to 150 px): the ones whose tile box holds more than 96 tiles are swept by
+    their whole warp, column by column, in the shared-memory count and emit; the
+    tile sets, keys and order must equal the oracle's sequential sweep bit for
+    bit."""
+    from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
+
+    rng = np.random.default_rng(41 + images)
+    I, W, H, N, ts = images, 640, 480, 600, 16
+    tw, th = math.ceil(W / ts), math.ceil(H / ts)
+    m2 = np.stack([rng.uniform(-50, W + 50, (I, N)), rng.uniform(-50, H + 50, (I, N))], -1).astype(np.float32)
+    sig = rng.uniform(2.0, 150.0, (I, N, 2))
+    th_ = rng.uniform(0, np.pi, (I, N))
+    c, s_ = np.cos(th_), np.sin(th_)
+    # covariance R diag(sig^2) R^T, conic = its inverse (a, b, c)
+    sxx = c * c * sig[..., 0] ** 2 + s_ * s_ * sig[..., 1] ** 2
+    syy = s_ * s_ * sig[..., 0] ** 2 + c * c * sig[..., 1] ** 2
+    sxy = c * s_ * (sig[..., 0] ** 2 - sig[..., 1] ** 2)
+    det = sxx * syy - sxy * sxy
+    con = np.stack([syy / det, -sxy / det, sxx / det], -1).astype(np.float32)
+    op = rng.uniform(0.02, 1.0, (I, N)).astype(np.float32)
+    r = np.ceil(3.5 * sig.max(-1, keepdims=True)).repeat(2, -1).astype(np.int32)
+    dep = (rng.integers(1, 50, (I, N)) * 0.25).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(DEV)
+    tpg, keys, ids, off = isect_tiles_with_offsets(t(m2), t(r), t(dep), ts, tw, th, conics=t(con),
+                                                   opacities=t(op))
+    etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th, conics=con, opacities=op)
+    assert etpg.max() > 300 and (etpg > 96).sum() > 20  # many splats take the warp sweep
+    assert_equal(tpg, etpg, "tiles_per_gauss")
+    assert_equal(keys, ekeys, "isect_ids")
+    assert_equal(ids, eids, "flatten_ids")
+    assert_equal(off, O.isect_offset_encode(ekeys, I, tw, th), "offsets")
+
+
 @pytest.mark.parametrize("case", ["dense", "packed_ordered", "packed_any", "large_images"])
 def test_isect_global_shards_multi_image_vs_oracle(case):
     """Three images with more (image, tile) buckets than one CTA's shared memory
