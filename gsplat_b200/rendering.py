@@ -299,15 +299,18 @@ def rasterization(
             viewmats, Ks = all_gather_tensor_list(world_size, [viewmats, Ks])
         else:
             # one all-gather for the cameras and the Gaussian count of every rank
-            # (the int64 count travels bit-cast in two float32 slots)
+            # (the int64 count travels bit-cast in the first two float32 slots of
+            # each row; copied out before the bit-cast, since a one-row slice
+            # already counts as contiguous but keeps the odd row stride)
             n_bits = torch.full((C, 1), N, dtype=torch.int64, device=viewmats.device).view(torch.float32)
-            row = torch.cat([viewmats.reshape(C, 16).float(), Ks.reshape(C, 9).float(), n_bits],
+            row = torch.cat([n_bits, viewmats.reshape(C, 16).float(), Ks.reshape(C, 9).float()],
                             dim=1).contiguous()
             gathered = torch.empty((world_size * C, 27), dtype=row.dtype, device=row.device)
             torch.distributed.all_gather_into_tensor(gathered, row)
-            viewmats = gathered[:, :16].reshape(world_size * C, 4, 4).to(viewmats.dtype)
-            Ks = gathered[:, 16:25].reshape(world_size * C, 3, 3).to(Ks.dtype)
-            N_world_dev = gathered[::C, 25:27].contiguous().view(torch.int64).reshape(world_size)
+            viewmats = gathered[:, 2:18].reshape(world_size * C, 4, 4).to(viewmats.dtype)
+            Ks = gathered[:, 18:27].reshape(world_size * C, 3, 3).to(Ks.dtype)
+            N_world_dev = gathered[::C, 0:2].clone(memory_format=torch.contiguous_format).view(
+                torch.int64).reshape(world_size)
         C = len(viewmats)
         if packed and peer_exchange_available(device):
             # the Gaussian counts size the peer exchange: copied to pinned host

@@ -99,10 +99,11 @@ def _worker(rank, world, store_path, q, C=1):
 
 @pytest.mark.parametrize("peer", ["1", "0"])
 @pytest.mark.parametrize("cams", [1, 3])
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_distributed_packed_matches_single_gpu(tmp_path, peer, cams, world, monkeypatch):
     """peer "1": the peer-memory exchange; "0": the NCCL all-to-all path; `cams`
-    cameras per rank (config 4 has 4 per rank at 8 GPUs); 2, 4 or 8 ranks."""
+    cameras per rank (config 4 has 4 per rank at 8 GPUs); 1 (a process group of
+    one: the distributed path against the plain one), 2, 4 or 8 ranks."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     monkeypatch.setenv("GSB_PEER_EXCHANGE", peer)
