@@ -79,15 +79,20 @@ _SAMPLER_CHILD = r"""
 import sys, time
 import pynvml as N
 N.nvmlInit()
-key, period = sys.argv[1], float(sys.argv[2])
-h = N.nvmlDeviceGetHandleByUUID(key) if key.startswith("GPU-") else N.nvmlDeviceGetHandleByIndex(int(key))
-mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+keys, period = sys.argv[1].split(";"), float(sys.argv[2])
+hs = [N.nvmlDeviceGetHandleByUUID(k) if k.startswith("GPU-") else N.nvmlDeviceGetHandleByIndex(int(k))
+      for k in keys]
+mx = min(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM) for h in hs)
 reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or N.nvmlDeviceGetCurrentClocksThrottleReasons
 while True:
+    # one line per tick over all the job's GPUs: the lowest SM clock, the
+    # highest power draw and the union of the active reasons
     t = time.time()
-    sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
-    r = reasons(h)
-    p = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+    sm = min(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM) for h in hs)
+    r = 0
+    for h in hs:
+        r |= reasons(h)
+    p = max(N.nvmlDeviceGetPowerUsage(h) for h in hs) / 1000.0
     sys.stdout.write(f"{t:.4f},{sm},{mx},{p:.1f},{r}\n")
     sys.stdout.flush()
     time.sleep(period)
@@ -98,27 +103,37 @@ _REASON_BITS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowd
                 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
 
+def gpu_key(device):
+    """NVML key of a CUDA device: its UUID, else its index."""
+    import torch
+
+    props = torch.cuda.get_device_properties(device)
+    uuid = str(getattr(props, "uuid", ""))
+    return uuid if uuid.startswith("GPU-") else ("GPU-" + uuid if uuid else str(device.index or 0))
+
+
 class ClockSampler:
     """Samples SM clocks and clock-event (throttle) reasons while the benchmark
     runs: started before the warm-up, confirmed running (first sample received)
     before returning, and summarised over the samples taken inside a given host
-    time window (the timed region)."""
+    time window (the timed region). One child process samples all the given
+    GPUs (rank 0 samples the whole job's; the other ranks start none, which keeps
+    the host cores for the ranks' own work)."""
 
     PERIOD = 0.01
 
-    def __init__(self, device):
-        import torch
-
-        props = torch.cuda.get_device_properties(device)
-        uuid = str(getattr(props, "uuid", ""))
-        self.key = uuid if uuid.startswith("GPU-") else ("GPU-" + uuid if uuid else str(device.index or 0))
-        self.samples = []  # (time, sm_mhz, max_mhz, watts, reasons bitmask)
+    def __init__(self, keys):
+        self.keys = list(keys)
+        self.samples = []  # (time, lowest sm_mhz, max_mhz, highest watts, reasons bitmask)
         self.proc = None
         self.error = None
 
     def __enter__(self):
+        if not self.keys:
+            return self
         try:
-            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, self.key, str(self.PERIOD)],
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_CHILD, ";".join(self.keys),
+                                          str(self.PERIOD)],
                                          stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
         except OSError as e:
             self.error = str(e)
@@ -165,7 +180,9 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": inside[-1][2],
                 "power_w": statistics.median(s[3] for s in inside),
                 "reasons": sorted(n for b, n in _REASON_BITS.items() if mask & b),
-                "samples": len(inside), "source": "nvml", "window_s": round(t1 - t0, 4)}
+                "samples": len(inside), "gpus": len(self.keys), "source": "nvml",
+                "window_s": round(t1 - t0, 4),
+                "aggregate": "per sample: lowest SM clock, highest power, union of reasons over the GPUs"}
 
 
 def make_params(n, seed, dev, rank=0, world=1, workload="config1"):
@@ -600,7 +617,13 @@ def run_gsb(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    sampler = ClockSampler(dev)
+    # rank 0 samples every rank's GPU in one child process
+    keys = [gpu_key(dev)]
+    if distributed:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, keys[0])
+        keys = gathered
+    sampler = ClockSampler(keys if rank == 0 else [])
     sampler.__enter__()
     for _ in range(args.warmup):
         train_step(params, opt, viewmat, K, W, H, *grads(), distributed, packed, mode)
