@@ -64,3 +64,28 @@ def test_config4_shards_and_cameras():
 def test_reference_arm_samples_config1_only():
     lines = _bench("--impl", "reference", "--workload", "config4", "--steps", "1", "--warmup", "1")
     assert len(lines) == 1 and "unavailable" in json.loads(lines[0])
+
+
+def test_clock_summary_window_and_reasons():
+    """The clock record keeps the samples inside the timed window only, takes
+    the median of the per-sample lowest SM clock over the job's GPUs and the
+    union of the throttle reasons, which the bench line must report by name
+    (hw_slowdown etc. make a run invalid)."""
+    import bench
+
+    s = bench.ClockSampler(["GPU-a", "GPU-b"])
+    # (host time, lowest SM MHz over the GPUs, max MHz, highest watts, reasons bitmask)
+    s.samples = [(0.5, 900.0, 1965.0, 100.0, 0x8),  # before the window: ignored
+                 (1.0, 1965.0, 1965.0, 900.0, 0x0),
+                 (1.1, 1900.0, 1965.0, 950.0, 0x4),
+                 (1.2, 1965.0, 1965.0, 990.0, 0x0),
+                 (3.0, 500.0, 1965.0, 100.0, 0x40)]  # after the window: ignored
+    out = s.summary(1.0, 1.2)
+    assert out["samples"] == 3 and out["gpus"] == 2
+    assert out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0
+    assert out["power_w"] == 950.0
+    assert out["reasons"] == ["sw_power_cap"]
+    empty = bench.ClockSampler([])
+    empty.__enter__()
+    empty.__exit__(None, None, None)
+    assert empty.summary(0.0, 1.0)["samples"] == 0
