@@ -536,7 +536,7 @@ __device__ __forceinline__ uint32_t splat_tiles_warp(const IsectParams &p, uint3
                                                      SinkOf sink_of) {
     uint32_t count = 0;
     bool big = false;
-    TileSweep s;
+    TileSweep s{}; // lanes without a swept splat shuffle defined values
     if (valid) {
         const int32_t rx = p.radii[(size_t)idx * 2], ry = p.radii[(size_t)idx * 2 + 1];
         if (rx > 0 && ry > 0) {
