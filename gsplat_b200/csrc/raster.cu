@@ -51,6 +51,7 @@
 #endif
 
 
+
 namespace gsb {
 
 #ifndef GSB_RAST_BATCH
@@ -532,11 +533,11 @@ __device__ __forceinline__ void flush_splat_grads(const RasterParams &p, const f
 // (a warp-uniform branch: the quarter mask is computed once per splat and warp).
 //
 // Per pixel the backward keeps T (recovered back to front), S = buf . v_colour
-// (the colour behind the current splat, only ever needed dotted with the
-// upstream colour gradient), the upstream colour gradient, tv = T_final
-// (v_alpha - bg . v_colour) and the last contributor. With cv = colour . v_colour
-// the reference's v_alpha = sum_c (colour_c T - buf_c ra) v_c + ra tv becomes
-// T cv - ra (S - tv), and S grows by alpha T cv.
+// - tv (buf: the colour behind the current splat, only ever needed dotted with
+// the upstream colour gradient; tv = T_final (v_alpha - bg . v_colour), folded in
+// once), the upstream colour gradient and the last contributor. With cv =
+// colour . v_colour the reference's v_alpha = sum_c (colour_c T - buf_c ra) v_c
+// + ra tv becomes T cv - ra S, and S grows by alpha T cv.
 template <int CDIM, int BX, int BY, bool ABS, bool IL>
 __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? GSB_BWD_MINB : 8) : GSB_BWD_MINB_SMALL))
     raster_bwd_kernel(RasterParams p) {
@@ -580,7 +581,6 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
         // the pixel is nearly opaque: alpha = 0.9999 carries T to ~3e-4).
         const float Tf = inside ? (p.T_final ? p.T_final[pix] : 1.f - p.alphas[pix]) : 0.f;
         T[k] = Tf;
-        S[k] = 0.f;
         bin_final[k] = inside ? p.last_ids[pix] : -1;
         float dotbg = 0.f;
 #pragma unroll
@@ -590,6 +590,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
         }
         const float va = (inside && p.first_chunk) ? p.v_alphas[pix] : 0.f;
         tv[k] = Tf * (va - dotbg);
+        S[k] = -tv[k]; // S - tv, accumulated directly
         if (inside) {
             has = true;
             my_max = max(my_max, bin_final[k]);
@@ -684,9 +685,12 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
                     acc[c] += fac * vc[k][c];
                     cv += col[c] * vc[k][c];
                 }
-                const float v_alpha = T[k] * cv - ra * (S[k] - tv[k]);
-                if (e.ov <= kMaxAlpha) {
-                    const float w = e.ov * v_alpha; // -v_sigma
+                const float v_alpha = T[k] * cv - ra * S[k];
+                {
+                    // no gradient through the opacity and the footprint where the
+                    // alpha clamp is active (a select instead of a branch)
+                    const bool g = e.ov <= kMaxAlpha;
+                    const float w = g ? e.ov * v_alpha : 0.f; // -v_sigma
                     const float wx = w * e.dx, wy = w * e.dy;
                     acc[CDIM + 0] += wx * e.dx;
                     acc[CDIM + 1] += wx * e.dy;
@@ -694,7 +698,7 @@ __global__ void __launch_bounds__(256 / (BX * BY), (BX * BY >= 4 ? (CDIM <= 3 ? 
                     const float gx = w * e.gx, gy = w * e.gy;
                     acc[CDIM + 3] += gx;
                     acc[CDIM + 4] += gy;
-                    acc[CDIM + 5] += e.vis * v_alpha;
+                    acc[CDIM + 5] += (g ? e.vis : 0.f) * v_alpha;
                     if constexpr (ABS) {
                         acc[CDIM + 6] += fabsf(gx);
                         acc[CDIM + 7] += fabsf(gy);
