@@ -382,20 +382,22 @@ def test_isect_bucket_sort_ties_and_fallback_vs_oracle(mode):
     assert (shards == 16) == (mode == "many_buckets"), shards
 
 
-@pytest.mark.parametrize("images", [1, 2])
-def test_isect_large_splats_warp_sweep_vs_oracle(images):
-    """Splats covering up to several hundred tiles (AccuTile ellipses with sigma
-    up to 150 px): the ones whose tile box holds more than 96 tiles are swept by
-    their whole warp, column by column, in the shared-memory count and emit; the
-    tile sets, keys and order must equal the oracle's sequential sweep bit for
-    bit."""
+@pytest.mark.parametrize("images,W,H,sig_max", [(1, 640, 480, 150.0), (2, 640, 480, 150.0),
+                                                 (1, 1280, 960, 450.0)])
+def test_isect_large_splats_warp_sweep_vs_oracle(images, W, H, sig_max):
+    """Splats covering up to thousands of tiles (AccuTile ellipses with sigma up
+    to 150 or 450 px): the ones whose tile box holds more than 96 tiles are swept
+    by their whole warp, column by column (more than 32 columns, so several
+    rounds of the warp, in the 1280x960 case), in the shared-memory count and
+    emit; the tile sets, keys and order must equal the oracle's sequential sweep
+    bit for bit."""
     from gsplat_b200.cuda._wrapper import isect_tiles_with_offsets
 
-    rng = np.random.default_rng(41 + images)
-    I, W, H, N, ts = images, 640, 480, 600, 16
+    rng = np.random.default_rng(41 + images + W)
+    I, N, ts = images, 600, 16
     tw, th = math.ceil(W / ts), math.ceil(H / ts)
     m2 = np.stack([rng.uniform(-50, W + 50, (I, N)), rng.uniform(-50, H + 50, (I, N))], -1).astype(np.float32)
-    sig = rng.uniform(2.0, 150.0, (I, N, 2))
+    sig = rng.uniform(2.0, sig_max, (I, N, 2))
     th_ = rng.uniform(0, np.pi, (I, N))
     c, s_ = np.cos(th_), np.sin(th_)
     # covariance R diag(sig^2) R^T, conic = its inverse (a, b, c)
@@ -412,6 +414,8 @@ def test_isect_large_splats_warp_sweep_vs_oracle(images):
                                                    opacities=t(op))
     etpg, ekeys, eids = O.isect_tiles(m2, r, dep, ts, tw, th, conics=con, opacities=op)
     assert etpg.max() > 300 and (etpg > 96).sum() > 20  # many splats take the warp sweep
+    if W > 640:
+        assert etpg.max() > 33 * 33  # some sweep more than 32 columns
     assert_equal(tpg, etpg, "tiles_per_gauss")
     assert_equal(keys, ekeys, "isect_ids")
     assert_equal(ids, eids, "flatten_ids")
